@@ -1,0 +1,87 @@
+"""ctypes binding of the native library libmxmlp.so (C ABI in include/mxmlp.h).
+
+The library is required: importing this module raises ImportError when it is missing or does
+not load, and every call checks the returned status and raises RuntimeError with the library's
+message.  There is no CPU or Python fallback for any kernel.
+"""
+import ctypes
+import os
+
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libmxmlp.so")
+
+if not os.path.exists(LIB_PATH):
+    raise ImportError(f"MXFP8 native library not built: {LIB_PATH} is missing (run build.py)")
+try:
+    _lib = ctypes.CDLL(LIB_PATH)
+except OSError as e:  # pragma: no cover - depends on the machine
+    raise ImportError(f"MXFP8 native library failed to load: {e}") from e
+
+_vp, _i64, _int = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int
+
+# name -> argument types (all return int status unless listed in _RESTYPE)
+_SIGS = {
+    "mxm_version": [],
+    "mxm_last_error": [],
+    "mxm_device_error": [ctypes.POINTER(ctypes.c_int), _int],
+    "mxm_num_sms": [],
+    "mxm_quant_rows": [_vp, _i64, _i64, _i64, _vp, _i64, _vp, _vp],
+    "mxm_quant_cols": [_vp, _i64, _i64, _i64, _vp, _vp, _vp],
+    "mxm_quant_both": [_vp, _i64, _i64, _i64, _vp, _vp, _vp, _vp, _vp],
+    "mxm_gemm": [_vp, _i64, _vp, _vp, _i64, _vp, _i64, _i64, _i64, _vp, _i64, _vp],
+}
+_RESTYPE = {"mxm_last_error": ctypes.c_char_p}
+
+for _name, _args in _SIGS.items():
+    _f = getattr(_lib, _name)
+    _f.argtypes = _args
+    _f.restype = _RESTYPE.get(_name, ctypes.c_int)
+
+EXPORTED = tuple(_SIGS)
+
+
+class MXError(RuntimeError):
+    """A native call returned a non-zero status."""
+
+    def __init__(self, fn, status, msg):
+        super().__init__(f"{fn} failed (status {status}): {msg}")
+        self.status = status
+
+
+def last_error():
+    m = _lib.mxm_last_error()
+    return m.decode() if m else ""
+
+
+def call(name, *args):
+    st = getattr(_lib, name)(*args)
+    if st != 0:
+        raise MXError(name, st, last_error())
+    return st
+
+
+def version():
+    return _lib.mxm_version()
+
+
+def device_error(clear=True):
+    c = ctypes.c_int(0)
+    call("mxm_device_error", ctypes.byref(c), 1 if clear else 0)
+    return c.value
+
+
+def num_sms():
+    return _lib.mxm_num_sms()
+
+
+def ptr(t):
+    """Device pointer of a tensor (None -> NULL)."""
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def stream_of(t=None):
+    """The current torch CUDA stream handle for t's device, as a void*."""
+    dev = t.device if t is not None else None
+    return ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)

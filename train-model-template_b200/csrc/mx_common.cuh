@@ -1,0 +1,228 @@
+// Shared device helpers for the sm_100a MXFP8 kernels: number formats, the E8M0
+// round-up, mbarriers with bounded waits, TMA, and the tcgen05 (TMEM / UMMA) wrappers.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp8.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/mxmlp.h"
+
+#define MX_DEV __device__ __forceinline__
+
+// ------------------------------------------------------------------------------------------------
+// Device-side error flag: a bounded wait that runs out records where it gave up and the kernel
+// returns instead of hanging.  Kernels get the flag's address as an argument (mx_dev_error_ptr()
+// on the host); the host reads and clears it with mxm_device_error().
+
+enum MxDevError : int {
+  MX_DEV_OK = 0,
+  MX_DEV_TIMEOUT_PRODUCER = 1,
+  MX_DEV_TIMEOUT_MMA = 2,
+  MX_DEV_TIMEOUT_EPILOGUE = 3,
+  MX_DEV_TIMEOUT_MMA_TMEM = 4,
+};
+
+MX_DEV void mx_set_error(int* flag, int code) {
+  if (flag) atomicCAS(flag, 0, code);
+}
+
+MX_DEV uint64_t mx_globaltimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// ------------------------------------------------------------------------------------------------
+// Number formats.
+
+// E8M0 scale of a block: the power of two >= descale (round toward +inf), saturating to 254,
+// NaN -> 255.  One PTX instruction on sm_100a (cvt.rp.satfinite.ue8m0x2.f32).
+MX_DEV uint32_t mx_e8m0_rceil(float descale) {
+  uint16_t r;
+  asm("cvt.rp.satfinite.ue8m0x2.f32 %0, %1, %2;" : "=h"(r) : "f"(0.0f), "f"(descale));
+  return r & 0xFFu;
+}
+
+// Multiplier applied to the block before the E4M3 cast: 255 -> NaN, 254 -> 2^-127,
+// 0 -> 1.0, else 2^(127 - e).  2^(127-e) is built from its exponent bits (exact).
+MX_DEV float mx_e8m0_rcp(uint32_t e) {
+  if (e == 255u) return __int_as_float(0x7fffffff);
+  if (e == 254u) return __int_as_float(0x00400000);  // 2^-127 (subnormal)
+  if (e == 0u) return 1.0f;
+  return __int_as_float((int)((254u - e) << 23));
+}
+
+// Two floats (already clamped to [-448, 448], or NaN) -> two E4M3 codes, RNE.
+// NaN always becomes the canonical code 0x7F.
+MX_DEV uint16_t mx_e4m3x2(float lo, float hi) {
+  uint16_t r;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(hi), "f"(lo));
+  if (lo != lo) r = (uint16_t)((r & 0xFF00u) | 0x7Fu);
+  if (hi != hi) r = (uint16_t)((r & 0x00FFu) | 0x7F00u);
+  return r;
+}
+
+MX_DEV float mx_clamp448(float v) {
+  // fminf/fmaxf would drop a NaN; the block's NaN must survive to the cast.
+  return (v != v) ? v : fminf(fmaxf(v, -448.0f), 448.0f);
+}
+
+MX_DEV float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }
+MX_DEV float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
+MX_DEV float bf16_round_f(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
+MX_DEV uint32_t pack_bf16x2(float lo, float hi) {
+  __nv_bfloat162 p = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&p);
+}
+
+// |x| maximum that propagates NaN (amax of a block is NaN when the block holds a NaN).
+MX_DEV float mx_absmax_nan(float a, float b) {
+  float r = fmaxf(fabsf(a), fabsf(b));
+  return (a != a || b != b) ? __int_as_float(0x7fffffff) : r;
+}
+MX_DEV float mx_max_nan(float a, float b) {
+  return (a != a || b != b) ? __int_as_float(0x7fffffff) : fmaxf(a, b);
+}
+
+// Offset of the scale of (row r, 32-block kb) in the blocked 128x4 layout of a [*, cols] operand.
+MX_DEV __host__ int64_t mx_scale_offset(int64_t r, int64_t kb, int64_t cols) {
+  return ((r >> 7) * (cols >> 7) + (kb >> 2)) * 512 + (r & 31) * 16 + ((r & 127) >> 5) * 4 + (kb & 3);
+}
+
+// ------------------------------------------------------------------------------------------------
+// Shared-memory addresses, mbarriers.
+MX_DEV uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+MX_DEV void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+MX_DEV void fence_barrier_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+MX_DEV void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+MX_DEV void mbar_arrive(uint64_t* bar) {
+  asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" ::"r"(smem_u32(bar)) : "memory");
+}
+MX_DEV void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t}"
+               ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+MX_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity) : "memory");
+  return ok != 0;
+}
+
+// Waits for the phase with the given parity to complete.  Gives up after `limit_ns` of wall
+// time (globaltimer), records `err` and returns false: no wait in these kernels is unbounded.
+#ifndef MX_WAIT_LIMIT_NS
+#define MX_WAIT_LIMIT_NS 2000000000ull  // 2 s
+#endif
+MX_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, int* flag, int err) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = mx_globaltimer();
+  while (true) {
+    for (int i = 0; i < 64; ++i)
+      if (mbar_try_wait(bar, parity)) return true;
+    if (mx_globaltimer() - t0 > MX_WAIT_LIMIT_NS) {
+      mx_set_error(flag, err);
+      return false;
+    }
+  }
+}
+
+// ------------------------------------------------------------------------------------------------
+// TMA (no multicast anywhere in this project).
+MX_DEV void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int32_t x, int32_t y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+      ::"r"(smem_u32(dst)), "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar)) : "memory");
+}
+// Plain bulk copy global -> shared (both 16-byte aligned, size a multiple of 16).
+MX_DEV void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+               ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar)) : "memory");
+}
+MX_DEV void prefetch_tmap(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
+}
+
+// ------------------------------------------------------------------------------------------------
+// tcgen05: TMEM allocation, MMA, copies, loads.
+MX_DEV void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
+               "r"(ncols) : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+MX_DEV void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+MX_DEV void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+MX_DEV void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// Shared-memory matrix descriptor (sm_100 format, version 1).
+// layout: 0 none, 2 = 128B swizzle.  lbo / sbo in bytes.
+MX_DEV uint64_t make_sdesc(uint32_t saddr, uint32_t lbo, uint32_t sbo, uint32_t layout) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
+  d |= (uint64_t)1 << 46;  // version
+  d |= (uint64_t)(layout & 7u) << 61;
+  return d;
+}
+
+// Instruction descriptor for kind::mxf8f6f4 with E4M3 A/B, K-major A/B, UE8M0 scales.
+__host__ __device__ constexpr uint32_t mx_idesc(int M, int N, uint32_t sfa_id, uint32_t sfb_id) {
+  return ((sfb_id & 3u) << 4) | ((uint32_t)(N >> 3) << 17) | (1u << 23) | ((uint32_t)(M >> 4) << 24) |
+         ((sfa_id & 3u) << 29);
+}
+
+MX_DEV void umma_mxf8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t tsfa,
+                      uint32_t tsfb, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;\n\t}"
+      ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(tsfa), "r"(tsfb) : "memory");
+}
+// bf16 x bf16 -> fp32 MMA into the same kind of accumulator (kind::f16).
+MX_DEV void umma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+      ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate) : "memory");
+}
+MX_DEV void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+// 32 rows x 128 bits from shared memory into TMEM, replicated to all four lane quarters.
+MX_DEV void tmem_cp_32x128b_x4(uint32_t taddr, uint64_t sdesc) {
+  asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
+}
+
+// 32 lanes x 32 consecutive 32-bit columns -> 32 registers per thread.
+MX_DEV void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+MX_DEV void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+MX_DEV uint32_t lane_id() { return threadIdx.x & 31u; }
+MX_DEV bool elect_one() {
+  uint32_t pred = 0;
+  asm volatile(
+      "{\n\t.reg .b32 rx;\n\t.reg .pred px;\n\telect.sync rx|px, 0xffffffff;\n\tselp.u32 %0, 1, 0, px;\n\t}"
+      : "=r"(pred));
+  return pred != 0;
+}

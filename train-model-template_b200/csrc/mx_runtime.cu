@@ -1,0 +1,116 @@
+// Host runtime shared by all entry points: error strings, status plumbing, device queries and
+// the TMA tensor-map encoder (driver entry point fetched through the runtime, no -lcuda).
+#include <stdarg.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <mutex>
+
+#include "mx_runtime.h"
+
+__device__ int g_mx_dev_error = 0;
+
+static thread_local char t_err[512] = "";
+
+void mx_set_last_error(const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(t_err, sizeof(t_err), fmt, ap);
+  va_end(ap);
+}
+
+int mx_cuda_status(cudaError_t e, const char* what) {
+  if (e == cudaSuccess) return MXM_OK;
+  mx_set_last_error("%s: %s (%s)", what, cudaGetErrorString(e), cudaGetErrorName(e));
+  return MXM_ERR_CUDA;
+}
+
+int mx_launch_status(const char* what) { return mx_cuda_status(cudaGetLastError(), what); }
+
+int* mx_dev_error_ptr() {
+  static int* cache[64] = {nullptr};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  if (!cache[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_mx_dev_error) == cudaSuccess) cache[dev] = static_cast<int*>(p);
+  }
+  return cache[dev];
+}
+
+extern "C" int mxm_version(void) { return MXM_ABI_VERSION; }
+
+extern "C" const char* mxm_last_error(void) { return t_err; }
+
+extern "C" int mxm_device_error(int* code, int clear) {
+  if (!code) {
+    mx_set_last_error("mxm_device_error: null output pointer");
+    return MXM_ERR_ARG;
+  }
+  int v = 0;
+  int st = mx_cuda_status(cudaMemcpyFromSymbol(&v, g_mx_dev_error, sizeof(int)), "read device error flag");
+  if (st) return st;
+  *code = v;
+  if (clear && v) {
+    const int zero = 0;
+    st = mx_cuda_status(cudaMemcpyToSymbol(g_mx_dev_error, &zero, sizeof(int)), "clear device error flag");
+  }
+  return st;
+}
+
+extern "C" int mxm_num_sms(void) {
+  static int cache[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (!cache[dev]) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    cache[dev] = n;
+  }
+  return cache[dev];
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn get_encoder() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+int mx_make_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, uint32_t elem_bytes, const void* base,
+                    uint64_t inner, uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner,
+                    uint32_t box_outer, CUtensorMapSwizzle swizzle) {
+  EncodeTiledFn enc = get_encoder();
+  if (!enc) {
+    mx_set_last_error("cuTensorMapEncodeTiled unavailable from the driver");
+    return MXM_ERR_CUDA;
+  }
+  if (((uintptr_t)base & 15) || (row_stride_bytes & 15)) {
+    mx_set_last_error("TMA operand not 16-byte aligned (base %p, row stride %llu bytes)", base,
+                      (unsigned long long)row_stride_bytes);
+    return MXM_ERR_ARG;
+  }
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_stride_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  (void)elem_bytes;
+  CUresult r = enc(map, dtype, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    mx_set_last_error("cuTensorMapEncodeTiled failed (%d) for [%llu x %llu] box [%u x %u]", (int)r,
+                      (unsigned long long)outer, (unsigned long long)inner, box_outer, box_inner);
+    return MXM_ERR_CUDA;
+  }
+  return MXM_OK;
+}
