@@ -74,6 +74,65 @@ int mxm_quant_both(const void* x, int64_t R, int64_t K, int64_t ldx, void* q, vo
 int mxm_gemm(const void* qa, int64_t lda, const void* sa, const void* qb, int64_t ldb, const void* sb,
              int64_t M, int64_t N, int64_t K, void* d, int64_t ldd, void* stream);
 
+
+/* mxm_gemm with a rank-kr LoRA term added in the epilogue, with the reference's two roundings:
+ *   D = bf16( bf16(dq(A) dq(B)^T) + alpha * L[M, kr] . Rm[N, kr]^T )
+ * L row stride ldl (elements), Rm contiguous [N, kr], kr in {16, 32}.
+ * Replaces `y = _scaled_mm(...); y.addmm_(xS_down, B_down^T, alpha=s_down)` and
+ * `dx = _scaled_mm(...); dx.addmm_(dxa, S)` (scripts/fused_mlp.py:283-284, :329-331). */
+int mxm_gemm_lora(const void* qa, int64_t lda, const void* sa, const void* qb, int64_t ldb, const void* sb,
+                  int64_t M, int64_t N, int64_t K, const void* L, int64_t ldl, const void* Rm, int kr, float alpha,
+                  void* d, int64_t ldd, void* stream);
+
+/* Column-group count for mxm_mlp_fwd_epilogue (reference mlp_fwd grid choice, scripts/fused_mlp.py:203-204). */
+int mxm_mlp_fwd_partitions(int64_t T, int64_t N, int r, int* col_groups);
+
+/* Forward epilogue of the fused MLP (reference mlp_fwd / _fwd_kernel, scripts/fused_mlp.py:65-109,198-215):
+ *   g = bf16(gu[:, :N] + s_g xs[:, :r] bg^T), u = bf16(gu[:, N:] + s_u xs[:, r:2r] bu^T),
+ *   h = bf16(g / (exp(-g) + 1) * u);  qh, sh = MXFP8(h) (row-wise, blocked scales; skipped when qh is NULL);
+ *   xsd = bf16(h ad^T).
+ * gu bf16 [T, 2N], xs bf16 [T, 2r], bg / bu bf16 [N, r], ad bf16 [r, N], qh [T, N], sh blocked for [T, N],
+ * xsd bf16 [T, r].  xsd_part: fp32 [col_groups, T, r] scratch (unused when col_groups == 1). */
+int mxm_mlp_fwd_epilogue(const void* gu, const void* xs, const void* bg, const void* bu, const void* ad, int64_t T,
+                         int64_t N, int r, float s_g, float s_u, void* qh, void* sh, void* xsd, void* xsd_part,
+                         int col_groups, void* stream);
+
+/* Super-block rows and column-group count for the backward epilogue (reference _bwd_grid,
+ * scripts/fused_mlp.py:218-232). */
+int mxm_mlp_bwd_partitions(int64_t T, int64_t N, int r, int* super_block, int* col_groups);
+
+/* Backward epilogue of the fused MLP (reference mlp_bwd / _bwd_kernel, scripts/fused_mlp.py:112-175,235-259).
+ * Recomputes g, u, h from gu; dh = bf16(dhm + dxd ad); du = bf16(dh silu(g)); dg = bf16(dh u sig (g (1-sig) + 1));
+ * q / s = MXFP8([dg | du]) [T, 2N] (skipped when q is NULL).  Partial sums (fp32, fixed-order reduction in
+ * mxm_mlp_bwd_reduce): dxa_part [col_groups, T, 3r] = [dg bg | du bu | h ad^T];
+ * dbg_part / dbu_part [n_super, N, r] = dg^T xa_g / du^T xa_u; dad_part [n_super, r, N] = dxd^T h,
+ * n_super = ceil(ceil128(T) / super_block). */
+int mxm_mlp_bwd_epilogue(const void* gu, const void* xs, const void* dhm, const void* dxd, const void* bg,
+                         const void* bu, const void* ad, int64_t T, int64_t N, int r, float s_g, float s_u, void* q,
+                         void* s, void* dxa_part, void* dbg_part, void* dbu_part, void* dad_part, int super_block,
+                         int col_groups, void* stream);
+
+/* Fixed-order reduction of the backward partials (scripts/fused_mlp.py:258-259,316-326):
+ * dxa bf16 [T, 2r] = [s_g sum(dxa_g) | s_u sum(dxa_u)], xsd bf16 [T, r] = sum(xS_down),
+ * dBg / dBu fp32 [N, r] = s_g / s_u times the sums, dAd fp32 [r, N]. */
+int mxm_mlp_bwd_reduce(const void* dxa_part, const void* dbg_part, const void* dbu_part, const void* dad_part,
+                       int64_t T, int64_t N, int r, float s_g, float s_u, int super_block, int col_groups, void* dxa,
+                       void* xsd, void* dBg, void* dBu, void* dAd, void* stream);
+
+/* out[T, n] = bf16( bf16(A[T, K] B[n, K]^T) * post ) (post == 1: one rounding); n in {16, 32}, K % 32 == 0.
+ * The rank-n LoRA-A products: xs = x S^T and dxd = s_d (dy B_down) (scripts/fused_mlp.py:277,311-313). */
+int mxm_rowdot(const void* A, int64_t lda, const void* B, int64_t T, int64_t K, int n, float post, void* out,
+               int64_t ldo, void* stream);
+
+/* Row chunking (rows per chunk, number of chunks) of mxm_coldot's partial buffer for a [T, K] operand. */
+int mxm_coldot_chunks(int64_t T, int64_t K, int* rows_per_chunk, int* chunks);
+
+/* out = bf16( bf16(A[T, K]^T E[T, n]) * post ), written [K, n] (or [n, K] when transpose_out).
+ * part: fp32 [chunks, K, n] scratch.  K % 64 == 0, n in {16, 32}.
+ * The LoRA weight gradients dA = dxa^T x and dB_down = s_d (dy^T xS_down) (scripts/fused_mlp.py:316-318,333). */
+int mxm_coldot(const void* A, int64_t lda, const void* E, int64_t lde, int64_t T, int64_t K, int n, float post,
+               int transpose_out, void* part, int rows_per_chunk, int chunks, void* out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

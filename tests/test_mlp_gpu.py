@@ -1,0 +1,133 @@
+"""Fused MXFP8 SwiGLU-LoRA MLP on the GPU vs the reference golden fixture and the CPU oracle.
+
+Parity bar (BASELINE): forward outputs and LoRA gradients within a relative Frobenius error of 5e-3
+of the dequantize-then-fp32-matmul oracle; MXFP8 codes / scales of h and [dg | du] byte-identical
+except where exp() differs by an ulp between CUDA and numpy (a bounded, tiny fraction).
+"""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import mx_oracle as O
+
+pytestmark = pytest.mark.gpu
+TOL = 5e-3
+G = os.path.join(os.path.dirname(__file__), "golden")
+NAMES = ("dAg", "dBg", "dAu", "dBu", "dAd", "dBd")
+
+
+def _bits_to_t(b):
+    return torch.from_numpy(np.ascontiguousarray(b).view(np.int16)).view(torch.bfloat16)
+
+
+def _run(x, Wg, Wu, Wd, lora, dy, s, need_out=True):
+    import fused_mlp
+    dev = torch.device("cuda")
+    layer = fused_mlp.MXMLPWeights.from_bf16(Wg.to(dev), Wu.to(dev), Wd.to(dev))
+    params = [p.to(dev).clone().requires_grad_(True) for p in lora]
+    xd = x.to(dev).clone().requires_grad_(True)
+    y = fused_mlp.mlp_apply(layer, xd, *params, scaling=(s, s, s), need_out=need_out)
+    y.backward(dy.to(dev))
+    torch.cuda.synchronize()
+    import _mxlib
+    assert _mxlib.device_error() == 0
+    return y.detach().float().cpu(), xd.grad.float().cpu(), [p.grad.float().cpu() for p in params]
+
+
+def _case(T, H, N, r, seed, outlier=0.0):
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(T, H, generator=g)
+    if outlier:
+        x = torch.where(torch.rand(T, H, generator=g) < 0.01, x * outlier, x)
+    x = x.to(torch.bfloat16)
+    Wg = (torch.randn(N, H, generator=g) * 0.02).to(torch.bfloat16)
+    Wu = (torch.randn(N, H, generator=g) * 0.02).to(torch.bfloat16)
+    Wd = (torch.randn(H, N, generator=g) * 0.02).to(torch.bfloat16)
+    lora = [torch.randn(*sh, generator=g) * 0.01 for sh in ((r, H), (N, r), (r, H), (N, r), (r, N), (H, r))]
+    dy = torch.randn(T, H, generator=g).to(torch.bfloat16)
+    return x, Wg, Wu, Wd, lora, dy
+
+
+def _oracle(x, Wg, Wu, Wd, lora, dy, s):
+    W = O.MXWeights(Wg.float().numpy(), Wu.float().numpy(), Wd.float().numpy())
+    yo, ctx = O.mlp_forward(x.float().numpy(), W, *[p.numpy() for p in lora], s, s, s)
+    go = O.mlp_backward(dy.float().numpy(), ctx)
+    return yo, go, ctx
+
+
+def test_mlp_vs_reference_golden():
+    z = np.load(os.path.join(G, "mlp_golden.npz"))
+    x, dy = _bits_to_t(z["x"]), _bits_to_t(z["dy"])
+    Wg, Wu, Wd = (_bits_to_t(z[k]) for k in ("Wg", "Wu", "Wd"))
+    lora = [torch.from_numpy(z[k]) for k in ("Ag", "Bg", "Au", "Bu", "Ad", "Bd")]
+    s = float(z["alpha"]) / float(z["r"])
+    y, dx, grads = _run(x, Wg, Wu, Wd, lora, dy, s)
+    assert O.rel_fro(y.numpy(), O.bf16_bits_to_f32(z["y"])) < TOL
+    assert O.rel_fro(dx.numpy(), O.bf16_bits_to_f32(z["dx"])) < TOL
+    for gr, k in zip(grads, NAMES):
+        assert O.rel_fro(gr.numpy(), z[k]) < TOL, k
+
+
+@pytest.mark.parametrize("T", [512, 1, 77, 1000, 2049])
+def test_mlp_08b_shape_vs_oracle(T):
+    """0.8B MLP shape (hidden 1024, intermediate 3584, r 16, alpha 32), ragged token counts."""
+    H, N, r, s = 1024, 3584, 16, 2.0
+    case = _case(T, H, N, r, seed=T, outlier=100.0 if T != 512 else 0.0)
+    y, dx, grads = _run(*case, s)
+    yo, go, _ = _oracle(*case, s)
+    assert O.rel_fro(y.numpy(), yo) < TOL
+    assert O.rel_fro(dx.numpy(), go["dx"]) < TOL
+    for gr, k in zip(grads, NAMES):
+        assert O.rel_fro(gr.numpy(), go[k]) < TOL, (k, O.rel_fro(gr.numpy(), go[k]))
+
+
+def test_mlp_rank32():
+    T, H, N, r, s = 300, 512, 1024, 32, 1.0
+    case = _case(T, H, N, r, seed=5)
+    y, dx, grads = _run(*case, s)
+    yo, go, _ = _oracle(*case, s)
+    assert O.rel_fro(y.numpy(), yo) < TOL
+    assert O.rel_fro(dx.numpy(), go["dx"]) < TOL
+    for gr, k in zip(grads, NAMES):
+        assert O.rel_fro(gr.numpy(), go[k]) < TOL, k
+
+
+def test_epilogue_bytes_vs_oracle():
+    """h's and [dg | du]'s MXFP8 bytes from the CUDA epilogues vs the oracle on the same gu / dh."""
+    import fused_mlp
+    T, H, N, r, s = 333, 512, 1024, 16, 2.0
+    x, Wg, Wu, Wd, lora, dy = _case(T, H, N, r, seed=11)
+    yo, go, ctx = _oracle(x, Wg, Wu, Wd, lora, dy, s)
+    dev = torch.device("cuda")
+    bf = lambda a: torch.from_numpy(a).to(torch.bfloat16).to(dev)  # noqa: E731
+    gu, xs = bf(ctx["gu"]), bf(ctx["xs"])
+    bg, bu, ad = bf(ctx["bg"]), bf(ctx["bu"]), bf(ctx["ad"])
+    qh, sh, xsd = fused_mlp.mlp_fwd(gu, xs, bg, bu, ad, s, s, True)
+    torch.cuda.synchronize()
+    dq = (qh.view(torch.uint8).cpu().numpy() != ctx["qh"]).mean()
+    ds = (sh.view(torch.uint8).cpu().numpy() != ctx["sh"]).mean()
+    assert dq < 1e-3 and ds < 1e-3, (dq, ds)
+    assert O.rel_fro(xsd.float().cpu().numpy(), ctx["xsd"]) < 2e-3
+    q, sc, dxa, dbg, dbu, dad = fused_mlp.mlp_bwd(gu, xs, bf(go["dhm"]), bf(go["dxd"]), bg, bu, ad, s, s, True)
+    torch.cuda.synchronize()
+    dq = (q.view(torch.uint8).cpu().numpy() != go["q_dgu"]).mean()
+    ds = (sc.view(torch.uint8).cpu().numpy() != go["s_dgu"]).mean()
+    assert dq < 1e-3 and ds < 1e-3, (dq, ds)
+    assert O.rel_fro(dbg.cpu().numpy() * s, go["dBg"]) < 2e-3
+    assert O.rel_fro(dbu.cpu().numpy() * s, go["dBu"]) < 2e-3
+    assert O.rel_fro(dad.cpu().numpy(), go["dAd"]) < 2e-3
+
+
+def test_need_out_false_and_determinism():
+    """need_out=False (checkpoint recompute) gives the same gradients; two runs are bitwise equal."""
+    T, H, N, r, s = 640, 1024, 3584, 16, 2.0
+    case = _case(T, H, N, r, seed=9)
+    y1, dx1, g1 = _run(*case, s)
+    y2, dx2, g2 = _run(*case, s)
+    assert torch.equal(y1, y2) and torch.equal(dx1, dx2)
+    assert all(torch.equal(a, b) for a, b in zip(g1, g2))
+    _, dx3, g3 = _run(*case, s, need_out=False)
+    assert torch.equal(dx1, dx3)
+    assert all(torch.equal(a, b) for a, b in zip(g1, g3))

@@ -31,6 +31,19 @@ _SIGS = {
     "mxm_quant_cols": [_vp, _i64, _i64, _i64, _vp, _vp, _vp],
     "mxm_quant_both": [_vp, _i64, _i64, _i64, _vp, _vp, _vp, _vp, _vp],
     "mxm_gemm": [_vp, _i64, _vp, _vp, _i64, _vp, _i64, _i64, _i64, _vp, _i64, _vp],
+    "mxm_gemm_lora": [_vp, _i64, _vp, _vp, _i64, _vp, _i64, _i64, _i64, _vp, _i64, _vp, _int, ctypes.c_float,
+                      _vp, _i64, _vp],
+    "mxm_mlp_fwd_partitions": [_i64, _i64, _int, ctypes.POINTER(ctypes.c_int)],
+    "mxm_mlp_fwd_epilogue": [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _int, ctypes.c_float, ctypes.c_float, _vp, _vp,
+                             _vp, _vp, _int, _vp],
+    "mxm_mlp_bwd_partitions": [_i64, _i64, _int, ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_int)],
+    "mxm_mlp_bwd_epilogue": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _int, ctypes.c_float, ctypes.c_float,
+                             _vp, _vp, _vp, _vp, _vp, _vp, _int, _int, _vp],
+    "mxm_mlp_bwd_reduce": [_vp, _vp, _vp, _vp, _i64, _i64, _int, ctypes.c_float, ctypes.c_float, _int, _int, _vp,
+                           _vp, _vp, _vp, _vp, _vp],
+    "mxm_rowdot": [_vp, _i64, _vp, _i64, _i64, _int, ctypes.c_float, _vp, _i64, _vp],
+    "mxm_coldot_chunks": [_i64, _i64, ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_int)],
+    "mxm_coldot": [_vp, _i64, _vp, _i64, _i64, _i64, _int, ctypes.c_float, _int, _vp, _int, _int, _vp, _vp],
 }
 _RESTYPE = {"mxm_last_error": ctypes.c_char_p}
 
@@ -74,6 +87,11 @@ def device_error(clear=True):
 
 def num_sms():
     return _lib.mxm_num_sms()
+
+
+def ctypes_ref(x):
+    """ctypes.byref, for the entry points that return values through int pointers."""
+    return ctypes.byref(x)
 
 
 def ptr(t):

@@ -43,10 +43,15 @@ struct __align__(8) Bars {
 
 constexpr size_t SMEM_BYTES = 1024 /*align slack*/ + STAGES * (A_BYTES + B_BYTES + SFA_BYTES + SFB_BYTES) + sizeof(Bars);
 
+// Epilogue variants: KR == 0 stores bf16(acc); KR in {16, 32} adds a rank-KR LoRA term with the
+// reference's two roundings: out = bf16( bf16(acc) + alpha * sum_j L[row, j] Rm[col, j] ), which is
+// `y = _scaled_mm(...); y.addmm_(L, Rm^T, alpha=alpha)` (scripts/fused_mlp.py:283-284, :329-331).
+template <int KR>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     k_mx_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
               const uint8_t* __restrict__ sa, const uint8_t* __restrict__ sb, int M, int N, int K,
-              __nv_bfloat16* __restrict__ D, int64_t ldd, int* err) {
+              __nv_bfloat16* __restrict__ D, int64_t ldd, const __nv_bfloat16* __restrict__ L, int64_t ldl,
+              const __nv_bfloat16* __restrict__ Rm, float alpha, int* err) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
@@ -159,20 +164,50 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       tc_fence_after();
       const int64_t row = (int64_t)tm * BM + q * 32 + lane;
       __nv_bfloat16* drow = D + row * ldd + (int64_t)tn * BN;
+      float lr[KR > 0 ? KR : 1];
+      if constexpr (KR > 0) {
+#pragma unroll
+        for (int j = 0; j < KR; j += 8) {
+          uint4 u = row < M ? __ldg(reinterpret_cast<const uint4*>(L + row * ldl + j)) : make_uint4(0u, 0u, 0u, 0u);
+          lr[j + 0] = bf16_lo(u.x); lr[j + 1] = bf16_hi(u.x);
+          lr[j + 2] = bf16_lo(u.y); lr[j + 3] = bf16_hi(u.y);
+          lr[j + 4] = bf16_lo(u.z); lr[j + 5] = bf16_hi(u.z);
+          lr[j + 6] = bf16_lo(u.w); lr[j + 7] = bf16_hi(u.w);
+        }
+      }
 #pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
         uint32_t r[32];
         tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + ACC_COL + c * 32, r);
         tmem_ld_wait();
+        float v[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+        if constexpr (KR > 0) {
+          const __nv_bfloat16* rc = Rm + ((int64_t)tn * BN + c * 32) * KR;
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            float dot = 0.f;
+#pragma unroll
+            for (int j = 0; j < KR; j += 8) {
+              const uint4 u = __ldg(reinterpret_cast<const uint4*>(rc + i * KR + j));
+              dot = fmaf(lr[j + 0], bf16_lo(u.x), dot); dot = fmaf(lr[j + 1], bf16_hi(u.x), dot);
+              dot = fmaf(lr[j + 2], bf16_lo(u.y), dot); dot = fmaf(lr[j + 3], bf16_hi(u.y), dot);
+              dot = fmaf(lr[j + 4], bf16_lo(u.z), dot); dot = fmaf(lr[j + 5], bf16_hi(u.z), dot);
+              dot = fmaf(lr[j + 6], bf16_lo(u.w), dot); dot = fmaf(lr[j + 7], bf16_hi(u.w), dot);
+            }
+            v[i] = bf16_round_f(v[i]) + alpha * dot;
+          }
+        }
         if (row < M) {
           uint4* dst = reinterpret_cast<uint4*>(drow + c * 32);
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
             uint4 o;
-            o.x = pack_bf16x2(__uint_as_float(r[8 * j + 0]), __uint_as_float(r[8 * j + 1]));
-            o.y = pack_bf16x2(__uint_as_float(r[8 * j + 2]), __uint_as_float(r[8 * j + 3]));
-            o.z = pack_bf16x2(__uint_as_float(r[8 * j + 4]), __uint_as_float(r[8 * j + 5]));
-            o.w = pack_bf16x2(__uint_as_float(r[8 * j + 6]), __uint_as_float(r[8 * j + 7]));
+            o.x = pack_bf16x2(v[8 * j + 0], v[8 * j + 1]);
+            o.y = pack_bf16x2(v[8 * j + 2], v[8 * j + 3]);
+            o.z = pack_bf16x2(v[8 * j + 4], v[8 * j + 5]);
+            o.w = pack_bf16x2(v[8 * j + 6], v[8 * j + 7]);
             dst[j] = o;
           }
         }
@@ -189,19 +224,21 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   if (warp == 2) tmem_dealloc(tmem, TMEM_COLS);
 }
 
-}  // namespace
-
-extern "C" int mxm_gemm(const void* qa, int64_t lda, const void* sa, const void* qb, int64_t ldb, const void* sb,
-                        int64_t M, int64_t N, int64_t K, void* d, int64_t ldd, void* stream) {
-  MX_CHECK_ARG(qa && sa && qb && sb && d, "mxm_gemm: null pointer");
-  MX_CHECK_ARG(M >= 1 && M < (1ll << 31), "mxm_gemm: M=%lld out of range", (long long)M);
-  MX_CHECK_ARG(N >= BN && N % BN == 0 && N < (1ll << 31), "mxm_gemm: N=%lld must be a multiple of %d", (long long)N,
-               BN);
-  MX_CHECK_ARG(K >= BK && K % BK == 0 && K < (1ll << 31), "mxm_gemm: K=%lld must be a multiple of %d", (long long)K,
-               BK);
-  MX_CHECK_ARG(lda >= K && ldb >= K && lda % 16 == 0 && ldb % 16 == 0, "mxm_gemm: lda/ldb must be >= K and 16-aligned");
-  MX_CHECK_ARG(ldd >= N && ldd % 8 == 0 && mx_aligned(d, 16), "mxm_gemm: output stride/alignment");
-  MX_CHECK_ARG(mx_aligned(sa, 16) && mx_aligned(sb, 16), "mxm_gemm: scale buffers must be 16-byte aligned");
+int gemm_launch(const void* qa, int64_t lda, const void* sa, const void* qb, int64_t ldb, const void* sb,
+                       int64_t M, int64_t N, int64_t K, void* d, int64_t ldd, const void* L, int64_t ldl,
+                       const void* Rm, int kr, float alpha, void* stream, const char* fn) {
+  MX_CHECK_ARG(qa && sa && qb && sb && d, "%s: null pointer", fn);
+  MX_CHECK_ARG(M >= 1 && M < (1ll << 31), "%s: M=%lld out of range", fn, (long long)M);
+  MX_CHECK_ARG(N >= BN && N % BN == 0 && N < (1ll << 31), "%s: N=%lld must be a multiple of %d", fn, (long long)N, BN);
+  MX_CHECK_ARG(K >= BK && K % BK == 0 && K < (1ll << 31), "%s: K=%lld must be a multiple of %d", fn, (long long)K, BK);
+  MX_CHECK_ARG(lda >= K && ldb >= K && lda % 16 == 0 && ldb % 16 == 0, "%s: lda/ldb must be >= K and 16-aligned", fn);
+  MX_CHECK_ARG(ldd >= N && ldd % 8 == 0 && mx_aligned(d, 16), "%s: output stride/alignment", fn);
+  MX_CHECK_ARG(mx_aligned(sa, 16) && mx_aligned(sb, 16), "%s: scale buffers must be 16-byte aligned", fn);
+  if (kr) {
+    MX_CHECK_ARG(kr == 16 || kr == 32, "%s: LoRA rank must be 16 or 32", fn);
+    MX_CHECK_ARG(L && Rm && ldl >= kr && ldl % 8 == 0 && mx_aligned(L, 16) && mx_aligned(Rm, 16),
+                 "%s: LoRA operands must be 16-byte aligned with row stride %% 8 == 0", fn);
+  }
 
   CUtensorMap tmA, tmB;
   if (int st = mx_make_tmap_2d(&tmA, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, qa, (uint64_t)K, (uint64_t)M, (uint64_t)lda, BK,
@@ -211,18 +248,41 @@ extern "C" int mxm_gemm(const void* qa, int64_t lda, const void* sa, const void*
                                BN, CU_TENSOR_MAP_SWIZZLE_128B))
     return st;
 
-  static bool attr_done[64] = {false};
+  static bool attr_done[3][64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && !attr_done[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(k_mx_gemm, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES);
-    if (e != cudaSuccess) return mx_cuda_status(e, "mxm_gemm: set smem");
-    attr_done[dev] = true;
+  const int vi = kr == 0 ? 0 : (kr == 16 ? 1 : 2);
+  const void* kfn = vi == 0 ? (const void*)k_mx_gemm<0> : (vi == 1 ? (const void*)k_mx_gemm<16> : (const void*)k_mx_gemm<32>);
+  if (dev >= 0 && dev < 64 && !attr_done[vi][dev]) {
+    cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES);
+    if (e != cudaSuccess) return mx_cuda_status(e, "gemm: set smem");
+    attr_done[vi][dev] = true;
   }
   const int num_tiles = (int)(((M + BM - 1) / BM) * (N / BN));
   const int grid = num_tiles < mxm_num_sms() ? num_tiles : mxm_num_sms();
-  k_mx_gemm<<<grid, NUM_THREADS, SMEM_BYTES, (cudaStream_t)stream>>>(
-      tmA, tmB, (const uint8_t*)sa, (const uint8_t*)sb, (int)M, (int)N, (int)K, (__nv_bfloat16*)d, ldd,
-      mx_dev_error_ptr());
-  return mx_launch_status("mxm_gemm launch");
+  auto args = [&](auto kern) {
+    kern<<<grid, NUM_THREADS, SMEM_BYTES, (cudaStream_t)stream>>>(
+        tmA, tmB, (const uint8_t*)sa, (const uint8_t*)sb, (int)M, (int)N, (int)K, (__nv_bfloat16*)d, ldd,
+        (const __nv_bfloat16*)L, ldl, (const __nv_bfloat16*)Rm, alpha, mx_dev_error_ptr());
+  };
+  if (vi == 0)
+    args(k_mx_gemm<0>);
+  else if (vi == 1)
+    args(k_mx_gemm<16>);
+  else
+    args(k_mx_gemm<32>);
+  return mx_launch_status(fn);
+}
+
+}  // namespace
+
+extern "C" int mxm_gemm(const void* qa, int64_t lda, const void* sa, const void* qb, int64_t ldb, const void* sb,
+                        int64_t M, int64_t N, int64_t K, void* d, int64_t ldd, void* stream) {
+  return gemm_launch(qa, lda, sa, qb, ldb, sb, M, N, K, d, ldd, nullptr, 0, nullptr, 0, 1.0f, stream, "mxm_gemm");
+}
+
+extern "C" int mxm_gemm_lora(const void* qa, int64_t lda, const void* sa, const void* qb, int64_t ldb, const void* sb,
+                             int64_t M, int64_t N, int64_t K, const void* L, int64_t ldl, const void* Rm, int kr,
+                             float alpha, void* d, int64_t ldd, void* stream) {
+  return gemm_launch(qa, lda, sa, qb, ldb, sb, M, N, K, d, ldd, L, ldl, Rm, kr, alpha, stream, "mxm_gemm_lora");
 }
