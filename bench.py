@@ -1,0 +1,384 @@
+"""Benchmark of the MXFP8 fused SwiGLU-LoRA MLP (forward + backward) on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload layer|stack]
+
+One step = the fused MLP forward + autograd backward (dX, dA, dB of the three LoRA adapters) over one
+batch of tokens, plus, with N > 1 ranks, the NCCL all-reduce of the LoRA gradients (the only data
+exchange of token-sharded data parallelism).
+
+Workloads:
+  layer  (default) one Qwen3.5-2B MLP layer (hidden 2048, intermediate 6144, LoRA r=16, alpha=32) over
+         16,384 tokens per rank -- configs[1] at N=1; every rank adds its own 16,384-token shard
+         ("scaling": "weak").
+  stack  the 24-layer 2B MLP stack over one 142,336-token step (16 packed conversations of 8,896
+         tokens), token-sharded over the ranks -- configs[3] ("scaling": "strong").
+
+The metric is MLP layer-tokens per second over the whole job (tokens x layers / step time, max over
+ranks), i.e. tokens/s for the single-layer workload.  Inputs are synthetic (seeded N(0,1)
+activations, N(0,0.02) frozen weights, N(0,0.01) LoRA A/B).  The per-step working set (gu alone is
+T x 2N bf16 = 384 MiB per layer) is larger than the 126 MB L2, so no explicit L2 flush is needed.
+
+`--impl reference` times the reference algorithm on the host CPU (the oracle port, all host threads)
+on a bounded token sample of the same workload, and prints the same JSON line with "impl": "reference".
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "train-model-template_b200")
+for _p in (ROOT, PKG):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+H, N, R, ALPHA = 2048, 6144, 16, 32
+SCALE = ALPHA / R
+LAYER_TOKENS = 16384
+STACK_TOKENS, STACK_LAYERS = 142336, 24
+METRIC = "MXFP8 fused-MLP fwd+bwd tokens/s (2B shape)"
+UNIT = "tokens/s"
+FLOP_PER_TOKEN = 12 * H * N             # MXFP8 GEMM flops per token per layer, fwd + bwd
+LORA_FLOP_PER_TOKEN = 2 * R * (9 * H + 12 * N)
+
+
+def _args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--workload", choices=("layer", "stack"), default="layer")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+# ----------------------------------------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms while the timed region runs."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        rows = []
+        for line in open(self.path):
+            f = [x.strip() for x in line.split(",")]
+            if len(f) >= 9:
+                rows.append(f)
+        os.unlink(self.path)
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower().startswith("active")})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+# ----------------------------------------------------------------------------------------------- our arm
+def _make_layer(torch, fused_mlp, dev, seed):
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    w = lambda *s: (torch.randn(*s, generator=g) * 0.02).to(torch.bfloat16).to(dev)   # noqa: E731
+    layer = fused_mlp.MXMLPWeights.from_bf16(w(N, H), w(N, H), w(H, N))
+    shapes = ((R, H), (N, R), (R, H), (N, R), (R, N), (H, R))
+    params = [(torch.randn(*s, generator=g) * 0.01).to(dev).requires_grad_(True) for s in shapes]
+    return layer, params
+
+
+def run_ours(a):
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
+
+    import __graft_entry__
+    __graft_entry__.build()
+    import _mxlib
+    import fused_linear
+    import fused_mlp
+    import mxfp8
+
+    if a.workload == "layer":
+        T, L = LAYER_TOKENS, 1
+        total_tokens = T * world
+    else:
+        assert STACK_TOKENS % world == 0
+        T, L = STACK_TOKENS // world, STACK_LAYERS
+        total_tokens = STACK_TOKENS
+    layers = [_make_layer(torch, fused_mlp, dev, seed=1000 + i) for i in range(L)]
+    params = [p for _, ps in layers for p in ps]
+    gx = torch.Generator(device="cpu").manual_seed(7 + rank)
+    x_host = torch.randn(T, H, generator=gx).to(torch.bfloat16).pin_memory()
+    dy_host = torch.randn(T, H, generator=gx).to(torch.bfloat16).pin_memory()
+    x = x_host.to(dev)
+    dy = dy_host.to(dev)
+    flat = torch.zeros(sum(p.numel() for p in params), dtype=torch.float32, device=dev)
+    flat_host = torch.empty(flat.shape, dtype=torch.float32).pin_memory()
+
+    def step(xin, dyin):
+        fused_linear.new_step()
+        h = xin.requires_grad_(False)
+        h = h.detach().requires_grad_(True)
+        y = h
+        for layer, ps in layers:
+            y = fused_mlp.mlp_apply(layer, y, *ps, scaling=(SCALE, SCALE, SCALE))
+        y.backward(dyin)
+        if world > 1:   # bucketed all-reduce of every LoRA gradient (NCCL over NVLink)
+            torch.cat([p.grad.reshape(-1) for p in params], out=flat)
+            dist.all_reduce(flat)
+        for p in params:
+            p.grad = None
+        return h
+
+    # GEMM launches timed with CUDA events on the launching stream (the roofline's dominant kernel)
+    gemm_ms, gemm_flops, recording = [], [], [False]
+    orig_mm, orig_lora = mxfp8.mx_mm, fused_mlp.mx_mm_lora
+
+    def timed(fn):
+        def wrap(a_, b_, *rest, **kw):
+            if not recording[0]:
+                return fn(a_, b_, *rest, **kw)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            out = fn(a_, b_, *rest, **kw)
+            e1.record()
+            gemm_ms.append((e0, e1))
+            gemm_flops.append(2 * a_.shape[0] * a_.shape[1] * b_.shape[1])
+            return out
+        return wrap
+
+    mxfp8.mx_mm = timed(orig_mm)
+    fused_mlp.mx_mm_lora = timed(orig_lora)
+
+    for _ in range(max(a.warmup, 3)):
+        step(x, dy)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clk = ClockSampler(local)
+    clk.start()
+    launches0 = _mxlib.launch_count()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    recording[0] = True
+    ev0.record()
+    for _ in range(a.steps):
+        step(x, dy)
+    ev1.record()
+    torch.cuda.synchronize()
+    recording[0] = False
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks = clk.stop()
+    launches = _mxlib.launch_count() - launches0
+    ms = ev0.elapsed_time(ev1) / a.steps
+    g_ms = sum(e0.elapsed_time(e1) for e0, e1 in gemm_ms)
+    g_fl = float(sum(gemm_flops))
+    gemm_ms.clear()
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = t.item()
+
+    # end to end through the public API: pinned host inputs -> device, step, LoRA grads -> host
+    recording[0] = False
+
+    def e2e_step():
+        x.copy_(x_host, non_blocking=True)
+        dy.copy_(dy_host, non_blocking=True)
+        fused_linear.new_step()
+        h = x.detach().requires_grad_(True)
+        y = h
+        for layer, ps in layers:
+            y = fused_mlp.mlp_apply(layer, y, *ps, scaling=(SCALE, SCALE, SCALE))
+        y.backward(dy)
+        torch.cat([p.grad.reshape(-1) for p in params], out=flat)
+        if world > 1:
+            dist.all_reduce(flat)
+        flat_host.copy_(flat, non_blocking=True)
+        for p in params:
+            p.grad = None
+
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(a.steps):
+        e2e_step()
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / a.steps
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = t.item()
+
+    cpu = None
+    if rank == 0 and world == 1 and not a.no_cpu_baseline:
+        cpu = cpu_baseline(a.workload)
+
+    if world > 1:
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    import json as _j
+    peaks = {}
+    try:
+        peaks = _j.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+    except Exception:
+        pass
+    if peaks.get("bf16_tflops_sustained"):
+        peak = 2.0 * float(peaks["bf16_tflops_sustained"])
+        peak_note = "2 x measured sustained bf16 cuBLAS (MEASURED_PEAKS.json): dense MXFP8 rate is twice bf16"
+    else:
+        peak = 2.0 * 1400.0
+        peak_note = "2 x fallback sustained bf16 1.4 PFLOP/s"
+    achieved = g_fl / (g_ms * 1e-3) / 1e12 if g_ms > 0 else None
+    tok = total_tokens * L
+    line = {
+        "metric": METRIC, "value": tok / (ms * 1e-3), "unit": UNIT, "n_gpus": world, "steps": a.steps,
+        "warmup": max(a.warmup, 3), "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "weak" if a.workload == "layer" else "strong", "vs_baseline": None, "dtype": "mxfp8-e4m3/bf16",
+        "data": "synthetic (seeded N(0,1) activations, N(0,0.02) frozen weights, N(0,0.01) LoRA A/B)",
+        "config": {"workload": ("configs[1]: one Qwen3.5-2B MLP layer, 16384 tokens per rank" if a.workload == "layer"
+                                else "configs[3]: 24-layer Qwen3.5-2B MLP stack, 142336-token step, token-sharded"),
+                   "hidden": H, "intermediate": N, "lora_rank": R, "lora_alpha": ALPHA, "layers": L,
+                   "tokens_per_rank": T, "parallelism": f"dp{world} (token shards, NCCL all-reduce of LoRA grads)",
+                   "l2": "per-step working set > L2 (gu alone 384 MiB per layer); no flush"},
+        "e2e": {"value": tok / (e2e_ms * 1e-3), "unit": UNIT,
+                "h2d_bytes_per_step": x_host.numel() * 2 + dy_host.numel() * 2,
+                "d2h_bytes_per_step": flat_host.numel() * 4},
+        "gpu_launches": int(launches),
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                     "frac": (achieved / peak) if achieved else None, "traffic": None,
+                     "kernel": "k_mx_gemm (tcgen05 MXFP8 GEMMs, 4 launches per layer per step)",
+                     "flops_per_step": g_fl / a.steps, "peak_source": peak_note},
+        "mlp_tflops": FLOP_PER_TOKEN * tok / (ms * 1e-3) / 1e12,
+        "clocks": clocks,
+        "cpu_baseline": cpu,
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------------------------------------------- CPU leg
+def _cpu_sample(workload, tokens):
+    """Time the oracle port (numpy, the reference algorithm) on `tokens` tokens of one 2B layer."""
+    import numpy as np
+    from oracle import mx_oracle as O
+    rng = np.random.default_rng(0)
+    bf = lambda a: O.bf16_round(a.astype(np.float32))  # noqa: E731
+    Wg, Wu = bf(rng.standard_normal((N, H)) * 0.02), bf(rng.standard_normal((N, H)) * 0.02)
+    Wd = bf(rng.standard_normal((H, N)) * 0.02)
+    W = O.MXWeights(Wg, Wu, Wd)              # frozen weights: quantized once per run, not per step
+    lora = [(rng.standard_normal(s) * 0.01).astype(np.float32)
+            for s in ((R, H), (N, R), (R, H), (N, R), (R, N), (H, R))]
+    x = bf(rng.standard_normal((tokens, H)))
+    dy = bf(rng.standard_normal((tokens, H)))
+    t0 = time.perf_counter()
+    reps = 0
+    while True:
+        y, ctx = O.mlp_forward(x, W, *lora, SCALE, SCALE, SCALE)
+        O.mlp_backward(dy, ctx)
+        reps += 1
+        if time.perf_counter() - t0 > 10.0 or reps >= 3:
+            break
+    dt = (time.perf_counter() - t0) / reps
+    return tokens / dt, dt
+
+
+def _threads():
+    try:
+        from threadpoolctl import threadpool_info
+        n = [i.get("num_threads", 1) for i in threadpool_info() if i.get("user_api") == "blas"]
+        return max(n) if n else os.cpu_count()
+    except Exception:
+        return os.cpu_count()
+
+
+def cpu_baseline(workload):
+    tokens = 1024
+    v, dt = _cpu_sample(workload, tokens)
+    return {"value": v, "unit": UNIT, "cores": _threads(), "kind": "port",
+            "sample": f"{tokens} tokens of one 2B MLP layer, fwd+bwd, numpy oracle port of the reference algorithm "
+                      f"({dt:.2f} s per sample step; layer-tokens/s)"}
+
+
+def run_reference(a):
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if rank != 0:
+        return
+    tokens = 1024
+    _cpu_sample(a.workload, 256)   # warm-up (numpy / BLAS thread start)
+    vals = []
+    for _ in range(max(1, min(a.steps, 3))):
+        v, dt = _cpu_sample(a.workload, tokens)
+        vals.append(v)
+    v = statistics.median(vals)
+    line = {
+        "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": world, "steps": len(vals), "warmup": 1,
+        "ms_per_step": tokens / v * 1e3, "higher_is_better": True, "scaling": "weak" if a.workload == "layer" else "strong",
+        "vs_baseline": None, "dtype": "mxfp8-e4m3/fp32 (CPU)", "data": "synthetic",
+        "config": {"workload": "one Qwen3.5-2B MLP layer (hidden 2048, intermediate 6144, r 16), bounded token sample",
+                   "tokens_per_sample": tokens},
+        "impl": "reference",
+        "cpu_baseline": {"value": v, "unit": UNIT, "cores": _threads(), "kind": "port",
+                         "sample": f"{tokens} tokens of one 2B MLP layer, fwd+bwd (numpy port of the reference algorithm)"},
+        "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    a = _args()
+    if a.impl == "reference":
+        run_reference(a)
+    else:
+        run_ours(a)
+
+
+if __name__ == "__main__":
+    main()

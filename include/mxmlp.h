@@ -47,6 +47,9 @@ const char* mxm_last_error(void);
  * `clear` is nonzero.  Synchronizes the device (host-side diagnostics only). */
 int mxm_device_error(int* code, int clear);
 
+/* Number of kernels this library has launched in this process (all devices, host-side count). */
+unsigned long long mxm_launch_count(void);
+
 /* Number of SMs of the current device (grid sizing; cached per device). */
 int mxm_num_sms(void);
 
@@ -77,7 +80,7 @@ int mxm_gemm(const void* qa, int64_t lda, const void* sa, const void* qb, int64_
 
 /* mxm_gemm with a rank-kr LoRA term added in the epilogue, with the reference's two roundings:
  *   D = bf16( bf16(dq(A) dq(B)^T) + alpha * L[M, kr] . Rm[N, kr]^T )
- * L row stride ldl (elements), Rm contiguous [N, kr], kr in {16, 32}.
+ * L row stride ldl (elements), Rm contiguous [N, kr], kr in {16, 32, 64}.
  * Replaces `y = _scaled_mm(...); y.addmm_(xS_down, B_down^T, alpha=s_down)` and
  * `dx = _scaled_mm(...); dx.addmm_(dxa, S)` (scripts/fused_mlp.py:283-284, :329-331). */
 int mxm_gemm_lora(const void* qa, int64_t lda, const void* sa, const void* qb, int64_t ldb, const void* sb,
@@ -119,7 +122,7 @@ int mxm_mlp_bwd_reduce(const void* dxa_part, const void* dbg_part, const void* d
                        int64_t T, int64_t N, int r, float s_g, float s_u, int super_block, int col_groups, void* dxa,
                        void* xsd, void* dBg, void* dBu, void* dAd, void* stream);
 
-/* out[T, n] = bf16( bf16(A[T, K] B[n, K]^T) * post ) (post == 1: one rounding); n in {16, 32}, K % 32 == 0.
+/* out[T, n] = bf16( bf16(A[T, K] B[n, K]^T) * post ) (post == 1: one rounding); n in {16, 32, 64}, K % 32 == 0.
  * The rank-n LoRA-A products: xs = x S^T and dxd = s_d (dy B_down) (scripts/fused_mlp.py:277,311-313). */
 int mxm_rowdot(const void* A, int64_t lda, const void* B, int64_t T, int64_t K, int n, float post, void* out,
                int64_t ldo, void* stream);
@@ -128,7 +131,7 @@ int mxm_rowdot(const void* A, int64_t lda, const void* B, int64_t T, int64_t K, 
 int mxm_coldot_chunks(int64_t T, int64_t K, int* rows_per_chunk, int* chunks);
 
 /* out = bf16( bf16(A[T, K]^T E[T, n]) * post ), written [K, n] (or [n, K] when transpose_out).
- * part: fp32 [chunks, K, n] scratch.  K % 64 == 0, n in {16, 32}.
+ * part: fp32 [chunks, K, n] scratch.  K % 64 == 0, n in {16, 32, 64}.
  * The LoRA weight gradients dA = dxa^T x and dB_down = s_d (dy^T xS_down) (scripts/fused_mlp.py:316-318,333). */
 int mxm_coldot(const void* A, int64_t lda, const void* E, int64_t lde, int64_t T, int64_t K, int n, float post,
                int transpose_out, void* part, int rows_per_chunk, int chunks, void* out, void* stream);

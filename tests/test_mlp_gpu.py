@@ -23,7 +23,9 @@ def _bits_to_t(b):
 
 
 def _run(x, Wg, Wu, Wd, lora, dy, s, need_out=True):
+    import fused_linear
     import fused_mlp
+    fused_linear.new_step()     # the per-step bf16 cast cache is keyed by parameter id
     dev = torch.device("cuda")
     layer = fused_mlp.MXMLPWeights.from_bf16(Wg.to(dev), Wu.to(dev), Wd.to(dev))
     params = [p.to(dev).clone().requires_grad_(True) for p in lora]
@@ -96,7 +98,9 @@ def test_mlp_rank32():
 
 def test_epilogue_bytes_vs_oracle():
     """h's and [dg | du]'s MXFP8 bytes from the CUDA epilogues vs the oracle on the same gu / dh."""
+    import fused_linear
     import fused_mlp
+    fused_linear.new_step()
     T, H, N, r, s = 333, 512, 1024, 16, 2.0
     x, Wg, Wu, Wd, lora, dy = _case(T, H, N, r, seed=11)
     yo, go, ctx = _oracle(x, Wg, Wu, Wd, lora, dy, s)

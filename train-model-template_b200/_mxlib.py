@@ -27,6 +27,7 @@ _SIGS = {
     "mxm_last_error": [],
     "mxm_device_error": [ctypes.POINTER(ctypes.c_int), _int],
     "mxm_num_sms": [],
+    "mxm_launch_count": [],
     "mxm_quant_rows": [_vp, _i64, _i64, _i64, _vp, _i64, _vp, _vp],
     "mxm_quant_cols": [_vp, _i64, _i64, _i64, _vp, _vp, _vp],
     "mxm_quant_both": [_vp, _i64, _i64, _i64, _vp, _vp, _vp, _vp, _vp],
@@ -45,7 +46,7 @@ _SIGS = {
     "mxm_coldot_chunks": [_i64, _i64, ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_int)],
     "mxm_coldot": [_vp, _i64, _vp, _i64, _i64, _i64, _int, ctypes.c_float, _int, _vp, _int, _int, _vp, _vp],
 }
-_RESTYPE = {"mxm_last_error": ctypes.c_char_p}
+_RESTYPE = {"mxm_last_error": ctypes.c_char_p, "mxm_launch_count": ctypes.c_ulonglong}
 
 for _name, _args in _SIGS.items():
     _f = getattr(_lib, _name)
@@ -83,6 +84,11 @@ def device_error(clear=True):
     c = ctypes.c_int(0)
     call("mxm_device_error", ctypes.byref(c), 1 if clear else 0)
     return c.value
+
+
+def launch_count():
+    """Kernels launched by the native library so far in this process."""
+    return int(_lib.mxm_launch_count())
 
 
 def num_sms():

@@ -235,7 +235,7 @@ int gemm_launch(const void* qa, int64_t lda, const void* sa, const void* qb, int
   MX_CHECK_ARG(ldd >= N && ldd % 8 == 0 && mx_aligned(d, 16), "%s: output stride/alignment", fn);
   MX_CHECK_ARG(mx_aligned(sa, 16) && mx_aligned(sb, 16), "%s: scale buffers must be 16-byte aligned", fn);
   if (kr) {
-    MX_CHECK_ARG(kr == 16 || kr == 32, "%s: LoRA rank must be 16 or 32", fn);
+    MX_CHECK_ARG(kr == 16 || kr == 32 || kr == 64, "%s: LoRA rank must be 16, 32 or 64", fn);
     MX_CHECK_ARG(L && Rm && ldl >= kr && ldl % 8 == 0 && mx_aligned(L, 16) && mx_aligned(Rm, 16),
                  "%s: LoRA operands must be 16-byte aligned with row stride %% 8 == 0", fn);
   }
@@ -248,11 +248,13 @@ int gemm_launch(const void* qa, int64_t lda, const void* sa, const void* qb, int
                                BN, CU_TENSOR_MAP_SWIZZLE_128B))
     return st;
 
-  static bool attr_done[3][64] = {};
+  static bool attr_done[4][64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
-  const int vi = kr == 0 ? 0 : (kr == 16 ? 1 : 2);
-  const void* kfn = vi == 0 ? (const void*)k_mx_gemm<0> : (vi == 1 ? (const void*)k_mx_gemm<16> : (const void*)k_mx_gemm<32>);
+  const int vi = kr == 0 ? 0 : (kr == 16 ? 1 : (kr == 32 ? 2 : 3));
+  const void* kfns[4] = {(const void*)k_mx_gemm<0>, (const void*)k_mx_gemm<16>, (const void*)k_mx_gemm<32>,
+                         (const void*)k_mx_gemm<64>};
+  const void* kfn = kfns[vi];
   if (dev >= 0 && dev < 64 && !attr_done[vi][dev]) {
     cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES);
     if (e != cudaSuccess) return mx_cuda_status(e, "gemm: set smem");
@@ -264,13 +266,16 @@ int gemm_launch(const void* qa, int64_t lda, const void* sa, const void* qb, int
     kern<<<grid, NUM_THREADS, SMEM_BYTES, (cudaStream_t)stream>>>(
         tmA, tmB, (const uint8_t*)sa, (const uint8_t*)sb, (int)M, (int)N, (int)K, (__nv_bfloat16*)d, ldd,
         (const __nv_bfloat16*)L, ldl, (const __nv_bfloat16*)Rm, alpha, mx_dev_error_ptr());
+    mx_note_launch();
   };
   if (vi == 0)
     args(k_mx_gemm<0>);
   else if (vi == 1)
     args(k_mx_gemm<16>);
-  else
+  else if (vi == 2)
     args(k_mx_gemm<32>);
+  else
+    args(k_mx_gemm<64>);
   return mx_launch_status(fn);
 }
 

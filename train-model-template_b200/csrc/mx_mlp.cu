@@ -521,12 +521,14 @@ extern "C" int mxm_mlp_fwd_epilogue(const void* gu, const void* xs, const void* 
     k_mlp_fwd<16, 128><<<grid, 128, 0, st>>>(FWD_ARGS);
   else
     k_mlp_fwd<32, 128><<<grid, 128, 0, st>>>(FWD_ARGS);
+  mx_note_launch();
 #undef FWD_ARGS
   if (int e = mx_launch_status("mlp fwd epilogue")) return e;
   if (col_groups > 1) {
     const int64_t n = T * r;
     k_sum_parts<<<grid_for(n, 256), 256, 0, st>>>((const float*)xsd_part, col_groups, n, n, 1.0f, 1.0f, nullptr,
                                                   (bf16*)xsd, 0, 0);
+    mx_note_launch();
     if (int e = mx_launch_status("mlp fwd xsd sum")) return e;
   }
   return MXM_OK;
@@ -587,9 +589,11 @@ extern "C" int mxm_mlp_bwd_epilogue(const void* gu, const void* xs, const void* 
   if (r == 16) {
     cudaFuncSetAttribute(k_mlp_bwd<16, 32>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     k_mlp_bwd<16, 32><<<grid, 128, smem, st>>>(BWD_ARGS);
+    mx_note_launch();
   } else {
     cudaFuncSetAttribute(k_mlp_bwd<32, 32>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     k_mlp_bwd<32, 32><<<grid, 128, smem, st>>>(BWD_ARGS);
+    mx_note_launch();
   }
 #undef BWD_ARGS
   return mx_launch_status("mlp bwd epilogue");
@@ -607,28 +611,35 @@ extern "C" int mxm_mlp_bwd_reduce(const void* dxa_part, const void* dbg_part, co
   const int64_t nd = T * 3 * r;
   k_reduce_dxa<<<grid_for(nd, 256), 256, 0, st>>>((const float*)dxa_part, col_groups, (int)T, r, s_g, s_u, (bf16*)dxa,
                                                   (bf16*)xsd);
+  mx_note_launch();
   const int64_t nb = N * r;
   k_sum_parts<<<grid_for(nb, 256), 256, 0, st>>>((const float*)dbg_part, nsb, nb, nb, s_g, 1.f, (float*)dBg, nullptr,
                                                  0, 0);
+  mx_note_launch();
   k_sum_parts<<<grid_for(nb, 256), 256, 0, st>>>((const float*)dbu_part, nsb, nb, nb, s_u, 1.f, (float*)dBu, nullptr,
                                                  0, 0);
+  mx_note_launch();
   k_sum_parts<<<grid_for(nb, 256), 256, 0, st>>>((const float*)dad_part, nsb, nb, nb, 1.f, 1.f, (float*)dAd, nullptr,
                                                  0, 0);
+  mx_note_launch();
   return mx_launch_status("mlp bwd reduce");
 }
 
 extern "C" int mxm_rowdot(const void* A, int64_t lda, const void* B, int64_t T, int64_t K, int n, float post,
                           void* out, int64_t ldo, void* stream) {
   MX_CHECK_ARG(A && B && out, "mxm_rowdot: null pointer");
-  MX_CHECK_ARG(T >= 1 && K >= 32 && K % 32 == 0 && (n == 16 || n == 32) && lda % 8 == 0 && ldo % 2 == 0,
-               "mxm_rowdot: need K %% 32 == 0, n in {16, 32}, lda %% 8 == 0");
+  MX_CHECK_ARG(T >= 1 && K >= 32 && K % 32 == 0 && (n == 16 || n == 32 || n == 64) && lda % 8 == 0 && ldo % 2 == 0,
+               "mxm_rowdot: need K %% 32 == 0, n in {16, 32, 64}, lda %% 8 == 0");
   MX_CHECK_ARG(mx_aligned(A, 16) && mx_aligned(B, 16) && mx_aligned(out, 4), "mxm_rowdot: alignment");
   const unsigned grid = (unsigned)((T + 63) / 64);
   cudaStream_t st = (cudaStream_t)stream;
   if (n == 16)
     k_rowdot<16><<<grid, 128, 0, st>>>((const bf16*)A, lda, (const bf16*)B, (int)T, (int)K, post, (bf16*)out, ldo);
-  else
+  else if (n == 32)
     k_rowdot<32><<<grid, 128, 0, st>>>((const bf16*)A, lda, (const bf16*)B, (int)T, (int)K, post, (bf16*)out, ldo);
+  else
+    k_rowdot<64><<<grid, 128, 0, st>>>((const bf16*)A, lda, (const bf16*)B, (int)T, (int)K, post, (bf16*)out, ldo);
+  mx_note_launch();
   return mx_launch_status("rowdot");
 }
 
@@ -650,7 +661,7 @@ extern "C" int mxm_coldot(const void* A, int64_t lda, const void* E, int64_t lde
                           float post, int transpose_out, void* part, int rows_per_chunk, int chunks, void* out,
                           void* stream) {
   MX_CHECK_ARG(A && E && part && out, "mxm_coldot: null pointer");
-  MX_CHECK_ARG(T >= 1 && K % 64 == 0 && (n == 16 || n == 32) && rows_per_chunk % 16 == 0 &&
+  MX_CHECK_ARG(T >= 1 && K % 64 == 0 && (n == 16 || n == 32 || n == 64) && rows_per_chunk % 16 == 0 &&
                    (int64_t)rows_per_chunk * chunks >= T,
                "mxm_coldot: bad shape or chunking");
   dim3 grid((unsigned)(K / 64), (unsigned)chunks);
@@ -658,12 +669,17 @@ extern "C" int mxm_coldot(const void* A, int64_t lda, const void* E, int64_t lde
   if (n == 16)
     k_coldot<16><<<grid, 128, 0, st>>>((const bf16*)A, lda, (const bf16*)E, lde, (int)T, (int)K, rows_per_chunk,
                                        (float*)part);
-  else
+  else if (n == 32)
     k_coldot<32><<<grid, 128, 0, st>>>((const bf16*)A, lda, (const bf16*)E, lde, (int)T, (int)K, rows_per_chunk,
                                        (float*)part);
+  else
+    k_coldot<64><<<grid, 128, 0, st>>>((const bf16*)A, lda, (const bf16*)E, lde, (int)T, (int)K, rows_per_chunk,
+                                       (float*)part);
+  mx_note_launch();
   if (int e = mx_launch_status("coldot")) return e;
   const int64_t nn = K * n;
   k_sum_parts<<<grid_for(nn, 256), 256, 0, st>>>((const float*)part, chunks, nn, nn, 1.f, post, nullptr, (bf16*)out,
                                                  transpose_out ? K : 0, transpose_out ? n : 0);
+  mx_note_launch();
   return mx_launch_status("coldot sum");
 }

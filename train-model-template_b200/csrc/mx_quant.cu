@@ -154,6 +154,7 @@ int launch(const void* x, int64_t R, int64_t K, int64_t ldx, void* q, int64_t ld
   dim3 grid((unsigned)((R + 127) / 128), (unsigned)(K / 128));
   k_quant<ROWS, COLS><<<grid, QT, smem, (cudaStream_t)stream>>>(
       (const __nv_bfloat16*)x, R, K, ldx, (uint8_t*)q, ldq, (uint8_t*)s, (uint8_t*)qt, (uint8_t*)st);
+  mx_note_launch();
   return mx_launch_status("quant kernel launch");
 }
 

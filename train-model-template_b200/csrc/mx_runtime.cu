@@ -4,6 +4,7 @@
 #include <stdio.h>
 #include <string.h>
 
+#include <atomic>
 #include <mutex>
 
 #include "mx_runtime.h"
@@ -37,6 +38,12 @@ int* mx_dev_error_ptr() {
   }
   return cache[dev];
 }
+
+static std::atomic<unsigned long long> g_launches{0};
+
+void mx_note_launch(int n) { g_launches.fetch_add((unsigned long long)n, std::memory_order_relaxed); }
+
+extern "C" unsigned long long mxm_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
 
 extern "C" int mxm_version(void) { return MXM_ABI_VERSION; }
 

@@ -11,6 +11,9 @@ void mx_set_last_error(const char* fmt, ...);
 int mx_cuda_status(cudaError_t e, const char* what);
 int mx_launch_status(const char* what);
 
+// Counts kernel launches made by this library (host side), read with mxm_launch_count().
+void mx_note_launch(int n = 1);
+
 // Device address of the device-side error flag on the current device (nullptr if unavailable).
 int* mx_dev_error_ptr();
 
