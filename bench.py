@@ -54,6 +54,9 @@ def _args():
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--workload", choices=("layer", "stack"), default="layer")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end (host buffers) measurement")
+    ap.add_argument("--tokens", type=int, default=0,
+                    help="tokens per rank for the layer workload (default 16384; smaller cases for profiling)")
     return ap.parse_args()
 
 
@@ -135,7 +138,7 @@ def run_ours(a):
     import mxfp8
 
     if a.workload == "layer":
-        T, L = LAYER_TOKENS, 1
+        T, L = (a.tokens or LAYER_TOKENS), 1
         total_tokens = T * world
     else:
         assert STACK_TOKENS % world == 0
@@ -239,19 +242,21 @@ def run_ours(a):
         for p in params:
             p.grad = None
 
-    for _ in range(2):
-        e2e_step()
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(a.steps):
-        e2e_step()
-    e1.record()
-    torch.cuda.synchronize()
-    e2e_ms = e0.elapsed_time(e1) / a.steps
-    if world > 1:
+    e2e_ms = float("nan")
+    if not a.no_e2e:
+        for _ in range(2):
+            e2e_step()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(a.steps):
+            e2e_step()
+        e1.record()
+        torch.cuda.synchronize()
+        e2e_ms = e0.elapsed_time(e1) / a.steps
+    if world > 1 and not a.no_e2e:
         t = torch.tensor([e2e_ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_ms = t.item()
@@ -288,7 +293,7 @@ def run_ours(a):
                    "hidden": H, "intermediate": N, "lora_rank": R, "lora_alpha": ALPHA, "layers": L,
                    "tokens_per_rank": T, "parallelism": f"dp{world} (token shards, NCCL all-reduce of LoRA grads)",
                    "l2": "per-step working set > L2 (gu alone 384 MiB per layer); no flush"},
-        "e2e": {"value": tok / (e2e_ms * 1e-3), "unit": UNIT,
+        "e2e": None if a.no_e2e else {"value": tok / (e2e_ms * 1e-3), "unit": UNIT,
                 "h2d_bytes_per_step": x_host.numel() * 2 + dy_host.numel() * 2,
                 "d2h_bytes_per_step": flat_host.numel() * 4},
         "gpu_launches": int(launches),

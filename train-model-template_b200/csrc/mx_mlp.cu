@@ -20,6 +20,31 @@ namespace {
 
 using bf16 = __nv_bfloat16;
 
+// ------------------------------------------------------------------------------------------------ helpers
+MX_DEV float nanmax_abs(float m, float v) {
+  float r;
+  asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(m), "f"(fabsf(v)));
+  return r;
+}
+MX_DEV float nanmax(float a, float b) {
+  float r;
+  asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+  return r;
+}
+// Division with the 2-ulp full-range PTX instruction (what a Triton `/` on fp32 lowers to).
+MX_DEV float fdiv_full(float a, float b) {
+  float r;
+  asm("div.full.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+  return r;
+}
+// Two floats -> two E4M3 codes (RNE, saturating: |v| <= 448 after the power-of-two block scaling,
+// and +-inf saturates to +-448 exactly as the reference's clamp does).
+MX_DEV uint32_t e4m3x2_sat(float lo, float hi) {
+  uint16_t r;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
 // Quantizes one 32-column block of a 16-row warp tile in D-fragment form:
 // v[i][0..1] = (row g, cols 8i+2t, +1), v[i][2..3] = (row g+8, same cols), i = 0..3.
 // Codes go to q[row * ldq + col0 + ...] for rows < T; scales of rows g and g+8 (always, padded rows
@@ -30,9 +55,9 @@ MX_DEV void quant_block16(const float (&v)[4][4], int64_t row_g, int64_t T, int6
   for (int h = 0; h < 2; ++h) {
     float m = 0.f;
 #pragma unroll
-    for (int i = 0; i < 4; ++i) m = mx_absmax_nan(m, mx_absmax_nan(v[i][2 * h], v[i][2 * h + 1]));
-    m = mx_max_nan(m, __shfl_xor_sync(0xffffffffu, m, 1));
-    m = mx_max_nan(m, __shfl_xor_sync(0xffffffffu, m, 2));
+    for (int i = 0; i < 4; ++i) m = nanmax_abs(nanmax_abs(m, v[i][2 * h]), v[i][2 * h + 1]);
+    m = nanmax(m, __shfl_xor_sync(0xffffffffu, m, 1));
+    m = nanmax(m, __shfl_xor_sync(0xffffffffu, m, 2));
     const uint32_t e = mx_e8m0_rceil(__fdiv_rn(m, 448.0f));
     const float rcp = mx_e8m0_rcp(e);
     const int64_t row = row_g + 8 * h;
@@ -40,31 +65,93 @@ MX_DEV void quant_block16(const float (&v)[4][4], int64_t row_g, int64_t T, int6
       uint8_t* dst = q + row * ldq + col0 + 2 * t;
 #pragma unroll
       for (int i = 0; i < 4; ++i)
-        *reinterpret_cast<uint16_t*>(dst + 8 * i) =
-            mx_e4m3x2(mx_clamp448(v[i][2 * h] * rcp), mx_clamp448(v[i][2 * h + 1] * rcp));
+        *reinterpret_cast<uint16_t*>(dst + 8 * i) = (uint16_t)e4m3x2_sat(v[i][2 * h] * rcp, v[i][2 * h + 1] * rcp);
     }
     if (t == 0) s[mx_scale_offset(row, col0 >> 5, scols)] = (uint8_t)e;
   }
 }
 
-MX_DEV float silu_part(float g) { return g / (expf(-g) + 1.0f); }
+// exp(-g) once per element; silu = g / (e + 1) and sigmoid = 1 / (1 + e) share it
+// (reference: g / (exp(-g) + 1), tl.sigmoid(g); scripts/fused_mlp.py:104,152,158).
+MX_DEV float exp_neg(float g) { return __expf(-g); }
+
+// bf16 pair (row r, cols c, c+1) of a [rows x 64] bf16 tile stored by TMA with the 128-byte swizzle
+// (16-byte chunk j of row r sits at chunk j ^ (r % 8)).
+MX_DEV uint32_t sw128_ld(const uint8_t* tile, int r, int c) {
+  const int b = c * 2;
+  return *reinterpret_cast<const uint32_t*>(tile + r * 128 + (((b >> 4) ^ (r & 7)) << 4) + (b & 15));
+}
+// Same for a [rows x 32] bf16 tile with 64-byte rows and the 64-byte swizzle (chunk j -> j ^ ((r / 2) % 4)).
+MX_DEV uint32_t sw64_ld(const uint8_t* tile, int r, int c) {
+  const int b = c * 2;
+  return *reinterpret_cast<const uint32_t*>(tile + r * 64 + (((b >> 4) ^ ((r >> 1) & 3)) << 4) + (b & 15));
+}
+
+MX_DEV uint8_t* align1024(uint8_t* p) {
+  return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
+}
+
+// Named barrier among the consumer warps only (the producer warp does not take part).
+MX_DEV void consumers_sync(int nthreads) { asm volatile("bar.sync 1, %0;" ::"r"(nthreads) : "memory"); }
+
+constexpr int CONSUMERS = 8;                      // consumer warps (16 rows each: 128-row blocks)
+constexpr int EPI_THREADS = 32 * (CONSUMERS + 1);  // + one TMA producer warp
 
 // ------------------------------------------------------------------------------------------------ forward
-// CTA = 4 warps x 16 rows; blockIdx.y = column group of `tpg` tiles of BN columns.
-template <int R, int BN>
-__global__ void __launch_bounds__(128) k_mlp_fwd(const bf16* __restrict__ gu, const bf16* __restrict__ xs,
-                                                 const bf16* __restrict__ bg, const bf16* __restrict__ bu,
-                                                 const bf16* __restrict__ ad, uint8_t* __restrict__ qh,
-                                                 uint8_t* __restrict__ sh, float* __restrict__ xsd_part,
-                                                 bf16* __restrict__ xsd_out, int T, int N, float s_g, float s_u,
-                                                 int tpg, int write_q) {
-  constexpr int KS = R / 16, NT = BN / 8;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-  const int64_t row0 = (int64_t)blockIdx.x * 64 + warp * 16;
-  const int64_t ra = row0 + g, rb = ra + 8;
-  const bool va = ra < T, vb = rb < T;
-  const int64_t N2 = 2 * (int64_t)N;
+// CTA = one 128-row block x one column group of `tpg` 64-column tiles.  Warp 8 streams the g and u
+// tiles ([128 x 64] bf16 each, 128-byte swizzle) into a 3-stage ring with TMA; warps 0-7 each own 16
+// rows, so the per-row xS_down accumulator stays in registers across the whole group.
+constexpr int FWD_BN = 64, FWD_ST = 3, FWD_TILE = 128 * FWD_BN * 2;  // 16 KB per tensor tile
+constexpr size_t FWD_SMEM = 1024 + FWD_ST * 2 * FWD_TILE + 2 * FWD_ST * sizeof(uint64_t);
 
+template <int R>
+__global__ void __launch_bounds__(EPI_THREADS, 1)
+    k_mlp_fwd(const __grid_constant__ CUtensorMap tm_gu, const bf16* __restrict__ xs, const bf16* __restrict__ bg,
+              const bf16* __restrict__ bu, const bf16* __restrict__ ad, uint8_t* __restrict__ qh,
+              uint8_t* __restrict__ sh, float* __restrict__ xsd_part, bf16* __restrict__ xsd_out, int T, int N,
+              float s_g, float s_u, int tpg, int write_q, int* err) {
+  constexpr int KS = R / 16, NT = FWD_BN / 8;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align1024(smem_raw);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + FWD_ST * 2 * FWD_TILE);
+  uint64_t* empty = full + FWD_ST;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t row0 = (int64_t)blockIdx.x * 128;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < FWD_ST; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], CONSUMERS);
+    }
+    fence_barrier_init();
+  }
+  __syncthreads();
+
+  if (warp == CONSUMERS) {  // TMA producer
+    if (lane == 0) prefetch_tmap(&tm_gu);
+    int stage = 0;
+    uint32_t phase = 0;
+    for (int ct = 0; ct < tpg; ++ct) {
+      const int n0 = (blockIdx.y * tpg + ct) * FWD_BN;
+      if (!mbar_wait(&empty[stage], phase ^ 1, err, MX_DEV_TIMEOUT_PRODUCER)) break;
+      if (lane == 0) {
+        uint8_t* dst = smem + stage * 2 * FWD_TILE;
+        mbar_arrive_expect_tx(&full[stage], 2 * FWD_TILE);
+        tma_load_2d(dst, &tm_gu, &full[stage], n0, (int)row0);
+        tma_load_2d(dst + FWD_TILE, &tm_gu, &full[stage], N + n0, (int)row0);
+      }
+      __syncwarp();
+      if (++stage == FWD_ST) {
+        stage = 0;
+        phase ^= 1;
+      }
+    }
+    return;
+  }
+
+  const int g = lane >> 2, t = lane & 3;
+  const int rl = warp * 16 + g;  // row within the block
+  const int64_t ra = row0 + rl, rb = ra + 8;
+  const bool va = ra < T, vb = rb < T;
   uint32_t axg[KS][4], axu[KS][4];
 #pragma unroll
   for (int kk = 0; kk < KS; ++kk) {
@@ -83,20 +170,30 @@ __global__ void __launch_bounds__(128) k_mlp_fwd(const bf16* __restrict__ gu, co
 #pragma unroll
   for (int j = 0; j < R / 8; ++j) accx[j][0] = accx[j][1] = accx[j][2] = accx[j][3] = 0.f;
 
+  int stage = 0;
+  uint32_t phase = 0;
   for (int ct = 0; ct < tpg; ++ct) {
-    const int n0 = (blockIdx.y * tpg + ct) * BN;
-    float hv[NT][4];
-    uint32_t hp[NT][2];
-    // issue the tile's gu loads first (independent, overlapping latency)
+    const int n0 = (blockIdx.y * tpg + ct) * FWD_BN;
+    if (!mbar_wait(&full[stage], phase, err, MX_DEV_TIMEOUT_EPILOGUE)) break;
+    const uint8_t* tg = smem + stage * 2 * FWD_TILE;
+    const uint8_t* tu = tg + FWD_TILE;
     uint32_t ga[NT], gb[NT], ua[NT], ub[NT];
 #pragma unroll
     for (int i = 0; i < NT; ++i) {
-      const int64_t c = n0 + 8 * i + 2 * t;
-      ga[i] = va ? ld32(gu + ra * N2 + c) : 0u;
-      gb[i] = vb ? ld32(gu + rb * N2 + c) : 0u;
-      ua[i] = va ? ld32(gu + ra * N2 + N + c) : 0u;
-      ub[i] = vb ? ld32(gu + rb * N2 + N + c) : 0u;
+      const int c = 8 * i + 2 * t;
+      ga[i] = sw128_ld(tg, rl, c);
+      gb[i] = sw128_ld(tg, rl + 8, c);
+      ua[i] = sw128_ld(tu, rl, c);
+      ub[i] = sw128_ld(tu, rl + 8, c);
     }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[stage]);
+    if (++stage == FWD_ST) {
+      stage = 0;
+      phase ^= 1;
+    }
+    float hv[NT][4];
+    uint32_t hp[NT][2];
 #pragma unroll
     for (int i = 0; i < NT; ++i) {
       const int nc = n0 + 8 * i;
@@ -114,20 +211,20 @@ __global__ void __launch_bounds__(128) k_mlp_fwd(const bf16* __restrict__ gu, co
       for (int e = 0; e < 4; ++e) {
         const float gg = bf16_round_f(gin[e] + s_g * dg[e]);
         const float uu = bf16_round_f(uin[e] + s_u * du[e]);
-        hv[i][e] = bf16_round_f(silu_part(gg) * uu);
+        hv[i][e] = bf16_round_f(fdiv_full(gg, exp_neg(gg) + 1.0f) * uu);
       }
       hp[i][0] = pack_bf16x2(hv[i][0], hv[i][1]);
       hp[i][1] = pack_bf16x2(hv[i][2], hv[i][3]);
     }
     if (write_q) {
 #pragma unroll
-      for (int b = 0; b < BN / 32; ++b) {
+      for (int b = 0; b < FWD_BN / 32; ++b) {
         const float(&blk)[4][4] = *reinterpret_cast<const float(*)[4][4]>(&hv[4 * b][0]);
-        quant_block16(blk, row0 + g, T, n0 + 32 * b, qh, N, sh, N, t);
+        quant_block16(blk, ra, T, n0 + 32 * b, qh, N, sh, N, t);
       }
     }
 #pragma unroll
-    for (int m = 0; m < BN / 16; ++m) {
+    for (int m = 0; m < FWD_BN / 16; ++m) {
       const uint32_t a[4] = {hp[2 * m][0], hp[2 * m][1], hp[2 * m + 1][0], hp[2 * m + 1][1]};
 #pragma unroll
       for (int jt = 0; jt < R / 8; ++jt) {
@@ -151,27 +248,91 @@ __global__ void __launch_bounds__(128) k_mlp_fwd(const bf16* __restrict__ gu, co
 }
 
 // ------------------------------------------------------------------------------------------------ backward
-// CTA = 4 warps; blockIdx.x = super-block of SB rows, blockIdx.y = column group of tpg tiles.
-// Column tiles outer (dB / dA accumulate in registers over the super-block's rows), rows inner
-// (dxa / xS_down accumulate across the group's tiles in the group's partial rows, which only this
-// thread touches).
-template <int R, int BN>
-__global__ void __launch_bounds__(128) k_mlp_bwd(
-    const bf16* __restrict__ gu, const bf16* __restrict__ xs, const bf16* __restrict__ dhm,
-    const bf16* __restrict__ dxd, const bf16* __restrict__ bg, const bf16* __restrict__ bu,
-    const bf16* __restrict__ ad, uint8_t* __restrict__ q, uint8_t* __restrict__ s, float* __restrict__ dxa_part,
-    float* __restrict__ dbg_part, float* __restrict__ dbu_part, float* __restrict__ dad_part, int T, int Tpad, int N,
-    float s_g, float s_u, int SB, int tpg, int write_q) {
-  constexpr int KS = R / 16, NT = BN / 8, R3 = 3 * R;
-  extern __shared__ float red[];  // [4 warps][3][R][BN]
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+// CTA = one super-block of SB rows x one column group of `tpg` 32-column tiles.  Warp 8 streams
+// [128 x 32] bf16 tiles of g, u and dh (64-byte swizzle) into a 4-stage ring with TMA, column tile
+// outer, 128-row step inner.  Warps 0-7 each own 16 rows of every step:
+//   * dB_gate, dB_up, dA_down (sums over rows) accumulate in registers over the super-block, then the
+//     8 warps' tiles are summed in a fixed order through shared memory -> one partial per super-block;
+//   * dxa_gate, dxa_up, xS_down (sums over columns) accumulate in a shared-memory [SB x 3r] buffer
+//     that each warp only touches in its own rows, written once per CTA as the group's partial.
+// No atomics: the result is deterministic.
+constexpr int BWD_BN = 32, BWD_ST = 4, BWD_TILE = 128 * BWD_BN * 2;  // 8 KB per tensor tile
+
+__host__ __device__ constexpr size_t bwd_smem(int R, int SB) {
+  return 1024 + (size_t)BWD_ST * 3 * BWD_TILE + (size_t)SB * 3 * R * 4 + (size_t)CONSUMERS * R * BWD_BN * 4 +
+         2 * BWD_ST * sizeof(uint64_t);
+}
+
+template <int R>
+__global__ void __launch_bounds__(EPI_THREADS, 1)
+    k_mlp_bwd(const __grid_constant__ CUtensorMap tm_gu, const __grid_constant__ CUtensorMap tm_dh,
+              const bf16* __restrict__ xs, const bf16* __restrict__ dxd, const bf16* __restrict__ bg,
+              const bf16* __restrict__ bu, const bf16* __restrict__ ad, uint8_t* __restrict__ q,
+              uint8_t* __restrict__ s, float* __restrict__ dxa_part, float* __restrict__ dbg_part,
+              float* __restrict__ dbu_part, float* __restrict__ dad_part, int T, int Tpad, int N, float s_g,
+              float s_u, int SB, int tpg, int write_q, int* err) {
+  constexpr int KS = R / 16, NT = BWD_BN / 8, R3 = 3 * R;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align1024(smem_raw);
+  float* acc_rows = reinterpret_cast<float*>(smem + BWD_ST * 3 * BWD_TILE);  // [SB][3R]
+  float* scratch = acc_rows + (size_t)SB * R3;                                 // [CONSUMERS][R][BN]
+  uint64_t* full = reinterpret_cast<uint64_t*>(scratch + CONSUMERS * R * BWD_BN);
+  uint64_t* empty = full + BWD_ST;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int sbi = blockIdx.x, cg = blockIdx.y;
   const int r_begin = sbi * SB, r_end = min(r_begin + SB, Tpad);
   const int64_t N2 = 2 * (int64_t)N;
-  float* P = dxa_part + (int64_t)cg * T * R3;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < BWD_ST; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], CONSUMERS);
+    }
+    fence_barrier_init();
+  }
+  __syncthreads();
 
-  for (int ct = 0; ct < tpg; ++ct) {
-    const int n0 = (cg * tpg + ct) * BN;
+  if (warp == CONSUMERS) {  // TMA producer
+    if (lane == 0) {
+      prefetch_tmap(&tm_gu);
+      prefetch_tmap(&tm_dh);
+    }
+    int stage = 0;
+    uint32_t phase = 0;
+    bool ok = true;
+    for (int ct = 0; ct < tpg && ok; ++ct) {
+      const int n0 = (cg * tpg + ct) * BWD_BN;
+      for (int r = r_begin; r < r_end; r += 128) {
+        if (!mbar_wait(&empty[stage], phase ^ 1, err, MX_DEV_TIMEOUT_PRODUCER)) {
+          ok = false;
+          break;
+        }
+        if (lane == 0) {
+          uint8_t* dst = smem + stage * 3 * BWD_TILE;
+          mbar_arrive_expect_tx(&full[stage], 3 * BWD_TILE);
+          tma_load_2d(dst, &tm_gu, &full[stage], n0, r);
+          tma_load_2d(dst + BWD_TILE, &tm_gu, &full[stage], N + n0, r);
+          tma_load_2d(dst + 2 * BWD_TILE, &tm_dh, &full[stage], n0, r);
+        }
+        __syncwarp();
+        if (++stage == BWD_ST) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+    }
+    return;
+  }
+
+  const int g = lane >> 2, t = lane & 3;
+  const int nthr = CONSUMERS * 32;
+  for (int i = threadIdx.x; i < SB * R3; i += nthr) acc_rows[i] = 0.f;
+  consumers_sync(nthr);
+
+  int stage = 0;
+  uint32_t phase = 0;
+  bool ok = true;
+  for (int ct = 0; ct < tpg && ok; ++ct) {
+    const int n0 = (cg * tpg + ct) * BWD_BN;
     float aBg[KS][NT][4], aBu[KS][NT][4], aAd[KS][NT][4];
 #pragma unroll
     for (int a = 0; a < KS; ++a)
@@ -179,9 +340,27 @@ __global__ void __launch_bounds__(128) k_mlp_bwd(
       for (int i = 0; i < NT; ++i)
 #pragma unroll
         for (int e = 0; e < 4; ++e) aBg[a][i][e] = aBu[a][i][e] = aAd[a][i][e] = 0.f;
+    // B fragments of this column tile (same for every row step)
+    uint32_t bgf[KS][NT][2], buf_[KS][NT][2], adf[KS][NT][2];
+#pragma unroll
+    for (int kk = 0; kk < KS; ++kk)
+#pragma unroll
+      for (int i = 0; i < NT; ++i) {
+        const int nc = n0 + 8 * i;
+        const bf16* pbg = bg + (int64_t)(nc + g) * R + 16 * kk + 2 * t;
+        const bf16* pbu = bu + (int64_t)(nc + g) * R + 16 * kk + 2 * t;
+        bgf[kk][i][0] = ld32g(pbg);
+        bgf[kk][i][1] = ld32g(pbg + 8);
+        buf_[kk][i][0] = ld32g(pbu);
+        buf_[kk][i][1] = ld32g(pbu + 8);
+        const bf16* p0 = ad + (int64_t)(16 * kk + 2 * t) * N + nc + g;
+        adf[kk][i][0] = ld16x2(p0, p0 + N);
+        adf[kk][i][1] = ld16x2(p0 + 8 * (int64_t)N, p0 + 9 * (int64_t)N);
+      }
 
-    for (int r = r_begin + warp * 16; r < r_end; r += 64) {
-      const int64_t ra = r + g, rb = ra + 8;
+    for (int r = r_begin; r < r_end; r += 128) {
+      const int rl = warp * 16 + g;                 // row within the step
+      const int64_t ra = r + rl, rb = ra + 8;
       const bool va = ra < T, vb = rb < T;
       uint32_t axg[KS][4], axu[KS][4], axd[KS][4];
 #pragma unroll
@@ -203,39 +382,56 @@ __global__ void __launch_bounds__(128) k_mlp_bwd(
         axd[kk][2] = va ? ld32(da + 8) : 0u;
         axd[kk][3] = vb ? ld32(db + 8) : 0u;
       }
+      if (!mbar_wait(&full[stage], phase, err, MX_DEV_TIMEOUT_EPILOGUE)) {
+        ok = false;
+        break;
+      }
+      const uint8_t* tg = smem + stage * 3 * BWD_TILE;
+      const uint8_t* tu = tg + BWD_TILE;
+      const uint8_t* th = tg + 2 * BWD_TILE;
+      uint32_t ga[NT], gb[NT], ua[NT], ub[NT], ha[NT], hb[NT];
+#pragma unroll
+      for (int i = 0; i < NT; ++i) {
+        const int c = 8 * i + 2 * t;
+        ga[i] = sw64_ld(tg, rl, c);
+        gb[i] = sw64_ld(tg, rl + 8, c);
+        ua[i] = sw64_ld(tu, rl, c);
+        ub[i] = sw64_ld(tu, rl + 8, c);
+        ha[i] = sw64_ld(th, rl, c);
+        hb[i] = sw64_ld(th, rl + 8, c);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[stage]);
+      if (++stage == BWD_ST) {
+        stage = 0;
+        phase ^= 1;
+      }
+
       uint32_t dgp[NT][2], dup[NT][2], hp[NT][2];
       float dgv[NT][4], duv[NT][4];
 #pragma unroll
       for (int i = 0; i < NT; ++i) {
-        const int nc = n0 + 8 * i;
-        const int64_t c = nc + 2 * t;
-        const uint32_t ga = va ? ld32(gu + ra * N2 + c) : 0u, gb = vb ? ld32(gu + rb * N2 + c) : 0u;
-        const uint32_t ua = va ? ld32(gu + ra * N2 + N + c) : 0u, ub = vb ? ld32(gu + rb * N2 + N + c) : 0u;
-        const uint32_t ha = va ? ld32(dhm + ra * N + c) : 0u, hb = vb ? ld32(dhm + rb * N + c) : 0u;
         float dg[4] = {0.f, 0.f, 0.f, 0.f}, du[4] = {0.f, 0.f, 0.f, 0.f}, dd[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
         for (int kk = 0; kk < KS; ++kk) {
-          const bf16* pbg = bg + (int64_t)(nc + g) * R + 16 * kk + 2 * t;
-          const bf16* pbu = bu + (int64_t)(nc + g) * R + 16 * kk + 2 * t;
-          mma16816(dg, axg[kk], ld32g(pbg), ld32g(pbg + 8));
-          mma16816(du, axu[kk], ld32g(pbu), ld32g(pbu + 8));
-          // B[k = j][n] = A_down[j][n]: (j 2t..2t+1, col g)
-          const bf16* p0 = ad + (int64_t)(16 * kk + 2 * t) * N + nc + g;
-          mma16816(dd, axd[kk], ld16x2(p0, p0 + N), ld16x2(p0 + 8 * (int64_t)N, p0 + 9 * (int64_t)N));
+          mma16816(dg, axg[kk], bgf[kk][i][0], bgf[kk][i][1]);
+          mma16816(du, axu[kk], buf_[kk][i][0], buf_[kk][i][1]);
+          mma16816(dd, axd[kk], adf[kk][i][0], adf[kk][i][1]);
         }
-        const float gin[4] = {bf16_lo(ga), bf16_hi(ga), bf16_lo(gb), bf16_hi(gb)};
-        const float uin[4] = {bf16_lo(ua), bf16_hi(ua), bf16_lo(ub), bf16_hi(ub)};
-        const float hin[4] = {bf16_lo(ha), bf16_hi(ha), bf16_lo(hb), bf16_hi(hb)};
+        const float gin[4] = {bf16_lo(ga[i]), bf16_hi(ga[i]), bf16_lo(gb[i]), bf16_hi(gb[i])};
+        const float uin[4] = {bf16_lo(ua[i]), bf16_hi(ua[i]), bf16_lo(ub[i]), bf16_hi(ub[i])};
+        const float hin[4] = {bf16_lo(ha[i]), bf16_hi(ha[i]), bf16_lo(hb[i]), bf16_hi(hb[i])};
         float hvv[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const float gg = bf16_round_f(gin[e] + s_g * dg[e]);
           const float uu = bf16_round_f(uin[e] + s_u * du[e]);
-          const float sl = silu_part(gg);
+          const float en = exp_neg(gg) + 1.0f;
+          const float sl = fdiv_full(gg, en);
+          const float sig = fdiv_full(1.0f, en);
           hvv[e] = bf16_round_f(sl * uu);
           const float dh = bf16_round_f(hin[e] + dd[e]);
           duv[i][e] = bf16_round_f(dh * sl);
-          const float sig = 1.0f / (1.0f + expf(-gg));
           dgv[i][e] = bf16_round_f(((dh * uu) * sig) * (gg * (1.0f - sig) + 1.0f));
         }
         hp[i][0] = pack_bf16x2(hvv[0], hvv[1]);
@@ -246,109 +442,102 @@ __global__ void __launch_bounds__(128) k_mlp_bwd(
         dup[i][1] = pack_bf16x2(duv[i][2], duv[i][3]);
       }
       if (write_q) {
-#pragma unroll
-        for (int b = 0; b < BN / 32; ++b) {
-          const float(&bgv)[4][4] = *reinterpret_cast<const float(*)[4][4]>(&dgv[4 * b][0]);
-          const float(&buv)[4][4] = *reinterpret_cast<const float(*)[4][4]>(&duv[4 * b][0]);
-          quant_block16(bgv, r + g, T, n0 + 32 * b, q, N2, s, N2, t);
-          quant_block16(buv, r + g, T, (int64_t)N + n0 + 32 * b, q, N2, s, N2, t);
-        }
+        const float(&bgv)[4][4] = *reinterpret_cast<const float(*)[4][4]>(&dgv[0][0]);
+        const float(&buv)[4][4] = *reinterpret_cast<const float(*)[4][4]>(&duv[0][0]);
+        quant_block16(bgv, ra, T, n0, q, N2, s, N2, t);
+        quant_block16(buv, ra, T, (int64_t)N + n0, q, N2, s, N2, t);
       }
-      // per-row products, accumulated across the group's column tiles
-      float pg[R / 8][4], pu[R / 8][4], px[R / 8][4];
+      // per-row products (sums over columns) into the shared-memory row accumulators
+      float* A0 = acc_rows + (int64_t)(ra - r_begin) * R3;
+      float* A1 = A0 + 8 * R3;
+      const uint32_t adg[4] = {dgp[0][0], dgp[0][1], dgp[1][0], dgp[1][1]};
+      const uint32_t adg2[4] = {dgp[2][0], dgp[2][1], dgp[3][0], dgp[3][1]};
+      const uint32_t adu[4] = {dup[0][0], dup[0][1], dup[1][0], dup[1][1]};
+      const uint32_t adu2[4] = {dup[2][0], dup[2][1], dup[3][0], dup[3][1]};
+      const uint32_t ah[4] = {hp[0][0], hp[0][1], hp[1][0], hp[1][1]};
+      const uint32_t ah2[4] = {hp[2][0], hp[2][1], hp[3][0], hp[3][1]};
 #pragma unroll
       for (int jt = 0; jt < R / 8; ++jt) {
         const int c = 8 * jt + 2 * t;
-        float2 z = make_float2(0.f, 0.f);
-        float2 g0 = z, g1 = z, u0 = z, u1 = z, x0 = z, x1 = z;
-        if (ct > 0) {
-          if (va) {
-            g0 = *reinterpret_cast<const float2*>(P + ra * R3 + c);
-            u0 = *reinterpret_cast<const float2*>(P + ra * R3 + R + c);
-            x0 = *reinterpret_cast<const float2*>(P + ra * R3 + 2 * R + c);
-          }
-          if (vb) {
-            g1 = *reinterpret_cast<const float2*>(P + rb * R3 + c);
-            u1 = *reinterpret_cast<const float2*>(P + rb * R3 + R + c);
-            x1 = *reinterpret_cast<const float2*>(P + rb * R3 + 2 * R + c);
-          }
+        const int j = 8 * jt + g;
+        float pg[4], pu[4], px[4];
+        {
+          const float2 a0 = *reinterpret_cast<const float2*>(A0 + c), a1 = *reinterpret_cast<const float2*>(A1 + c);
+          pg[0] = a0.x; pg[1] = a0.y; pg[2] = a1.x; pg[3] = a1.y;
+          const float2 b0 = *reinterpret_cast<const float2*>(A0 + R + c), b1 = *reinterpret_cast<const float2*>(A1 + R + c);
+          pu[0] = b0.x; pu[1] = b0.y; pu[2] = b1.x; pu[3] = b1.y;
+          const float2 c0 = *reinterpret_cast<const float2*>(A0 + 2 * R + c), c1 = *reinterpret_cast<const float2*>(A1 + 2 * R + c);
+          px[0] = c0.x; px[1] = c0.y; px[2] = c1.x; px[3] = c1.y;
         }
-        pg[jt][0] = g0.x; pg[jt][1] = g0.y; pg[jt][2] = g1.x; pg[jt][3] = g1.y;
-        pu[jt][0] = u0.x; pu[jt][1] = u0.y; pu[jt][2] = u1.x; pu[jt][3] = u1.y;
-        px[jt][0] = x0.x; px[jt][1] = x0.y; px[jt][2] = x1.x; px[jt][3] = x1.y;
-      }
+        // B[k = n][col j]: (n 2t..2t+1 | 2t+8..2t+9, col j), two 16-column halves of the tile
 #pragma unroll
-      for (int m = 0; m < BN / 16; ++m) {
-        const uint32_t adg[4] = {dgp[2 * m][0], dgp[2 * m][1], dgp[2 * m + 1][0], dgp[2 * m + 1][1]};
-        const uint32_t adu[4] = {dup[2 * m][0], dup[2 * m][1], dup[2 * m + 1][0], dup[2 * m + 1][1]};
-        const uint32_t ah[4] = {hp[2 * m][0], hp[2 * m][1], hp[2 * m + 1][0], hp[2 * m + 1][1]};
-#pragma unroll
-        for (int jt = 0; jt < R / 8; ++jt) {
-          const int j = 8 * jt + g;
+        for (int m = 0; m < 2; ++m) {
           const int64_t nn = n0 + 16 * m + 2 * t;
           const bf16* pb = bg + nn * R + j;
-          mma16816(pg[jt], adg, ld16x2(pb, pb + R), ld16x2(pb + 8 * R, pb + 9 * R));
           const bf16* pu_ = bu + nn * R + j;
-          mma16816(pu[jt], adu, ld16x2(pu_, pu_ + R), ld16x2(pu_ + 8 * R, pu_ + 9 * R));
           const bf16* pad = ad + (int64_t)j * N + nn;
-          mma16816(px[jt], ah, ld32g(pad), ld32g(pad + 8));
+          mma16816(pg, m ? adg2 : adg, ld16x2(pb, pb + R), ld16x2(pb + 8 * R, pb + 9 * R));
+          mma16816(pu, m ? adu2 : adu, ld16x2(pu_, pu_ + R), ld16x2(pu_ + 8 * R, pu_ + 9 * R));
+          mma16816(px, m ? ah2 : ah, ld32g(pad), ld32g(pad + 8));
         }
+        *reinterpret_cast<float2*>(A0 + c) = make_float2(pg[0], pg[1]);
+        *reinterpret_cast<float2*>(A1 + c) = make_float2(pg[2], pg[3]);
+        *reinterpret_cast<float2*>(A0 + R + c) = make_float2(pu[0], pu[1]);
+        *reinterpret_cast<float2*>(A1 + R + c) = make_float2(pu[2], pu[3]);
+        *reinterpret_cast<float2*>(A0 + 2 * R + c) = make_float2(px[0], px[1]);
+        *reinterpret_cast<float2*>(A1 + 2 * R + c) = make_float2(px[2], px[3]);
       }
-#pragma unroll
-      for (int jt = 0; jt < R / 8; ++jt) {
-        const int c = 8 * jt + 2 * t;
-        if (va) {
-          *reinterpret_cast<float2*>(P + ra * R3 + c) = make_float2(pg[jt][0], pg[jt][1]);
-          *reinterpret_cast<float2*>(P + ra * R3 + R + c) = make_float2(pu[jt][0], pu[jt][1]);
-          *reinterpret_cast<float2*>(P + ra * R3 + 2 * R + c) = make_float2(px[jt][0], px[jt][1]);
-        }
-        if (vb) {
-          *reinterpret_cast<float2*>(P + rb * R3 + c) = make_float2(pg[jt][2], pg[jt][3]);
-          *reinterpret_cast<float2*>(P + rb * R3 + R + c) = make_float2(pu[jt][2], pu[jt][3]);
-          *reinterpret_cast<float2*>(P + rb * R3 + 2 * R + c) = make_float2(px[jt][2], px[jt][3]);
-        }
-      }
-      // column products: [j x n] += xa^T (j x rows) . [dg | du | h] (rows x n)
+      // column products (sums over rows): [j x n] += xa^T (j x rows) . [dg | du | h] (rows x n)
 #pragma unroll
       for (int jm = 0; jm < KS; ++jm) {
-        const uint32_t tg[4] = {movtrans(axg[jm][0]), movtrans(axg[jm][2]), movtrans(axg[jm][1]), movtrans(axg[jm][3])};
-        const uint32_t tu[4] = {movtrans(axu[jm][0]), movtrans(axu[jm][2]), movtrans(axu[jm][1]), movtrans(axu[jm][3])};
-        const uint32_t td[4] = {movtrans(axd[jm][0]), movtrans(axd[jm][2]), movtrans(axd[jm][1]), movtrans(axd[jm][3])};
+        const uint32_t tg4[4] = {movtrans(axg[jm][0]), movtrans(axg[jm][2]), movtrans(axg[jm][1]), movtrans(axg[jm][3])};
+        const uint32_t tu4[4] = {movtrans(axu[jm][0]), movtrans(axu[jm][2]), movtrans(axu[jm][1]), movtrans(axu[jm][3])};
+        const uint32_t td4[4] = {movtrans(axd[jm][0]), movtrans(axd[jm][2]), movtrans(axd[jm][1]), movtrans(axd[jm][3])};
 #pragma unroll
         for (int i = 0; i < NT; ++i) {
-          mma16816(aBg[jm][i], tg, movtrans(dgp[i][0]), movtrans(dgp[i][1]));
-          mma16816(aBu[jm][i], tu, movtrans(dup[i][0]), movtrans(dup[i][1]));
-          mma16816(aAd[jm][i], td, movtrans(hp[i][0]), movtrans(hp[i][1]));
+          mma16816(aBg[jm][i], tg4, movtrans(dgp[i][0]), movtrans(dgp[i][1]));
+          mma16816(aBu[jm][i], tu4, movtrans(dup[i][0]), movtrans(dup[i][1]));
+          mma16816(aAd[jm][i], td4, movtrans(hp[i][0]), movtrans(hp[i][1]));
         }
       }
     }
-    // cross-warp reduction of the column products (fixed order), one partial per super-block
-    float* W = red + warp * (3 * R * BN);
+    if (!ok) break;
+    // fixed-order sum of the 8 warps' column products, one product at a time through `scratch`
 #pragma unroll
-    for (int jm = 0; jm < KS; ++jm)
+    for (int which = 0; which < 3; ++which) {
+      float* W = scratch + warp * (R * BWD_BN);
 #pragma unroll
-      for (int i = 0; i < NT; ++i) {
-        const int j0 = 16 * jm + g, nn = 8 * i + 2 * t;
+      for (int jm = 0; jm < KS; ++jm)
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int j = j0 + (e >> 1) * 8, n = nn + (e & 1);
-          W[(0 * R + j) * BN + n] = aBg[jm][i][e];
-          W[(1 * R + j) * BN + n] = aBu[jm][i][e];
-          W[(2 * R + j) * BN + n] = aAd[jm][i][e];
+        for (int i = 0; i < NT; ++i) {
+          const float* a = which == 0 ? aBg[jm][i] : (which == 1 ? aBu[jm][i] : aAd[jm][i]);
+          const int j0 = 16 * jm + g, nn = 8 * i + 2 * t;
+          W[j0 * BWD_BN + nn] = a[0];
+          W[j0 * BWD_BN + nn + 1] = a[1];
+          W[(j0 + 8) * BWD_BN + nn] = a[2];
+          W[(j0 + 8) * BWD_BN + nn + 1] = a[3];
         }
+      consumers_sync(nthr);
+      for (int idx = threadIdx.x; idx < R * BWD_BN; idx += nthr) {
+        float v = 0.f;
+#pragma unroll
+        for (int w = 0; w < CONSUMERS; ++w) v += scratch[w * R * BWD_BN + idx];
+        const int j = idx / BWD_BN, n = idx % BWD_BN;
+        if (which == 0)
+          dbg_part[((int64_t)sbi * N + n0 + n) * R + j] = v;
+        else if (which == 1)
+          dbu_part[((int64_t)sbi * N + n0 + n) * R + j] = v;
+        else
+          dad_part[((int64_t)sbi * R + j) * N + n0 + n] = v;
       }
-    __syncthreads();
-    for (int idx = threadIdx.x; idx < 3 * R * BN; idx += blockDim.x) {
-      const float v = red[idx] + red[3 * R * BN + idx] + red[2 * 3 * R * BN + idx] + red[3 * 3 * R * BN + idx];
-      const int which = idx / (R * BN), rem = idx % (R * BN), j = rem / BN, n = rem % BN;
-      if (which == 0)
-        dbg_part[((int64_t)sbi * N + n0 + n) * R + j] = v;
-      else if (which == 1)
-        dbu_part[((int64_t)sbi * N + n0 + n) * R + j] = v;
-      else
-        dad_part[((int64_t)sbi * R + j) * N + n0 + n] = v;
+      consumers_sync(nthr);
     }
-    __syncthreads();
+  }
+  // the group's partial of the per-row products
+  float* P = dxa_part + (int64_t)cg * T * R3;
+  for (int i = threadIdx.x; i < (r_end - r_begin) * R3; i += nthr) {
+    const int64_t row = r_begin + i / R3;
+    if (row < T) P[row * R3 + i % R3] = acc_rows[i];
   }
 }
 
@@ -486,12 +675,12 @@ int grid_for(int64_t n, int threads) {
 // ================================================================================================ C ABI
 extern "C" int mxm_mlp_fwd_partitions(int64_t T, int64_t N, int r, int* col_groups) {
   MX_CHECK_ARG(T >= 1 && N >= 128 && N % 128 == 0 && (r == 16 || r == 32) && col_groups, "mxm_mlp_fwd_partitions: bad args");
-  const int64_t tpad = (T + 127) / 128 * 128;
-  const int64_t nrb = tpad / 64;
-  const int nt = (int)(N / 128);
+  // one CTA per SM: the fewest column groups that still fill every SM twice
+  const int64_t nrb = (T + 127) / 128;
+  const int nt = (int)(N / FWD_BN);
   int cs = nt;
   for (int d = 1; d <= nt; ++d)
-    if (nt % d == 0 && nrb * d >= 4 * (int64_t)mxm_num_sms()) {
+    if (nt % d == 0 && nrb * d >= 2 * (int64_t)mxm_num_sms()) {
       cs = d;
       break;
     }
@@ -506,24 +695,28 @@ extern "C" int mxm_mlp_fwd_epilogue(const void* gu, const void* xs, const void* 
   MX_CHECK_ARG(T >= 1 && T < (1ll << 31) && N >= 128 && N % 128 == 0 && (r == 16 || r == 32),
                "mxm_mlp_fwd_epilogue: need T >= 1, N %% 128 == 0, r in {16, 32}");
   MX_CHECK_ARG((qh == nullptr) == (sh == nullptr), "mxm_mlp_fwd_epilogue: qh and sh go together");
-  const int nt = (int)(N / 128);
-  MX_CHECK_ARG(col_groups >= 1 && nt % col_groups == 0, "mxm_mlp_fwd_epilogue: col_groups must divide N/128");
+  const int nt = (int)(N / FWD_BN);
+  MX_CHECK_ARG(col_groups >= 1 && nt % col_groups == 0, "mxm_mlp_fwd_epilogue: col_groups must divide N/64");
   MX_CHECK_ARG(col_groups == 1 || xsd_part, "mxm_mlp_fwd_epilogue: partial buffer needed for col_groups > 1");
-  const int64_t tpad = (T + 127) / 128 * 128;
-  dim3 grid((unsigned)(tpad / 64), (unsigned)col_groups);
+  MX_CHECK_ARG(mx_aligned(gu, 16), "mxm_mlp_fwd_epilogue: gu must be 16-byte aligned");
+  CUtensorMap tm;
+  if (int e = mx_make_tmap_2d(&tm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, gu, (uint64_t)(2 * N), (uint64_t)T,
+                              (uint64_t)(4 * N), FWD_BN, 128, CU_TENSOR_MAP_SWIZZLE_128B))
+    return e;
+  dim3 grid((unsigned)((T + 127) / 128), (unsigned)col_groups);
   cudaStream_t st = (cudaStream_t)stream;
   const int tpg = nt / col_groups;
   bf16* direct = col_groups == 1 ? (bf16*)xsd : nullptr;
-#define FWD_ARGS                                                                                         \
-  (const bf16*)gu, (const bf16*)xs, (const bf16*)bg, (const bf16*)bu, (const bf16*)ad, (uint8_t*)qh,    \
-      (uint8_t*)sh, (float*)xsd_part, direct, (int)T, (int)N, s_g, s_u, tpg, qh != nullptr
-  if (r == 16)
-    k_mlp_fwd<16, 128><<<grid, 128, 0, st>>>(FWD_ARGS);
-  else
-    k_mlp_fwd<32, 128><<<grid, 128, 0, st>>>(FWD_ARGS);
-  mx_note_launch();
-#undef FWD_ARGS
-  if (int e = mx_launch_status("mlp fwd epilogue")) return e;
+  auto go = [&](auto kern) -> int {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)FWD_SMEM);
+    if (e != cudaSuccess) return mx_cuda_status(e, "mlp fwd epilogue: set smem");
+    kern<<<grid, EPI_THREADS, FWD_SMEM, st>>>(tm, (const bf16*)xs, (const bf16*)bg, (const bf16*)bu, (const bf16*)ad,
+                                              (uint8_t*)qh, (uint8_t*)sh, (float*)xsd_part, direct, (int)T, (int)N,
+                                              s_g, s_u, tpg, qh != nullptr, mx_dev_error_ptr());
+    mx_note_launch();
+    return mx_launch_status("mlp fwd epilogue");
+  };
+  if (int e = (r == 16 ? go(k_mlp_fwd<16>) : go(k_mlp_fwd<32>))) return e;
   if (col_groups > 1) {
     const int64_t n = T * r;
     k_sum_parts<<<grid_for(n, 256), 256, 0, st>>>((const float*)xsd_part, col_groups, n, n, 1.0f, 1.0f, nullptr,
@@ -534,32 +727,28 @@ extern "C" int mxm_mlp_fwd_epilogue(const void* gu, const void* xs, const void* 
   return MXM_OK;
 }
 
-// Backward partition (reference _bwd_grid, scripts/fused_mlp.py:218-232): the fewest partial bytes
-// with at least `min_ctas` CTAs per SM.
+static int bwd_super_block(int r) { return r == 16 ? 512 : 256; }
+
+// Backward partition: super-blocks of SB rows (shared-memory row accumulators bound SB) and the
+// column-group count that minimises partial-sum bytes while giving every SM at least two CTAs
+// (the same trade-off as the reference's _bwd_grid, scripts/fused_mlp.py:218-232).
 extern "C" int mxm_mlp_bwd_partitions(int64_t T, int64_t N, int r, int* super_block, int* col_groups) {
   MX_CHECK_ARG(T >= 1 && N >= 128 && N % 128 == 0 && (r == 16 || r == 32) && super_block && col_groups,
                "mxm_mlp_bwd_partitions: bad args");
-  const int BN = 32;
   const int64_t tpad = (T + 127) / 128 * 128;
-  const int nt = (int)(N / BN);
-  const int64_t want = 4 * (int64_t)mxm_num_sms();
-  int64_t best = -1;
-  int bsb = 128, bcg = nt;
-  for (int ncg = 1; ncg <= nt; ++ncg) {
-    if (nt % ncg) continue;
-    for (int64_t sb = 128; sb <= tpad; sb += 128) {
-      const int64_t nsb = (tpad + sb - 1) / sb;
-      if (nsb * ncg < want && !(sb == 128 && ncg == nt)) continue;
-      const int64_t cost = nsb * N * r * 3 * 4 + (int64_t)ncg * T * 3 * r * 4;
-      if (best < 0 || cost < best) {
-        best = cost;
-        bsb = (int)sb;
-        bcg = ncg;
-      }
+  int sb = bwd_super_block(r);
+  while (sb > 128 && (tpad + sb - 1) / sb < 2) sb /= 2;   // small T: smaller super-blocks, more CTAs
+  const int64_t nsb = (tpad + sb - 1) / sb;
+  const int nt = (int)(N / BWD_BN);
+  const int64_t want = 2 * (int64_t)mxm_num_sms();
+  int best = nt;
+  for (int ncg = 1; ncg <= nt; ++ncg)
+    if (nt % ncg == 0 && nsb * ncg >= want) {
+      best = ncg;
+      break;
     }
-  }
-  *super_block = bsb;
-  *col_groups = bcg;
+  *super_block = sb;
+  *col_groups = best;
   return MXM_OK;
 }
 
@@ -572,31 +761,36 @@ extern "C" int mxm_mlp_bwd_epilogue(const void* gu, const void* xs, const void* 
   MX_CHECK_ARG(T >= 1 && T < (1ll << 31) && N >= 128 && N % 128 == 0 && (r == 16 || r == 32),
                "mxm_mlp_bwd_epilogue: need T >= 1, N %% 128 == 0, r in {16, 32}");
   MX_CHECK_ARG((q == nullptr) == (s == nullptr), "mxm_mlp_bwd_epilogue: q and s go together");
-  const int BN = 32;
-  const int nt = (int)(N / BN);
-  MX_CHECK_ARG(col_groups >= 1 && nt % col_groups == 0 && super_block >= 64 && super_block % 64 == 0,
+  const int nt = (int)(N / BWD_BN);
+  MX_CHECK_ARG(col_groups >= 1 && nt % col_groups == 0 && super_block >= 128 && super_block % 128 == 0 &&
+                   super_block <= bwd_super_block(r),
                "mxm_mlp_bwd_epilogue: bad partition (%d, %d)", super_block, col_groups);
+  MX_CHECK_ARG(mx_aligned(gu, 16) && mx_aligned(dhm, 16), "mxm_mlp_bwd_epilogue: gu / dhm must be 16-byte aligned");
+  CUtensorMap tgu, tdh;
+  if (int e = mx_make_tmap_2d(&tgu, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, gu, (uint64_t)(2 * N), (uint64_t)T,
+                              (uint64_t)(4 * N), BWD_BN, 128, CU_TENSOR_MAP_SWIZZLE_64B))
+    return e;
+  if (int e = mx_make_tmap_2d(&tdh, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, dhm, (uint64_t)N, (uint64_t)T,
+                              (uint64_t)(2 * N), BWD_BN, 128, CU_TENSOR_MAP_SWIZZLE_64B))
+    return e;
   const int64_t tpad = (T + 127) / 128 * 128;
   const int nsb = (int)((tpad + super_block - 1) / super_block);
   dim3 grid((unsigned)nsb, (unsigned)col_groups);
-  const size_t smem = 4 * 3 * (size_t)r * BN * sizeof(float);
+  const size_t smem = bwd_smem(r, super_block);
   cudaStream_t st = (cudaStream_t)stream;
   const int tpg = nt / col_groups;
-#define BWD_ARGS                                                                                          \
-  (const bf16*)gu, (const bf16*)xs, (const bf16*)dhm, (const bf16*)dxd, (const bf16*)bg, (const bf16*)bu, \
-      (const bf16*)ad, (uint8_t*)q, (uint8_t*)s, (float*)dxa_part, (float*)dbg_part, (float*)dbu_part,    \
-      (float*)dad_part, (int)T, (int)tpad, (int)N, s_g, s_u, super_block, tpg, q != nullptr
-  if (r == 16) {
-    cudaFuncSetAttribute(k_mlp_bwd<16, 32>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    k_mlp_bwd<16, 32><<<grid, 128, smem, st>>>(BWD_ARGS);
+  auto go = [&](auto kern) -> int {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return mx_cuda_status(e, "mlp bwd epilogue: set smem");
+    kern<<<grid, EPI_THREADS, smem, st>>>(tgu, tdh, (const bf16*)xs, (const bf16*)dxd, (const bf16*)bg,
+                                          (const bf16*)bu, (const bf16*)ad, (uint8_t*)q, (uint8_t*)s,
+                                          (float*)dxa_part, (float*)dbg_part, (float*)dbu_part, (float*)dad_part,
+                                          (int)T, (int)tpad, (int)N, s_g, s_u, super_block, tpg, q != nullptr,
+                                          mx_dev_error_ptr());
     mx_note_launch();
-  } else {
-    cudaFuncSetAttribute(k_mlp_bwd<32, 32>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    k_mlp_bwd<32, 32><<<grid, 128, smem, st>>>(BWD_ARGS);
-    mx_note_launch();
-  }
-#undef BWD_ARGS
-  return mx_launch_status("mlp bwd epilogue");
+    return mx_launch_status("mlp bwd epilogue");
+  };
+  return r == 16 ? go(k_mlp_bwd<16>) : go(k_mlp_bwd<32>);
 }
 
 extern "C" int mxm_mlp_bwd_reduce(const void* dxa_part, const void* dbg_part, const void* dbu_part,
