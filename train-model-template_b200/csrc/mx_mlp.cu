@@ -98,22 +98,27 @@ constexpr int CONSUMERS = 8;                      // consumer warps (16 rows eac
 constexpr int EPI_THREADS = 32 * (CONSUMERS + 1);  // + one TMA producer warp
 
 // ------------------------------------------------------------------------------------------------ forward
-// CTA = one 128-row block x one column group of `tpg` 64-column tiles.  Warp 8 streams the g and u
-// tiles ([128 x 64] bf16 each, 128-byte swizzle) into a 3-stage ring with TMA; warps 0-7 each own 16
-// rows, so the per-row xS_down accumulator stays in registers across the whole group.
-constexpr int FWD_BN = 64, FWD_ST = 3, FWD_TILE = 128 * FWD_BN * 2;  // 16 KB per tensor tile
-constexpr size_t FWD_SMEM = 1024 + FWD_ST * 2 * FWD_TILE + 2 * FWD_ST * sizeof(uint64_t);
+// CTA = one 128-row block x one column group of `tpg` 64-column tiles.  Warp 8 streams, per tile,
+// the g and u tiles ([128 x 64] bf16, 128-byte swizzle) and the tile's slices of B_gate, B_up
+// ([64 x r]) and A_down ([r x 64], 128-byte swizzle) into a 3-stage ring with TMA.  Warps 0-7 each
+// own 16 rows; every MMA operand comes from shared memory through ldmatrix, and the per-row
+// xS_down accumulator stays in registers across the whole group.
+constexpr int FWD_BN = 64, FWD_ST = 3, FWD_TILE = 128 * FWD_BN * 2;  // 16 KB per g / u tile
+__host__ __device__ constexpr int fwd_btile(int R) { return FWD_BN * R * 2; }
+__host__ __device__ constexpr int fwd_stage(int R) { return 2 * FWD_TILE + 3 * fwd_btile(R); }
+__host__ __device__ constexpr size_t fwd_smem(int R) { return 1024 + (size_t)FWD_ST * fwd_stage(R) + 2 * FWD_ST * 8; }
 
 template <int R>
 __global__ void __launch_bounds__(EPI_THREADS, 1)
-    k_mlp_fwd(const __grid_constant__ CUtensorMap tm_gu, const bf16* __restrict__ xs, const bf16* __restrict__ bg,
-              const bf16* __restrict__ bu, const bf16* __restrict__ ad, uint8_t* __restrict__ qh,
-              uint8_t* __restrict__ sh, float* __restrict__ xsd_part, bf16* __restrict__ xsd_out, int T, int N,
-              float s_g, float s_u, int tpg, int write_q, int* err) {
-  constexpr int KS = R / 16, NT = FWD_BN / 8;
+    k_mlp_fwd(const __grid_constant__ CUtensorMap tm_gu, const __grid_constant__ CUtensorMap tm_bg,
+              const __grid_constant__ CUtensorMap tm_bu, const __grid_constant__ CUtensorMap tm_ad,
+              const bf16* __restrict__ xs, uint8_t* __restrict__ qh, uint8_t* __restrict__ sh,
+              float* __restrict__ xsd_part, bf16* __restrict__ xsd_out, int T, int N, float s_g, float s_u, int tpg,
+              int write_q, int* err) {
+  constexpr int KS = R / 16, BT = fwd_btile(R), STG = fwd_stage(R);
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + FWD_ST * 2 * FWD_TILE);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + FWD_ST * STG);
   uint64_t* empty = full + FWD_ST;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t row0 = (int64_t)blockIdx.x * 128;
@@ -127,17 +132,26 @@ __global__ void __launch_bounds__(EPI_THREADS, 1)
   __syncthreads();
 
   if (warp == CONSUMERS) {  // TMA producer
-    if (lane == 0) prefetch_tmap(&tm_gu);
+    if (lane == 0) {
+      prefetch_tmap(&tm_gu);
+      prefetch_tmap(&tm_bg);
+      prefetch_tmap(&tm_bu);
+      prefetch_tmap(&tm_ad);
+    }
     int stage = 0;
     uint32_t phase = 0;
     for (int ct = 0; ct < tpg; ++ct) {
       const int n0 = (blockIdx.y * tpg + ct) * FWD_BN;
       if (!mbar_wait(&empty[stage], phase ^ 1, err, MX_DEV_TIMEOUT_PRODUCER)) break;
       if (lane == 0) {
-        uint8_t* dst = smem + stage * 2 * FWD_TILE;
-        mbar_arrive_expect_tx(&full[stage], 2 * FWD_TILE);
-        tma_load_2d(dst, &tm_gu, &full[stage], n0, (int)row0);
-        tma_load_2d(dst + FWD_TILE, &tm_gu, &full[stage], N + n0, (int)row0);
+        uint8_t* dst = smem + stage * STG;
+        uint64_t* fb = &full[stage];
+        mbar_arrive_expect_tx(fb, STG);
+        tma_load_2d(dst, &tm_gu, fb, n0, (int)row0);
+        tma_load_2d(dst + FWD_TILE, &tm_gu, fb, N + n0, (int)row0);
+        tma_load_2d(dst + 2 * FWD_TILE, &tm_bg, fb, 0, n0);
+        tma_load_2d(dst + 2 * FWD_TILE + BT, &tm_bu, fb, 0, n0);
+        tma_load_2d(dst + 2 * FWD_TILE + 2 * BT, &tm_ad, fb, n0, 0);
       }
       __syncwarp();
       if (++stage == FWD_ST) {
@@ -170,67 +184,84 @@ __global__ void __launch_bounds__(EPI_THREADS, 1)
 #pragma unroll
   for (int j = 0; j < R / 8; ++j) accx[j][0] = accx[j][1] = accx[j][2] = accx[j][3] = 0.f;
 
+  // ldmatrix lane roles: matrix mi = lane / 8, row-in-matrix lr = lane % 8
+  const int mi = lane >> 3, lr = lane & 7;
+  // g / u tiles: matrices (rows +0 / +8 of the warp's 16) x (tile 2p / 2p+1)
+  const int lrow = warp * 16 + (mi & 1) * 8 + lr;
+  const uint32_t gu_row = (uint32_t)lrow * 128, gu_sw = (uint32_t)(lrow & 7), gu_hi = (uint32_t)(mi >> 1);
   int stage = 0;
   uint32_t phase = 0;
   for (int ct = 0; ct < tpg; ++ct) {
     const int n0 = (blockIdx.y * tpg + ct) * FWD_BN;
     if (!mbar_wait(&full[stage], phase, err, MX_DEV_TIMEOUT_EPILOGUE)) break;
-    const uint8_t* tg = smem + stage * 2 * FWD_TILE;
-    const uint8_t* tu = tg + FWD_TILE;
-    uint32_t ga[NT], gb[NT], ua[NT], ub[NT];
+    const uint32_t sb = smem_u32(smem + stage * STG);
+    const uint32_t tg = sb, tu = sb + FWD_TILE, tbg = sb + 2 * FWD_TILE, tbu = tbg + BT, tad = tbu + BT;
 #pragma unroll
-    for (int i = 0; i < NT; ++i) {
-      const int c = 8 * i + 2 * t;
-      ga[i] = sw128_ld(tg, rl, c);
-      gb[i] = sw128_ld(tg, rl + 8, c);
-      ua[i] = sw128_ld(tu, rl, c);
-      ub[i] = sw128_ld(tu, rl + 8, c);
+    for (int b = 0; b < FWD_BN / 32; ++b) {
+      float hv[4][4];
+      uint32_t hp[4][2];
+#pragma unroll
+      for (int pp = 0; pp < 2; ++pp) {
+        const int p = 2 * b + pp;  // pair of n8 tiles (2p, 2p+1)
+        uint32_t G[4], U[4];
+        const uint32_t off = gu_row + ((((uint32_t)(2 * p) + gu_hi) ^ gu_sw) << 4);
+        ldsm4(G, tg + off);
+        ldsm4(U, tu + off);
+        float dg0[4] = {0.f, 0.f, 0.f, 0.f}, dg1[4] = {0.f, 0.f, 0.f, 0.f};
+        float du0[4] = {0.f, 0.f, 0.f, 0.f}, du1[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int kk = 0; kk < KS; ++kk) {
+          // B_gate / B_up slices [64 n x r], rows of 2r bytes: matrices (n-tile 2p / 2p+1) x (j 16kk.. / +8)
+          const uint32_t boff = (uint32_t)(8 * (2 * p + (mi >> 1)) + lr) * (2 * R) + (uint32_t)(2 * kk + (mi & 1)) * 16;
+          uint32_t BG[4], BU[4];
+          ldsm4(BG, tbg + boff);
+          ldsm4(BU, tbu + boff);
+          mma16816(dg0, axg[kk], BG[0], BG[1]);
+          mma16816(dg1, axg[kk], BG[2], BG[3]);
+          mma16816(du0, axu[kk], BU[0], BU[1]);
+          mma16816(du1, axu[kk], BU[2], BU[3]);
+        }
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+          const uint32_t ga = G[2 * q], gb = G[2 * q + 1], ua = U[2 * q], ub = U[2 * q + 1];
+          const float* dg = q ? dg1 : dg0;
+          const float* du = q ? du1 : du0;
+          const float gin[4] = {bf16_lo(ga), bf16_hi(ga), bf16_lo(gb), bf16_hi(gb)};
+          const float uin[4] = {bf16_lo(ua), bf16_hi(ua), bf16_lo(ub), bf16_hi(ub)};
+          float* h = hv[2 * pp + q];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float gg = bf16_round_f(gin[e] + s_g * dg[e]);
+            const float uu = bf16_round_f(uin[e] + s_u * du[e]);
+            h[e] = bf16_round_f(fdiv_full(gg, exp_neg(gg) + 1.0f) * uu);
+          }
+          hp[2 * pp + q][0] = pack_bf16x2(h[0], h[1]);
+          hp[2 * pp + q][1] = pack_bf16x2(h[2], h[3]);
+        }
+      }
+      if (write_q) quant_block16(hv, ra, T, n0 + 32 * b, qh, N, sh, N, t);
+      // xS_down += h (16 x 32 block) A_down^T: two k-slices of 16 columns
+#pragma unroll
+      for (int mm = 0; mm < 2; ++mm) {
+        const uint32_t a[4] = {hp[2 * mm][0], hp[2 * mm][1], hp[2 * mm + 1][0], hp[2 * mm + 1][1]};
+        const int m = 2 * b + mm;  // k-slice within the 64-column tile
+#pragma unroll
+        for (int jp = 0; jp < R / 16; ++jp) {
+          // A_down slice [r x 64], 128-byte rows, 128-byte swizzle: matrices (j 16jp.. / +8) x (cols 16m / +8)
+          const uint32_t j = (uint32_t)(16 * jp + 8 * (mi >> 1) + lr);
+          const uint32_t chunk = (uint32_t)(2 * m + (mi & 1));
+          uint32_t AD[4];
+          ldsm4(AD, tad + j * 128 + ((chunk ^ (j & 7)) << 4));
+          mma16816(accx[2 * jp], a, AD[0], AD[1]);
+          mma16816(accx[2 * jp + 1], a, AD[2], AD[3]);
+        }
+      }
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[stage]);
     if (++stage == FWD_ST) {
       stage = 0;
       phase ^= 1;
-    }
-    float hv[NT][4];
-    uint32_t hp[NT][2];
-#pragma unroll
-    for (int i = 0; i < NT; ++i) {
-      const int nc = n0 + 8 * i;
-      float dg[4] = {0.f, 0.f, 0.f, 0.f}, du[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-      for (int kk = 0; kk < KS; ++kk) {
-        const bf16* pbg = bg + (int64_t)(nc + g) * R + 16 * kk + 2 * t;
-        const bf16* pbu = bu + (int64_t)(nc + g) * R + 16 * kk + 2 * t;
-        mma16816(dg, axg[kk], ld32g(pbg), ld32g(pbg + 8));
-        mma16816(du, axu[kk], ld32g(pbu), ld32g(pbu + 8));
-      }
-      const float gin[4] = {bf16_lo(ga[i]), bf16_hi(ga[i]), bf16_lo(gb[i]), bf16_hi(gb[i])};
-      const float uin[4] = {bf16_lo(ua[i]), bf16_hi(ua[i]), bf16_lo(ub[i]), bf16_hi(ub[i])};
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float gg = bf16_round_f(gin[e] + s_g * dg[e]);
-        const float uu = bf16_round_f(uin[e] + s_u * du[e]);
-        hv[i][e] = bf16_round_f(fdiv_full(gg, exp_neg(gg) + 1.0f) * uu);
-      }
-      hp[i][0] = pack_bf16x2(hv[i][0], hv[i][1]);
-      hp[i][1] = pack_bf16x2(hv[i][2], hv[i][3]);
-    }
-    if (write_q) {
-#pragma unroll
-      for (int b = 0; b < FWD_BN / 32; ++b) {
-        const float(&blk)[4][4] = *reinterpret_cast<const float(*)[4][4]>(&hv[4 * b][0]);
-        quant_block16(blk, ra, T, n0 + 32 * b, qh, N, sh, N, t);
-      }
-    }
-#pragma unroll
-    for (int m = 0; m < FWD_BN / 16; ++m) {
-      const uint32_t a[4] = {hp[2 * m][0], hp[2 * m][1], hp[2 * m + 1][0], hp[2 * m + 1][1]};
-#pragma unroll
-      for (int jt = 0; jt < R / 8; ++jt) {
-        const bf16* pad = ad + (int64_t)(8 * jt + g) * N + n0 + 16 * m + 2 * t;
-        mma16816(accx[jt], a, ld32g(pad), ld32g(pad + 8));
-      }
     }
   }
 #pragma unroll
@@ -248,35 +279,42 @@ __global__ void __launch_bounds__(EPI_THREADS, 1)
 }
 
 // ------------------------------------------------------------------------------------------------ backward
-// CTA = one super-block of SB rows x one column group of `tpg` 32-column tiles.  Warp 8 streams
-// [128 x 32] bf16 tiles of g, u and dh (64-byte swizzle) into a 4-stage ring with TMA, column tile
-// outer, 128-row step inner.  Warps 0-7 each own 16 rows of every step:
+// CTA = one super-block of SB rows x one column group of `tpg` 32-column tiles.  Warp 8 streams, per
+// (column tile, 128-row step), the [128 x 32] bf16 tiles of g, u and dh (64-byte swizzle) plus the
+// column tile's slices of B_gate, B_up ([32 x r]) and A_down ([r x 32]) into a 4-stage ring with TMA;
+// column tile outer, row step inner.  Warps 0-7 each own 16 rows of every step:
 //   * dB_gate, dB_up, dA_down (sums over rows) accumulate in registers over the super-block, then the
 //     8 warps' tiles are summed in a fixed order through shared memory -> one partial per super-block;
 //   * dxa_gate, dxa_up, xS_down (sums over columns) accumulate in a shared-memory [SB x 3r] buffer
-//     that each warp only touches in its own rows, written once per CTA as the group's partial.
-// No atomics: the result is deterministic.
-constexpr int BWD_BN = 32, BWD_ST = 4, BWD_TILE = 128 * BWD_BN * 2;  // 8 KB per tensor tile
-
+//     (row stride padded for conflict-free access) that each warp only touches in its own rows,
+//     written once per CTA as the group's partial.
+// No atomics: the result is deterministic.  All MMA operands come from shared memory through
+// ldmatrix (.trans where the tile is stored transposed to the operand).
+constexpr int BWD_BN = 32, BWD_ST = 4, BWD_TILE = 128 * BWD_BN * 2;  // 8 KB per g / u / dh tile
+__host__ __device__ constexpr int bwd_btile(int R) { return BWD_BN * R * 2; }
+__host__ __device__ constexpr int bwd_stage(int R) { return 3 * BWD_TILE + 3 * bwd_btile(R); }
+__host__ __device__ constexpr int bwd_rs(int R) { return 3 * R + 8; }      // padded row stride of the row sums
+__host__ __device__ constexpr int bwd_ws() { return BWD_BN + 8; }          // padded stride of the reduction tiles
 __host__ __device__ constexpr size_t bwd_smem(int R, int SB) {
-  return 1024 + (size_t)BWD_ST * 3 * BWD_TILE + (size_t)SB * 3 * R * 4 + (size_t)CONSUMERS * R * BWD_BN * 4 +
+  return 1024 + (size_t)BWD_ST * bwd_stage(R) + (size_t)SB * bwd_rs(R) * 4 + (size_t)CONSUMERS * R * bwd_ws() * 4 +
          2 * BWD_ST * sizeof(uint64_t);
 }
 
 template <int R>
 __global__ void __launch_bounds__(EPI_THREADS, 1)
     k_mlp_bwd(const __grid_constant__ CUtensorMap tm_gu, const __grid_constant__ CUtensorMap tm_dh,
-              const bf16* __restrict__ xs, const bf16* __restrict__ dxd, const bf16* __restrict__ bg,
-              const bf16* __restrict__ bu, const bf16* __restrict__ ad, uint8_t* __restrict__ q,
-              uint8_t* __restrict__ s, float* __restrict__ dxa_part, float* __restrict__ dbg_part,
-              float* __restrict__ dbu_part, float* __restrict__ dad_part, int T, int Tpad, int N, float s_g,
-              float s_u, int SB, int tpg, int write_q, int* err) {
-  constexpr int KS = R / 16, NT = BWD_BN / 8, R3 = 3 * R;
+              const __grid_constant__ CUtensorMap tm_bg, const __grid_constant__ CUtensorMap tm_bu,
+              const __grid_constant__ CUtensorMap tm_ad, const bf16* __restrict__ xs, const bf16* __restrict__ dxd,
+              uint8_t* __restrict__ q, uint8_t* __restrict__ s, float* __restrict__ dxa_part,
+              float* __restrict__ dbg_part, float* __restrict__ dbu_part, float* __restrict__ dad_part, int T,
+              int Tpad, int N, float s_g, float s_u, int SB, int tpg, int write_q, int* err) {
+  constexpr int KS = R / 16, NT = BWD_BN / 8, R3 = 3 * R, RS = bwd_rs(R), WS = bwd_ws();
+  constexpr int BT = bwd_btile(R), STG = bwd_stage(R);
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
-  float* acc_rows = reinterpret_cast<float*>(smem + BWD_ST * 3 * BWD_TILE);  // [SB][3R]
-  float* scratch = acc_rows + (size_t)SB * R3;                                 // [CONSUMERS][R][BN]
-  uint64_t* full = reinterpret_cast<uint64_t*>(scratch + CONSUMERS * R * BWD_BN);
+  float* acc_rows = reinterpret_cast<float*>(smem + BWD_ST * STG);  // [SB][RS]
+  float* scratch = acc_rows + (size_t)SB * RS;                        // [CONSUMERS][R][WS]
+  uint64_t* full = reinterpret_cast<uint64_t*>(scratch + CONSUMERS * R * WS);
   uint64_t* empty = full + BWD_ST;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int sbi = blockIdx.x, cg = blockIdx.y;
@@ -295,6 +333,9 @@ __global__ void __launch_bounds__(EPI_THREADS, 1)
     if (lane == 0) {
       prefetch_tmap(&tm_gu);
       prefetch_tmap(&tm_dh);
+      prefetch_tmap(&tm_bg);
+      prefetch_tmap(&tm_bu);
+      prefetch_tmap(&tm_ad);
     }
     int stage = 0;
     uint32_t phase = 0;
@@ -307,11 +348,15 @@ __global__ void __launch_bounds__(EPI_THREADS, 1)
           break;
         }
         if (lane == 0) {
-          uint8_t* dst = smem + stage * 3 * BWD_TILE;
-          mbar_arrive_expect_tx(&full[stage], 3 * BWD_TILE);
-          tma_load_2d(dst, &tm_gu, &full[stage], n0, r);
-          tma_load_2d(dst + BWD_TILE, &tm_gu, &full[stage], N + n0, r);
-          tma_load_2d(dst + 2 * BWD_TILE, &tm_dh, &full[stage], n0, r);
+          uint8_t* dst = smem + stage * STG;
+          uint64_t* fb = &full[stage];
+          mbar_arrive_expect_tx(fb, STG);
+          tma_load_2d(dst, &tm_gu, fb, n0, r);
+          tma_load_2d(dst + BWD_TILE, &tm_gu, fb, N + n0, r);
+          tma_load_2d(dst + 2 * BWD_TILE, &tm_dh, fb, n0, r);
+          tma_load_2d(dst + 3 * BWD_TILE, &tm_bg, fb, 0, n0);
+          tma_load_2d(dst + 3 * BWD_TILE + BT, &tm_bu, fb, 0, n0);
+          tma_load_2d(dst + 3 * BWD_TILE + 2 * BT, &tm_ad, fb, n0, 0);
         }
         __syncwarp();
         if (++stage == BWD_ST) {
@@ -324,9 +369,14 @@ __global__ void __launch_bounds__(EPI_THREADS, 1)
   }
 
   const int g = lane >> 2, t = lane & 3;
+  const int mi = lane >> 3, lr = lane & 7;
   const int nthr = CONSUMERS * 32;
-  for (int i = threadIdx.x; i < SB * R3; i += nthr) acc_rows[i] = 0.f;
+  for (int i = threadIdx.x; i < SB * RS; i += nthr) acc_rows[i] = 0.f;
   consumers_sync(nthr);
+
+  // g / u / dh tiles (64-byte rows, 64-byte swizzle): this lane's ldmatrix row
+  const int lrow = warp * 16 + (mi & 1) * 8 + lr;
+  const uint32_t t_row = (uint32_t)lrow * 64, t_sw = (uint32_t)((lrow >> 1) & 3), t_hi = (uint32_t)(mi >> 1);
 
   int stage = 0;
   uint32_t phase = 0;
@@ -340,26 +390,9 @@ __global__ void __launch_bounds__(EPI_THREADS, 1)
       for (int i = 0; i < NT; ++i)
 #pragma unroll
         for (int e = 0; e < 4; ++e) aBg[a][i][e] = aBu[a][i][e] = aAd[a][i][e] = 0.f;
-    // B fragments of this column tile (same for every row step)
-    uint32_t bgf[KS][NT][2], buf_[KS][NT][2], adf[KS][NT][2];
-#pragma unroll
-    for (int kk = 0; kk < KS; ++kk)
-#pragma unroll
-      for (int i = 0; i < NT; ++i) {
-        const int nc = n0 + 8 * i;
-        const bf16* pbg = bg + (int64_t)(nc + g) * R + 16 * kk + 2 * t;
-        const bf16* pbu = bu + (int64_t)(nc + g) * R + 16 * kk + 2 * t;
-        bgf[kk][i][0] = ld32g(pbg);
-        bgf[kk][i][1] = ld32g(pbg + 8);
-        buf_[kk][i][0] = ld32g(pbu);
-        buf_[kk][i][1] = ld32g(pbu + 8);
-        const bf16* p0 = ad + (int64_t)(16 * kk + 2 * t) * N + nc + g;
-        adf[kk][i][0] = ld16x2(p0, p0 + N);
-        adf[kk][i][1] = ld16x2(p0 + 8 * (int64_t)N, p0 + 9 * (int64_t)N);
-      }
 
     for (int r = r_begin; r < r_end; r += 128) {
-      const int rl = warp * 16 + g;                 // row within the step
+      const int rl = warp * 16 + g;
       const int64_t ra = r + rl, rb = ra + 8;
       const bool va = ra < T, vb = rb < T;
       uint32_t axg[KS][4], axu[KS][4], axd[KS][4];
@@ -386,106 +419,120 @@ __global__ void __launch_bounds__(EPI_THREADS, 1)
         ok = false;
         break;
       }
-      const uint8_t* tg = smem + stage * 3 * BWD_TILE;
-      const uint8_t* tu = tg + BWD_TILE;
-      const uint8_t* th = tg + 2 * BWD_TILE;
-      uint32_t ga[NT], gb[NT], ua[NT], ub[NT], ha[NT], hb[NT];
+      const uint32_t sb = smem_u32(smem + stage * STG);
+      const uint32_t tg = sb, tu = sb + BWD_TILE, th = sb + 2 * BWD_TILE;
+      const uint32_t tbg = sb + 3 * BWD_TILE, tbu = tbg + BT, tad = tbu + BT;
+
+      uint32_t dgp[NT][2], dup[NT][2], hp[NT][2];
+      float dgv[NT][4], duv[NT][4];
 #pragma unroll
-      for (int i = 0; i < NT; ++i) {
-        const int c = 8 * i + 2 * t;
-        ga[i] = sw64_ld(tg, rl, c);
-        gb[i] = sw64_ld(tg, rl + 8, c);
-        ua[i] = sw64_ld(tu, rl, c);
-        ub[i] = sw64_ld(tu, rl + 8, c);
-        ha[i] = sw64_ld(th, rl, c);
-        hb[i] = sw64_ld(th, rl + 8, c);
+      for (int p = 0; p < NT / 2; ++p) {
+        uint32_t G[4], U[4], D[4];
+        const uint32_t off = t_row + ((((uint32_t)(2 * p) + t_hi) ^ t_sw) << 4);
+        ldsm4(G, tg + off);
+        ldsm4(U, tu + off);
+        ldsm4(D, th + off);
+        float dg[2][4] = {}, du[2][4] = {}, dd[2][4] = {};
+#pragma unroll
+        for (int kk = 0; kk < KS; ++kk) {
+          // B_gate / B_up slices [32 n x r]: (n-tile 2p / 2p+1) x (j 16kk / +8)
+          const uint32_t boff = (uint32_t)(8 * (2 * p + (mi >> 1)) + lr) * (2 * R) + (uint32_t)(2 * kk + (mi & 1)) * 16;
+          uint32_t BG[4], BU[4], AD[4];
+          ldsm4(BG, tbg + boff);
+          ldsm4(BU, tbu + boff);
+          // A_down slice [r x 32 n] (64-byte rows) transposed: (n-tile 2p / 2p+1) x (j 16kk / +8)
+          const uint32_t aoff = (uint32_t)(16 * kk + 8 * (mi & 1) + lr) * 64 + (uint32_t)(2 * p + (mi >> 1)) * 16;
+          ldsm4t(AD, tad + aoff);
+#pragma unroll
+          for (int qq = 0; qq < 2; ++qq) {
+            mma16816(dg[qq], axg[kk], BG[2 * qq], BG[2 * qq + 1]);
+            mma16816(du[qq], axu[kk], BU[2 * qq], BU[2 * qq + 1]);
+            mma16816(dd[qq], axd[kk], AD[2 * qq], AD[2 * qq + 1]);
+          }
+        }
+#pragma unroll
+        for (int qq = 0; qq < 2; ++qq) {
+          const int i = 2 * p + qq;
+          const float gin[4] = {bf16_lo(G[2 * qq]), bf16_hi(G[2 * qq]), bf16_lo(G[2 * qq + 1]), bf16_hi(G[2 * qq + 1])};
+          const float uin[4] = {bf16_lo(U[2 * qq]), bf16_hi(U[2 * qq]), bf16_lo(U[2 * qq + 1]), bf16_hi(U[2 * qq + 1])};
+          const float hin[4] = {bf16_lo(D[2 * qq]), bf16_hi(D[2 * qq]), bf16_lo(D[2 * qq + 1]), bf16_hi(D[2 * qq + 1])};
+          float hvv[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float gg = bf16_round_f(gin[e] + s_g * dg[qq][e]);
+            const float uu = bf16_round_f(uin[e] + s_u * du[qq][e]);
+            const float en = exp_neg(gg) + 1.0f;
+            const float sl = fdiv_full(gg, en);
+            const float sig = fdiv_full(1.0f, en);
+            hvv[e] = bf16_round_f(sl * uu);
+            const float dh = bf16_round_f(hin[e] + dd[qq][e]);
+            duv[i][e] = bf16_round_f(dh * sl);
+            dgv[i][e] = bf16_round_f(((dh * uu) * sig) * (gg * (1.0f - sig) + 1.0f));
+          }
+          hp[i][0] = pack_bf16x2(hvv[0], hvv[1]);
+          hp[i][1] = pack_bf16x2(hvv[2], hvv[3]);
+          dgp[i][0] = pack_bf16x2(dgv[i][0], dgv[i][1]);
+          dgp[i][1] = pack_bf16x2(dgv[i][2], dgv[i][3]);
+          dup[i][0] = pack_bf16x2(duv[i][0], duv[i][1]);
+          dup[i][1] = pack_bf16x2(duv[i][2], duv[i][3]);
+        }
+      }
+      if (write_q) {
+        quant_block16(dgv, ra, T, n0, q, N2, s, N2, t);
+        quant_block16(duv, ra, T, (int64_t)N + n0, q, N2, s, N2, t);
+      }
+      // per-row products (sums over columns) into the shared-memory row accumulators
+      float* A0 = acc_rows + (int64_t)(ra - r_begin) * RS;
+      float* A1 = A0 + 8 * RS;
+#pragma unroll
+      for (int jp = 0; jp < R / 16; ++jp) {
+        float pg[2][4], pu[2][4], px[2][4];
+#pragma unroll
+        for (int h2 = 0; h2 < 2; ++h2) {
+          const int c = 16 * jp + 8 * h2 + 2 * t;
+          const float2 a0 = *reinterpret_cast<const float2*>(A0 + c), a1 = *reinterpret_cast<const float2*>(A1 + c);
+          pg[h2][0] = a0.x; pg[h2][1] = a0.y; pg[h2][2] = a1.x; pg[h2][3] = a1.y;
+          const float2 b0 = *reinterpret_cast<const float2*>(A0 + R + c), b1 = *reinterpret_cast<const float2*>(A1 + R + c);
+          pu[h2][0] = b0.x; pu[h2][1] = b0.y; pu[h2][2] = b1.x; pu[h2][3] = b1.y;
+          const float2 c0 = *reinterpret_cast<const float2*>(A0 + 2 * R + c), c1 = *reinterpret_cast<const float2*>(A1 + 2 * R + c);
+          px[h2][0] = c0.x; px[h2][1] = c0.y; px[h2][2] = c1.x; px[h2][3] = c1.y;
+        }
+#pragma unroll
+        for (int mm = 0; mm < NT / 2; ++mm) {
+          const uint32_t adg[4] = {dgp[2 * mm][0], dgp[2 * mm][1], dgp[2 * mm + 1][0], dgp[2 * mm + 1][1]};
+          const uint32_t adu[4] = {dup[2 * mm][0], dup[2 * mm][1], dup[2 * mm + 1][0], dup[2 * mm + 1][1]};
+          const uint32_t ah[4] = {hp[2 * mm][0], hp[2 * mm][1], hp[2 * mm + 1][0], hp[2 * mm + 1][1]};
+          // B[k = n][col j] = B_gate[n][j]: transposed ldmatrix of (n 16mm / +8) x (j-tile 2jp / 2jp+1)
+          const uint32_t boff = (uint32_t)(16 * mm + 8 * (mi & 1) + lr) * (2 * R) + (uint32_t)(2 * jp + (mi >> 1)) * 16;
+          uint32_t BG[4], BU[4], AD[4];
+          ldsm4t(BG, tbg + boff);
+          ldsm4t(BU, tbu + boff);
+          // B[k = n][col j] = A_down[j][n]: ldmatrix of (j-tile 2jp / 2jp+1) x (n 16mm / +8)
+          const uint32_t aoff = (uint32_t)(16 * jp + 8 * (mi >> 1) + lr) * 64 + (uint32_t)(2 * mm + (mi & 1)) * 16;
+          ldsm4(AD, tad + aoff);
+#pragma unroll
+          for (int h2 = 0; h2 < 2; ++h2) {
+            mma16816(pg[h2], adg, BG[2 * h2], BG[2 * h2 + 1]);
+            mma16816(pu[h2], adu, BU[2 * h2], BU[2 * h2 + 1]);
+            mma16816(px[h2], ah, AD[2 * h2], AD[2 * h2 + 1]);
+          }
+        }
+#pragma unroll
+        for (int h2 = 0; h2 < 2; ++h2) {
+          const int c = 16 * jp + 8 * h2 + 2 * t;
+          *reinterpret_cast<float2*>(A0 + c) = make_float2(pg[h2][0], pg[h2][1]);
+          *reinterpret_cast<float2*>(A1 + c) = make_float2(pg[h2][2], pg[h2][3]);
+          *reinterpret_cast<float2*>(A0 + R + c) = make_float2(pu[h2][0], pu[h2][1]);
+          *reinterpret_cast<float2*>(A1 + R + c) = make_float2(pu[h2][2], pu[h2][3]);
+          *reinterpret_cast<float2*>(A0 + 2 * R + c) = make_float2(px[h2][0], px[h2][1]);
+          *reinterpret_cast<float2*>(A1 + 2 * R + c) = make_float2(px[h2][2], px[h2][3]);
+        }
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[stage]);
       if (++stage == BWD_ST) {
         stage = 0;
         phase ^= 1;
-      }
-
-      uint32_t dgp[NT][2], dup[NT][2], hp[NT][2];
-      float dgv[NT][4], duv[NT][4];
-#pragma unroll
-      for (int i = 0; i < NT; ++i) {
-        float dg[4] = {0.f, 0.f, 0.f, 0.f}, du[4] = {0.f, 0.f, 0.f, 0.f}, dd[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-        for (int kk = 0; kk < KS; ++kk) {
-          mma16816(dg, axg[kk], bgf[kk][i][0], bgf[kk][i][1]);
-          mma16816(du, axu[kk], buf_[kk][i][0], buf_[kk][i][1]);
-          mma16816(dd, axd[kk], adf[kk][i][0], adf[kk][i][1]);
-        }
-        const float gin[4] = {bf16_lo(ga[i]), bf16_hi(ga[i]), bf16_lo(gb[i]), bf16_hi(gb[i])};
-        const float uin[4] = {bf16_lo(ua[i]), bf16_hi(ua[i]), bf16_lo(ub[i]), bf16_hi(ub[i])};
-        const float hin[4] = {bf16_lo(ha[i]), bf16_hi(ha[i]), bf16_lo(hb[i]), bf16_hi(hb[i])};
-        float hvv[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float gg = bf16_round_f(gin[e] + s_g * dg[e]);
-          const float uu = bf16_round_f(uin[e] + s_u * du[e]);
-          const float en = exp_neg(gg) + 1.0f;
-          const float sl = fdiv_full(gg, en);
-          const float sig = fdiv_full(1.0f, en);
-          hvv[e] = bf16_round_f(sl * uu);
-          const float dh = bf16_round_f(hin[e] + dd[e]);
-          duv[i][e] = bf16_round_f(dh * sl);
-          dgv[i][e] = bf16_round_f(((dh * uu) * sig) * (gg * (1.0f - sig) + 1.0f));
-        }
-        hp[i][0] = pack_bf16x2(hvv[0], hvv[1]);
-        hp[i][1] = pack_bf16x2(hvv[2], hvv[3]);
-        dgp[i][0] = pack_bf16x2(dgv[i][0], dgv[i][1]);
-        dgp[i][1] = pack_bf16x2(dgv[i][2], dgv[i][3]);
-        dup[i][0] = pack_bf16x2(duv[i][0], duv[i][1]);
-        dup[i][1] = pack_bf16x2(duv[i][2], duv[i][3]);
-      }
-      if (write_q) {
-        const float(&bgv)[4][4] = *reinterpret_cast<const float(*)[4][4]>(&dgv[0][0]);
-        const float(&buv)[4][4] = *reinterpret_cast<const float(*)[4][4]>(&duv[0][0]);
-        quant_block16(bgv, ra, T, n0, q, N2, s, N2, t);
-        quant_block16(buv, ra, T, (int64_t)N + n0, q, N2, s, N2, t);
-      }
-      // per-row products (sums over columns) into the shared-memory row accumulators
-      float* A0 = acc_rows + (int64_t)(ra - r_begin) * R3;
-      float* A1 = A0 + 8 * R3;
-      const uint32_t adg[4] = {dgp[0][0], dgp[0][1], dgp[1][0], dgp[1][1]};
-      const uint32_t adg2[4] = {dgp[2][0], dgp[2][1], dgp[3][0], dgp[3][1]};
-      const uint32_t adu[4] = {dup[0][0], dup[0][1], dup[1][0], dup[1][1]};
-      const uint32_t adu2[4] = {dup[2][0], dup[2][1], dup[3][0], dup[3][1]};
-      const uint32_t ah[4] = {hp[0][0], hp[0][1], hp[1][0], hp[1][1]};
-      const uint32_t ah2[4] = {hp[2][0], hp[2][1], hp[3][0], hp[3][1]};
-#pragma unroll
-      for (int jt = 0; jt < R / 8; ++jt) {
-        const int c = 8 * jt + 2 * t;
-        const int j = 8 * jt + g;
-        float pg[4], pu[4], px[4];
-        {
-          const float2 a0 = *reinterpret_cast<const float2*>(A0 + c), a1 = *reinterpret_cast<const float2*>(A1 + c);
-          pg[0] = a0.x; pg[1] = a0.y; pg[2] = a1.x; pg[3] = a1.y;
-          const float2 b0 = *reinterpret_cast<const float2*>(A0 + R + c), b1 = *reinterpret_cast<const float2*>(A1 + R + c);
-          pu[0] = b0.x; pu[1] = b0.y; pu[2] = b1.x; pu[3] = b1.y;
-          const float2 c0 = *reinterpret_cast<const float2*>(A0 + 2 * R + c), c1 = *reinterpret_cast<const float2*>(A1 + 2 * R + c);
-          px[0] = c0.x; px[1] = c0.y; px[2] = c1.x; px[3] = c1.y;
-        }
-        // B[k = n][col j]: (n 2t..2t+1 | 2t+8..2t+9, col j), two 16-column halves of the tile
-#pragma unroll
-        for (int m = 0; m < 2; ++m) {
-          const int64_t nn = n0 + 16 * m + 2 * t;
-          const bf16* pb = bg + nn * R + j;
-          const bf16* pu_ = bu + nn * R + j;
-          const bf16* pad = ad + (int64_t)j * N + nn;
-          mma16816(pg, m ? adg2 : adg, ld16x2(pb, pb + R), ld16x2(pb + 8 * R, pb + 9 * R));
-          mma16816(pu, m ? adu2 : adu, ld16x2(pu_, pu_ + R), ld16x2(pu_ + 8 * R, pu_ + 9 * R));
-          mma16816(px, m ? ah2 : ah, ld32g(pad), ld32g(pad + 8));
-        }
-        *reinterpret_cast<float2*>(A0 + c) = make_float2(pg[0], pg[1]);
-        *reinterpret_cast<float2*>(A1 + c) = make_float2(pg[2], pg[3]);
-        *reinterpret_cast<float2*>(A0 + R + c) = make_float2(pu[0], pu[1]);
-        *reinterpret_cast<float2*>(A1 + R + c) = make_float2(pu[2], pu[3]);
-        *reinterpret_cast<float2*>(A0 + 2 * R + c) = make_float2(px[0], px[1]);
-        *reinterpret_cast<float2*>(A1 + 2 * R + c) = make_float2(px[2], px[3]);
       }
       // column products (sums over rows): [j x n] += xa^T (j x rows) . [dg | du | h] (rows x n)
 #pragma unroll
@@ -505,24 +552,22 @@ __global__ void __launch_bounds__(EPI_THREADS, 1)
     // fixed-order sum of the 8 warps' column products, one product at a time through `scratch`
 #pragma unroll
     for (int which = 0; which < 3; ++which) {
-      float* W = scratch + warp * (R * BWD_BN);
+      float* W = scratch + warp * (R * WS);
 #pragma unroll
       for (int jm = 0; jm < KS; ++jm)
 #pragma unroll
         for (int i = 0; i < NT; ++i) {
           const float* a = which == 0 ? aBg[jm][i] : (which == 1 ? aBu[jm][i] : aAd[jm][i]);
           const int j0 = 16 * jm + g, nn = 8 * i + 2 * t;
-          W[j0 * BWD_BN + nn] = a[0];
-          W[j0 * BWD_BN + nn + 1] = a[1];
-          W[(j0 + 8) * BWD_BN + nn] = a[2];
-          W[(j0 + 8) * BWD_BN + nn + 1] = a[3];
+          *reinterpret_cast<float2*>(W + j0 * WS + nn) = make_float2(a[0], a[1]);
+          *reinterpret_cast<float2*>(W + (j0 + 8) * WS + nn) = make_float2(a[2], a[3]);
         }
       consumers_sync(nthr);
       for (int idx = threadIdx.x; idx < R * BWD_BN; idx += nthr) {
+        const int j = idx / BWD_BN, n = idx % BWD_BN;
         float v = 0.f;
 #pragma unroll
-        for (int w = 0; w < CONSUMERS; ++w) v += scratch[w * R * BWD_BN + idx];
-        const int j = idx / BWD_BN, n = idx % BWD_BN;
+        for (int w = 0; w < CONSUMERS; ++w) v += scratch[w * R * WS + j * WS + n];
         if (which == 0)
           dbg_part[((int64_t)sbi * N + n0 + n) * R + j] = v;
         else if (which == 1)
@@ -537,7 +582,7 @@ __global__ void __launch_bounds__(EPI_THREADS, 1)
   float* P = dxa_part + (int64_t)cg * T * R3;
   for (int i = threadIdx.x; i < (r_end - r_begin) * R3; i += nthr) {
     const int64_t row = r_begin + i / R3;
-    if (row < T) P[row * R3 + i % R3] = acc_rows[i];
+    if (row < T) P[row * R3 + i % R3] = acc_rows[(i / R3) * RS + i % R3];
   }
 }
 
@@ -698,21 +743,32 @@ extern "C" int mxm_mlp_fwd_epilogue(const void* gu, const void* xs, const void* 
   const int nt = (int)(N / FWD_BN);
   MX_CHECK_ARG(col_groups >= 1 && nt % col_groups == 0, "mxm_mlp_fwd_epilogue: col_groups must divide N/64");
   MX_CHECK_ARG(col_groups == 1 || xsd_part, "mxm_mlp_fwd_epilogue: partial buffer needed for col_groups > 1");
-  MX_CHECK_ARG(mx_aligned(gu, 16), "mxm_mlp_fwd_epilogue: gu must be 16-byte aligned");
-  CUtensorMap tm;
+  MX_CHECK_ARG(mx_aligned(gu, 16) && mx_aligned(bg, 16) && mx_aligned(bu, 16) && mx_aligned(ad, 16),
+               "mxm_mlp_fwd_epilogue: gu / bg / bu / ad must be 16-byte aligned");
+  CUtensorMap tm, tbg, tbu, tad;
   if (int e = mx_make_tmap_2d(&tm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, gu, (uint64_t)(2 * N), (uint64_t)T,
                               (uint64_t)(4 * N), FWD_BN, 128, CU_TENSOR_MAP_SWIZZLE_128B))
+    return e;
+  if (int e = mx_make_tmap_2d(&tbg, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, bg, (uint64_t)r, (uint64_t)N,
+                              (uint64_t)(2 * r), r, FWD_BN, CU_TENSOR_MAP_SWIZZLE_NONE))
+    return e;
+  if (int e = mx_make_tmap_2d(&tbu, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, bu, (uint64_t)r, (uint64_t)N,
+                              (uint64_t)(2 * r), r, FWD_BN, CU_TENSOR_MAP_SWIZZLE_NONE))
+    return e;
+  if (int e = mx_make_tmap_2d(&tad, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, ad, (uint64_t)N, (uint64_t)r,
+                              (uint64_t)(2 * N), FWD_BN, r, CU_TENSOR_MAP_SWIZZLE_128B))
     return e;
   dim3 grid((unsigned)((T + 127) / 128), (unsigned)col_groups);
   cudaStream_t st = (cudaStream_t)stream;
   const int tpg = nt / col_groups;
   bf16* direct = col_groups == 1 ? (bf16*)xsd : nullptr;
+  const size_t smem = fwd_smem(r);
   auto go = [&](auto kern) -> int {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)FWD_SMEM);
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return mx_cuda_status(e, "mlp fwd epilogue: set smem");
-    kern<<<grid, EPI_THREADS, FWD_SMEM, st>>>(tm, (const bf16*)xs, (const bf16*)bg, (const bf16*)bu, (const bf16*)ad,
-                                              (uint8_t*)qh, (uint8_t*)sh, (float*)xsd_part, direct, (int)T, (int)N,
-                                              s_g, s_u, tpg, qh != nullptr, mx_dev_error_ptr());
+    kern<<<grid, EPI_THREADS, smem, st>>>(tm, tbg, tbu, tad, (const bf16*)xs, (uint8_t*)qh, (uint8_t*)sh,
+                                          (float*)xsd_part, direct, (int)T, (int)N, s_g, s_u, tpg, qh != nullptr,
+                                          mx_dev_error_ptr());
     mx_note_launch();
     return mx_launch_status("mlp fwd epilogue");
   };
@@ -727,7 +783,7 @@ extern "C" int mxm_mlp_fwd_epilogue(const void* gu, const void* xs, const void* 
   return MXM_OK;
 }
 
-static int bwd_super_block(int r) { return r == 16 ? 512 : 256; }
+static int bwd_super_block(int r) { return r == 16 ? 384 : 128; }
 
 // Backward partition: super-blocks of SB rows (shared-memory row accumulators bound SB) and the
 // column-group count that minimises partial-sum bytes while giving every SM at least two CTAs
@@ -737,7 +793,7 @@ extern "C" int mxm_mlp_bwd_partitions(int64_t T, int64_t N, int r, int* super_bl
                "mxm_mlp_bwd_partitions: bad args");
   const int64_t tpad = (T + 127) / 128 * 128;
   int sb = bwd_super_block(r);
-  while (sb > 128 && (tpad + sb - 1) / sb < 2) sb /= 2;   // small T: smaller super-blocks, more CTAs
+  while (sb > 128 && (tpad + sb - 1) / sb < 2) sb -= 128;  // small T: smaller super-blocks, more CTAs
   const int64_t nsb = (tpad + sb - 1) / sb;
   const int nt = (int)(N / BWD_BN);
   const int64_t want = 2 * (int64_t)mxm_num_sms();
@@ -765,13 +821,24 @@ extern "C" int mxm_mlp_bwd_epilogue(const void* gu, const void* xs, const void* 
   MX_CHECK_ARG(col_groups >= 1 && nt % col_groups == 0 && super_block >= 128 && super_block % 128 == 0 &&
                    super_block <= bwd_super_block(r),
                "mxm_mlp_bwd_epilogue: bad partition (%d, %d)", super_block, col_groups);
-  MX_CHECK_ARG(mx_aligned(gu, 16) && mx_aligned(dhm, 16), "mxm_mlp_bwd_epilogue: gu / dhm must be 16-byte aligned");
-  CUtensorMap tgu, tdh;
+  MX_CHECK_ARG(mx_aligned(gu, 16) && mx_aligned(dhm, 16) && mx_aligned(bg, 16) && mx_aligned(bu, 16) &&
+                   mx_aligned(ad, 16),
+               "mxm_mlp_bwd_epilogue: gu / dhm / bg / bu / ad must be 16-byte aligned");
+  CUtensorMap tgu, tdh, tbg, tbu, tad;
   if (int e = mx_make_tmap_2d(&tgu, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, gu, (uint64_t)(2 * N), (uint64_t)T,
                               (uint64_t)(4 * N), BWD_BN, 128, CU_TENSOR_MAP_SWIZZLE_64B))
     return e;
   if (int e = mx_make_tmap_2d(&tdh, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, dhm, (uint64_t)N, (uint64_t)T,
                               (uint64_t)(2 * N), BWD_BN, 128, CU_TENSOR_MAP_SWIZZLE_64B))
+    return e;
+  if (int e = mx_make_tmap_2d(&tbg, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, bg, (uint64_t)r, (uint64_t)N,
+                              (uint64_t)(2 * r), r, BWD_BN, CU_TENSOR_MAP_SWIZZLE_NONE))
+    return e;
+  if (int e = mx_make_tmap_2d(&tbu, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, bu, (uint64_t)r, (uint64_t)N,
+                              (uint64_t)(2 * r), r, BWD_BN, CU_TENSOR_MAP_SWIZZLE_NONE))
+    return e;
+  if (int e = mx_make_tmap_2d(&tad, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, ad, (uint64_t)N, (uint64_t)r,
+                              (uint64_t)(2 * N), BWD_BN, r, CU_TENSOR_MAP_SWIZZLE_NONE))
     return e;
   const int64_t tpad = (T + 127) / 128 * 128;
   const int nsb = (int)((tpad + super_block - 1) / super_block);
@@ -782,11 +849,10 @@ extern "C" int mxm_mlp_bwd_epilogue(const void* gu, const void* xs, const void* 
   auto go = [&](auto kern) -> int {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return mx_cuda_status(e, "mlp bwd epilogue: set smem");
-    kern<<<grid, EPI_THREADS, smem, st>>>(tgu, tdh, (const bf16*)xs, (const bf16*)dxd, (const bf16*)bg,
-                                          (const bf16*)bu, (const bf16*)ad, (uint8_t*)q, (uint8_t*)s,
-                                          (float*)dxa_part, (float*)dbg_part, (float*)dbu_part, (float*)dad_part,
-                                          (int)T, (int)tpad, (int)N, s_g, s_u, super_block, tpg, q != nullptr,
-                                          mx_dev_error_ptr());
+    kern<<<grid, EPI_THREADS, smem, st>>>(tgu, tdh, tbg, tbu, tad, (const bf16*)xs, (const bf16*)dxd, (uint8_t*)q,
+                                          (uint8_t*)s, (float*)dxa_part, (float*)dbg_part, (float*)dbu_part,
+                                          (float*)dad_part, (int)T, (int)tpad, (int)N, s_g, s_u, super_block, tpg,
+                                          q != nullptr, mx_dev_error_ptr());
     mx_note_launch();
     return mx_launch_status("mlp bwd epilogue");
   };

@@ -37,3 +37,14 @@ MX_DEV uint32_t ld16x2(const __nv_bfloat16* p0, const __nv_bfloat16* p1) {
 MX_DEV uint32_t ld16z(const __nv_bfloat16* p, bool valid) {
   return valid ? (uint32_t)__ldg(reinterpret_cast<const unsigned short*>(p)) : 0u;
 }
+
+// ldmatrix: four 8x8 bf16 matrices from shared memory in fragment layout; lane L supplies the
+// address of row (L % 8) of matrix (L / 8).  .trans delivers the transposed matrices.
+MX_DEV void ldsm4(uint32_t (&r)[4], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(addr));
+}
+MX_DEV void ldsm4t(uint32_t (&r)[4], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(addr));
+}
