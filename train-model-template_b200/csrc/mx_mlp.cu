@@ -75,16 +75,16 @@ MX_DEV void quant_block16(const float (&v)[4][4], int64_t row_g, int64_t T, int6
 // (reference: g / (exp(-g) + 1), tl.sigmoid(g); scripts/fused_mlp.py:104,152,158).
 MX_DEV float exp_neg(float g) { return __expf(-g); }
 
-// bf16 pair (row r, cols c, c+1) of a [rows x 64] bf16 tile stored by TMA with the 128-byte swizzle
-// (16-byte chunk j of row r sits at chunk j ^ (r % 8)).
-MX_DEV uint32_t sw128_ld(const uint8_t* tile, int r, int c) {
-  const int b = c * 2;
-  return *reinterpret_cast<const uint32_t*>(tile + r * 128 + (((b >> 4) ^ (r & 7)) << 4) + (b & 15));
+// Byte offset of 16-byte chunk `chunk` of row `row` in a tile with RB-byte rows stored by TMA with the
+// matching RB-byte swizzle (RB = 32, 64, 128): chunk bits [4, 4+b) are XORed with address bits [7, 7+b).
+template <int RB>
+MX_DEV uint32_t swz(uint32_t row, uint32_t chunk) {
+  constexpr uint32_t SH = RB == 128 ? 0 : (RB == 64 ? 1 : 2), MK = RB / 16 - 1;
+  return row * RB + ((chunk ^ ((row >> SH) & MK)) << 4);
 }
-// Same for a [rows x 32] bf16 tile with 64-byte rows and the 64-byte swizzle (chunk j -> j ^ ((r / 2) % 4)).
-MX_DEV uint32_t sw64_ld(const uint8_t* tile, int r, int c) {
-  const int b = c * 2;
-  return *reinterpret_cast<const uint32_t*>(tile + r * 64 + (((b >> 4) ^ ((r >> 1) & 3)) << 4) + (b & 15));
+template <int RB>
+__host__ __device__ constexpr CUtensorMapSwizzle swz_mode() {
+  return RB == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : (RB == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B);
 }
 
 MX_DEV uint8_t* align1024(uint8_t* p) {
@@ -212,7 +212,7 @@ __global__ void __launch_bounds__(EPI_THREADS, 1)
 #pragma unroll
         for (int kk = 0; kk < KS; ++kk) {
           // B_gate / B_up slices [64 n x r], rows of 2r bytes: matrices (n-tile 2p / 2p+1) x (j 16kk.. / +8)
-          const uint32_t boff = (uint32_t)(8 * (2 * p + (mi >> 1)) + lr) * (2 * R) + (uint32_t)(2 * kk + (mi & 1)) * 16;
+          const uint32_t boff = swz<2 * R>((uint32_t)(8 * (2 * p + (mi >> 1)) + lr), (uint32_t)(2 * kk + (mi & 1)));
           uint32_t BG[4], BU[4];
           ldsm4(BG, tbg + boff);
           ldsm4(BU, tbu + boff);
@@ -290,32 +290,40 @@ __global__ void __launch_bounds__(EPI_THREADS, 1)
 //     written once per CTA as the group's partial.
 // No atomics: the result is deterministic.  All MMA operands come from shared memory through
 // ldmatrix (.trans where the tile is stored transposed to the operand).
-constexpr int BWD_BN = 32, BWD_ST = 4, BWD_TILE = 128 * BWD_BN * 2;  // 8 KB per g / u / dh tile
+constexpr int BWD_BN = 32, BWD_TILE = 128 * BWD_BN * 2;  // 8 KB per g / u / dh tile
+__host__ __device__ constexpr int bwd_st(int R) { return R == 16 ? 4 : 3; }  // ring stages
 __host__ __device__ constexpr int bwd_btile(int R) { return BWD_BN * R * 2; }
 __host__ __device__ constexpr int bwd_stage(int R) { return 3 * BWD_TILE + 3 * bwd_btile(R); }
 __host__ __device__ constexpr int bwd_rs(int R) { return 3 * R + 8; }      // padded row stride of the row sums
 __host__ __device__ constexpr int bwd_ws() { return BWD_BN + 8; }          // padded stride of the reduction tiles
+__host__ __device__ constexpr size_t bwd_rowbuf(int SB, int R) { return (size_t)SB * 3 * R * 2; }  // xs + dxd rows
 __host__ __device__ constexpr size_t bwd_smem(int R, int SB) {
-  return 1024 + (size_t)BWD_ST * bwd_stage(R) + (size_t)SB * bwd_rs(R) * 4 + (size_t)CONSUMERS * R * bwd_ws() * 4 +
-         2 * BWD_ST * sizeof(uint64_t);
+  return 1024 + (size_t)bwd_st(R) * bwd_stage(R) + bwd_rowbuf(SB, R) + (size_t)SB * bwd_rs(R) * 4 +
+         (size_t)CONSUMERS * R * bwd_ws() * 4 + (2 * bwd_st(R) + 1) * sizeof(uint64_t);
 }
 
 template <int R>
 __global__ void __launch_bounds__(EPI_THREADS, 1)
     k_mlp_bwd(const __grid_constant__ CUtensorMap tm_gu, const __grid_constant__ CUtensorMap tm_dh,
               const __grid_constant__ CUtensorMap tm_bg, const __grid_constant__ CUtensorMap tm_bu,
-              const __grid_constant__ CUtensorMap tm_ad, const bf16* __restrict__ xs, const bf16* __restrict__ dxd,
-              uint8_t* __restrict__ q, uint8_t* __restrict__ s, float* __restrict__ dxa_part,
+              const __grid_constant__ CUtensorMap tm_ad, const __grid_constant__ CUtensorMap tm_xs,
+              const __grid_constant__ CUtensorMap tm_dxd, uint8_t* __restrict__ q, uint8_t* __restrict__ s,
+              float* __restrict__ dxa_part,
               float* __restrict__ dbg_part, float* __restrict__ dbu_part, float* __restrict__ dad_part, int T,
               int Tpad, int N, float s_g, float s_u, int SB, int tpg, int write_q, int* err) {
   constexpr int KS = R / 16, NT = BWD_BN / 8, R3 = 3 * R, RS = bwd_rs(R), WS = bwd_ws();
-  constexpr int BT = bwd_btile(R), STG = bwd_stage(R);
+  constexpr int BT = bwd_btile(R), STG = bwd_stage(R), BWD_ST = bwd_st(R);
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
-  float* acc_rows = reinterpret_cast<float*>(smem + BWD_ST * STG);  // [SB][RS]
-  float* scratch = acc_rows + (size_t)SB * RS;                        // [CONSUMERS][R][WS]
+  // the super-block's xs rows ([128 x 2r] per 128-row step) then its dxd rows ([128 x r] per step),
+  // both TMA-swizzled, loaded once; then the row accumulators, the reduction scratch, the barriers
+  uint8_t* rows_xs = smem + BWD_ST * STG;
+  uint8_t* rows_dxd = rows_xs + (size_t)SB * 2 * R * 2;
+  float* acc_rows = reinterpret_cast<float*>(rows_xs + bwd_rowbuf(SB, R));  // [SB][RS]
+  float* scratch = acc_rows + (size_t)SB * RS;                              // [CONSUMERS][R][WS]
   uint64_t* full = reinterpret_cast<uint64_t*>(scratch + CONSUMERS * R * WS);
   uint64_t* empty = full + BWD_ST;
+  uint64_t* rows_full = empty + BWD_ST;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int sbi = blockIdx.x, cg = blockIdx.y;
   const int r_begin = sbi * SB, r_end = min(r_begin + SB, Tpad);
@@ -325,6 +333,7 @@ __global__ void __launch_bounds__(EPI_THREADS, 1)
       mbar_init(&full[i], 1);
       mbar_init(&empty[i], CONSUMERS);
     }
+    mbar_init(rows_full, 1);
     fence_barrier_init();
   }
   __syncthreads();
@@ -336,6 +345,12 @@ __global__ void __launch_bounds__(EPI_THREADS, 1)
       prefetch_tmap(&tm_bg);
       prefetch_tmap(&tm_bu);
       prefetch_tmap(&tm_ad);
+      const int nsteps = (r_end - r_begin) / 128;
+      mbar_arrive_expect_tx(rows_full, (uint32_t)(nsteps * 128 * 3 * R * 2));
+      for (int k = 0; k < nsteps; ++k) {
+        tma_load_2d(rows_xs + (size_t)k * 128 * 2 * R * 2, &tm_xs, rows_full, 0, r_begin + 128 * k);
+        tma_load_2d(rows_dxd + (size_t)k * 128 * R * 2, &tm_dxd, rows_full, 0, r_begin + 128 * k);
+      }
     }
     int stage = 0;
     uint32_t phase = 0;
@@ -373,6 +388,7 @@ __global__ void __launch_bounds__(EPI_THREADS, 1)
   const int nthr = CONSUMERS * 32;
   for (int i = threadIdx.x; i < SB * RS; i += nthr) acc_rows[i] = 0.f;
   consumers_sync(nthr);
+  bool ok = mbar_wait(rows_full, 0, err, MX_DEV_TIMEOUT_EPILOGUE);
 
   // g / u / dh tiles (64-byte rows, 64-byte swizzle): this lane's ldmatrix row
   const int lrow = warp * 16 + (mi & 1) * 8 + lr;
@@ -380,7 +396,6 @@ __global__ void __launch_bounds__(EPI_THREADS, 1)
 
   int stage = 0;
   uint32_t phase = 0;
-  bool ok = true;
   for (int ct = 0; ct < tpg && ok; ++ct) {
     const int n0 = (cg * tpg + ct) * BWD_BN;
     float aBg[KS][NT][4], aBu[KS][NT][4], aAd[KS][NT][4];
@@ -393,27 +408,20 @@ __global__ void __launch_bounds__(EPI_THREADS, 1)
 
     for (int r = r_begin; r < r_end; r += 128) {
       const int rl = warp * 16 + g;
-      const int64_t ra = r + rl, rb = ra + 8;
-      const bool va = ra < T, vb = rb < T;
+      const int64_t ra = r + rl;
+      // A fragments of xa_gate, xa_up, dxd for this warp's 16 rows, from the super-block's row buffers
       uint32_t axg[KS][4], axu[KS][4], axd[KS][4];
+      {
+        const int step = (r - r_begin) / 128;
+        const uint32_t xrow = (uint32_t)(warp * 16 + (mi & 1) * 8 + lr);
+        const uint32_t bx = smem_u32(rows_xs + (size_t)step * 128 * 2 * R * 2);
+        const uint32_t bd = smem_u32(rows_dxd + (size_t)step * 128 * R * 2);
 #pragma unroll
-      for (int kk = 0; kk < KS; ++kk) {
-        const bf16* pa = xs + ra * (2 * R) + 16 * kk + 2 * t;
-        const bf16* pb = xs + rb * (2 * R) + 16 * kk + 2 * t;
-        const bf16* da = dxd + ra * R + 16 * kk + 2 * t;
-        const bf16* db = dxd + rb * R + 16 * kk + 2 * t;
-        axg[kk][0] = va ? ld32(pa) : 0u;
-        axg[kk][1] = vb ? ld32(pb) : 0u;
-        axg[kk][2] = va ? ld32(pa + 8) : 0u;
-        axg[kk][3] = vb ? ld32(pb + 8) : 0u;
-        axu[kk][0] = va ? ld32(pa + R) : 0u;
-        axu[kk][1] = vb ? ld32(pb + R) : 0u;
-        axu[kk][2] = va ? ld32(pa + R + 8) : 0u;
-        axu[kk][3] = vb ? ld32(pb + R + 8) : 0u;
-        axd[kk][0] = va ? ld32(da) : 0u;
-        axd[kk][1] = vb ? ld32(db) : 0u;
-        axd[kk][2] = va ? ld32(da + 8) : 0u;
-        axd[kk][3] = vb ? ld32(db + 8) : 0u;
+        for (int kk = 0; kk < KS; ++kk) {
+          ldsm4(axg[kk], bx + swz<4 * R>(xrow, (uint32_t)(2 * kk + (mi >> 1))));
+          ldsm4(axu[kk], bx + swz<4 * R>(xrow, (uint32_t)(2 * KS + 2 * kk + (mi >> 1))));
+          ldsm4(axd[kk], bd + swz<2 * R>(xrow, (uint32_t)(2 * kk + (mi >> 1))));
+        }
       }
       if (!mbar_wait(&full[stage], phase, err, MX_DEV_TIMEOUT_EPILOGUE)) {
         ok = false;
@@ -436,12 +444,12 @@ __global__ void __launch_bounds__(EPI_THREADS, 1)
 #pragma unroll
         for (int kk = 0; kk < KS; ++kk) {
           // B_gate / B_up slices [32 n x r]: (n-tile 2p / 2p+1) x (j 16kk / +8)
-          const uint32_t boff = (uint32_t)(8 * (2 * p + (mi >> 1)) + lr) * (2 * R) + (uint32_t)(2 * kk + (mi & 1)) * 16;
+          const uint32_t boff = swz<2 * R>((uint32_t)(8 * (2 * p + (mi >> 1)) + lr), (uint32_t)(2 * kk + (mi & 1)));
           uint32_t BG[4], BU[4], AD[4];
           ldsm4(BG, tbg + boff);
           ldsm4(BU, tbu + boff);
           // A_down slice [r x 32 n] (64-byte rows) transposed: (n-tile 2p / 2p+1) x (j 16kk / +8)
-          const uint32_t aoff = (uint32_t)(16 * kk + 8 * (mi & 1) + lr) * 64 + (uint32_t)(2 * p + (mi >> 1)) * 16;
+          const uint32_t aoff = swz<64>((uint32_t)(16 * kk + 8 * (mi & 1) + lr), (uint32_t)(2 * p + (mi >> 1)));
           ldsm4t(AD, tad + aoff);
 #pragma unroll
           for (int qq = 0; qq < 2; ++qq) {
@@ -503,12 +511,12 @@ __global__ void __launch_bounds__(EPI_THREADS, 1)
           const uint32_t adu[4] = {dup[2 * mm][0], dup[2 * mm][1], dup[2 * mm + 1][0], dup[2 * mm + 1][1]};
           const uint32_t ah[4] = {hp[2 * mm][0], hp[2 * mm][1], hp[2 * mm + 1][0], hp[2 * mm + 1][1]};
           // B[k = n][col j] = B_gate[n][j]: transposed ldmatrix of (n 16mm / +8) x (j-tile 2jp / 2jp+1)
-          const uint32_t boff = (uint32_t)(16 * mm + 8 * (mi & 1) + lr) * (2 * R) + (uint32_t)(2 * jp + (mi >> 1)) * 16;
+          const uint32_t boff = swz<2 * R>((uint32_t)(16 * mm + 8 * (mi & 1) + lr), (uint32_t)(2 * jp + (mi >> 1)));
           uint32_t BG[4], BU[4], AD[4];
           ldsm4t(BG, tbg + boff);
           ldsm4t(BU, tbu + boff);
           // B[k = n][col j] = A_down[j][n]: ldmatrix of (j-tile 2jp / 2jp+1) x (n 16mm / +8)
-          const uint32_t aoff = (uint32_t)(16 * jp + 8 * (mi >> 1) + lr) * 64 + (uint32_t)(2 * mm + (mi & 1)) * 16;
+          const uint32_t aoff = swz<64>((uint32_t)(16 * jp + 8 * (mi >> 1) + lr), (uint32_t)(2 * mm + (mi & 1)));
           ldsm4(AD, tad + aoff);
 #pragma unroll
           for (int h2 = 0; h2 < 2; ++h2) {
@@ -750,10 +758,10 @@ extern "C" int mxm_mlp_fwd_epilogue(const void* gu, const void* xs, const void* 
                               (uint64_t)(4 * N), FWD_BN, 128, CU_TENSOR_MAP_SWIZZLE_128B))
     return e;
   if (int e = mx_make_tmap_2d(&tbg, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, bg, (uint64_t)r, (uint64_t)N,
-                              (uint64_t)(2 * r), r, FWD_BN, CU_TENSOR_MAP_SWIZZLE_NONE))
+                              (uint64_t)(2 * r), r, FWD_BN, r == 16 ? CU_TENSOR_MAP_SWIZZLE_32B : CU_TENSOR_MAP_SWIZZLE_64B))
     return e;
   if (int e = mx_make_tmap_2d(&tbu, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, bu, (uint64_t)r, (uint64_t)N,
-                              (uint64_t)(2 * r), r, FWD_BN, CU_TENSOR_MAP_SWIZZLE_NONE))
+                              (uint64_t)(2 * r), r, FWD_BN, r == 16 ? CU_TENSOR_MAP_SWIZZLE_32B : CU_TENSOR_MAP_SWIZZLE_64B))
     return e;
   if (int e = mx_make_tmap_2d(&tad, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, ad, (uint64_t)N, (uint64_t)r,
                               (uint64_t)(2 * N), FWD_BN, r, CU_TENSOR_MAP_SWIZZLE_128B))
@@ -783,7 +791,7 @@ extern "C" int mxm_mlp_fwd_epilogue(const void* gu, const void* xs, const void* 
   return MXM_OK;
 }
 
-static int bwd_super_block(int r) { return r == 16 ? 384 : 128; }
+static int bwd_super_block(int r) { return r == 16 ? 256 : 128; }
 
 // Backward partition: super-blocks of SB rows (shared-memory row accumulators bound SB) and the
 // column-group count that minimises partial-sum bytes while giving every SM at least two CTAs
@@ -832,13 +840,20 @@ extern "C" int mxm_mlp_bwd_epilogue(const void* gu, const void* xs, const void* 
                               (uint64_t)(2 * N), BWD_BN, 128, CU_TENSOR_MAP_SWIZZLE_64B))
     return e;
   if (int e = mx_make_tmap_2d(&tbg, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, bg, (uint64_t)r, (uint64_t)N,
-                              (uint64_t)(2 * r), r, BWD_BN, CU_TENSOR_MAP_SWIZZLE_NONE))
+                              (uint64_t)(2 * r), r, BWD_BN, r == 16 ? CU_TENSOR_MAP_SWIZZLE_32B : CU_TENSOR_MAP_SWIZZLE_64B))
     return e;
   if (int e = mx_make_tmap_2d(&tbu, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, bu, (uint64_t)r, (uint64_t)N,
-                              (uint64_t)(2 * r), r, BWD_BN, CU_TENSOR_MAP_SWIZZLE_NONE))
+                              (uint64_t)(2 * r), r, BWD_BN, r == 16 ? CU_TENSOR_MAP_SWIZZLE_32B : CU_TENSOR_MAP_SWIZZLE_64B))
     return e;
   if (int e = mx_make_tmap_2d(&tad, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, ad, (uint64_t)N, (uint64_t)r,
-                              (uint64_t)(2 * N), BWD_BN, r, CU_TENSOR_MAP_SWIZZLE_NONE))
+                              (uint64_t)(2 * N), BWD_BN, r, CU_TENSOR_MAP_SWIZZLE_64B))
+    return e;
+  CUtensorMap txs, tdxd;
+  if (int e = mx_make_tmap_2d(&txs, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, xs, (uint64_t)(2 * r), (uint64_t)T,
+                              (uint64_t)(4 * r), 2 * r, 128, r == 16 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B))
+    return e;
+  if (int e = mx_make_tmap_2d(&tdxd, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, dxd, (uint64_t)r, (uint64_t)T,
+                              (uint64_t)(2 * r), r, 128, r == 16 ? CU_TENSOR_MAP_SWIZZLE_32B : CU_TENSOR_MAP_SWIZZLE_64B))
     return e;
   const int64_t tpad = (T + 127) / 128 * 128;
   const int nsb = (int)((tpad + super_block - 1) / super_block);
@@ -849,7 +864,7 @@ extern "C" int mxm_mlp_bwd_epilogue(const void* gu, const void* xs, const void* 
   auto go = [&](auto kern) -> int {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return mx_cuda_status(e, "mlp bwd epilogue: set smem");
-    kern<<<grid, EPI_THREADS, smem, st>>>(tgu, tdh, tbg, tbu, tad, (const bf16*)xs, (const bf16*)dxd, (uint8_t*)q,
+    kern<<<grid, EPI_THREADS, smem, st>>>(tgu, tdh, tbg, tbu, tad, txs, tdxd, (uint8_t*)q,
                                           (uint8_t*)s, (float*)dxa_part, (float*)dbg_part, (float*)dbu_part,
                                           (float*)dad_part, (int)T, (int)tpad, (int)N, s_g, s_u, super_block, tpg,
                                           q != nullptr, mx_dev_error_ptr());
