@@ -136,6 +136,21 @@ int mxm_coldot_chunks(int64_t T, int64_t K, int* rows_per_chunk, int* chunks);
 int mxm_coldot(const void* A, int64_t lda, const void* E, int64_t lde, int64_t T, int64_t K, int n, float post,
                int transpose_out, void* part, int rows_per_chunk, int chunks, void* out, void* stream);
 
+/* Allocation-free variant of mxm_coldot, for callers that cannot allocate device memory: code running
+ * inside a custom device allocator (a nested allocation would re-enter it) and services that reserve
+ * their whole memory budget up front.  No counterpart in the reference.
+ * Same arguments and result as mxm_coldot without the `part` / chunking arguments: the partial sums use
+ * one fixed 16 MiB array in device memory that the library holds on every GPU that loads it until the
+ * process exits.  Requires K * n <= 4,194,304 (one row chunk of fp32 partials must fit); larger
+ * requests fail with MXM_ERR_ARG and a message.  It calls no cudaMalloc / cudaFree and no allocating
+ * library routine.  The first call on each device looks up the array's device address (with that device
+ * current) and caches it: make that first call before any stream capture.  All calls share the array
+ * and it keeps the last call's partials (every value read is written first in the same call, so
+ * nothing needs clearing); calls whose executions overlap on the GPU race on it, so serialize them
+ * (one stream, or events). */
+int mxm_coldot_noalloc(const void* A, int64_t lda, const void* E, int64_t lde, int64_t T, int64_t K, int n,
+                       float post, int transpose_out, void* out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -13,6 +13,8 @@
 //
 // All rank-r products run on the tensor cores with warp-level m16n8k16 bf16 MMAs; the element-wise
 // math keeps the reference's rounding points (bf16 after each fp32 expression it rounds).
+#include <mutex>
+
 #include "mx_mma.cuh"
 #include "mx_runtime.h"
 
@@ -957,4 +959,58 @@ extern "C" int mxm_coldot(const void* A, int64_t lda, const void* E, int64_t lde
                                                  transpose_out ? K : 0, transpose_out ? n : 0);
   mx_note_launch();
   return mx_launch_status("coldot sum");
+}
+
+// ================================================================================================ no-alloc
+// An allocation-free variant of mxm_coldot for callers that cannot allocate device memory: code that
+// runs inside a custom device allocator (a call back into the allocator would re-enter it), and
+// services that reserve their whole memory budget up front and may not grow it afterwards.  Its
+// partial sums live in one fixed array in device memory, allocated when the library is loaded and
+// held by every GPU that loads the library until the process exits.
+#define MXM_NOALLOC_SCRATCH_BYTES (16u << 20)  // 16 MiB
+static __device__ __align__(256) unsigned char g_noalloc_scratch[MXM_NOALLOC_SCRATCH_BYTES];
+
+// Device address of g_noalloc_scratch on the current device.  The array's name in host code is only a
+// host-side handle, so the address is looked up once per device (with that device current) and cached.
+static int noalloc_scratch(float** out) {
+  static std::mutex mu;
+  static void* addr[64] = {nullptr};
+  int dev = 0;
+  if (int e = mx_cuda_status(cudaGetDevice(&dev), "mxm_coldot_noalloc: cudaGetDevice")) return e;
+  MX_CHECK_ARG(dev >= 0 && dev < 64, "mxm_coldot_noalloc: device index %d out of range", dev);
+  std::lock_guard<std::mutex> lock(mu);
+  if (!addr[dev]) {
+    void* p = nullptr;
+    if (int e = mx_cuda_status(cudaGetSymbolAddress(&p, g_noalloc_scratch), "mxm_coldot_noalloc: cudaGetSymbolAddress"))
+      return e;
+    addr[dev] = p;
+  }
+  *out = static_cast<float*>(addr[dev]);
+  return MXM_OK;
+}
+
+extern "C" int mxm_coldot_noalloc(const void* A, int64_t lda, const void* E, int64_t lde, int64_t T, int64_t K, int n,
+                                  float post, int transpose_out, void* out, void* stream) {
+  MX_CHECK_ARG(A && E && out, "mxm_coldot_noalloc: null pointer");
+  MX_CHECK_ARG(T >= 1 && K >= 64 && K % 64 == 0 && (n == 16 || n == 32 || n == 64),
+               "mxm_coldot_noalloc: need T >= 1, K %% 64 == 0, n in {16, 32, 64}");
+  const int64_t per_chunk = K * n * (int64_t)sizeof(float);
+  MX_CHECK_ARG(per_chunk <= (int64_t)MXM_NOALLOC_SCRATCH_BYTES,
+               "mxm_coldot_noalloc: K * n = %lld needs %lld bytes of scratch per row chunk, more than the fixed "
+               "%u-byte scratch (K * n must be <= %u)",
+               (long long)(K * n), (long long)per_chunk, MXM_NOALLOC_SCRATCH_BYTES,
+               MXM_NOALLOC_SCRATCH_BYTES / (unsigned)sizeof(float));
+  int rpc = 0, chunks = 0;
+  if (int e = mxm_coldot_chunks(T, K, &rpc, &chunks)) return e;
+  const int64_t max_chunks = (int64_t)MXM_NOALLOC_SCRATCH_BYTES / per_chunk;
+  if (chunks > max_chunks) {  // fewer, taller row chunks so the partials fit the fixed scratch
+    int64_t r = (T + max_chunks - 1) / max_chunks;
+    r = (r + 15) / 16 * 16;
+    rpc = (int)r;
+    chunks = (int)((T + r - 1) / r);
+  }
+  float* scratch = nullptr;
+  if (int e = noalloc_scratch(&scratch)) return e;
+  // every partial the reduction reads is written by k_coldot first: nothing needs clearing
+  return mxm_coldot(A, lda, E, lde, T, K, n, post, transpose_out, scratch, rpc, chunks, out, stream);
 }
