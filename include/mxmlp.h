@@ -78,14 +78,15 @@ int mxm_gemm(const void* qa, int64_t lda, const void* sa, const void* qb, int64_
              int64_t M, int64_t N, int64_t K, void* d, int64_t ldd, void* stream);
 
 
-/* mxm_gemm with a rank-kr LoRA term added in the epilogue, with the reference's two roundings:
- *   D = bf16( bf16(dq(A) dq(B)^T) + alpha * L[M, kr] . Rm[N, kr]^T )
- * L row stride ldl (elements), Rm contiguous [N, kr], kr in {16, 32, 64}.
- * Replaces `y = _scaled_mm(...); y.addmm_(xS_down, B_down^T, alpha=s_down)` and
- * `dx = _scaled_mm(...); dx.addmm_(dxa, S)` (scripts/fused_mlp.py:283-284, :329-331). */
+/* mxm_gemm with a rank-kr LoRA term accumulated on the tensor core into the same fp32 accumulator:
+ *   D = bf16( dq(A) dq(B)^T + L[M, kr] . Rm[N, kr]^T )
+ * L bf16 with row stride ldl (elements, % 8 == 0), Rm bf16 contiguous [N, kr] (the caller folds the LoRA
+ * scaling into Rm), kr in {16, 32, 64}.  Replaces `y = _scaled_mm(...); y.addmm_(xS_down, B_down^T,
+ * alpha=s_down)` and `dx = _scaled_mm(...); dx.addmm_(dxa, S)` (scripts/fused_mlp.py:283-284, :329-331);
+ * the MX product is not rounded to bf16 before the LoRA add (one rounding instead of the reference's two). */
 int mxm_gemm_lora(const void* qa, int64_t lda, const void* sa, const void* qb, int64_t ldb, const void* sb,
-                  int64_t M, int64_t N, int64_t K, const void* L, int64_t ldl, const void* Rm, int kr, float alpha,
-                  void* d, int64_t ldd, void* stream);
+                  int64_t M, int64_t N, int64_t K, const void* L, int64_t ldl, const void* Rm, int kr, void* d,
+                  int64_t ldd, void* stream);
 
 /* Column-group count for mxm_mlp_fwd_epilogue (reference mlp_fwd grid choice, scripts/fused_mlp.py:203-204). */
 int mxm_mlp_fwd_partitions(int64_t T, int64_t N, int r, int* col_groups);

@@ -62,3 +62,24 @@ def test_gemm_strided_operand_and_determinism():
     assert torch.equal(full[:, N:], half)
     again = mxfp8.mx_mm(qa, qw.t(), sa, sw)
     assert torch.equal(full, again)
+
+
+@pytest.mark.parametrize("M,N,K,kr", [(300, 512, 256, 16), (1000, 2048, 1024, 32), (129, 256, 384, 64)])
+def test_gemm_lora_vs_oracle(M, N, K, kr):
+    """D = bf16(dq(A) dq(B)^T + L Rm^T): the LoRA term accumulated by a bf16 tcgen05 MMA."""
+    import fused_mlp
+    import mxfp8
+    g = torch.Generator().manual_seed(M + kr)
+    a = torch.randn(M, K, generator=g).to(torch.bfloat16)
+    b = (torch.randn(N, K, generator=g) * 0.02).to(torch.bfloat16)
+    L = (torch.randn(M, kr, generator=g) * 0.5).to(torch.bfloat16)
+    Rm = (torch.randn(N, kr, generator=g) * 0.1).to(torch.bfloat16)
+    qa, sa = mxfp8.mx_quant(a.cuda())
+    qb, sb = mxfp8.mx_quant(b.cuda())
+    d = fused_mlp.mx_mm_lora(qa, qb.t(), sa, sb, L.cuda(), Rm.cuda())
+    torch.cuda.synchronize()
+    A = O.mx_dequant(qa.view(torch.uint8).cpu().numpy(), sa.view(torch.uint8).cpu().numpy(), M, K)
+    B = O.mx_dequant(qb.view(torch.uint8).cpu().numpy(), sb.view(torch.uint8).cpu().numpy(), N, K)
+    ref = A @ B.T + L.float().numpy() @ Rm.float().numpy().T
+    err = _rel(d.float().cpu(), torch.from_numpy(ref))
+    assert err < 2e-3, err

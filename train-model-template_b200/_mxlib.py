@@ -32,8 +32,7 @@ _SIGS = {
     "mxm_quant_cols": [_vp, _i64, _i64, _i64, _vp, _vp, _vp],
     "mxm_quant_both": [_vp, _i64, _i64, _i64, _vp, _vp, _vp, _vp, _vp],
     "mxm_gemm": [_vp, _i64, _vp, _vp, _i64, _vp, _i64, _i64, _i64, _vp, _i64, _vp],
-    "mxm_gemm_lora": [_vp, _i64, _vp, _vp, _i64, _vp, _i64, _i64, _i64, _vp, _i64, _vp, _int, ctypes.c_float,
-                      _vp, _i64, _vp],
+    "mxm_gemm_lora": [_vp, _i64, _vp, _vp, _i64, _vp, _i64, _i64, _i64, _vp, _i64, _vp, _int, _vp, _i64, _vp],
     "mxm_mlp_fwd_partitions": [_i64, _i64, _int, ctypes.POINTER(ctypes.c_int)],
     "mxm_mlp_fwd_epilogue": [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _int, ctypes.c_float, ctypes.c_float, _vp, _vp,
                              _vp, _vp, _int, _vp],

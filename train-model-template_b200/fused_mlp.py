@@ -8,13 +8,15 @@ Per layer call (T tokens, H hidden, N intermediate, r LoRA rank):
   forward : xs = x S^T (rank-2r, tensor-core rowdot)  |  q, s = MXFP8(x)
             gu = [x W_gate^T | x W_up^T]          -- tcgen05 block-scaled GEMM, K = H
             q_h, s_h, xS_down = epilogue(gu)       -- LoRA-B add, SwiGLU, MX quantize h
-            y = h W_down^T + s_d xS_down B_down^T  -- tcgen05 GEMM with the LoRA add in its epilogue
+            y = h W_down^T + xS_down (s_d B_down)^T -- tcgen05 GEMM; the LoRA term is a bf16 tcgen05 MMA
+                                                       into the same TMEM accumulator
   backward: q, s = MXFP8(dy); dh_mx = dy W_down (tcgen05); dxd = s_d dy B_down
             [dg | du] MXFP8 + dB_g, dB_u, dA_d, dxa, xS_down = epilogue(gu, dh_mx)
-            dx = [dg | du] W_gu + dxa S (tcgen05 GEMM, K = 2N, LoRA add in its epilogue)
+            dx = [dg | du] W_gu + dxa S (tcgen05 GEMM, K = 2N, LoRA term as a bf16 MMA)
             dB_d = s_d dy^T xS_down;  dA = dxa^T x (tensor-core coldot)
-The math and every bf16 rounding point follow the reference (scripts/fused_mlp.py:262-336); only the
-fp32 summation order differs.  h is not saved (the backward recomputes it from gu).
+The math and the bf16 rounding points follow the reference (scripts/fused_mlp.py:262-336), except that y
+and dx are rounded to bf16 once after the LoRA add (the reference rounds the MX product first), and the
+fp32 summation order.  h is not saved (the backward recomputes it from gu).
 """
 import types
 
@@ -65,8 +67,9 @@ def coldot(A, E, post=1.0, transpose_out=False):
     return out
 
 
-def mx_mm_lora(a, b, scale_a, scale_b, L, Rm, alpha):
-    """bf16(bf16(mx_mm(a, b, ...)) + alpha * L @ Rm^T): the MX GEMM with the rank-r LoRA add in its epilogue."""
+def mx_mm_lora(a, b, scale_a, scale_b, L, Rm):
+    """bf16(mx_mm(a, b, ...) + L @ Rm^T): the MX GEMM with the rank-r LoRA term accumulated on the tensor
+    core (Rm [N, r] bf16 contiguous already carries the LoRA scaling)."""
     M, K = a.shape
     N = b.shape[1]
     bt = b.t()
@@ -74,8 +77,7 @@ def mx_mm_lora(a, b, scale_a, scale_b, L, Rm, alpha):
     assert Rm.is_contiguous() and Rm.shape == (N, kr) and L.stride(1) == 1
     out = torch.empty((M, N), dtype=torch.bfloat16, device=a.device)
     _nx.call("mxm_gemm_lora", _nx.ptr(a), a.stride(0), _nx.ptr(scale_a), _nx.ptr(bt), bt.stride(0), _nx.ptr(scale_b),
-             M, N, K, _nx.ptr(L), L.stride(0), _nx.ptr(Rm), kr, float(alpha), _nx.ptr(out), out.stride(0),
-             _nx.stream_of(a))
+             M, N, K, _nx.ptr(L), L.stride(0), _nx.ptr(Rm), kr, _nx.ptr(out), out.stride(0), _nx.stream_of(a))
     return out
 
 
@@ -151,7 +153,8 @@ class _MLP(torch.autograd.Function):
         del q, sc
         if need_out:
             qh, sh, xsd = mlp_fwd(gu, xs, bg, bu, ad, s_g, s_u, True)
-            y = mx_mm_lora(qh, down._mx_w.t(), sh, down._mx_ws, xsd, bd, s_d)
+            bds = _cast(("s", id(Bd), s_d, dt), lambda: (bd.float() * s_d).to(dt).contiguous())
+            y = mx_mm_lora(qh, down._mx_w.t(), sh, down._mx_ws, xsd, bds)
             del qh, sh, xsd
         else:   # graph only (checkpoint recompute): nobody reads the output value
             STATS["bỏ đầu ra"] = STATS.get("bỏ đầu ra", 0) + 1
@@ -194,7 +197,7 @@ class _MLP(torch.autograd.Function):
         dx = None
         if need_x:
             ST = _cast(("T", id(S)), lambda: S.t().contiguous())
-            dx = mx_mm_lora(qg, hold.wt.t(), sg.view(_E8), hold.wts, dxa, ST, 1.0)   # K = 2N: gate + up
+            dx = mx_mm_lora(qg, hold.wt.t(), sg.view(_E8), hold.wts, dxa, ST)   # K = 2N: gate + up
             del qg, sg
             dx = dx.view(*lead, K).to(xdt)
         dA = coldot(x2, dxa, transpose_out=True)                          # [2R, H]
