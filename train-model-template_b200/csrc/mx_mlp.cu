@@ -33,12 +33,6 @@ MX_DEV float nanmax(float a, float b) {
   asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
   return r;
 }
-// Division with the 2-ulp full-range PTX instruction (what a Triton `/` on fp32 lowers to).
-MX_DEV float fdiv_full(float a, float b) {
-  float r;
-  asm("div.full.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
-  return r;
-}
 // Two floats -> two E4M3 codes (RNE, saturating: |v| <= 448 after the power-of-two block scaling,
 // and +-inf saturates to +-448 exactly as the reference's clamp does).
 MX_DEV uint32_t e4m3x2_sat(float lo, float hi) {
@@ -47,17 +41,46 @@ MX_DEV uint32_t e4m3x2_sat(float lo, float hi) {
   return r;
 }
 
-// Quantizes one 32-column block of a 16-row warp tile in D-fragment form:
-// v[i][0..1] = (row g, cols 8i+2t, +1), v[i][2..3] = (row g+8, same cols), i = 0..3.
-// Codes go to q[row * ldq + col0 + ...] for rows < T; scales of rows g and g+8 (always, padded rows
-// included) to the blocked layout of a [*, scols] operand.
-MX_DEV void quant_block16(const float (&v)[4][4], int64_t row_g, int64_t T, int64_t col0, uint8_t* q, int64_t ldq,
-                          uint8_t* s, int64_t scols, int t) {
+// ---- packed helpers: two values per instruction (Blackwell f32x2 ALU ops, bf16x2 conversions)
+MX_DEV float2 up2(uint32_t p) { return make_float2(bf16_lo(p), bf16_hi(p)); }
+MX_DEV uint32_t rn2(float2 v) { return pack_bf16x2(v.x, v.y); }   // round both to bf16 (RNE)
+MX_DEV float ex2a(float x) {
+  float r;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
+MX_DEV float rcpa(float x) {
+  float r;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
+// sigmoid(g) = 1 / (1 + exp(-g)) for a pair (exp via ex2 of -g*log2(e))
+MX_DEV float2 sigmoid2(float2 g) {
+  const float2 t = __fmul2_rn(g, make_float2(-1.4426950408889634f, -1.4426950408889634f));
+  return make_float2(rcpa(ex2a(t.x) + 1.0f), rcpa(ex2a(t.y) + 1.0f));
+}
+MX_DEV uint32_t absmax_bf16x2(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("{\n\t.reg .b32 x, y;\n\tabs.bf16x2 x, %1;\n\tabs.bf16x2 y, %2;\n\tmax.NaN.bf16x2 %0, x, y;\n\t}"
+      : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+MX_DEV uint32_t max_bf16x2(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("max.NaN.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+
+// Quantizes one 32-column block of a 16-row warp tile whose bf16 values are held packed in
+// D-fragment form: pk[i][h] = (row g + 8h, cols 8i+2t, +1), i = 0..3 (t = lane % 4).  Codes go to
+// q[row * ldq + col0 + ...] for rows < T; the scales of rows g and g+8 (always, padded rows included)
+// to the blocked layout of a [*, scols] operand.
+MX_DEV void quant_block16p(const uint32_t (&pk)[4][2], int64_t row_g, int64_t T, int64_t col0, uint8_t* q,
+                           int64_t ldq, uint8_t* s, int64_t scols, int t) {
 #pragma unroll
   for (int h = 0; h < 2; ++h) {
-    float m = 0.f;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) m = nanmax_abs(nanmax_abs(m, v[i][2 * h]), v[i][2 * h + 1]);
+    const uint32_t m2 = max_bf16x2(absmax_bf16x2(pk[0][h], pk[1][h]), absmax_bf16x2(pk[2][h], pk[3][h]));
+    float m = nanmax(bf16_lo(m2), bf16_hi(m2));
     m = nanmax(m, __shfl_xor_sync(0xffffffffu, m, 1));
     m = nanmax(m, __shfl_xor_sync(0xffffffffu, m, 2));
     const uint32_t e = mx_e8m0_rceil(__fdiv_rn(m, 448.0f));
@@ -65,17 +88,16 @@ MX_DEV void quant_block16(const float (&v)[4][4], int64_t row_g, int64_t T, int6
     const int64_t row = row_g + 8 * h;
     if (row < T) {
       uint8_t* dst = q + row * ldq + col0 + 2 * t;
+      const float2 r2 = make_float2(rcp, rcp);
 #pragma unroll
-      for (int i = 0; i < 4; ++i)
-        *reinterpret_cast<uint16_t*>(dst + 8 * i) = (uint16_t)e4m3x2_sat(v[i][2 * h] * rcp, v[i][2 * h + 1] * rcp);
+      for (int i = 0; i < 4; ++i) {
+        const float2 v = __fmul2_rn(up2(pk[i][h]), r2);
+        *reinterpret_cast<uint16_t*>(dst + 8 * i) = (uint16_t)e4m3x2_sat(v.x, v.y);
+      }
     }
     if (t == 0) s[mx_scale_offset(row, col0 >> 5, scols)] = (uint8_t)e;
   }
 }
-
-// exp(-g) once per element; silu = g / (e + 1) and sigmoid = 1 / (1 + e) share it
-// (reference: g / (exp(-g) + 1), tl.sigmoid(g); scripts/fused_mlp.py:104,152,158).
-MX_DEV float exp_neg(float g) { return __expf(-g); }
 
 // Byte offset of 16-byte chunk `chunk` of row `row` in a tile with RB-byte rows stored by TMA with the
 // matching RB-byte swizzle (RB = 32, 64, 128): chunk bits [4, 4+b) are XORed with address bits [7, 7+b).
@@ -191,6 +213,7 @@ __global__ void __launch_bounds__(EPI_THREADS, 1)
   // g / u tiles: matrices (rows +0 / +8 of the warp's 16) x (tile 2p / 2p+1)
   const int lrow = warp * 16 + (mi & 1) * 8 + lr;
   const uint32_t gu_row = (uint32_t)lrow * 128, gu_sw = (uint32_t)(lrow & 7), gu_hi = (uint32_t)(mi >> 1);
+  const float2 sg2 = make_float2(s_g, s_g), su2 = make_float2(s_u, s_u);
   int stage = 0;
   uint32_t phase = 0;
   for (int ct = 0; ct < tpg; ++ct) {
@@ -200,7 +223,6 @@ __global__ void __launch_bounds__(EPI_THREADS, 1)
     const uint32_t tg = sb, tu = sb + FWD_TILE, tbg = sb + 2 * FWD_TILE, tbu = tbg + BT, tad = tbu + BT;
 #pragma unroll
     for (int b = 0; b < FWD_BN / 32; ++b) {
-      float hv[4][4];
       uint32_t hp[4][2];
 #pragma unroll
       for (int pp = 0; pp < 2; ++pp) {
@@ -225,23 +247,17 @@ __global__ void __launch_bounds__(EPI_THREADS, 1)
         }
 #pragma unroll
         for (int q = 0; q < 2; ++q) {
-          const uint32_t ga = G[2 * q], gb = G[2 * q + 1], ua = U[2 * q], ub = U[2 * q + 1];
           const float* dg = q ? dg1 : dg0;
           const float* du = q ? du1 : du0;
-          const float gin[4] = {bf16_lo(ga), bf16_hi(ga), bf16_lo(gb), bf16_hi(gb)};
-          const float uin[4] = {bf16_lo(ua), bf16_hi(ua), bf16_lo(ub), bf16_hi(ub)};
-          float* h = hv[2 * pp + q];
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float gg = bf16_round_f(gin[e] + s_g * dg[e]);
-            const float uu = bf16_round_f(uin[e] + s_u * du[e]);
-            h[e] = bf16_round_f(fdiv_full(gg, exp_neg(gg) + 1.0f) * uu);
+          for (int h = 0; h < 2; ++h) {   // h = 0: row g, h = 1: row g + 8
+            const float2 gg = up2(rn2(__ffma2_rn(sg2, make_float2(dg[2 * h], dg[2 * h + 1]), up2(G[2 * q + h]))));
+            const float2 uu = up2(rn2(__ffma2_rn(su2, make_float2(du[2 * h], du[2 * h + 1]), up2(U[2 * q + h]))));
+            hp[2 * pp + q][h] = rn2(__fmul2_rn(__fmul2_rn(gg, sigmoid2(gg)), uu));   // h = bf16(silu(g) * u)
           }
-          hp[2 * pp + q][0] = pack_bf16x2(h[0], h[1]);
-          hp[2 * pp + q][1] = pack_bf16x2(h[2], h[3]);
         }
       }
-      if (write_q) quant_block16(hv, ra, T, n0 + 32 * b, qh, N, sh, N, t);
+      if (write_q) quant_block16p(hp, ra, T, n0 + 32 * b, qh, N, sh, N, t);
       // xS_down += h (16 x 32 block) A_down^T: two k-slices of 16 columns
 #pragma unroll
       for (int mm = 0; mm < 2; ++mm) {
@@ -396,6 +412,7 @@ __global__ void __launch_bounds__(EPI_THREADS, 1)
   const int lrow = warp * 16 + (mi & 1) * 8 + lr;
   const uint32_t t_row = (uint32_t)lrow * 64, t_sw = (uint32_t)((lrow >> 1) & 3), t_hi = (uint32_t)(mi >> 1);
 
+  const float2 sg2 = make_float2(s_g, s_g), su2 = make_float2(s_u, s_u);
   int stage = 0;
   uint32_t phase = 0;
   for (int ct = 0; ct < tpg && ok; ++ct) {
@@ -434,7 +451,6 @@ __global__ void __launch_bounds__(EPI_THREADS, 1)
       const uint32_t tbg = sb + 3 * BWD_TILE, tbu = tbg + BT, tad = tbu + BT;
 
       uint32_t dgp[NT][2], dup[NT][2], hp[NT][2];
-      float dgv[NT][4], duv[NT][4];
 #pragma unroll
       for (int p = 0; p < NT / 2; ++p) {
         uint32_t G[4], U[4], D[4];
@@ -463,33 +479,24 @@ __global__ void __launch_bounds__(EPI_THREADS, 1)
 #pragma unroll
         for (int qq = 0; qq < 2; ++qq) {
           const int i = 2 * p + qq;
-          const float gin[4] = {bf16_lo(G[2 * qq]), bf16_hi(G[2 * qq]), bf16_lo(G[2 * qq + 1]), bf16_hi(G[2 * qq + 1])};
-          const float uin[4] = {bf16_lo(U[2 * qq]), bf16_hi(U[2 * qq]), bf16_lo(U[2 * qq + 1]), bf16_hi(U[2 * qq + 1])};
-          const float hin[4] = {bf16_lo(D[2 * qq]), bf16_hi(D[2 * qq]), bf16_lo(D[2 * qq + 1]), bf16_hi(D[2 * qq + 1])};
-          float hvv[4];
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float gg = bf16_round_f(gin[e] + s_g * dg[qq][e]);
-            const float uu = bf16_round_f(uin[e] + s_u * du[qq][e]);
-            const float en = exp_neg(gg) + 1.0f;
-            const float sl = fdiv_full(gg, en);
-            const float sig = fdiv_full(1.0f, en);
-            hvv[e] = bf16_round_f(sl * uu);
-            const float dh = bf16_round_f(hin[e] + dd[qq][e]);
-            duv[i][e] = bf16_round_f(dh * sl);
-            dgv[i][e] = bf16_round_f(((dh * uu) * sig) * (gg * (1.0f - sig) + 1.0f));
+          for (int h = 0; h < 2; ++h) {   // h = 0: row g, h = 1: row g + 8
+            const float2 gg = up2(rn2(__ffma2_rn(sg2, make_float2(dg[qq][2 * h], dg[qq][2 * h + 1]), up2(G[2 * qq + h]))));
+            const float2 uu = up2(rn2(__ffma2_rn(su2, make_float2(du[qq][2 * h], du[qq][2 * h + 1]), up2(U[2 * qq + h]))));
+            const float2 sig = sigmoid2(gg);
+            const float2 sl = __fmul2_rn(gg, sig);                                 // silu(g)
+            hp[i][h] = rn2(__fmul2_rn(sl, uu));                                     // h = bf16(silu * u)
+            const float2 dh = up2(rn2(__fadd2_rn(up2(D[2 * qq + h]), make_float2(dd[qq][2 * h], dd[qq][2 * h + 1]))));
+            dup[i][h] = rn2(__fmul2_rn(dh, sl));                                    // du = bf16(dh * silu)
+            const float2 om = __ffma2_rn(sig, make_float2(-1.f, -1.f), make_float2(1.f, 1.f));  // 1 - sig
+            const float2 f = __ffma2_rn(gg, om, make_float2(1.f, 1.f));             // g (1 - sig) + 1
+            dgp[i][h] = rn2(__fmul2_rn(__fmul2_rn(__fmul2_rn(dh, uu), sig), f));    // dg
           }
-          hp[i][0] = pack_bf16x2(hvv[0], hvv[1]);
-          hp[i][1] = pack_bf16x2(hvv[2], hvv[3]);
-          dgp[i][0] = pack_bf16x2(dgv[i][0], dgv[i][1]);
-          dgp[i][1] = pack_bf16x2(dgv[i][2], dgv[i][3]);
-          dup[i][0] = pack_bf16x2(duv[i][0], duv[i][1]);
-          dup[i][1] = pack_bf16x2(duv[i][2], duv[i][3]);
         }
       }
       if (write_q) {
-        quant_block16(dgv, ra, T, n0, q, N2, s, N2, t);
-        quant_block16(duv, ra, T, (int64_t)N + n0, q, N2, s, N2, t);
+        quant_block16p(dgp, ra, T, n0, q, N2, s, N2, t);
+        quant_block16p(dup, ra, T, (int64_t)N + n0, q, N2, s, N2, t);
       }
       // per-row products (sums over columns) into the shared-memory row accumulators
       float* A0 = acc_rows + (int64_t)(ra - r_begin) * RS;
