@@ -135,14 +135,15 @@ def run_ours(a):
     import _mxlib
     import fused_linear
     import fused_mlp
+    import mx_dp
     import mxfp8
 
     if a.workload == "layer":
         T, L = (a.tokens or LAYER_TOKENS), 1
         total_tokens = T * world
     else:
-        assert STACK_TOKENS % world == 0
-        T, L = STACK_TOKENS // world, STACK_LAYERS
+        r0, r1 = mx_dp.shard_rows(STACK_TOKENS, world, rank)
+        T, L = r1 - r0, STACK_LAYERS
         total_tokens = STACK_TOKENS
     layers = [_make_layer(torch, fused_mlp, dev, seed=1000 + i) for i in range(L)]
     params = [p for _, ps in layers for p in ps]
@@ -151,8 +152,8 @@ def run_ours(a):
     dy_host = torch.randn(T, H, generator=gx).to(torch.bfloat16).pin_memory()
     x = x_host.to(dev)
     dy = dy_host.to(dev)
-    flat = torch.zeros(sum(p.numel() for p in params), dtype=torch.float32, device=dev)
-    flat_host = torch.empty(flat.shape, dtype=torch.float32).pin_memory()
+    bucket = mx_dp.GradBucket(params, device=dev)    # the LoRA gradients: the only cross-rank exchange
+    flat_host = torch.empty(bucket.flat.shape, dtype=torch.float32).pin_memory()
 
     def step(xin, dyin):
         fused_linear.new_step()
@@ -163,8 +164,7 @@ def run_ours(a):
             y = fused_mlp.mlp_apply(layer, y, *ps, scaling=(SCALE, SCALE, SCALE))
         y.backward(dyin)
         if world > 1:   # bucketed all-reduce of every LoRA gradient (NCCL over NVLink)
-            torch.cat([p.grad.reshape(-1) for p in params], out=flat)
-            dist.all_reduce(flat)
+            bucket.allreduce()
         for p in params:
             p.grad = None
         return h
@@ -235,10 +235,8 @@ def run_ours(a):
         for layer, ps in layers:
             y = fused_mlp.mlp_apply(layer, y, *ps, scaling=(SCALE, SCALE, SCALE))
         y.backward(dy)
-        torch.cat([p.grad.reshape(-1) for p in params], out=flat)
-        if world > 1:
-            dist.all_reduce(flat)
-        flat_host.copy_(flat, non_blocking=True)
+        bucket.allreduce()
+        flat_host.copy_(bucket.flat, non_blocking=True)
         for p in params:
             p.grad = None
 

@@ -123,7 +123,7 @@ int mxm_mlp_bwd_reduce(const void* dxa_part, const void* dbg_part, const void* d
                        int64_t T, int64_t N, int r, float s_g, float s_u, int super_block, int col_groups, void* dxa,
                        void* xsd, void* dBg, void* dBu, void* dAd, void* stream);
 
-/* out[T, n] = bf16( bf16(A[T, K] B[n, K]^T) * post ) (post == 1: one rounding); n in {16, 32, 64}, K % 32 == 0.
+/* out[T, n] = bf16( bf16(A[T, K] B[n, K]^T) * post ) (post == 1: one rounding); n in {16, 32, 64}, K % 128 == 0.
  * The rank-n LoRA-A products: xs = x S^T and dxd = s_d (dy B_down) (scripts/fused_mlp.py:277,311-313). */
 int mxm_rowdot(const void* A, int64_t lda, const void* B, int64_t T, int64_t K, int n, float post, void* out,
                int64_t ldo, void* stream);

@@ -23,11 +23,6 @@ namespace {
 using bf16 = __nv_bfloat16;
 
 // ------------------------------------------------------------------------------------------------ helpers
-MX_DEV float nanmax_abs(float m, float v) {
-  float r;
-  asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(m), "f"(fabsf(v)));
-  return r;
-}
 MX_DEV float nanmax(float a, float b) {
   float r;
   asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
@@ -39,6 +34,22 @@ MX_DEV uint32_t e4m3x2_sat(float lo, float hi) {
   uint16_t r;
   asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(hi), "f"(lo));
   return r;
+}
+
+MX_DEV float2 lds2(uint32_t a) {
+  float2 v;
+  asm volatile("ld.shared.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(a));
+  return v;
+}
+MX_DEV void sts2(uint32_t a, float2 v) { asm volatile("st.shared.v2.f32 [%0], {%1, %2};" ::"r"(a), "f"(v.x), "f"(v.y)); }
+// Predicated global stores (no branch around them).
+MX_DEV void stg16_if(void* p, uint32_t v, bool pred) {
+  asm volatile("{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %2, 0;\n\t@q st.global.b16 [%0], %1;\n\t}" ::"l"(p),
+               "h"((uint16_t)v), "r"((int)pred));
+}
+MX_DEV void stg8_if(void* p, uint32_t v, bool pred) {
+  asm volatile("{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %2, 0;\n\t@q st.global.b8 [%0], %1;\n\t}" ::"l"(p),
+               "h"((uint16_t)v), "r"((int)pred));
 }
 
 // ---- packed helpers: two values per instruction (Blackwell f32x2 ALU ops, bf16x2 conversions)
@@ -86,16 +97,15 @@ MX_DEV void quant_block16p(const uint32_t (&pk)[4][2], int64_t row_g, int64_t T,
     const uint32_t e = mx_e8m0_rceil(__fdiv_rn(m, 448.0f));
     const float rcp = mx_e8m0_rcp(e);
     const int64_t row = row_g + 8 * h;
-    if (row < T) {
-      uint8_t* dst = q + row * ldq + col0 + 2 * t;
-      const float2 r2 = make_float2(rcp, rcp);
+    const bool live = row < T;
+    uint8_t* dst = q + (live ? row : 0) * ldq + col0 + 2 * t;
+    const float2 r2 = make_float2(rcp, rcp);
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float2 v = __fmul2_rn(up2(pk[i][h]), r2);
-        *reinterpret_cast<uint16_t*>(dst + 8 * i) = (uint16_t)e4m3x2_sat(v.x, v.y);
-      }
+    for (int i = 0; i < 4; ++i) {
+      const float2 v = __fmul2_rn(up2(pk[i][h]), r2);
+      stg16_if(dst + 8 * i, e4m3x2_sat(v.x, v.y), live);
     }
-    if (t == 0) s[mx_scale_offset(row, col0 >> 5, scols)] = (uint8_t)e;
+    stg8_if(s + mx_scale_offset(row, col0 >> 5, scols), e, t == 0);
   }
 }
 
@@ -111,9 +121,9 @@ __host__ __device__ constexpr CUtensorMapSwizzle swz_mode() {
   return RB == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : (RB == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B);
 }
 
-MX_DEV uint8_t* align1024(uint8_t* p) {
-  return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
-}
+// Rounds a pointer into dynamic shared memory up to 1024 bytes by pointer arithmetic, so the result
+// keeps the shared state space (and the compiler keeps emitting shared-memory instructions for it).
+MX_DEV uint8_t* align1024(uint8_t* p) { return p + ((1024u - (smem_u32(p) & 1023u)) & 1023u); }
 
 // Named barrier among the consumer warps only (the producer warp does not take part).
 MX_DEV void consumers_sync(int nthreads) { asm volatile("bar.sync 1, %0;" ::"r"(nthreads) : "memory"); }
@@ -208,18 +218,32 @@ __global__ void __launch_bounds__(EPI_THREADS, 1)
 #pragma unroll
   for (int j = 0; j < R / 8; ++j) accx[j][0] = accx[j][1] = accx[j][2] = accx[j][3] = 0.f;
 
-  // ldmatrix lane roles: matrix mi = lane / 8, row-in-matrix lr = lane % 8
+  // ldmatrix lane roles: matrix mi = lane / 8, row-in-matrix lr = lane % 8.  Per-lane shared-memory
+  // offsets are fixed for the whole kernel (the swizzles make them non-affine), so they are hoisted.
   const int mi = lane >> 3, lr = lane & 7;
-  // g / u tiles: matrices (rows +0 / +8 of the warp's 16) x (tile 2p / 2p+1)
   const int lrow = warp * 16 + (mi & 1) * 8 + lr;
-  const uint32_t gu_row = (uint32_t)lrow * 128, gu_sw = (uint32_t)(lrow & 7), gu_hi = (uint32_t)(mi >> 1);
+  uint32_t o_gu[FWD_BN / 16], o_b[FWD_BN / 16][KS], o_ad[FWD_BN / 16][R / 16];
+#pragma unroll
+  for (int p = 0; p < FWD_BN / 16; ++p) {
+    // g / u tiles (128-byte rows, 128-byte swizzle): matrices (rows +0 / +8) x (n-tile 2p / 2p+1)
+    o_gu[p] = swz<128>((uint32_t)lrow, (uint32_t)(2 * p + (mi >> 1)));
+    // B_gate / B_up slices [64 n x r]: matrices (n-tile 2p / 2p+1) x (j 16kk / +8)
+#pragma unroll
+    for (int kk = 0; kk < KS; ++kk)
+      o_b[p][kk] = swz<2 * R>((uint32_t)(8 * (2 * p + (mi >> 1)) + lr), (uint32_t)(2 * kk + (mi & 1)));
+    // A_down slice [r x 64] (128-byte rows): matrices (j 16jp / +8) x (k-slice p: cols 16p / +8)
+#pragma unroll
+    for (int jp = 0; jp < R / 16; ++jp)
+      o_ad[p][jp] = swz<128>((uint32_t)(16 * jp + 8 * (mi >> 1) + lr), (uint32_t)(2 * p + (mi & 1)));
+  }
+  const uint32_t s_ring = smem_u32(smem);
   const float2 sg2 = make_float2(s_g, s_g), su2 = make_float2(s_u, s_u);
   int stage = 0;
   uint32_t phase = 0;
   for (int ct = 0; ct < tpg; ++ct) {
     const int n0 = (blockIdx.y * tpg + ct) * FWD_BN;
     if (!mbar_wait(&full[stage], phase, err, MX_DEV_TIMEOUT_EPILOGUE)) break;
-    const uint32_t sb = smem_u32(smem + stage * STG);
+    const uint32_t sb = s_ring + (uint32_t)stage * STG;
     const uint32_t tg = sb, tu = sb + FWD_TILE, tbg = sb + 2 * FWD_TILE, tbu = tbg + BT, tad = tbu + BT;
 #pragma unroll
     for (int b = 0; b < FWD_BN / 32; ++b) {
@@ -228,18 +252,15 @@ __global__ void __launch_bounds__(EPI_THREADS, 1)
       for (int pp = 0; pp < 2; ++pp) {
         const int p = 2 * b + pp;  // pair of n8 tiles (2p, 2p+1)
         uint32_t G[4], U[4];
-        const uint32_t off = gu_row + ((((uint32_t)(2 * p) + gu_hi) ^ gu_sw) << 4);
-        ldsm4(G, tg + off);
-        ldsm4(U, tu + off);
+        ldsm4(G, tg + o_gu[p]);
+        ldsm4(U, tu + o_gu[p]);
         float dg0[4] = {0.f, 0.f, 0.f, 0.f}, dg1[4] = {0.f, 0.f, 0.f, 0.f};
         float du0[4] = {0.f, 0.f, 0.f, 0.f}, du1[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
         for (int kk = 0; kk < KS; ++kk) {
-          // B_gate / B_up slices [64 n x r], rows of 2r bytes: matrices (n-tile 2p / 2p+1) x (j 16kk.. / +8)
-          const uint32_t boff = swz<2 * R>((uint32_t)(8 * (2 * p + (mi >> 1)) + lr), (uint32_t)(2 * kk + (mi & 1)));
           uint32_t BG[4], BU[4];
-          ldsm4(BG, tbg + boff);
-          ldsm4(BU, tbu + boff);
+          ldsm4(BG, tbg + o_b[p][kk]);
+          ldsm4(BU, tbu + o_b[p][kk]);
           mma16816(dg0, axg[kk], BG[0], BG[1]);
           mma16816(dg1, axg[kk], BG[2], BG[3]);
           mma16816(du0, axu[kk], BU[0], BU[1]);
@@ -262,14 +283,10 @@ __global__ void __launch_bounds__(EPI_THREADS, 1)
 #pragma unroll
       for (int mm = 0; mm < 2; ++mm) {
         const uint32_t a[4] = {hp[2 * mm][0], hp[2 * mm][1], hp[2 * mm + 1][0], hp[2 * mm + 1][1]};
-        const int m = 2 * b + mm;  // k-slice within the 64-column tile
 #pragma unroll
         for (int jp = 0; jp < R / 16; ++jp) {
-          // A_down slice [r x 64], 128-byte rows, 128-byte swizzle: matrices (j 16jp.. / +8) x (cols 16m / +8)
-          const uint32_t j = (uint32_t)(16 * jp + 8 * (mi >> 1) + lr);
-          const uint32_t chunk = (uint32_t)(2 * m + (mi & 1));
           uint32_t AD[4];
-          ldsm4(AD, tad + j * 128 + ((chunk ^ (j & 7)) << 4));
+          ldsm4(AD, tad + o_ad[2 * b + mm][jp]);
           mma16816(accx[2 * jp], a, AD[0], AD[1]);
           mma16816(accx[2 * jp + 1], a, AD[2], AD[3]);
         }
@@ -408,9 +425,39 @@ __global__ void __launch_bounds__(EPI_THREADS, 1)
   consumers_sync(nthr);
   bool ok = mbar_wait(rows_full, 0, err, MX_DEV_TIMEOUT_EPILOGUE);
 
-  // g / u / dh tiles (64-byte rows, 64-byte swizzle): this lane's ldmatrix row
+  // Per-lane shared-memory offsets, fixed for the whole kernel (the swizzles make them non-affine).
+  // g / u / dh tiles (64-byte rows, 64-byte swizzle): matrices (rows +0 / +8) x (n-tile 2p / 2p+1)
   const int lrow = warp * 16 + (mi & 1) * 8 + lr;
-  const uint32_t t_row = (uint32_t)lrow * 64, t_sw = (uint32_t)((lrow >> 1) & 3), t_hi = (uint32_t)(mi >> 1);
+  uint32_t o_tile[NT / 2];
+#pragma unroll
+  for (int p = 0; p < NT / 2; ++p) o_tile[p] = swz<64>((uint32_t)lrow, (uint32_t)(2 * p + (mi >> 1)));
+  // B_gate / B_up slices [32 n x r]: non-transposed for the LoRA-B terms, transposed for the row sums
+  uint32_t o_b[NT / 2][KS], o_bt[NT / 2][R / 16], o_a[NT / 2][KS], o_at[NT / 2][R / 16];
+#pragma unroll
+  for (int p = 0; p < NT / 2; ++p) {
+#pragma unroll
+    for (int kk = 0; kk < KS; ++kk) {
+      o_b[p][kk] = swz<2 * R>((uint32_t)(8 * (2 * p + (mi >> 1)) + lr), (uint32_t)(2 * kk + (mi & 1)));
+      o_a[p][kk] = swz<64>((uint32_t)(16 * kk + 8 * (mi & 1) + lr), (uint32_t)(2 * p + (mi >> 1)));
+    }
+#pragma unroll
+    for (int jp = 0; jp < R / 16; ++jp) {
+      o_bt[p][jp] = swz<2 * R>((uint32_t)(16 * p + 8 * (mi & 1) + lr), (uint32_t)(2 * jp + (mi >> 1)));
+      o_at[p][jp] = swz<64>((uint32_t)(16 * jp + 8 * (mi >> 1) + lr), (uint32_t)(2 * p + (mi & 1)));
+    }
+  }
+  // xs / dxd rows of the super-block: this lane's A-fragment rows
+  uint32_t o_xg[KS], o_xu[KS], o_xd[KS];
+#pragma unroll
+  for (int kk = 0; kk < KS; ++kk) {
+    o_xg[kk] = swz<4 * R>((uint32_t)lrow, (uint32_t)(2 * kk + (mi >> 1)));
+    o_xu[kk] = swz<4 * R>((uint32_t)lrow, (uint32_t)(2 * KS + 2 * kk + (mi >> 1)));
+    o_xd[kk] = swz<2 * R>((uint32_t)lrow, (uint32_t)(2 * kk + (mi >> 1)));
+  }
+  const uint32_t s_xs = smem_u32(rows_xs), s_dxd = smem_u32(rows_dxd), s_ring = smem_u32(smem);
+  // this thread's row-accumulator addresses for step 0 (rows g and g + 8 of the warp's 16)
+  const uint32_t s_acc0 = smem_u32(acc_rows) + (uint32_t)((warp * 16 + g) * RS + 2 * t) * 4u;
+  const uint32_t s_acc1 = s_acc0 + 8u * RS * 4u;
 
   const float2 sg2 = make_float2(s_g, s_g), su2 = make_float2(s_u, s_u);
   int stage = 0;
@@ -426,27 +473,23 @@ __global__ void __launch_bounds__(EPI_THREADS, 1)
         for (int e = 0; e < 4; ++e) aBg[a][i][e] = aBu[a][i][e] = aAd[a][i][e] = 0.f;
 
     for (int r = r_begin; r < r_end; r += 128) {
-      const int rl = warp * 16 + g;
-      const int64_t ra = r + rl;
-      // A fragments of xa_gate, xa_up, dxd for this warp's 16 rows, from the super-block's row buffers
+      const int step = (r - r_begin) >> 7;
+      const int64_t ra = r + warp * 16 + g;
       uint32_t axg[KS][4], axu[KS][4], axd[KS][4];
       {
-        const int step = (r - r_begin) / 128;
-        const uint32_t xrow = (uint32_t)(warp * 16 + (mi & 1) * 8 + lr);
-        const uint32_t bx = smem_u32(rows_xs + (size_t)step * 128 * 2 * R * 2);
-        const uint32_t bd = smem_u32(rows_dxd + (size_t)step * 128 * R * 2);
+        const uint32_t bx = s_xs + (uint32_t)step * (128u * 4u * R), bd = s_dxd + (uint32_t)step * (128u * 2u * R);
 #pragma unroll
         for (int kk = 0; kk < KS; ++kk) {
-          ldsm4(axg[kk], bx + swz<4 * R>(xrow, (uint32_t)(2 * kk + (mi >> 1))));
-          ldsm4(axu[kk], bx + swz<4 * R>(xrow, (uint32_t)(2 * KS + 2 * kk + (mi >> 1))));
-          ldsm4(axd[kk], bd + swz<2 * R>(xrow, (uint32_t)(2 * kk + (mi >> 1))));
+          ldsm4(axg[kk], bx + o_xg[kk]);
+          ldsm4(axu[kk], bx + o_xu[kk]);
+          ldsm4(axd[kk], bd + o_xd[kk]);
         }
       }
       if (!mbar_wait(&full[stage], phase, err, MX_DEV_TIMEOUT_EPILOGUE)) {
         ok = false;
         break;
       }
-      const uint32_t sb = smem_u32(smem + stage * STG);
+      const uint32_t sb = s_ring + (uint32_t)stage * STG;
       const uint32_t tg = sb, tu = sb + BWD_TILE, th = sb + 2 * BWD_TILE;
       const uint32_t tbg = sb + 3 * BWD_TILE, tbu = tbg + BT, tad = tbu + BT;
 
@@ -454,21 +497,16 @@ __global__ void __launch_bounds__(EPI_THREADS, 1)
 #pragma unroll
       for (int p = 0; p < NT / 2; ++p) {
         uint32_t G[4], U[4], D[4];
-        const uint32_t off = t_row + ((((uint32_t)(2 * p) + t_hi) ^ t_sw) << 4);
-        ldsm4(G, tg + off);
-        ldsm4(U, tu + off);
-        ldsm4(D, th + off);
+        ldsm4(G, tg + o_tile[p]);
+        ldsm4(U, tu + o_tile[p]);
+        ldsm4(D, th + o_tile[p]);
         float dg[2][4] = {}, du[2][4] = {}, dd[2][4] = {};
 #pragma unroll
         for (int kk = 0; kk < KS; ++kk) {
-          // B_gate / B_up slices [32 n x r]: (n-tile 2p / 2p+1) x (j 16kk / +8)
-          const uint32_t boff = swz<2 * R>((uint32_t)(8 * (2 * p + (mi >> 1)) + lr), (uint32_t)(2 * kk + (mi & 1)));
           uint32_t BG[4], BU[4], AD[4];
-          ldsm4(BG, tbg + boff);
-          ldsm4(BU, tbu + boff);
-          // A_down slice [r x 32 n] (64-byte rows) transposed: (n-tile 2p / 2p+1) x (j 16kk / +8)
-          const uint32_t aoff = swz<64>((uint32_t)(16 * kk + 8 * (mi & 1) + lr), (uint32_t)(2 * p + (mi >> 1)));
-          ldsm4t(AD, tad + aoff);
+          ldsm4(BG, tbg + o_b[p][kk]);
+          ldsm4(BU, tbu + o_b[p][kk]);
+          ldsm4t(AD, tad + o_a[p][kk]);   // A_down slice [r x 32 n] transposed: B[k = j][col n]
 #pragma unroll
           for (int qq = 0; qq < 2; ++qq) {
             mma16816(dg[qq], axg[kk], BG[2 * qq], BG[2 * qq + 1]);
@@ -499,34 +537,29 @@ __global__ void __launch_bounds__(EPI_THREADS, 1)
         quant_block16p(dup, ra, T, (int64_t)N + n0, q, N2, s, N2, t);
       }
       // per-row products (sums over columns) into the shared-memory row accumulators
-      float* A0 = acc_rows + (int64_t)(ra - r_begin) * RS;
-      float* A1 = A0 + 8 * RS;
+      const uint32_t a0 = s_acc0 + (uint32_t)step * (128u * RS * 4u), a1 = s_acc1 + (uint32_t)step * (128u * RS * 4u);
 #pragma unroll
       for (int jp = 0; jp < R / 16; ++jp) {
         float pg[2][4], pu[2][4], px[2][4];
 #pragma unroll
         for (int h2 = 0; h2 < 2; ++h2) {
-          const int c = 16 * jp + 8 * h2 + 2 * t;
-          const float2 a0 = *reinterpret_cast<const float2*>(A0 + c), a1 = *reinterpret_cast<const float2*>(A1 + c);
-          pg[h2][0] = a0.x; pg[h2][1] = a0.y; pg[h2][2] = a1.x; pg[h2][3] = a1.y;
-          const float2 b0 = *reinterpret_cast<const float2*>(A0 + R + c), b1 = *reinterpret_cast<const float2*>(A1 + R + c);
-          pu[h2][0] = b0.x; pu[h2][1] = b0.y; pu[h2][2] = b1.x; pu[h2][3] = b1.y;
-          const float2 c0 = *reinterpret_cast<const float2*>(A0 + 2 * R + c), c1 = *reinterpret_cast<const float2*>(A1 + 2 * R + c);
-          px[h2][0] = c0.x; px[h2][1] = c0.y; px[h2][2] = c1.x; px[h2][3] = c1.y;
+          const uint32_t c = (uint32_t)(16 * jp + 8 * h2) * 4u;
+          const float2 x0 = lds2(a0 + c), x1 = lds2(a1 + c);
+          pg[h2][0] = x0.x; pg[h2][1] = x0.y; pg[h2][2] = x1.x; pg[h2][3] = x1.y;
+          const float2 y0 = lds2(a0 + R * 4u + c), y1 = lds2(a1 + R * 4u + c);
+          pu[h2][0] = y0.x; pu[h2][1] = y0.y; pu[h2][2] = y1.x; pu[h2][3] = y1.y;
+          const float2 z0 = lds2(a0 + 2u * R * 4u + c), z1 = lds2(a1 + 2u * R * 4u + c);
+          px[h2][0] = z0.x; px[h2][1] = z0.y; px[h2][2] = z1.x; px[h2][3] = z1.y;
         }
 #pragma unroll
         for (int mm = 0; mm < NT / 2; ++mm) {
           const uint32_t adg[4] = {dgp[2 * mm][0], dgp[2 * mm][1], dgp[2 * mm + 1][0], dgp[2 * mm + 1][1]};
           const uint32_t adu[4] = {dup[2 * mm][0], dup[2 * mm][1], dup[2 * mm + 1][0], dup[2 * mm + 1][1]};
           const uint32_t ah[4] = {hp[2 * mm][0], hp[2 * mm][1], hp[2 * mm + 1][0], hp[2 * mm + 1][1]};
-          // B[k = n][col j] = B_gate[n][j]: transposed ldmatrix of (n 16mm / +8) x (j-tile 2jp / 2jp+1)
-          const uint32_t boff = swz<2 * R>((uint32_t)(16 * mm + 8 * (mi & 1) + lr), (uint32_t)(2 * jp + (mi >> 1)));
           uint32_t BG[4], BU[4], AD[4];
-          ldsm4t(BG, tbg + boff);
-          ldsm4t(BU, tbu + boff);
-          // B[k = n][col j] = A_down[j][n]: ldmatrix of (j-tile 2jp / 2jp+1) x (n 16mm / +8)
-          const uint32_t aoff = swz<64>((uint32_t)(16 * jp + 8 * (mi >> 1) + lr), (uint32_t)(2 * mm + (mi & 1)));
-          ldsm4(AD, tad + aoff);
+          ldsm4t(BG, tbg + o_bt[mm][jp]);   // B[k = n][col j] = B_gate[n][j]
+          ldsm4t(BU, tbu + o_bt[mm][jp]);
+          ldsm4(AD, tad + o_at[mm][jp]);    // B[k = n][col j] = A_down[j][n]
 #pragma unroll
           for (int h2 = 0; h2 < 2; ++h2) {
             mma16816(pg[h2], adg, BG[2 * h2], BG[2 * h2 + 1]);
@@ -536,13 +569,13 @@ __global__ void __launch_bounds__(EPI_THREADS, 1)
         }
 #pragma unroll
         for (int h2 = 0; h2 < 2; ++h2) {
-          const int c = 16 * jp + 8 * h2 + 2 * t;
-          *reinterpret_cast<float2*>(A0 + c) = make_float2(pg[h2][0], pg[h2][1]);
-          *reinterpret_cast<float2*>(A1 + c) = make_float2(pg[h2][2], pg[h2][3]);
-          *reinterpret_cast<float2*>(A0 + R + c) = make_float2(pu[h2][0], pu[h2][1]);
-          *reinterpret_cast<float2*>(A1 + R + c) = make_float2(pu[h2][2], pu[h2][3]);
-          *reinterpret_cast<float2*>(A0 + 2 * R + c) = make_float2(px[h2][0], px[h2][1]);
-          *reinterpret_cast<float2*>(A1 + 2 * R + c) = make_float2(px[h2][2], px[h2][3]);
+          const uint32_t c = (uint32_t)(16 * jp + 8 * h2) * 4u;
+          sts2(a0 + c, make_float2(pg[h2][0], pg[h2][1]));
+          sts2(a1 + c, make_float2(pg[h2][2], pg[h2][3]));
+          sts2(a0 + R * 4u + c, make_float2(pu[h2][0], pu[h2][1]));
+          sts2(a1 + R * 4u + c, make_float2(pu[h2][2], pu[h2][3]));
+          sts2(a0 + 2u * R * 4u + c, make_float2(px[h2][0], px[h2][1]));
+          sts2(a1 + 2u * R * 4u + c, make_float2(px[h2][2], px[h2][3]));
         }
       }
       __syncwarp();
@@ -604,20 +637,26 @@ __global__ void __launch_bounds__(EPI_THREADS, 1)
 }
 
 // ------------------------------------------------------------------------------------------------ skinny
-// out[t, j] = bf16( bf16(sum_k A[t, k] B[j, k]) * post ) for j < n (n = 16 or 32); post == 1 skips
-// the second rounding.  Warp = 16 rows; the reduction index k is permuted consistently in A and B
-// so each lane loads 16 contiguous bytes per row per 32 k.
+// out[t, j] = bf16( bf16(sum_k A[t, k] B[j, k]) * post ) for j < NJ (16, 32 or 64); post == 1 skips
+// the second rounding.  CTA = 16 rows; its 4 warps split K in four and their fp32 partials are summed
+// through shared memory in a fixed order.  The reduction index k is permuted consistently in A and B so
+// each lane loads 16 contiguous bytes per row per 32 k; two k-steps are in flight per warp.
 template <int NJ>
 __global__ void __launch_bounds__(128) k_rowdot(const bf16* __restrict__ A, int64_t lda, const bf16* __restrict__ B,
                                                 int T, int K, float post, bf16* __restrict__ out, int64_t ldo) {
+  __shared__ float red[4][16][NJ + 1];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-  const int64_t ra = ((int64_t)blockIdx.x * 4 + warp) * 16 + g, rb = ra + 8;
+  const int64_t r0 = (int64_t)blockIdx.x * 16;
+  const int64_t ra = r0 + g, rb = ra + 8;
   const bool va = ra < T, vb = rb < T;
   float acc[NJ / 8][4];
 #pragma unroll
   for (int j = 0; j < NJ / 8; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
   const uint4 z = make_uint4(0u, 0u, 0u, 0u);
-  for (int k0 = 0; k0 < K; k0 += 32) {
+  const int kq = K / 4;  // this warp's quarter of K (K % 128 == 0)
+  const int kb = warp * kq;
+#pragma unroll 2
+  for (int k0 = kb; k0 < kb + kq; k0 += 32) {
     const uint4 xa = va ? __ldg(reinterpret_cast<const uint4*>(A + ra * lda + k0 + 8 * t)) : z;
     const uint4 xb = vb ? __ldg(reinterpret_cast<const uint4*>(A + rb * lda + k0 + 8 * t)) : z;
     // fragment k slots (2t, 2t+1 | 2t+8, 2t+9) <- actual k (8t, 8t+1 | 8t+2, 8t+3), then (8t+4.. | 8t+6..)
@@ -633,14 +672,22 @@ __global__ void __launch_bounds__(128) k_rowdot(const bf16* __restrict__ A, int6
 #pragma unroll
   for (int jt = 0; jt < NJ / 8; ++jt) {
     const int c = 8 * jt + 2 * t;
-    float v[4];
+    red[warp][g][c] = acc[jt][0];
+    red[warp][g][c + 1] = acc[jt][1];
+    red[warp][g + 8][c] = acc[jt][2];
+    red[warp][g + 8][c + 1] = acc[jt][3];
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < 16 * NJ / 2; i += 128) {
+    const int rr = i / (NJ / 2), c = 2 * (i % (NJ / 2));
+    float v[2];
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      v[e] = bf16_round_f(acc[jt][e]);
+    for (int e = 0; e < 2; ++e) {
+      const float sum = (red[0][rr][c + e] + red[1][rr][c + e]) + (red[2][rr][c + e] + red[3][rr][c + e]);
+      v[e] = bf16_round_f(sum);
       if (post != 1.0f) v[e] = bf16_round_f(v[e] * post);
     }
-    if (va) *reinterpret_cast<uint32_t*>(out + ra * ldo + c) = pack_bf16x2(v[0], v[1]);
-    if (vb) *reinterpret_cast<uint32_t*>(out + rb * ldo + c) = pack_bf16x2(v[2], v[3]);
+    if (r0 + rr < T) *reinterpret_cast<uint32_t*>(out + (r0 + rr) * ldo + c) = pack_bf16x2(v[0], v[1]);
   }
 }
 
@@ -658,6 +705,7 @@ __global__ void __launch_bounds__(128) k_coldot(const bf16* __restrict__ A, int6
   float acc[NJ / 8][4];
 #pragma unroll
   for (int j = 0; j < NJ / 8; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
+#pragma unroll 4
   for (int r = r0; r < r1; r += 16) {
     const int64_t ra = r + g, rb = ra + 8;
     const bool va = ra < r1, vb = rb < r1;
@@ -912,10 +960,10 @@ extern "C" int mxm_mlp_bwd_reduce(const void* dxa_part, const void* dbg_part, co
 extern "C" int mxm_rowdot(const void* A, int64_t lda, const void* B, int64_t T, int64_t K, int n, float post,
                           void* out, int64_t ldo, void* stream) {
   MX_CHECK_ARG(A && B && out, "mxm_rowdot: null pointer");
-  MX_CHECK_ARG(T >= 1 && K >= 32 && K % 32 == 0 && (n == 16 || n == 32 || n == 64) && lda % 8 == 0 && ldo % 2 == 0,
-               "mxm_rowdot: need K %% 32 == 0, n in {16, 32, 64}, lda %% 8 == 0");
+  MX_CHECK_ARG(T >= 1 && K >= 128 && K % 128 == 0 && (n == 16 || n == 32 || n == 64) && lda % 8 == 0 && ldo % 2 == 0,
+               "mxm_rowdot: need K %% 128 == 0, n in {16, 32, 64}, lda %% 8 == 0");
   MX_CHECK_ARG(mx_aligned(A, 16) && mx_aligned(B, 16) && mx_aligned(out, 4), "mxm_rowdot: alignment");
-  const unsigned grid = (unsigned)((T + 63) / 64);
+  const unsigned grid = (unsigned)((T + 15) / 16);
   cudaStream_t st = (cudaStream_t)stream;
   if (n == 16)
     k_rowdot<16><<<grid, 128, 0, st>>>((const bf16*)A, lda, (const bf16*)B, (int)T, (int)K, post, (bf16*)out, ldo);
