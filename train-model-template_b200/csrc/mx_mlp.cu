@@ -85,9 +85,9 @@ MX_DEV uint32_t max_bf16x2(uint32_t a, uint32_t b) {
 // Quantizes one 32-column block of a 16-row warp tile whose bf16 values are held packed in
 // D-fragment form: pk[i][h] = (row g + 8h, cols 8i+2t, +1), i = 0..3 (t = lane % 4).  Codes go to
 // q[row * ldq + col0 + ...] for rows < T; the scales of rows g and g+8 (always, padded rows included)
-// to the blocked layout of a [*, scols] operand.
-MX_DEV void quant_block16p(const uint32_t (&pk)[4][2], int64_t row_g, int64_t T, int64_t col0, uint8_t* q,
-                           int64_t ldq, uint8_t* s, int64_t scols, int t) {
+// to the blocked layout of a [*, scols] operand for rows < Tpad.
+MX_DEV void quant_block16p(const uint32_t (&pk)[4][2], int64_t row_g, int64_t T, int64_t Tpad, int64_t col0,
+                           uint8_t* q, int64_t ldq, uint8_t* s, int64_t scols, int t) {
 #pragma unroll
   for (int h = 0; h < 2; ++h) {
     const uint32_t m2 = max_bf16x2(absmax_bf16x2(pk[0][h], pk[1][h]), absmax_bf16x2(pk[2][h], pk[3][h]));
@@ -105,7 +105,7 @@ MX_DEV void quant_block16p(const uint32_t (&pk)[4][2], int64_t row_g, int64_t T,
       const float2 v = __fmul2_rn(up2(pk[i][h]), r2);
       stg16_if(dst + 8 * i, e4m3x2_sat(v.x, v.y), live);
     }
-    stg8_if(s + mx_scale_offset(row, col0 >> 5, scols), e, t == 0);
+    stg8_if(s + mx_scale_offset(row < Tpad ? row : 0, col0 >> 5, scols), e, t == 0 && row < Tpad);
   }
 }
 
@@ -132,40 +132,42 @@ constexpr int CONSUMERS = 8;                      // consumer warps (16 rows eac
 constexpr int EPI_THREADS = 32 * (CONSUMERS + 1);  // + one TMA producer warp
 
 // ------------------------------------------------------------------------------------------------ forward
-// CTA = one 128-row block x one column group of `tpg` 64-column tiles.  Warp 8 streams, per tile,
-// the g and u tiles ([128 x 64] bf16, 128-byte swizzle) and the tile's slices of B_gate, B_up
-// ([64 x r]) and A_down ([r x 64], 128-byte swizzle) into a 3-stage ring with TMA.  Warps 0-7 each
-// own 16 rows; every MMA operand comes from shared memory through ldmatrix, and the per-row
-// xS_down accumulator stays in registers across the whole group.
-constexpr int FWD_BN = 64, FWD_ST = 3, FWD_TILE = 128 * FWD_BN * 2;  // 16 KB per g / u tile
+// CTA = one 240-row block x one column group of `tpg` 64-column tiles.  Warp 15 streams, per tile,
+// the g and u tiles ([240 x 64] bf16, 128-byte swizzle) and the tile's slices of B_gate, B_up
+// ([64 x r]) and A_down ([r x 64], 128-byte swizzle) into a 3-stage ring with TMA.  Warps 0-14 each
+// own 16 rows (four warps per scheduler to hide latency); every MMA operand comes from shared memory
+// through ldmatrix, and the per-row xS_down accumulator stays in registers across the whole group.
+constexpr int FWD_CONS = 15, FWD_ROWS = 16 * FWD_CONS;             // consumer warps, rows per CTA
+constexpr int FWD_THREADS = 32 * (FWD_CONS + 1);                       // + one TMA producer warp
+constexpr int FWD_BN = 64, FWD_ST = 3, FWD_TILE = FWD_ROWS * FWD_BN * 2;  // 30 KB per g / u tile
 __host__ __device__ constexpr int fwd_btile(int R) { return FWD_BN * R * 2; }
 __host__ __device__ constexpr int fwd_stage(int R) { return 2 * FWD_TILE + 3 * fwd_btile(R); }
 __host__ __device__ constexpr size_t fwd_smem(int R) { return 1024 + (size_t)FWD_ST * fwd_stage(R) + 2 * FWD_ST * 8; }
 
 template <int R>
-__global__ void __launch_bounds__(EPI_THREADS, 1)
+__global__ void __launch_bounds__(FWD_THREADS, 1)
     k_mlp_fwd(const __grid_constant__ CUtensorMap tm_gu, const __grid_constant__ CUtensorMap tm_bg,
               const __grid_constant__ CUtensorMap tm_bu, const __grid_constant__ CUtensorMap tm_ad,
               const bf16* __restrict__ xs, uint8_t* __restrict__ qh, uint8_t* __restrict__ sh,
-              float* __restrict__ xsd_part, bf16* __restrict__ xsd_out, int T, int N, float s_g, float s_u, int tpg,
-              int write_q, int* err) {
+              float* __restrict__ xsd_part, bf16* __restrict__ xsd_out, int T, int Tpad, int N, float s_g,
+              float s_u, int tpg, int write_q, int* err) {
   constexpr int KS = R / 16, BT = fwd_btile(R), STG = fwd_stage(R);
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + FWD_ST * STG);
   uint64_t* empty = full + FWD_ST;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t row0 = (int64_t)blockIdx.x * 128;
+  const int64_t row0 = (int64_t)blockIdx.x * FWD_ROWS;
   if (threadIdx.x == 0) {
     for (int i = 0; i < FWD_ST; ++i) {
       mbar_init(&full[i], 1);
-      mbar_init(&empty[i], CONSUMERS);
+      mbar_init(&empty[i], FWD_CONS);
     }
     fence_barrier_init();
   }
   __syncthreads();
 
-  if (warp == CONSUMERS) {  // TMA producer
+  if (warp == FWD_CONS) {  // TMA producer
     if (lane == 0) {
       prefetch_tmap(&tm_gu);
       prefetch_tmap(&tm_bg);
@@ -278,7 +280,7 @@ __global__ void __launch_bounds__(EPI_THREADS, 1)
           }
         }
       }
-      if (write_q) quant_block16p(hp, ra, T, n0 + 32 * b, qh, N, sh, N, t);
+      if (write_q) quant_block16p(hp, ra, T, Tpad, n0 + 32 * b, qh, N, sh, N, t);
       // xS_down += h (16 x 32 block) A_down^T: two k-slices of 16 columns
 #pragma unroll
       for (int mm = 0; mm < 2; ++mm) {
@@ -533,8 +535,8 @@ __global__ void __launch_bounds__(EPI_THREADS, 1)
         }
       }
       if (write_q) {
-        quant_block16p(dgp, ra, T, n0, q, N2, s, N2, t);
-        quant_block16p(dup, ra, T, (int64_t)N + n0, q, N2, s, N2, t);
+        quant_block16p(dgp, ra, T, Tpad, n0, q, N2, s, N2, t);
+        quant_block16p(dup, ra, T, Tpad, (int64_t)N + n0, q, N2, s, N2, t);
       }
       // per-row products (sums over columns) into the shared-memory row accumulators
       const uint32_t a0 = s_acc0 + (uint32_t)step * (128u * RS * 4u), a1 = s_acc1 + (uint32_t)step * (128u * RS * 4u);
@@ -786,7 +788,7 @@ int grid_for(int64_t n, int threads) {
 extern "C" int mxm_mlp_fwd_partitions(int64_t T, int64_t N, int r, int* col_groups) {
   MX_CHECK_ARG(T >= 1 && N >= 128 && N % 128 == 0 && (r == 16 || r == 32) && col_groups, "mxm_mlp_fwd_partitions: bad args");
   // one CTA per SM: the fewest column groups that still fill every SM twice
-  const int64_t nrb = (T + 127) / 128;
+  const int64_t nrb = (T + FWD_ROWS - 1) / FWD_ROWS;
   const int nt = (int)(N / FWD_BN);
   int cs = nt;
   for (int d = 1; d <= nt; ++d)
@@ -812,7 +814,7 @@ extern "C" int mxm_mlp_fwd_epilogue(const void* gu, const void* xs, const void* 
                "mxm_mlp_fwd_epilogue: gu / bg / bu / ad must be 16-byte aligned");
   CUtensorMap tm, tbg, tbu, tad;
   if (int e = mx_make_tmap_2d(&tm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, gu, (uint64_t)(2 * N), (uint64_t)T,
-                              (uint64_t)(4 * N), FWD_BN, 128, CU_TENSOR_MAP_SWIZZLE_128B))
+                              (uint64_t)(4 * N), FWD_BN, FWD_ROWS, CU_TENSOR_MAP_SWIZZLE_128B))
     return e;
   if (int e = mx_make_tmap_2d(&tbg, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, bg, (uint64_t)r, (uint64_t)N,
                               (uint64_t)(2 * r), r, FWD_BN, r == 16 ? CU_TENSOR_MAP_SWIZZLE_32B : CU_TENSOR_MAP_SWIZZLE_64B))
@@ -823,17 +825,18 @@ extern "C" int mxm_mlp_fwd_epilogue(const void* gu, const void* xs, const void* 
   if (int e = mx_make_tmap_2d(&tad, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, ad, (uint64_t)N, (uint64_t)r,
                               (uint64_t)(2 * N), FWD_BN, r, CU_TENSOR_MAP_SWIZZLE_128B))
     return e;
-  dim3 grid((unsigned)((T + 127) / 128), (unsigned)col_groups);
+  dim3 grid((unsigned)((T + FWD_ROWS - 1) / FWD_ROWS), (unsigned)col_groups);
   cudaStream_t st = (cudaStream_t)stream;
   const int tpg = nt / col_groups;
+  const int Tpad = (int)((T + 127) / 128 * 128);  // rows of the blocked scale layout
   bf16* direct = col_groups == 1 ? (bf16*)xsd : nullptr;
   const size_t smem = fwd_smem(r);
   auto go = [&](auto kern) -> int {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return mx_cuda_status(e, "mlp fwd epilogue: set smem");
-    kern<<<grid, EPI_THREADS, smem, st>>>(tm, tbg, tbu, tad, (const bf16*)xs, (uint8_t*)qh, (uint8_t*)sh,
-                                          (float*)xsd_part, direct, (int)T, (int)N, s_g, s_u, tpg, qh != nullptr,
-                                          mx_dev_error_ptr());
+    kern<<<grid, FWD_THREADS, smem, st>>>(tm, tbg, tbu, tad, (const bf16*)xs, (uint8_t*)qh, (uint8_t*)sh,
+                                          (float*)xsd_part, direct, (int)T, Tpad, (int)N, s_g, s_u, tpg,
+                                          qh != nullptr, mx_dev_error_ptr());
     mx_note_launch();
     return mx_launch_status("mlp fwd epilogue");
   };
