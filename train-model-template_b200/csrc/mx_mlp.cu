@@ -36,12 +36,6 @@ MX_DEV uint32_t e4m3x2_sat(float lo, float hi) {
   return r;
 }
 
-MX_DEV float2 lds2(uint32_t a) {
-  float2 v;
-  asm volatile("ld.shared.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(a));
-  return v;
-}
-MX_DEV void sts2(uint32_t a, float2 v) { asm volatile("st.shared.v2.f32 [%0], {%1, %2};" ::"r"(a), "f"(v.x), "f"(v.y)); }
 // Predicated global stores (no branch around them).
 MX_DEV void stg16_if(void* p, uint32_t v, bool pred) {
   asm volatile("{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %2, 0;\n\t@q st.global.b16 [%0], %1;\n\t}" ::"l"(p),
@@ -125,11 +119,7 @@ __host__ __device__ constexpr CUtensorMapSwizzle swz_mode() {
 // keeps the shared state space (and the compiler keeps emitting shared-memory instructions for it).
 MX_DEV uint8_t* align1024(uint8_t* p) { return p + ((1024u - (smem_u32(p) & 1023u)) & 1023u); }
 
-// Named barrier among the consumer warps only (the producer warp does not take part).
-MX_DEV void consumers_sync(int nthreads) { asm volatile("bar.sync 1, %0;" ::"r"(nthreads) : "memory"); }
 
-constexpr int CONSUMERS = 8;                      // consumer warps (16 rows each: 128-row blocks)
-constexpr int EPI_THREADS = 32 * (CONSUMERS + 1);  // + one TMA producer warp
 
 // ------------------------------------------------------------------------------------------------ forward
 // CTA = one 240-row block x one column group of `tpg` 64-column tiles.  Warp 15 streams, per tile,
@@ -316,119 +306,130 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
 }
 
 // ------------------------------------------------------------------------------------------------ backward
-// CTA = one super-block of SB rows x one column group of `tpg` 32-column tiles.  Warp 8 streams, per
-// (column tile, 128-row step), the [128 x 32] bf16 tiles of g, u and dh (64-byte swizzle) plus the
-// column tile's slices of B_gate, B_up ([32 x r]) and A_down ([r x 32]) into a 4-stage ring with TMA;
-// column tile outer, row step inner.  Warps 0-7 each own 16 rows of every step:
-//   * dB_gate, dB_up, dA_down (sums over rows) accumulate in registers over the super-block, then the
-//     8 warps' tiles are summed in a fixed order through shared memory -> one partial per super-block;
-//   * dxa_gate, dxa_up, xS_down (sums over columns) accumulate in a shared-memory [SB x 3r] buffer
-//     (row stride padded for conflict-free access) that each warp only touches in its own rows,
-//     written once per CTA as the group's partial.
-// No atomics: the result is deterministic.  All MMA operands come from shared memory through
-// ldmatrix (.trans where the tile is stored transposed to the operand).
-constexpr int BWD_BN = 32, BWD_TILE = 128 * BWD_BN * 2;  // 8 KB per g / u / dh tile
-__host__ __device__ constexpr int bwd_st(int R) { return R == 16 ? 4 : 3; }  // ring stages
+// CTA = one block of SB = 16 x CONS rows x one column group of `tpg` 32-column tiles.  Warp CONS streams,
+// per column tile, the [SB x 32] bf16 tiles of g, u and dh (64-byte swizzle) plus the tile's slices of
+// B_gate, B_up ([32 x r]) and A_down ([r x 32]) into a 2-stage ring with TMA; the block's xs and dxd
+// rows are loaded once.  Consumer warps 0 .. CONS-1 each own 16 rows:
+//   * dg, du, h of the tile are computed in registers, quantized, and multiplied by the B slices into
+//     the per-row sums dxa_gate, dxa_up, xS_down, which stay in registers over all of the group's tiles;
+//   * dg, du, h are also stored (bf16, the same swizzle) into a double-buffered shared tile; after one
+//     named barrier, the 6 (r = 16) or 12 (r = 32) 16 x 16 blocks of dB_gate^T, dB_up^T and dA_down are
+//     dealt out to the warps, each reduced over the block's SB rows with mma (xa^T from the row buffer)
+//     and stored as the block's partial.  Warps without a block go straight on to the next tile.
+// Four warps per scheduler (r = 16) hide the latency of the per-element chains.  No atomics: the result
+// is deterministic.
+constexpr int BWD_BN = 32, BWD_ST = 2;
+// consumer warps: 16 warps in all (4 per scheduler, 128 registers) for r = 16; 12 (3 per scheduler,
+// 168 registers) for r = 32, whose per-row sums and fragments need more registers
+__host__ __device__ constexpr int bwd_cons(int R) { return R == 16 ? 15 : 11; }
+__host__ __device__ constexpr int bwd_rows(int R) { return 16 * bwd_cons(R); }   // rows per CTA
+__host__ __device__ constexpr int bwd_tile(int R) { return bwd_rows(R) * BWD_BN * 2; }
 __host__ __device__ constexpr int bwd_btile(int R) { return BWD_BN * R * 2; }
-__host__ __device__ constexpr int bwd_stage(int R) { return 3 * BWD_TILE + 3 * bwd_btile(R); }
-__host__ __device__ constexpr int bwd_rs(int R) { return 3 * R + 8; }      // padded row stride of the row sums
-__host__ __device__ constexpr int bwd_ws() { return BWD_BN + 8; }          // padded stride of the reduction tiles
-__host__ __device__ constexpr size_t bwd_rowbuf(int SB, int R) { return (size_t)SB * 3 * R * 2; }  // xs + dxd rows
-__host__ __device__ constexpr size_t bwd_smem(int R, int SB) {
-  return 1024 + (size_t)bwd_st(R) * bwd_stage(R) + bwd_rowbuf(SB, R) + (size_t)SB * bwd_rs(R) * 4 +
-         (size_t)CONSUMERS * R * bwd_ws() * 4 + (2 * bwd_st(R) + 1) * sizeof(uint64_t);
+__host__ __device__ constexpr int bwd_stage(int R) { return 3 * bwd_tile(R) + 3 * bwd_btile(R); }
+__host__ __device__ constexpr size_t bwd_rowbuf(int R) { return ((size_t)bwd_rows(R) * 3 * R * 2 + 1023) / 1024 * 1024; }
+__host__ __device__ constexpr size_t bwd_smem(int R) {
+  return 1024 + (size_t)BWD_ST * bwd_stage(R) + bwd_rowbuf(R) + 2 * 3 * (size_t)bwd_tile(R) +
+         (2 * BWD_ST + 1) * sizeof(uint64_t);
+}
+
+// bar.sync among the consumer warps that also returns, to every thread, whether any thread passed
+// `v` = true (a uniform decision to leave the loop after a timed-out wait).
+MX_DEV bool consumers_sync_or(int nthreads, bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.or.pred q, 1, %2, p;\n selp.u32 %0, 1, 0, q;\n}"
+      : "=r"(r)
+      : "r"((uint32_t)v), "r"(nthreads)
+      : "memory");
+  return r != 0;
 }
 
 template <int R>
-__global__ void __launch_bounds__(EPI_THREADS, 1)
+__global__ void __launch_bounds__(32 * (bwd_cons(R) + 1), 1)
     k_mlp_bwd(const __grid_constant__ CUtensorMap tm_gu, const __grid_constant__ CUtensorMap tm_dh,
               const __grid_constant__ CUtensorMap tm_bg, const __grid_constant__ CUtensorMap tm_bu,
               const __grid_constant__ CUtensorMap tm_ad, const __grid_constant__ CUtensorMap tm_xs,
               const __grid_constant__ CUtensorMap tm_dxd, uint8_t* __restrict__ q, uint8_t* __restrict__ s,
-              float* __restrict__ dxa_part,
-              float* __restrict__ dbg_part, float* __restrict__ dbu_part, float* __restrict__ dad_part, int T,
-              int Tpad, int N, float s_g, float s_u, int SB, int tpg, int write_q, int* err) {
-  constexpr int KS = R / 16, NT = BWD_BN / 8, R3 = 3 * R, RS = bwd_rs(R), WS = bwd_ws();
-  constexpr int BT = bwd_btile(R), STG = bwd_stage(R), BWD_ST = bwd_st(R);
+              float* __restrict__ dxa_part, float* __restrict__ dbg_part, float* __restrict__ dbu_part,
+              float* __restrict__ dad_part, int T, int Tpad, int N, float s_g, float s_u, int tpg, int write_q,
+              int* err) {
+  constexpr int CONS = bwd_cons(R), SB = bwd_rows(R), KS = R / 16, NT = BWD_BN / 8, R3 = 3 * R;
+  constexpr int TILE = bwd_tile(R), BT = bwd_btile(R), STG = bwd_stage(R);
+  constexpr int TASKS = 3 * 2 * KS;  // column-product blocks: {dBg, dBu, dAd} x (r / 16) x 2 column halves
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
-  // the super-block's xs rows ([128 x 2r] per 128-row step) then its dxd rows ([128 x r] per step),
-  // both TMA-swizzled, loaded once; then the row accumulators, the reduction scratch, the barriers
-  uint8_t* rows_xs = smem + BWD_ST * STG;
-  uint8_t* rows_dxd = rows_xs + (size_t)SB * 2 * R * 2;
-  float* acc_rows = reinterpret_cast<float*>(rows_xs + bwd_rowbuf(SB, R));  // [SB][RS]
-  float* scratch = acc_rows + (size_t)SB * RS;                              // [CONSUMERS][R][WS]
-  uint64_t* full = reinterpret_cast<uint64_t*>(scratch + CONSUMERS * R * WS);
+  uint8_t* rows_xs = smem + BWD_ST * STG;             // [SB][2r] bf16, TMA-swizzled
+  uint8_t* rows_dxd = rows_xs + (size_t)SB * 4 * R;    // [SB][r]
+  uint8_t* opbuf = rows_xs + bwd_rowbuf(R);            // [2][3][SB][32] bf16: dg | du | h, 64-byte swizzle
+  uint64_t* full = reinterpret_cast<uint64_t*>(opbuf + 2 * 3 * TILE);
   uint64_t* empty = full + BWD_ST;
   uint64_t* rows_full = empty + BWD_ST;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int sbi = blockIdx.x, cg = blockIdx.y;
-  const int r_begin = sbi * SB, r_end = min(r_begin + SB, Tpad);
+  const int cg = blockIdx.y, r0 = blockIdx.x * SB;
   const int64_t N2 = 2 * (int64_t)N;
   if (threadIdx.x == 0) {
     for (int i = 0; i < BWD_ST; ++i) {
       mbar_init(&full[i], 1);
-      mbar_init(&empty[i], CONSUMERS);
+      mbar_init(&empty[i], CONS);
     }
     mbar_init(rows_full, 1);
     fence_barrier_init();
   }
   __syncthreads();
 
-  if (warp == CONSUMERS) {  // TMA producer
+  if (warp == CONS) {  // TMA producer
     if (lane == 0) {
       prefetch_tmap(&tm_gu);
       prefetch_tmap(&tm_dh);
       prefetch_tmap(&tm_bg);
       prefetch_tmap(&tm_bu);
       prefetch_tmap(&tm_ad);
-      const int nsteps = (r_end - r_begin) / 128;
-      mbar_arrive_expect_tx(rows_full, (uint32_t)(nsteps * 128 * 3 * R * 2));
-      for (int k = 0; k < nsteps; ++k) {
-        tma_load_2d(rows_xs + (size_t)k * 128 * 2 * R * 2, &tm_xs, rows_full, 0, r_begin + 128 * k);
-        tma_load_2d(rows_dxd + (size_t)k * 128 * R * 2, &tm_dxd, rows_full, 0, r_begin + 128 * k);
-      }
+      mbar_arrive_expect_tx(rows_full, (uint32_t)(SB * 3 * R * 2));
+      tma_load_2d(rows_xs, &tm_xs, rows_full, 0, r0);
+      tma_load_2d(rows_dxd, &tm_dxd, rows_full, 0, r0);
     }
     int stage = 0;
     uint32_t phase = 0;
-    bool ok = true;
-    for (int ct = 0; ct < tpg && ok; ++ct) {
+    int issued = 0;
+    for (int ct = 0; ct < tpg; ++ct) {
       const int n0 = (cg * tpg + ct) * BWD_BN;
-      for (int r = r_begin; r < r_end; r += 128) {
-        if (!mbar_wait(&empty[stage], phase ^ 1, err, MX_DEV_TIMEOUT_PRODUCER)) {
-          ok = false;
-          break;
-        }
-        if (lane == 0) {
-          uint8_t* dst = smem + stage * STG;
-          uint64_t* fb = &full[stage];
-          mbar_arrive_expect_tx(fb, STG);
-          tma_load_2d(dst, &tm_gu, fb, n0, r);
-          tma_load_2d(dst + BWD_TILE, &tm_gu, fb, N + n0, r);
-          tma_load_2d(dst + 2 * BWD_TILE, &tm_dh, fb, n0, r);
-          tma_load_2d(dst + 3 * BWD_TILE, &tm_bg, fb, 0, n0);
-          tma_load_2d(dst + 3 * BWD_TILE + BT, &tm_bu, fb, 0, n0);
-          tma_load_2d(dst + 3 * BWD_TILE + 2 * BT, &tm_ad, fb, n0, 0);
-        }
-        __syncwarp();
-        if (++stage == BWD_ST) {
-          stage = 0;
-          phase ^= 1;
-        }
+      if (!mbar_wait(&empty[stage], phase ^ 1, err, MX_DEV_TIMEOUT_PRODUCER)) break;
+      if (lane == 0) {
+        uint8_t* dst = smem + stage * STG;
+        uint64_t* fb = &full[stage];
+        mbar_arrive_expect_tx(fb, STG);
+        tma_load_2d(dst, &tm_gu, fb, n0, r0);
+        tma_load_2d(dst + TILE, &tm_gu, fb, N + n0, r0);
+        tma_load_2d(dst + 2 * TILE, &tm_dh, fb, n0, r0);
+        tma_load_2d(dst + 3 * TILE, &tm_bg, fb, 0, n0);
+        tma_load_2d(dst + 3 * TILE + BT, &tm_bu, fb, 0, n0);
+        tma_load_2d(dst + 3 * TILE + 2 * BT, &tm_ad, fb, n0, 0);
+      }
+      __syncwarp();
+      ++issued;
+      if (++stage == BWD_ST) {
+        stage = 0;
+        phase ^= 1;
       }
     }
+    // leave no copy in flight: wait (bounded) for the last load of every stage that was used
+    for (int k = 0; k < BWD_ST && k < issued; ++k) {
+      const int i = issued - 1 - k, st = i % BWD_ST;
+      mbar_wait(&full[st], (uint32_t)((i / BWD_ST) & 1), err, MX_DEV_TIMEOUT_PRODUCER);
+    }
+    mbar_wait(rows_full, 0, err, MX_DEV_TIMEOUT_PRODUCER);
     return;
   }
 
   const int g = lane >> 2, t = lane & 3;
   const int mi = lane >> 3, lr = lane & 7;
-  const int nthr = CONSUMERS * 32;
-  for (int i = threadIdx.x; i < SB * RS; i += nthr) acc_rows[i] = 0.f;
-  consumers_sync(nthr);
-  bool ok = mbar_wait(rows_full, 0, err, MX_DEV_TIMEOUT_EPILOGUE);
+  const int nthr = CONS * 32;
+  const bool rows_ok = mbar_wait(rows_full, 0, err, MX_DEV_TIMEOUT_EPILOGUE);
+  if (consumers_sync_or(nthr, !rows_ok)) return;
 
   // Per-lane shared-memory offsets, fixed for the whole kernel (the swizzles make them non-affine).
-  // g / u / dh tiles (64-byte rows, 64-byte swizzle): matrices (rows +0 / +8) x (n-tile 2p / 2p+1)
+  // g / u / dh tiles and the dg / du / h operand tile (64-byte rows, 64-byte swizzle): matrices
+  // (rows +0 / +8) x (n-tile 2p / 2p+1)
   const int lrow = warp * 16 + (mi & 1) * 8 + lr;
   uint32_t o_tile[NT / 2];
 #pragma unroll
@@ -448,52 +449,34 @@ __global__ void __launch_bounds__(EPI_THREADS, 1)
       o_at[p][jp] = swz<64>((uint32_t)(16 * jp + 8 * (mi >> 1) + lr), (uint32_t)(2 * p + (mi & 1)));
     }
   }
-  // xs / dxd rows of the super-block: this lane's A-fragment rows
-  uint32_t o_xg[KS], o_xu[KS], o_xd[KS];
+  const uint32_t s_xs = smem_u32(rows_xs), s_dxd = smem_u32(rows_dxd), s_ring = smem_u32(smem);
+  const uint32_t s_op = smem_u32(opbuf);
+  // this warp's rows of xa_gate | xa_up | dxd as MMA A fragments, for the whole kernel
+  uint32_t axg[KS][4], axu[KS][4], axd[KS][4];
 #pragma unroll
   for (int kk = 0; kk < KS; ++kk) {
-    o_xg[kk] = swz<4 * R>((uint32_t)lrow, (uint32_t)(2 * kk + (mi >> 1)));
-    o_xu[kk] = swz<4 * R>((uint32_t)lrow, (uint32_t)(2 * KS + 2 * kk + (mi >> 1)));
-    o_xd[kk] = swz<2 * R>((uint32_t)lrow, (uint32_t)(2 * kk + (mi >> 1)));
+    ldsm4(axg[kk], s_xs + swz<4 * R>((uint32_t)lrow, (uint32_t)(2 * kk + (mi >> 1))));
+    ldsm4(axu[kk], s_xs + swz<4 * R>((uint32_t)lrow, (uint32_t)(2 * KS + 2 * kk + (mi >> 1))));
+    ldsm4(axd[kk], s_dxd + swz<2 * R>((uint32_t)lrow, (uint32_t)(2 * kk + (mi >> 1))));
   }
-  const uint32_t s_xs = smem_u32(rows_xs), s_dxd = smem_u32(rows_dxd), s_ring = smem_u32(smem);
-  // this thread's row-accumulator addresses for step 0 (rows g and g + 8 of the warp's 16)
-  const uint32_t s_acc0 = smem_u32(acc_rows) + (uint32_t)((warp * 16 + g) * RS + 2 * t) * 4u;
-  const uint32_t s_acc1 = s_acc0 + 8u * RS * 4u;
+  float rg[R / 8][4], ru[R / 8][4], rx[R / 8][4];  // per-row sums over the group's columns
+#pragma unroll
+  for (int j = 0; j < R / 8; ++j)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) rg[j][e] = ru[j][e] = rx[j][e] = 0.f;
 
+  const int64_t ra = (int64_t)r0 + warp * 16 + g;
   const float2 sg2 = make_float2(s_g, s_g), su2 = make_float2(s_u, s_u);
   int stage = 0;
   uint32_t phase = 0;
-  for (int ct = 0; ct < tpg && ok; ++ct) {
+  for (int ct = 0; ct < tpg; ++ct) {
     const int n0 = (cg * tpg + ct) * BWD_BN;
-    float aBg[KS][NT][4], aBu[KS][NT][4], aAd[KS][NT][4];
-#pragma unroll
-    for (int a = 0; a < KS; ++a)
-#pragma unroll
-      for (int i = 0; i < NT; ++i)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) aBg[a][i][e] = aBu[a][i][e] = aAd[a][i][e] = 0.f;
-
-    for (int r = r_begin; r < r_end; r += 128) {
-      const int step = (r - r_begin) >> 7;
-      const int64_t ra = r + warp * 16 + g;
-      uint32_t axg[KS][4], axu[KS][4], axd[KS][4];
-      {
-        const uint32_t bx = s_xs + (uint32_t)step * (128u * 4u * R), bd = s_dxd + (uint32_t)step * (128u * 2u * R);
-#pragma unroll
-        for (int kk = 0; kk < KS; ++kk) {
-          ldsm4(axg[kk], bx + o_xg[kk]);
-          ldsm4(axu[kk], bx + o_xu[kk]);
-          ldsm4(axd[kk], bd + o_xd[kk]);
-        }
-      }
-      if (!mbar_wait(&full[stage], phase, err, MX_DEV_TIMEOUT_EPILOGUE)) {
-        ok = false;
-        break;
-      }
+    const bool okw = mbar_wait(&full[stage], phase, err, MX_DEV_TIMEOUT_EPILOGUE);
+    const uint32_t ob = s_op + (uint32_t)(ct & 1) * (3u * TILE);
+    if (okw) {
       const uint32_t sb = s_ring + (uint32_t)stage * STG;
-      const uint32_t tg = sb, tu = sb + BWD_TILE, th = sb + 2 * BWD_TILE;
-      const uint32_t tbg = sb + 3 * BWD_TILE, tbu = tbg + BT, tad = tbu + BT;
+      const uint32_t tg = sb, tu = sb + TILE, th = sb + 2 * TILE;
+      const uint32_t tbg = sb + 3 * TILE, tbu = tbg + BT, tad = tbu + BT;
 
       uint32_t dgp[NT][2], dup[NT][2], hp[NT][2];
 #pragma unroll
@@ -538,103 +521,97 @@ __global__ void __launch_bounds__(EPI_THREADS, 1)
         quant_block16p(dgp, ra, T, Tpad, n0, q, N2, s, N2, t);
         quant_block16p(dup, ra, T, Tpad, (int64_t)N + n0, q, N2, s, N2, t);
       }
-      // per-row products (sums over columns) into the shared-memory row accumulators
-      const uint32_t a0 = s_acc0 + (uint32_t)step * (128u * RS * 4u), a1 = s_acc1 + (uint32_t)step * (128u * RS * 4u);
+      // per-row products (sums over columns): [dg Bg | du Bu | h Ad^T]
 #pragma unroll
-      for (int jp = 0; jp < R / 16; ++jp) {
-        float pg[2][4], pu[2][4], px[2][4];
+      for (int mm = 0; mm < NT / 2; ++mm) {
+        const uint32_t adg[4] = {dgp[2 * mm][0], dgp[2 * mm][1], dgp[2 * mm + 1][0], dgp[2 * mm + 1][1]};
+        const uint32_t adu[4] = {dup[2 * mm][0], dup[2 * mm][1], dup[2 * mm + 1][0], dup[2 * mm + 1][1]};
+        const uint32_t ah[4] = {hp[2 * mm][0], hp[2 * mm][1], hp[2 * mm + 1][0], hp[2 * mm + 1][1]};
 #pragma unroll
-        for (int h2 = 0; h2 < 2; ++h2) {
-          const uint32_t c = (uint32_t)(16 * jp + 8 * h2) * 4u;
-          const float2 x0 = lds2(a0 + c), x1 = lds2(a1 + c);
-          pg[h2][0] = x0.x; pg[h2][1] = x0.y; pg[h2][2] = x1.x; pg[h2][3] = x1.y;
-          const float2 y0 = lds2(a0 + R * 4u + c), y1 = lds2(a1 + R * 4u + c);
-          pu[h2][0] = y0.x; pu[h2][1] = y0.y; pu[h2][2] = y1.x; pu[h2][3] = y1.y;
-          const float2 z0 = lds2(a0 + 2u * R * 4u + c), z1 = lds2(a1 + 2u * R * 4u + c);
-          px[h2][0] = z0.x; px[h2][1] = z0.y; px[h2][2] = z1.x; px[h2][3] = z1.y;
-        }
-#pragma unroll
-        for (int mm = 0; mm < NT / 2; ++mm) {
-          const uint32_t adg[4] = {dgp[2 * mm][0], dgp[2 * mm][1], dgp[2 * mm + 1][0], dgp[2 * mm + 1][1]};
-          const uint32_t adu[4] = {dup[2 * mm][0], dup[2 * mm][1], dup[2 * mm + 1][0], dup[2 * mm + 1][1]};
-          const uint32_t ah[4] = {hp[2 * mm][0], hp[2 * mm][1], hp[2 * mm + 1][0], hp[2 * mm + 1][1]};
+        for (int jp = 0; jp < R / 16; ++jp) {
           uint32_t BG[4], BU[4], AD[4];
           ldsm4t(BG, tbg + o_bt[mm][jp]);   // B[k = n][col j] = B_gate[n][j]
           ldsm4t(BU, tbu + o_bt[mm][jp]);
           ldsm4(AD, tad + o_at[mm][jp]);    // B[k = n][col j] = A_down[j][n]
 #pragma unroll
           for (int h2 = 0; h2 < 2; ++h2) {
-            mma16816(pg[h2], adg, BG[2 * h2], BG[2 * h2 + 1]);
-            mma16816(pu[h2], adu, BU[2 * h2], BU[2 * h2 + 1]);
-            mma16816(px[h2], ah, AD[2 * h2], AD[2 * h2 + 1]);
+            mma16816(rg[2 * jp + h2], adg, BG[2 * h2], BG[2 * h2 + 1]);
+            mma16816(ru[2 * jp + h2], adu, BU[2 * h2], BU[2 * h2 + 1]);
+            mma16816(rx[2 * jp + h2], ah, AD[2 * h2], AD[2 * h2 + 1]);
           }
-        }
-#pragma unroll
-        for (int h2 = 0; h2 < 2; ++h2) {
-          const uint32_t c = (uint32_t)(16 * jp + 8 * h2) * 4u;
-          sts2(a0 + c, make_float2(pg[h2][0], pg[h2][1]));
-          sts2(a1 + c, make_float2(pg[h2][2], pg[h2][3]));
-          sts2(a0 + R * 4u + c, make_float2(pu[h2][0], pu[h2][1]));
-          sts2(a1 + R * 4u + c, make_float2(pu[h2][2], pu[h2][3]));
-          sts2(a0 + 2u * R * 4u + c, make_float2(px[h2][0], px[h2][1]));
-          sts2(a1 + 2u * R * 4u + c, make_float2(px[h2][2], px[h2][3]));
         }
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[stage]);
-      if (++stage == BWD_ST) {
-        stage = 0;
-        phase ^= 1;
-      }
-      // column products (sums over rows): [j x n] += xa^T (j x rows) . [dg | du | h] (rows x n)
+      // dg | du | h of this warp's rows into the operand tile
 #pragma unroll
-      for (int jm = 0; jm < KS; ++jm) {
-        const uint32_t tg4[4] = {movtrans(axg[jm][0]), movtrans(axg[jm][2]), movtrans(axg[jm][1]), movtrans(axg[jm][3])};
-        const uint32_t tu4[4] = {movtrans(axu[jm][0]), movtrans(axu[jm][2]), movtrans(axu[jm][1]), movtrans(axu[jm][3])};
-        const uint32_t td4[4] = {movtrans(axd[jm][0]), movtrans(axd[jm][2]), movtrans(axd[jm][1]), movtrans(axd[jm][3])};
-#pragma unroll
-        for (int i = 0; i < NT; ++i) {
-          mma16816(aBg[jm][i], tg4, movtrans(dgp[i][0]), movtrans(dgp[i][1]));
-          mma16816(aBu[jm][i], tu4, movtrans(dup[i][0]), movtrans(dup[i][1]));
-          mma16816(aAd[jm][i], td4, movtrans(hp[i][0]), movtrans(hp[i][1]));
-        }
+      for (int p = 0; p < NT / 2; ++p) {
+        stsm4(ob + o_tile[p], dgp[2 * p][0], dgp[2 * p][1], dgp[2 * p + 1][0], dgp[2 * p + 1][1]);
+        stsm4(ob + TILE + o_tile[p], dup[2 * p][0], dup[2 * p][1], dup[2 * p + 1][0], dup[2 * p + 1][1]);
+        stsm4(ob + 2 * TILE + o_tile[p], hp[2 * p][0], hp[2 * p][1], hp[2 * p + 1][0], hp[2 * p + 1][1]);
       }
     }
-    if (!ok) break;
-    // fixed-order sum of the 8 warps' column products, one product at a time through `scratch`
-#pragma unroll
-    for (int which = 0; which < 3; ++which) {
-      float* W = scratch + warp * (R * WS);
-#pragma unroll
-      for (int jm = 0; jm < KS; ++jm)
-#pragma unroll
-        for (int i = 0; i < NT; ++i) {
-          const float* a = which == 0 ? aBg[jm][i] : (which == 1 ? aBu[jm][i] : aAd[jm][i]);
-          const int j0 = 16 * jm + g, nn = 8 * i + 2 * t;
-          *reinterpret_cast<float2*>(W + j0 * WS + nn) = make_float2(a[0], a[1]);
-          *reinterpret_cast<float2*>(W + (j0 + 8) * WS + nn) = make_float2(a[2], a[3]);
-        }
-      consumers_sync(nthr);
-      for (int idx = threadIdx.x; idx < R * BWD_BN; idx += nthr) {
-        const int j = idx / BWD_BN, n = idx % BWD_BN;
-        float v = 0.f;
-#pragma unroll
-        for (int w = 0; w < CONSUMERS; ++w) v += scratch[w * R * WS + j * WS + n];
-        if (which == 0)
-          dbg_part[((int64_t)sbi * N + n0 + n) * R + j] = v;
-        else if (which == 1)
-          dbu_part[((int64_t)sbi * N + n0 + n) * R + j] = v;
-        else
-          dad_part[((int64_t)sbi * R + j) * N + n0 + n] = v;
+    if (++stage == BWD_ST) {
+      stage = 0;
+      phase ^= 1;
+    }
+    // the operand tile of `ct` is complete; the other buffer's readers (tile ct - 1) have all arrived
+    if (consumers_sync_or(nthr, !okw)) break;
+    // column-product blocks: task -> product prod (0: dB_gate^T = xa_gate^T dg, 1: dB_up^T = xa_up^T du,
+    // 2: dA_down = dxd^T h), rows j 16 mt .. +15, tile columns 16 nh .. +15.  A = xa^T through
+    // ldmatrix.trans of the row buffer, B = the operand tile through ldmatrix.trans; both offsets
+    // advance by 16 rows per k-step (the swizzles only use row bits 0-2).
+    for (int task = warp; task < TASKS; task += CONS) {
+      const int prod = task / (2 * KS), mt = (task >> 1) % KS, nh = task & 1;
+      const uint32_t arow = (uint32_t)((mi >> 1) * 8 + lr);
+      uint32_t pa = prod < 2 ? s_xs + swz<4 * R>(arow, (uint32_t)(prod * 2 * KS + 2 * mt + (mi & 1)))
+                             : s_dxd + swz<2 * R>(arow, (uint32_t)(2 * mt + (mi & 1)));
+      const uint32_t a_step = prod < 2 ? 16u * 4u * R : 16u * 2u * R;
+      uint32_t pb = ob + (uint32_t)prod * TILE + swz<64>((uint32_t)((mi & 1) * 8 + lr), (uint32_t)(2 * nh + (mi >> 1)));
+      float acc[2][4] = {};
+#pragma unroll 4
+      for (int kk = 0; kk < CONS; ++kk) {
+        uint32_t A[4], B[4];
+        ldsm4t(A, pa);
+        ldsm4t(B, pb);
+        mma16816(acc[0], A, B[0], B[1]);
+        mma16816(acc[1], A, B[2], B[3]);
+        pa += a_step;
+        pb += 16u * 64u;
       }
-      consumers_sync(nthr);
+      const int j = 16 * mt + g;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int n = n0 + 16 * nh + 8 * h + 2 * t;
+        if (prod < 2) {   // [n_blocks, N, r]: element (n, j)
+          float* P = (prod == 0 ? dbg_part : dbu_part) + ((int64_t)blockIdx.x * N + n) * R + j;
+          P[0] = acc[h][0];
+          P[R] = acc[h][1];
+          P[8] = acc[h][2];
+          P[R + 8] = acc[h][3];
+        } else {          // [n_blocks, r, N]: element (j, n)
+          float* P = dad_part + ((int64_t)blockIdx.x * R + j) * N + n;
+          *reinterpret_cast<float2*>(P) = make_float2(acc[h][0], acc[h][1]);
+          *reinterpret_cast<float2*>(P + 8 * (int64_t)N) = make_float2(acc[h][2], acc[h][3]);
+        }
+      }
     }
   }
   // the group's partial of the per-row products
   float* P = dxa_part + (int64_t)cg * T * R3;
-  for (int i = threadIdx.x; i < (r_end - r_begin) * R3; i += nthr) {
-    const int64_t row = r_begin + i / R3;
-    if (row < T) P[row * R3 + i % R3] = acc_rows[(i / R3) * RS + i % R3];
+#pragma unroll
+  for (int jt = 0; jt < R / 8; ++jt) {
+    const int c = 8 * jt + 2 * t;
+    if (ra < T) {
+      *reinterpret_cast<float2*>(P + ra * R3 + c) = make_float2(rg[jt][0], rg[jt][1]);
+      *reinterpret_cast<float2*>(P + ra * R3 + R + c) = make_float2(ru[jt][0], ru[jt][1]);
+      *reinterpret_cast<float2*>(P + ra * R3 + 2 * R + c) = make_float2(rx[jt][0], rx[jt][1]);
+    }
+    if (ra + 8 < T) {
+      *reinterpret_cast<float2*>(P + (ra + 8) * R3 + c) = make_float2(rg[jt][2], rg[jt][3]);
+      *reinterpret_cast<float2*>(P + (ra + 8) * R3 + R + c) = make_float2(ru[jt][2], ru[jt][3]);
+      *reinterpret_cast<float2*>(P + (ra + 8) * R3 + 2 * R + c) = make_float2(rx[jt][2], rx[jt][3]);
+    }
   }
 }
 
@@ -851,26 +828,31 @@ extern "C" int mxm_mlp_fwd_epilogue(const void* gu, const void* xs, const void* 
   return MXM_OK;
 }
 
-static int bwd_super_block(int r) { return r == 16 ? 256 : 128; }
-
-// Backward partition: super-blocks of SB rows (shared-memory row accumulators bound SB) and the
-// column-group count that minimises partial-sum bytes while giving every SM at least two CTAs
-// (the same trade-off as the reference's _bwd_grid, scripts/fused_mlp.py:218-232).
+// Backward partition: row blocks of SB = 16 x (consumer warps) rows (fixed by the kernel) and the
+// column-group count.  One CTA fits per SM, so the time is about (waves) x (tiles per CTA); each extra
+// group adds a [T, 3r] fp32 partial of the row sums that is written and read once more, charged as
+// the fraction of a tile time those bytes take.  The reference's _bwd_grid
+// (scripts/fused_mlp.py:218-232) makes the same partial-bytes / parallelism trade-off.
 extern "C" int mxm_mlp_bwd_partitions(int64_t T, int64_t N, int r, int* super_block, int* col_groups) {
   MX_CHECK_ARG(T >= 1 && N >= 128 && N % 128 == 0 && (r == 16 || r == 32) && super_block && col_groups,
                "mxm_mlp_bwd_partitions: bad args");
+  const int sb = r == 16 ? bwd_rows(16) : bwd_rows(32);
   const int64_t tpad = (T + 127) / 128 * 128;
-  int sb = bwd_super_block(r);
-  while (sb > 128 && (tpad + sb - 1) / sb < 2) sb -= 128;  // small T: smaller super-blocks, more CTAs
   const int64_t nsb = (tpad + sb - 1) / sb;
   const int nt = (int)(N / BWD_BN);
-  const int64_t want = 2 * (int64_t)mxm_num_sms();
-  int best = nt;
-  for (int ncg = 1; ncg <= nt; ++ncg)
-    if (nt % ncg == 0 && nsb * ncg >= want) {
+  const int64_t nsm = mxm_num_sms();
+  const double group_cost = 1.1e-6 * (double)T * r;
+  int best = 1;
+  double best_cost = 1e300;
+  for (int ncg = 1; ncg <= nt; ++ncg) {
+    if (nt % ncg) continue;
+    const int64_t waves = (nsb * ncg + nsm - 1) / nsm;
+    const double cost = (double)waves * (nt / ncg) + group_cost * ncg;
+    if (cost < best_cost) {
+      best_cost = cost;
       best = ncg;
-      break;
     }
+  }
   *super_block = sb;
   *col_groups = best;
   return MXM_OK;
@@ -886,18 +868,17 @@ extern "C" int mxm_mlp_bwd_epilogue(const void* gu, const void* xs, const void* 
                "mxm_mlp_bwd_epilogue: need T >= 1, N %% 128 == 0, r in {16, 32}");
   MX_CHECK_ARG((q == nullptr) == (s == nullptr), "mxm_mlp_bwd_epilogue: q and s go together");
   const int nt = (int)(N / BWD_BN);
-  MX_CHECK_ARG(col_groups >= 1 && nt % col_groups == 0 && super_block >= 128 && super_block % 128 == 0 &&
-                   super_block <= bwd_super_block(r),
+  MX_CHECK_ARG(col_groups >= 1 && nt % col_groups == 0 && super_block == (r == 16 ? bwd_rows(16) : bwd_rows(32)),
                "mxm_mlp_bwd_epilogue: bad partition (%d, %d)", super_block, col_groups);
   MX_CHECK_ARG(mx_aligned(gu, 16) && mx_aligned(dhm, 16) && mx_aligned(bg, 16) && mx_aligned(bu, 16) &&
                    mx_aligned(ad, 16),
                "mxm_mlp_bwd_epilogue: gu / dhm / bg / bu / ad must be 16-byte aligned");
   CUtensorMap tgu, tdh, tbg, tbu, tad;
   if (int e = mx_make_tmap_2d(&tgu, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, gu, (uint64_t)(2 * N), (uint64_t)T,
-                              (uint64_t)(4 * N), BWD_BN, 128, CU_TENSOR_MAP_SWIZZLE_64B))
+                              (uint64_t)(4 * N), BWD_BN, super_block, CU_TENSOR_MAP_SWIZZLE_64B))
     return e;
   if (int e = mx_make_tmap_2d(&tdh, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, dhm, (uint64_t)N, (uint64_t)T,
-                              (uint64_t)(2 * N), BWD_BN, 128, CU_TENSOR_MAP_SWIZZLE_64B))
+                              (uint64_t)(2 * N), BWD_BN, super_block, CU_TENSOR_MAP_SWIZZLE_64B))
     return e;
   if (int e = mx_make_tmap_2d(&tbg, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, bg, (uint64_t)r, (uint64_t)N,
                               (uint64_t)(2 * r), r, BWD_BN, r == 16 ? CU_TENSOR_MAP_SWIZZLE_32B : CU_TENSOR_MAP_SWIZZLE_64B))
@@ -910,24 +891,24 @@ extern "C" int mxm_mlp_bwd_epilogue(const void* gu, const void* xs, const void* 
     return e;
   CUtensorMap txs, tdxd;
   if (int e = mx_make_tmap_2d(&txs, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, xs, (uint64_t)(2 * r), (uint64_t)T,
-                              (uint64_t)(4 * r), 2 * r, 128, r == 16 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B))
+                              (uint64_t)(4 * r), 2 * r, super_block, r == 16 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B))
     return e;
   if (int e = mx_make_tmap_2d(&tdxd, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, dxd, (uint64_t)r, (uint64_t)T,
-                              (uint64_t)(2 * r), r, 128, r == 16 ? CU_TENSOR_MAP_SWIZZLE_32B : CU_TENSOR_MAP_SWIZZLE_64B))
+                              (uint64_t)(2 * r), r, super_block, r == 16 ? CU_TENSOR_MAP_SWIZZLE_32B : CU_TENSOR_MAP_SWIZZLE_64B))
     return e;
   const int64_t tpad = (T + 127) / 128 * 128;
   const int nsb = (int)((tpad + super_block - 1) / super_block);
   dim3 grid((unsigned)nsb, (unsigned)col_groups);
-  const size_t smem = bwd_smem(r, super_block);
+  const size_t smem = bwd_smem(r);
   cudaStream_t st = (cudaStream_t)stream;
   const int tpg = nt / col_groups;
   auto go = [&](auto kern) -> int {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return mx_cuda_status(e, "mlp bwd epilogue: set smem");
-    kern<<<grid, EPI_THREADS, smem, st>>>(tgu, tdh, tbg, tbu, tad, txs, tdxd, (uint8_t*)q,
-                                          (uint8_t*)s, (float*)dxa_part, (float*)dbg_part, (float*)dbu_part,
-                                          (float*)dad_part, (int)T, (int)tpad, (int)N, s_g, s_u, super_block, tpg,
-                                          q != nullptr, mx_dev_error_ptr());
+    kern<<<grid, 32 * (bwd_cons(r) + 1), smem, st>>>(tgu, tdh, tbg, tbu, tad, txs, tdxd, (uint8_t*)q, (uint8_t*)s,
+                                                     (float*)dxa_part, (float*)dbg_part, (float*)dbu_part,
+                                                     (float*)dad_part, (int)T, (int)tpad, (int)N, s_g, s_u, tpg,
+                                                     q != nullptr, mx_dev_error_ptr());
     mx_note_launch();
     return mx_launch_status("mlp bwd epilogue");
   };
