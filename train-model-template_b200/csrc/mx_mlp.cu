@@ -308,17 +308,19 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
 // ------------------------------------------------------------------------------------------------ backward
 // CTA = one block of SB = 16 x CONS rows x one column group of `tpg` 32-column tiles.  Warp CONS streams,
 // per column tile, the [SB x 32] bf16 tiles of g, u and dh (64-byte swizzle) plus the tile's slices of
-// B_gate, B_up ([32 x r]) and A_down ([r x 32]) into a 2-stage ring with TMA; the block's xs and dxd
+// B_gate, B_up ([32 x r]) and A_down ([r x 32]) into a 3-stage ring with TMA; the block's xs and dxd
 // rows are loaded once.  Consumer warps 0 .. CONS-1 each own 16 rows:
 //   * dg, du, h of the tile are computed in registers, quantized, and multiplied by the B slices into
 //     the per-row sums dxa_gate, dxa_up, xS_down, which stay in registers over all of the group's tiles;
-//   * dg, du, h are also stored (bf16, the same swizzle) into a double-buffered shared tile; after one
-//     named barrier, the 6 (r = 16) or 12 (r = 32) 16 x 16 blocks of dB_gate^T, dB_up^T and dA_down are
-//     dealt out to the warps, each reduced over the block's SB rows with mma (xa^T from the row buffer)
-//     and stored as the block's partial.  Warps without a block go straight on to the next tile.
+//   * dg, du, h are also stored (bf16, the same swizzle) into a shared operand tile.  When every warp has
+//     stored its rows (mbarrier op_full), the 6 (r = 16) or 12 (r = 32) 16 x 16 blocks of dB_gate^T,
+//     dB_up^T and dA_down -- dealt out to the warps in turn, a different set each tile -- are each
+//     reduced over the block's SB rows with mma (xa^T from the row buffer) and stored as the block's
+//     partial; the operand tile is released (op_empty) for the next tile's stores.  Warps without a
+//     block go straight on to the next tile.
 // Four warps per scheduler (r = 16) hide the latency of the per-element chains.  No atomics: the result
 // is deterministic.
-constexpr int BWD_BN = 32, BWD_ST = 2;
+constexpr int BWD_BN = 32, BWD_ST = 3;
 // consumer warps: 16 warps in all (4 per scheduler, 128 registers) for r = 16; 12 (3 per scheduler,
 // 168 registers) for r = 32, whose per-row sums and fragments need more registers
 __host__ __device__ constexpr int bwd_cons(int R) { return R == 16 ? 15 : 11; }
@@ -328,20 +330,8 @@ __host__ __device__ constexpr int bwd_btile(int R) { return BWD_BN * R * 2; }
 __host__ __device__ constexpr int bwd_stage(int R) { return 3 * bwd_tile(R) + 3 * bwd_btile(R); }
 __host__ __device__ constexpr size_t bwd_rowbuf(int R) { return ((size_t)bwd_rows(R) * 3 * R * 2 + 1023) / 1024 * 1024; }
 __host__ __device__ constexpr size_t bwd_smem(int R) {
-  return 1024 + (size_t)BWD_ST * bwd_stage(R) + bwd_rowbuf(R) + 2 * 3 * (size_t)bwd_tile(R) +
-         (2 * BWD_ST + 1) * sizeof(uint64_t);
-}
-
-// bar.sync among the consumer warps that also returns, to every thread, whether any thread passed
-// `v` = true (a uniform decision to leave the loop after a timed-out wait).
-MX_DEV bool consumers_sync_or(int nthreads, bool v) {
-  uint32_t r;
-  asm volatile(
-      "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.or.pred q, 1, %2, p;\n selp.u32 %0, 1, 0, q;\n}"
-      : "=r"(r)
-      : "r"((uint32_t)v), "r"(nthreads)
-      : "memory");
-  return r != 0;
+  return 1024 + (size_t)BWD_ST * bwd_stage(R) + bwd_rowbuf(R) + 3 * (size_t)bwd_tile(R) +
+         (2 * BWD_ST + 3) * sizeof(uint64_t);
 }
 
 template <int R>
@@ -360,10 +350,12 @@ __global__ void __launch_bounds__(32 * (bwd_cons(R) + 1), 1)
   uint8_t* smem = align1024(smem_raw);
   uint8_t* rows_xs = smem + BWD_ST * STG;             // [SB][2r] bf16, TMA-swizzled
   uint8_t* rows_dxd = rows_xs + (size_t)SB * 4 * R;    // [SB][r]
-  uint8_t* opbuf = rows_xs + bwd_rowbuf(R);            // [2][3][SB][32] bf16: dg | du | h, 64-byte swizzle
-  uint64_t* full = reinterpret_cast<uint64_t*>(opbuf + 2 * 3 * TILE);
+  uint8_t* opbuf = rows_xs + bwd_rowbuf(R);            // [3][SB][32] bf16: dg | du | h, 64-byte swizzle
+  uint64_t* full = reinterpret_cast<uint64_t*>(opbuf + 3 * TILE);
   uint64_t* empty = full + BWD_ST;
   uint64_t* rows_full = empty + BWD_ST;
+  uint64_t* op_full = rows_full + 1;   // all consumer warps stored the tile's dg | du | h
+  uint64_t* op_empty = op_full + 1;    // all column-product blocks of the tile were read
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int cg = blockIdx.y, r0 = blockIdx.x * SB;
   const int64_t N2 = 2 * (int64_t)N;
@@ -373,6 +365,8 @@ __global__ void __launch_bounds__(32 * (bwd_cons(R) + 1), 1)
       mbar_init(&empty[i], CONS);
     }
     mbar_init(rows_full, 1);
+    mbar_init(op_full, CONS);
+    mbar_init(op_empty, TASKS);
     fence_barrier_init();
   }
   __syncthreads();
@@ -423,9 +417,7 @@ __global__ void __launch_bounds__(32 * (bwd_cons(R) + 1), 1)
 
   const int g = lane >> 2, t = lane & 3;
   const int mi = lane >> 3, lr = lane & 7;
-  const int nthr = CONS * 32;
-  const bool rows_ok = mbar_wait(rows_full, 0, err, MX_DEV_TIMEOUT_EPILOGUE);
-  if (consumers_sync_or(nthr, !rows_ok)) return;
+  if (!mbar_wait(rows_full, 0, err, MX_DEV_TIMEOUT_EPILOGUE)) return;
 
   // Per-lane shared-memory offsets, fixed for the whole kernel (the swizzles make them non-affine).
   // g / u / dh tiles and the dg / du / h operand tile (64-byte rows, 64-byte swizzle): matrices
@@ -450,7 +442,7 @@ __global__ void __launch_bounds__(32 * (bwd_cons(R) + 1), 1)
     }
   }
   const uint32_t s_xs = smem_u32(rows_xs), s_dxd = smem_u32(rows_dxd), s_ring = smem_u32(smem);
-  const uint32_t s_op = smem_u32(opbuf);
+  const uint32_t ob = smem_u32(opbuf);
   // this warp's rows of xa_gate | xa_up | dxd as MMA A fragments, for the whole kernel
   uint32_t axg[KS][4], axu[KS][4], axd[KS][4];
 #pragma unroll
@@ -471,9 +463,8 @@ __global__ void __launch_bounds__(32 * (bwd_cons(R) + 1), 1)
   uint32_t phase = 0;
   for (int ct = 0; ct < tpg; ++ct) {
     const int n0 = (cg * tpg + ct) * BWD_BN;
-    const bool okw = mbar_wait(&full[stage], phase, err, MX_DEV_TIMEOUT_EPILOGUE);
-    const uint32_t ob = s_op + (uint32_t)(ct & 1) * (3u * TILE);
-    if (okw) {
+    if (!mbar_wait(&full[stage], phase, err, MX_DEV_TIMEOUT_EPILOGUE)) break;
+    {
       const uint32_t sb = s_ring + (uint32_t)stage * STG;
       const uint32_t tg = sb, tu = sb + TILE, th = sb + 2 * TILE;
       const uint32_t tbg = sb + 3 * TILE, tbu = tbg + BT, tad = tbu + BT;
@@ -543,25 +534,31 @@ __global__ void __launch_bounds__(32 * (bwd_cons(R) + 1), 1)
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[stage]);
-      // dg | du | h of this warp's rows into the operand tile
+      // dg | du | h of this warp's rows into the operand tile, once the previous tile's blocks were read
+      if (ct > 0 && !mbar_wait(op_empty, (uint32_t)((ct - 1) & 1), err, MX_DEV_TIMEOUT_EPILOGUE)) break;
 #pragma unroll
       for (int p = 0; p < NT / 2; ++p) {
         stsm4(ob + o_tile[p], dgp[2 * p][0], dgp[2 * p][1], dgp[2 * p + 1][0], dgp[2 * p + 1][1]);
         stsm4(ob + TILE + o_tile[p], dup[2 * p][0], dup[2 * p][1], dup[2 * p + 1][0], dup[2 * p + 1][1]);
         stsm4(ob + 2 * TILE + o_tile[p], hp[2 * p][0], hp[2 * p][1], hp[2 * p + 1][0], hp[2 * p + 1][1]);
       }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(op_full);
     }
     if (++stage == BWD_ST) {
       stage = 0;
       phase ^= 1;
     }
-    // the operand tile of `ct` is complete; the other buffer's readers (tile ct - 1) have all arrived
-    if (consumers_sync_or(nthr, !okw)) break;
     // column-product blocks: task -> product prod (0: dB_gate^T = xa_gate^T dg, 1: dB_up^T = xa_up^T du,
     // 2: dA_down = dxd^T h), rows j 16 mt .. +15, tile columns 16 nh .. +15.  A = xa^T through
     // ldmatrix.trans of the row buffer, B = the operand tile through ldmatrix.trans; both offsets
     // advance by 16 rows per k-step (the swizzles only use row bits 0-2).
-    for (int task = warp; task < TASKS; task += CONS) {
+    bool ok = true;
+    for (int task = (warp + CONS - (ct * TASKS) % CONS) % CONS; task < TASKS; task += CONS) {
+      if (!mbar_wait(op_full, (uint32_t)(ct & 1), err, MX_DEV_TIMEOUT_EPILOGUE)) {
+        ok = false;
+        break;
+      }
       const int prod = task / (2 * KS), mt = (task >> 1) % KS, nh = task & 1;
       const uint32_t arow = (uint32_t)((mi >> 1) * 8 + lr);
       uint32_t pa = prod < 2 ? s_xs + swz<4 * R>(arow, (uint32_t)(prod * 2 * KS + 2 * mt + (mi & 1)))
@@ -595,7 +592,10 @@ __global__ void __launch_bounds__(32 * (bwd_cons(R) + 1), 1)
           *reinterpret_cast<float2*>(P + 8 * (int64_t)N) = make_float2(acc[h][2], acc[h][3]);
         }
       }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(op_empty);
     }
+    if (!ok) break;
   }
   // the group's partial of the per-row products
   float* P = dxa_part + (int64_t)cg * T * R3;
