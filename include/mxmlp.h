@@ -128,6 +128,12 @@ int mxm_mlp_bwd_reduce(const void* dxa_part, const void* dbg_part, const void* d
 int mxm_rowdot(const void* A, int64_t lda, const void* B, int64_t T, int64_t K, int n, float post, void* out,
                int64_t ldo, void* stream);
 
+/* mxm_rowdot plus the row-wise MXFP8 quantization of A from the same read of A: q [T, K] (row stride ldq)
+ * and s (blocked layout of a [ceil128(T), K] operand) are exactly mxm_quant_rows(A).  The reference
+ * quantizes and multiplies in two passes (scripts/fused_mlp.py:277-278 for x, :307,311 for dy). */
+int mxm_rowdot_quant(const void* A, int64_t lda, const void* B, int64_t T, int64_t K, int n, float post, void* out,
+                     int64_t ldo, void* q, int64_t ldq, void* s, void* stream);
+
 /* Row chunking (rows per chunk, number of chunks) of mxm_coldot's partial buffer for a [T, K] operand. */
 int mxm_coldot_chunks(int64_t T, int64_t K, int* rows_per_chunk, int* chunks);
 

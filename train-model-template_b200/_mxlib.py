@@ -42,6 +42,7 @@ _SIGS = {
     "mxm_mlp_bwd_reduce": [_vp, _vp, _vp, _vp, _i64, _i64, _int, ctypes.c_float, ctypes.c_float, _int, _int, _vp,
                            _vp, _vp, _vp, _vp, _vp],
     "mxm_rowdot": [_vp, _i64, _vp, _i64, _i64, _int, ctypes.c_float, _vp, _i64, _vp],
+    "mxm_rowdot_quant": [_vp, _i64, _vp, _i64, _i64, _int, ctypes.c_float, _vp, _i64, _vp, _i64, _vp, _vp],
     "mxm_coldot_chunks": [_i64, _i64, ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_int)],
     "mxm_coldot": [_vp, _i64, _vp, _i64, _i64, _i64, _int, ctypes.c_float, _int, _vp, _int, _int, _vp, _vp],
     "mxm_coldot_noalloc": [_vp, _i64, _vp, _i64, _i64, _i64, _int, ctypes.c_float, _int, _vp, _vp],

@@ -13,6 +13,7 @@
 //
 // All rank-r products run on the tensor cores with warp-level m16n8k16 bf16 MMAs; the element-wise
 // math keeps the reference's rounding points (bf16 after each fp32 expression it rounds).
+#include <algorithm>
 #include <mutex>
 
 #include "mx_mma.cuh"
@@ -616,13 +617,40 @@ __global__ void __launch_bounds__(32 * (bwd_cons(R) + 1), 1)
 }
 
 // ------------------------------------------------------------------------------------------------ skinny
+// E4M3 bytes that are NaN (S.1111.111) -> the canonical 0x7F, four codes per word.
+MX_DEV uint32_t nan_canon4(uint32_t w) {
+  const uint32_t m = ((w & 0x7F7F7F7Fu) + 0x01010101u) & 0x80808080u;
+  return w & ~m;
+}
+
+// Row-wise MXFP8 of the 8 bf16 of a 16-byte vector held by this lane, where lanes 4g .. 4g+3 hold
+// one 32-element block of a row (the quantizer's algorithm, scripts/mxfp8.py:46-75): the block's
+// E8M0 scale goes to `e`, the 8 E4M3 codes are returned.
+MX_DEV uint2 quant8_lane(const uint4& v, uint32_t& e) {
+  const uint32_t m2 = max_bf16x2(absmax_bf16x2(v.x, v.y), absmax_bf16x2(v.z, v.w));
+  float m = nanmax(bf16_lo(m2), bf16_hi(m2));
+  m = nanmax(m, __shfl_xor_sync(0xffffffffu, m, 1));
+  m = nanmax(m, __shfl_xor_sync(0xffffffffu, m, 2));
+  e = mx_e8m0_rceil(__fdiv_rn(m, 448.0f));
+  const float rcp = mx_e8m0_rcp(e);
+  const float2 r2 = make_float2(rcp, rcp);
+  const float2 f0 = __fmul2_rn(up2(v.x), r2), f1 = __fmul2_rn(up2(v.y), r2);
+  const float2 f2 = __fmul2_rn(up2(v.z), r2), f3 = __fmul2_rn(up2(v.w), r2);
+  return make_uint2(nan_canon4(e4m3x2_sat(f0.x, f0.y) | (e4m3x2_sat(f1.x, f1.y) << 16)),
+                    nan_canon4(e4m3x2_sat(f2.x, f2.y) | (e4m3x2_sat(f3.x, f3.y) << 16)));
+}
+
 // out[t, j] = bf16( bf16(sum_k A[t, k] B[j, k]) * post ) for j < NJ (16, 32 or 64); post == 1 skips
 // the second rounding.  CTA = 16 rows; its 4 warps split K in four and their fp32 partials are summed
 // through shared memory in a fixed order.  The reduction index k is permuted consistently in A and B so
-// each lane loads 16 contiguous bytes per row per 32 k; two k-steps are in flight per warp.
-template <int NJ>
+// each lane loads 16 contiguous bytes per row per 32 k; four 32-k steps (8 x 16 bytes per lane) are
+// loaded before they are used.  With QUANT the same registers are also quantized row-wise to MXFP8
+// (codes q [T, K], scales s in the blocked layout of a [Tpad, K] operand), since the 4 lanes holding a
+// row's 32 k are exactly one MX block: one read of A serves both.  The QUANT grid covers Tpad rows.
+template <int NJ, bool QUANT>
 __global__ void __launch_bounds__(128) k_rowdot(const bf16* __restrict__ A, int64_t lda, const bf16* __restrict__ B,
-                                                int T, int K, float post, bf16* __restrict__ out, int64_t ldo) {
+                                                int T, int K, float post, bf16* __restrict__ out, int64_t ldo,
+                                                uint8_t* __restrict__ q, int64_t ldq, uint8_t* __restrict__ s) {
   __shared__ float red[4][16][NJ + 1];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
   const int64_t r0 = (int64_t)blockIdx.x * 16;
@@ -633,11 +661,20 @@ __global__ void __launch_bounds__(128) k_rowdot(const bf16* __restrict__ A, int6
   for (int j = 0; j < NJ / 8; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
   const uint4 z = make_uint4(0u, 0u, 0u, 0u);
   const int kq = K / 4;  // this warp's quarter of K (K % 128 == 0)
-  const int kb = warp * kq;
-#pragma unroll 2
-  for (int k0 = kb; k0 < kb + kq; k0 += 32) {
-    const uint4 xa = va ? __ldg(reinterpret_cast<const uint4*>(A + ra * lda + k0 + 8 * t)) : z;
-    const uint4 xb = vb ? __ldg(reinterpret_cast<const uint4*>(A + rb * lda + k0 + 8 * t)) : z;
+  const int kb = warp * kq, ke = kb + kq;
+  const bf16* pa = A + ra * lda + 8 * t;
+  const bf16* pb = A + rb * lda + 8 * t;
+  auto step = [&](const uint4& xa, const uint4& xb, int k0) {
+    if (QUANT) {
+      uint32_t ea, eb;
+      const uint2 ca = quant8_lane(xa, ea), cb = quant8_lane(xb, eb);
+      if (va) *reinterpret_cast<uint2*>(q + ra * ldq + k0 + 8 * t) = ca;
+      if (vb) *reinterpret_cast<uint2*>(q + rb * ldq + k0 + 8 * t) = cb;
+      if (t == 0) {
+        s[mx_scale_offset(ra, k0 >> 5, K)] = (uint8_t)ea;
+        s[mx_scale_offset(rb, k0 >> 5, K)] = (uint8_t)eb;
+      }
+    }
     // fragment k slots (2t, 2t+1 | 2t+8, 2t+9) <- actual k (8t, 8t+1 | 8t+2, 8t+3), then (8t+4.. | 8t+6..)
     const uint32_t a0[4] = {xa.x, xb.x, xa.y, xb.y};
     const uint32_t a1[4] = {xa.z, xb.z, xa.w, xb.w};
@@ -647,6 +684,22 @@ __global__ void __launch_bounds__(128) k_rowdot(const bf16* __restrict__ A, int6
       mma16816(acc[jt], a0, bb.x, bb.y);
       mma16816(acc[jt], a1, bb.z, bb.w);
     }
+  };
+  int k0 = kb;
+  for (; k0 + 128 <= ke; k0 += 128) {
+    uint4 xa[4], xb[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      xa[u] = va ? __ldg(reinterpret_cast<const uint4*>(pa + k0 + 32 * u)) : z;
+      xb[u] = vb ? __ldg(reinterpret_cast<const uint4*>(pb + k0 + 32 * u)) : z;
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) step(xa[u], xb[u], k0 + 32 * u);
+  }
+  for (; k0 < ke; k0 += 32) {
+    const uint4 xa = va ? __ldg(reinterpret_cast<const uint4*>(pa + k0)) : z;
+    const uint4 xb = vb ? __ldg(reinterpret_cast<const uint4*>(pb + k0)) : z;
+    step(xa, xb, k0);
   }
 #pragma unroll
   for (int jt = 0; jt < NJ / 8; ++jt) {
@@ -731,6 +784,33 @@ __global__ void k_sum_parts(const float* __restrict__ src, int nparts, int64_t n
     } else {
       out_f[o] = v;
     }
+  }
+}
+
+// Up to three independent fp32 partial sums in one launch (blockIdx.y = job), 4 floats per thread:
+// out[i] = scale * sum_{p < nparts} src[p * stride + i], the same fixed order as k_sum_parts.
+struct SumJob {
+  const float4* src;
+  float4* out;
+  float scale;
+};
+struct SumJobs {
+  SumJob j[3];
+};
+__global__ void __launch_bounds__(256) k_sum_parts4(SumJobs jobs, int nparts, int64_t n4, int64_t stride4) {
+  const SumJob jb = blockIdx.y == 0 ? jobs.j[0] : (blockIdx.y == 1 ? jobs.j[1] : jobs.j[2]);
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (int64_t)gridDim.x * blockDim.x) {
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    const float4* p = jb.src + i;
+#pragma unroll 8
+    for (int k = 0; k < nparts; ++k) {
+      const float4 x = __ldg(p + k * stride4);
+      v.x += x.x;
+      v.y += x.y;
+      v.z += x.z;
+      v.w += x.w;
+    }
+    jb.out[i] = make_float4(v.x * jb.scale, v.y * jb.scale, v.z * jb.scale, v.w * jb.scale);
   }
 }
 
@@ -928,15 +1008,13 @@ extern "C" int mxm_mlp_bwd_reduce(const void* dxa_part, const void* dbg_part, co
   k_reduce_dxa<<<grid_for(nd, 256), 256, 0, st>>>((const float*)dxa_part, col_groups, (int)T, r, s_g, s_u, (bf16*)dxa,
                                                   (bf16*)xsd);
   mx_note_launch();
-  const int64_t nb = N * r;
-  k_sum_parts<<<grid_for(nb, 256), 256, 0, st>>>((const float*)dbg_part, nsb, nb, nb, s_g, 1.f, (float*)dBg, nullptr,
-                                                 0, 0);
-  mx_note_launch();
-  k_sum_parts<<<grid_for(nb, 256), 256, 0, st>>>((const float*)dbu_part, nsb, nb, nb, s_u, 1.f, (float*)dBu, nullptr,
-                                                 0, 0);
-  mx_note_launch();
-  k_sum_parts<<<grid_for(nb, 256), 256, 0, st>>>((const float*)dad_part, nsb, nb, nb, 1.f, 1.f, (float*)dAd, nullptr,
-                                                 0, 0);
+  const int64_t nb4 = N * r / 4;  // N % 128 == 0
+  SumJobs jobs;
+  jobs.j[0] = {(const float4*)dbg_part, (float4*)dBg, s_g};
+  jobs.j[1] = {(const float4*)dbu_part, (float4*)dBu, s_u};
+  jobs.j[2] = {(const float4*)dad_part, (float4*)dAd, 1.f};
+  const int gx = (int)std::min<int64_t>((nb4 + 255) / 256, (int64_t)mxm_num_sms() * 8);
+  k_sum_parts4<<<dim3((unsigned)gx, 3u), 256, 0, st>>>(jobs, nsb, nb4, nb4);
   mx_note_launch();
   return mx_launch_status("mlp bwd reduce");
 }
@@ -949,14 +1027,42 @@ extern "C" int mxm_rowdot(const void* A, int64_t lda, const void* B, int64_t T, 
   MX_CHECK_ARG(mx_aligned(A, 16) && mx_aligned(B, 16) && mx_aligned(out, 4), "mxm_rowdot: alignment");
   const unsigned grid = (unsigned)((T + 15) / 16);
   cudaStream_t st = (cudaStream_t)stream;
+  auto go = [&](auto kern) {
+    kern<<<grid, 128, 0, st>>>((const bf16*)A, lda, (const bf16*)B, (int)T, (int)K, post, (bf16*)out, ldo, nullptr, 0,
+                               nullptr);
+  };
   if (n == 16)
-    k_rowdot<16><<<grid, 128, 0, st>>>((const bf16*)A, lda, (const bf16*)B, (int)T, (int)K, post, (bf16*)out, ldo);
+    go(k_rowdot<16, false>);
   else if (n == 32)
-    k_rowdot<32><<<grid, 128, 0, st>>>((const bf16*)A, lda, (const bf16*)B, (int)T, (int)K, post, (bf16*)out, ldo);
+    go(k_rowdot<32, false>);
   else
-    k_rowdot<64><<<grid, 128, 0, st>>>((const bf16*)A, lda, (const bf16*)B, (int)T, (int)K, post, (bf16*)out, ldo);
+    go(k_rowdot<64, false>);
   mx_note_launch();
   return mx_launch_status("rowdot");
+}
+
+extern "C" int mxm_rowdot_quant(const void* A, int64_t lda, const void* B, int64_t T, int64_t K, int n, float post,
+                                void* out, int64_t ldo, void* q, int64_t ldq, void* s, void* stream) {
+  MX_CHECK_ARG(A && B && out && q && s, "mxm_rowdot_quant: null pointer");
+  MX_CHECK_ARG(T >= 1 && T < (1ll << 31) && K >= 128 && K % 128 == 0 && (n == 16 || n == 32 || n == 64) &&
+                   lda % 8 == 0 && ldo % 2 == 0 && ldq >= K && ldq % 8 == 0,
+               "mxm_rowdot_quant: need K %% 128 == 0, n in {16, 32, 64}, lda %% 8 == 0, ldq >= K, ldq %% 8 == 0");
+  MX_CHECK_ARG(mx_aligned(A, 16) && mx_aligned(B, 16) && mx_aligned(out, 4) && mx_aligned(q, 8),
+               "mxm_rowdot_quant: alignment");
+  const unsigned grid = (unsigned)((T + 127) / 128 * 8);  // 16-row CTAs over the padded rows
+  cudaStream_t st = (cudaStream_t)stream;
+  auto go = [&](auto kern) {
+    kern<<<grid, 128, 0, st>>>((const bf16*)A, lda, (const bf16*)B, (int)T, (int)K, post, (bf16*)out, ldo,
+                               (uint8_t*)q, ldq, (uint8_t*)s);
+  };
+  if (n == 16)
+    go(k_rowdot<16, true>);
+  else if (n == 32)
+    go(k_rowdot<32, true>);
+  else
+    go(k_rowdot<64, true>);
+  mx_note_launch();
+  return mx_launch_status("rowdot quant");
 }
 
 extern "C" int mxm_coldot_chunks(int64_t T, int64_t K, int* rows_per_chunk, int* chunks) {

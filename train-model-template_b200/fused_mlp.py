@@ -5,12 +5,12 @@ need_out)``, ``_MLP`` autograd contract (9 inputs, 9 gradients, the same saved t
 ``need_out`` modes) and ``mlp_fwd`` / ``mlp_bwd`` helpers.
 
 Per layer call (T tokens, H hidden, N intermediate, r LoRA rank):
-  forward : xs = x S^T (rank-2r, tensor-core rowdot)  |  q, s = MXFP8(x)
+  forward : xs = x S^T (rank-2r, tensor-core rowdot) and q, s = MXFP8(x) from one read of x
             gu = [x W_gate^T | x W_up^T]          -- tcgen05 block-scaled GEMM, K = H
             q_h, s_h, xS_down = epilogue(gu)       -- LoRA-B add, SwiGLU, MX quantize h
             y = h W_down^T + xS_down (s_d B_down)^T -- tcgen05 GEMM; the LoRA term is a bf16 tcgen05 MMA
                                                        into the same TMEM accumulator
-  backward: q, s = MXFP8(dy); dh_mx = dy W_down (tcgen05); dxd = s_d dy B_down
+  backward: q, s = MXFP8(dy) and dxd = s_d dy B_down from one read of dy; dh_mx = dy W_down (tcgen05)
             [dg | du] MXFP8 + dB_g, dB_u, dA_d, dxa, xS_down = epilogue(gu, dh_mx)
             dx = [dg | du] W_gu + dxa S (tcgen05 GEMM, K = 2N, LoRA term as a bf16 MMA)
             dB_d = s_d dy^T xS_down;  dA = dxa^T x (tensor-core coldot)
@@ -52,6 +52,19 @@ def rowdot(A, B, post=1.0, out=None):
     _nx.call("mxm_rowdot", _nx.ptr(A), A.stride(0), _nx.ptr(B), T, K, n, float(post), _nx.ptr(out), out.stride(0),
              _nx.stream_of(A))
     return out
+
+
+def rowdot_quant(A, B, post=1.0):
+    """(rowdot(A, B, post), *mxfp8.mx_quant(A)) from one read of A: A [T, K] bf16 contiguous, K % 128 == 0."""
+    T, K = A.shape
+    n = B.shape[0]
+    assert A.is_contiguous() and B.is_contiguous() and B.shape[1] == K
+    out = torch.empty((T, n), dtype=torch.bfloat16, device=A.device)
+    q = torch.empty((T, K), dtype=_F8, device=A.device)
+    s = torch.empty(mxfp8.scale_numel(T, K), dtype=torch.uint8, device=A.device)
+    _nx.call("mxm_rowdot_quant", _nx.ptr(A), K, _nx.ptr(B), T, K, n, float(post), _nx.ptr(out), out.stride(0),
+             _nx.ptr(q), K, _nx.ptr(s), _nx.stream_of(A))
+    return out, q, s.view(_E8)
 
 
 def coldot(A, E, post=1.0, transpose_out=False):
@@ -147,8 +160,7 @@ class _MLP(torch.autograd.Function):
         bu = _cast((id(Bu), dt), lambda: Bu.detach().to(dt).contiguous())
         ad = _cast(((id(Ad),), dt), lambda: torch.cat([Ad.detach().to(dt)]))
         bd = _cast((id(Bd), dt), lambda: Bd.detach().to(dt).contiguous())
-        xs = rowdot(x2, S)                                               # [T, 2R] = xa_gate | xa_up
-        q, sc = mxfp8.mx_quant(x2)
+        xs, q, sc = rowdot_quant(x2, S)                                  # [T, 2R] = xa_gate | xa_up; MXFP8(x)
         gu = mxfp8.mx_mm(q, hold.w.t(), sc, hold.ws)                     # [T, 2N] gate | up
         del q, sc
         if need_out:
@@ -175,12 +187,11 @@ class _MLP(torch.autograd.Function):
         if not dy2.is_contiguous():
             dy2 = dy2.contiguous()
         T, N = gu.shape[0], gu.shape[1] // 2
-        qd, sd = mxfp8.mx_quant(dy2)
+        bdT = _cast(("T", id(bd)), lambda: bd.t().contiguous())
+        dxd, qd, sd = rowdot_quant(dy2, bdT, post=s_d)                    # bf16(bf16(dy @ Bd) * s_d); MXFP8(dy)
         wt, wts = mxfp8.mx_wt(down)
         dhm = mxfp8.mx_mm(qd, wt.t(), sd, wts)                           # [T, N]
         del qd, sd
-        bdT = _cast(("T", id(bd)), lambda: bd.t().contiguous())
-        dxd = rowdot(dy2, bdT, post=s_d)                                  # bf16(bf16(dy @ Bd) * s_d)
         qg, sg, (dxa_p, dbg_p, dbu_p, dad_p, sb, ncg) = _bwd_launch(gu, xs, dhm, dxd, bg, bu, ad, s_g, s_u, need_x)
         del dhm
         dev = gu.device
