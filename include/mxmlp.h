@@ -134,11 +134,13 @@ int mxm_rowdot(const void* A, int64_t lda, const void* B, int64_t T, int64_t K, 
 int mxm_rowdot_quant(const void* A, int64_t lda, const void* B, int64_t T, int64_t K, int n, float post, void* out,
                      int64_t ldo, void* q, int64_t ldq, void* s, void* stream);
 
-/* Row chunking (rows per chunk, number of chunks) of mxm_coldot's partial buffer for a [T, K] operand. */
+/* Row chunking (rows per chunk: a multiple of 64, number of chunks) of mxm_coldot's partial buffer for a
+ * [T, K] operand. */
 int mxm_coldot_chunks(int64_t T, int64_t K, int* rows_per_chunk, int* chunks);
 
 /* out = bf16( bf16(A[T, K]^T E[T, n]) * post ), written [K, n] (or [n, K] when transpose_out).
- * part: fp32 [chunks, K, n] scratch.  K % 64 == 0, n in {16, 32, 64}.
+ * part: fp32 [chunks, K, n] scratch; rows_per_chunk a multiple of 64.  K % 64 == 0, n in {16, 32, 64},
+ * lda and lde multiples of 8 (16-byte rows), A and E 16-byte aligned.
  * The LoRA weight gradients dA = dxa^T x and dB_down = s_d (dy^T xS_down) (scripts/fused_mlp.py:316-318,333). */
 int mxm_coldot(const void* A, int64_t lda, const void* E, int64_t lde, int64_t T, int64_t K, int n, float post,
                int transpose_out, void* part, int rows_per_chunk, int chunks, void* out, void* stream);

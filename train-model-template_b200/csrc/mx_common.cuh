@@ -49,10 +49,11 @@ MX_DEV uint32_t mx_e8m0_rceil(float descale) {
 // Multiplier applied to the block before the E4M3 cast: 255 -> NaN, 254 -> 2^-127,
 // 0 -> 1.0, else 2^(127 - e).  2^(127-e) is built from its exponent bits (exact).
 MX_DEV float mx_e8m0_rcp(uint32_t e) {
-  if (e == 255u) return __int_as_float(0x7fffffff);
-  if (e == 254u) return __int_as_float(0x00400000);  // 2^-127 (subnormal)
-  if (e == 0u) return 1.0f;
-  return __int_as_float((int)((254u - e) << 23));
+  uint32_t r = (254u - e) << 23;        // 2^(127 - e) for e in 1 .. 253
+  r = e == 0u ? 0x3f800000u : r;        // 1.0
+  r = e == 254u ? 0x00400000u : r;      // 2^-127 (subnormal)
+  r = e == 255u ? 0x7fffffffu : r;      // NaN
+  return __uint_as_float(r);
 }
 
 // Two floats (already clamped to [-448, 448], or NaN) -> two E4M3 codes, RNE.

@@ -643,8 +643,9 @@ MX_DEV uint2 quant8_lane(const uint4& v, uint32_t& e) {
 // out[t, j] = bf16( bf16(sum_k A[t, k] B[j, k]) * post ) for j < NJ (16, 32 or 64); post == 1 skips
 // the second rounding.  CTA = 16 rows; its 4 warps split K in four and their fp32 partials are summed
 // through shared memory in a fixed order.  The reduction index k is permuted consistently in A and B so
-// each lane loads 16 contiguous bytes per row per 32 k; four 32-k steps (8 x 16 bytes per lane) are
-// loaded before they are used.  With QUANT the same registers are also quantized row-wise to MXFP8
+// each lane loads 16 contiguous bytes per row per 32 k; a group of 32-k steps (four for n <= 32, two
+// for n = 64) has all its A vectors and B fragments requested before any is used, so a group costs
+// one memory latency.  With QUANT the same registers are also quantized row-wise to MXFP8
 // (codes q [T, K], scales s in the blocked layout of a [Tpad, K] operand), since the 4 lanes holding a
 // row's 32 k are exactly one MX block: one read of A serves both.  The QUANT grid covers Tpad rows.
 template <int NJ, bool QUANT>
@@ -664,7 +665,8 @@ __global__ void __launch_bounds__(128) k_rowdot(const bf16* __restrict__ A, int6
   const int kb = warp * kq, ke = kb + kq;
   const bf16* pa = A + ra * lda + 8 * t;
   const bf16* pb = A + rb * lda + 8 * t;
-  auto step = [&](const uint4& xa, const uint4& xb, int k0) {
+  const bf16* pB = B + (int64_t)g * K + 8 * t;   // row 8 jt + g of B at + 8 jt K
+  auto step = [&](const uint4& xa, const uint4& xb, const uint4 (&bb)[NJ / 8], int k0) {
     if (QUANT) {
       uint32_t ea, eb;
       const uint2 ca = quant8_lane(xa, ea), cb = quant8_lane(xb, eb);
@@ -680,26 +682,33 @@ __global__ void __launch_bounds__(128) k_rowdot(const bf16* __restrict__ A, int6
     const uint32_t a1[4] = {xa.z, xb.z, xa.w, xb.w};
 #pragma unroll
     for (int jt = 0; jt < NJ / 8; ++jt) {
-      const uint4 bb = __ldg(reinterpret_cast<const uint4*>(B + (int64_t)(8 * jt + g) * K + k0 + 8 * t));
-      mma16816(acc[jt], a0, bb.x, bb.y);
-      mma16816(acc[jt], a1, bb.z, bb.w);
+      mma16816(acc[jt], a0, bb[jt].x, bb[jt].y);
+      mma16816(acc[jt], a1, bb[jt].z, bb[jt].w);
     }
   };
+  // GS 32-k steps per group: all of a group's A vectors and B fragments are requested before any is used
+  constexpr int GS = NJ <= 32 ? 4 : 2;
   int k0 = kb;
-  for (; k0 + 128 <= ke; k0 += 128) {
-    uint4 xa[4], xb[4];
+  for (; k0 + 32 * GS <= ke; k0 += 32 * GS) {
+    uint4 xa[GS], xb[GS], bb[GS][NJ / 8];
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
+    for (int u = 0; u < GS; ++u) {
       xa[u] = va ? __ldg(reinterpret_cast<const uint4*>(pa + k0 + 32 * u)) : z;
       xb[u] = vb ? __ldg(reinterpret_cast<const uint4*>(pb + k0 + 32 * u)) : z;
+#pragma unroll
+      for (int jt = 0; jt < NJ / 8; ++jt)
+        bb[u][jt] = __ldg(reinterpret_cast<const uint4*>(pB + (int64_t)8 * jt * K + k0 + 32 * u));
     }
 #pragma unroll
-    for (int u = 0; u < 4; ++u) step(xa[u], xb[u], k0 + 32 * u);
+    for (int u = 0; u < GS; ++u) step(xa[u], xb[u], bb[u], k0 + 32 * u);
   }
   for (; k0 < ke; k0 += 32) {
     const uint4 xa = va ? __ldg(reinterpret_cast<const uint4*>(pa + k0)) : z;
     const uint4 xb = vb ? __ldg(reinterpret_cast<const uint4*>(pb + k0)) : z;
-    step(xa, xb, k0);
+    uint4 bb[NJ / 8];
+#pragma unroll
+    for (int jt = 0; jt < NJ / 8; ++jt) bb[jt] = __ldg(reinterpret_cast<const uint4*>(pB + (int64_t)8 * jt * K + k0));
+    step(xa, xb, bb, k0);
   }
 #pragma unroll
   for (int jt = 0; jt < NJ / 8; ++jt) {
@@ -724,45 +733,112 @@ __global__ void __launch_bounds__(128) k_rowdot(const bf16* __restrict__ A, int6
 }
 
 // part[chunk, k, j] = sum over the chunk's rows t of A[t, k] E[t, j]   (k < K, j < NJ)
-// Warp = 16 consecutive k columns x all NJ; CTA = 4 warps = 64 columns; blockIdx.y = row chunk.
-// A^T fragments come from A row-fragments through movmatrix; E is read as the B operand.
+// CTA = 64 columns k of one row chunk: warp 4 streams [64 rows x 64 k] tiles of A (128-byte swizzle)
+// and the matching [64 rows x NJ] rows of E into a 5-stage ring with TMA; warps 0-3 each own 16
+// columns and accumulate D[k x j] = A^T E with m16n8k16 MMAs whose operands come from ldmatrix.trans
+// (A^T and E^T are the transposes of the stored tiles).  Rows past T read as zero.
+constexpr int CD_ST = 5, CD_ROWS = 64, CD_COLS = 64;
+__host__ __device__ constexpr int cd_stage(int NJ) { return CD_ROWS * CD_COLS * 2 + CD_ROWS * NJ * 2; }
+__host__ __device__ constexpr size_t cd_smem(int NJ) { return 1024 + (size_t)CD_ST * cd_stage(NJ) + 2 * CD_ST * 8; }
+
 template <int NJ>
-__global__ void __launch_bounds__(128) k_coldot(const bf16* __restrict__ A, int64_t lda, const bf16* __restrict__ E,
-                                                int64_t lde, int T, int K, int rows_per_chunk,
-                                                float* __restrict__ part) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-  const int k0 = (blockIdx.x * 4 + warp) * 16;
-  if (k0 >= K) return;
+__global__ void __launch_bounds__(160) k_coldot(const __grid_constant__ CUtensorMap tm_a,
+                                                const __grid_constant__ CUtensorMap tm_e, int K, int rows_per_chunk,
+                                                int T, float* __restrict__ part, int* err) {
+  constexpr int STG = cd_stage(NJ), AT = CD_ROWS * CD_COLS * 2;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align1024(smem_raw);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + CD_ST * STG);
+  uint64_t* empty = full + CD_ST;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int kc = blockIdx.x * CD_COLS;
   const int r0 = blockIdx.y * rows_per_chunk, r1 = min(r0 + rows_per_chunk, T);
+  const int nsteps = r1 > r0 ? (r1 - r0 + CD_ROWS - 1) / CD_ROWS : 0;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < CD_ST; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 4);
+    }
+    fence_barrier_init();
+  }
+  __syncthreads();
+
+  if (warp == 4) {  // TMA producer
+    if (lane == 0) {
+      prefetch_tmap(&tm_a);
+      prefetch_tmap(&tm_e);
+    }
+    int stage = 0;
+    uint32_t phase = 0;
+    int issued = 0;
+    for (int i = 0; i < nsteps; ++i) {
+      if (!mbar_wait(&empty[stage], phase ^ 1, err, MX_DEV_TIMEOUT_PRODUCER)) break;
+      if (lane == 0) {
+        uint8_t* dst = smem + stage * STG;
+        mbar_arrive_expect_tx(&full[stage], STG);
+        tma_load_2d(dst, &tm_a, &full[stage], kc, r0 + i * CD_ROWS);
+        tma_load_2d(dst + AT, &tm_e, &full[stage], 0, r0 + i * CD_ROWS);
+      }
+      __syncwarp();
+      ++issued;
+      if (++stage == CD_ST) {
+        stage = 0;
+        phase ^= 1;
+      }
+    }
+    for (int k = 0; k < CD_ST && k < issued; ++k) {  // leave no copy in flight
+      const int i = issued - 1 - k;
+      mbar_wait(&full[i % CD_ST], (uint32_t)((i / CD_ST) & 1), err, MX_DEV_TIMEOUT_PRODUCER);
+    }
+    return;
+  }
+
+  const int g = lane >> 2, t = lane & 3, mi = lane >> 3, lr = lane & 7;
   float acc[NJ / 8][4];
 #pragma unroll
   for (int j = 0; j < NJ / 8; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
-#pragma unroll 4
-  for (int r = r0; r < r1; r += 16) {
-    const int64_t ra = r + g, rb = ra + 8;
-    const bool va = ra < r1, vb = rb < r1;
-    // A tile [16 rows x 16 k] in row-fragment form, then transposed into the A operand [k x rows]
-    const bf16* pa = A + ra * lda + k0 + 2 * t;
-    const bf16* pb = A + rb * lda + k0 + 2 * t;
-    const uint32_t f0 = va ? ld32g(pa) : 0u, f1 = vb ? ld32g(pb) : 0u;
-    const uint32_t f2 = va ? ld32g(pa + 8) : 0u, f3 = vb ? ld32g(pb + 8) : 0u;
-    const uint32_t at[4] = {movtrans(f0), movtrans(f2), movtrans(f1), movtrans(f3)};
+  // A^T fragment (m = k: 16 warp columns, kdim = 16 rows): matrix mi = (k half mi & 1, row half mi >> 1)
+  // E^T as the B operand (kdim = rows, n = j): matrix mi = (row half mi & 1, j half mi >> 1)
+  uint32_t o_a[4], o_e[4][NJ / 16];
 #pragma unroll
-    for (int jt = 0; jt < NJ / 8; ++jt) {
-      // B[k = rows][col j]: (rows 2t..2t+1, col g)
-      const int64_t r2 = r + 2 * t;
-      const bf16* pe = E + r2 * lde + 8 * jt + g;
-      const uint32_t b0 = ld16z(pe, r2 < r1) | (ld16z(pe + lde, r2 + 1 < r1) << 16);
-      const uint32_t b1 = ld16z(pe + 8 * lde, r2 + 8 < r1) | (ld16z(pe + 9 * lde, r2 + 9 < r1) << 16);
-      mma16816(acc[jt], at, b0, b1);
+  for (int s4 = 0; s4 < 4; ++s4) {
+    o_a[s4] = swz<128>((uint32_t)(16 * s4 + (mi >> 1) * 8 + lr), (uint32_t)(2 * warp + (mi & 1)));
+#pragma unroll
+    for (int jp = 0; jp < NJ / 16; ++jp)
+      o_e[s4][jp] = AT + swz<2 * NJ>((uint32_t)(16 * s4 + (mi & 1) * 8 + lr), (uint32_t)(2 * jp + (mi >> 1)));
+  }
+  const uint32_t s_ring = smem_u32(smem);
+  int stage = 0;
+  uint32_t phase = 0;
+  for (int i = 0; i < nsteps; ++i) {
+    if (!mbar_wait(&full[stage], phase, err, MX_DEV_TIMEOUT_EPILOGUE)) break;
+    const uint32_t sb = s_ring + (uint32_t)stage * STG;
+#pragma unroll
+    for (int s4 = 0; s4 < 4; ++s4) {
+      uint32_t a[4];
+      ldsm4t(a, sb + o_a[s4]);
+#pragma unroll
+      for (int jp = 0; jp < NJ / 16; ++jp) {
+        uint32_t e[4];
+        ldsm4t(e, sb + o_e[s4][jp]);
+        mma16816(acc[2 * jp], a, e[0], e[1]);
+        mma16816(acc[2 * jp + 1], a, e[2], e[3]);
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[stage]);
+    if (++stage == CD_ST) {
+      stage = 0;
+      phase ^= 1;
     }
   }
   float* P = part + (int64_t)blockIdx.y * K * NJ;
+  const int k = kc + 16 * warp + g;
 #pragma unroll
   for (int jt = 0; jt < NJ / 8; ++jt) {
     const int j = 8 * jt + 2 * t;
-    *reinterpret_cast<float2*>(P + (int64_t)(k0 + g) * NJ + j) = make_float2(acc[jt][0], acc[jt][1]);
-    *reinterpret_cast<float2*>(P + (int64_t)(k0 + g + 8) * NJ + j) = make_float2(acc[jt][2], acc[jt][3]);
+    *reinterpret_cast<float2*>(P + (int64_t)k * NJ + j) = make_float2(acc[jt][0], acc[jt][1]);
+    *reinterpret_cast<float2*>(P + (int64_t)(k + 8) * NJ + j) = make_float2(acc[jt][2], acc[jt][3]);
   }
 }
 
@@ -1067,12 +1143,13 @@ extern "C" int mxm_rowdot_quant(const void* A, int64_t lda, const void* B, int64
 
 extern "C" int mxm_coldot_chunks(int64_t T, int64_t K, int* rows_per_chunk, int* chunks) {
   MX_CHECK_ARG(T >= 1 && K >= 64 && rows_per_chunk && chunks, "mxm_coldot_chunks: bad args");
-  const int64_t ctas_k = (K + 63) / 64;
+  // about four CTAs per SM in all: (K / 64) column blocks x row chunks of a multiple of 64 rows
+  const int64_t ctas_k = (K + CD_COLS - 1) / CD_COLS;
   const int64_t want = 4 * (int64_t)mxm_num_sms();
-  int64_t nch = (want + ctas_k - 1) / ctas_k;
+  const int64_t nch = (want + ctas_k - 1) / ctas_k;
   int64_t rpc = (T + nch - 1) / nch;
-  rpc = (rpc + 15) / 16 * 16;
-  if (rpc < 256) rpc = 256;
+  rpc = (rpc + CD_ROWS - 1) / CD_ROWS * CD_ROWS;
+  if (rpc < 4 * CD_ROWS) rpc = 4 * CD_ROWS;
   *rows_per_chunk = (int)rpc;
   *chunks = (int)((T + rpc - 1) / rpc);
   return MXM_OK;
@@ -1083,22 +1160,32 @@ extern "C" int mxm_coldot(const void* A, int64_t lda, const void* E, int64_t lde
                           float post, int transpose_out, void* part, int rows_per_chunk, int chunks, void* out,
                           void* stream) {
   MX_CHECK_ARG(A && E && part && out, "mxm_coldot: null pointer");
-  MX_CHECK_ARG(T >= 1 && K % 64 == 0 && (n == 16 || n == 32 || n == 64) && rows_per_chunk % 16 == 0 &&
-                   (int64_t)rows_per_chunk * chunks >= T,
-               "mxm_coldot: bad shape or chunking");
-  dim3 grid((unsigned)(K / 64), (unsigned)chunks);
+  MX_CHECK_ARG(T >= 1 && T < (1ll << 31) && K % 64 == 0 && (n == 16 || n == 32 || n == 64) &&
+                   rows_per_chunk % CD_ROWS == 0 && rows_per_chunk > 0 && (int64_t)rows_per_chunk * chunks >= T,
+               "mxm_coldot: bad shape or chunking (rows per chunk must be a multiple of 64)");
+  MX_CHECK_ARG(lda % 8 == 0 && lde % 8 == 0 && mx_aligned(A, 16) && mx_aligned(E, 16),
+               "mxm_coldot: A and E need 16-byte aligned rows (strides %% 8 == 0)");
+  CUtensorMap ta, te;
+  if (int e = mx_make_tmap_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, A, (uint64_t)K, (uint64_t)T,
+                              (uint64_t)(lda * 2), CD_COLS, CD_ROWS, CU_TENSOR_MAP_SWIZZLE_128B))
+    return e;
+  if (int e = mx_make_tmap_2d(&te, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, E, (uint64_t)n, (uint64_t)T,
+                              (uint64_t)(lde * 2), (uint32_t)n, CD_ROWS,
+                              n == 16 ? CU_TENSOR_MAP_SWIZZLE_32B
+                                      : (n == 32 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B)))
+    return e;
+  dim3 grid((unsigned)(K / CD_COLS), (unsigned)chunks);
   cudaStream_t st = (cudaStream_t)stream;
-  if (n == 16)
-    k_coldot<16><<<grid, 128, 0, st>>>((const bf16*)A, lda, (const bf16*)E, lde, (int)T, (int)K, rows_per_chunk,
-                                       (float*)part);
-  else if (n == 32)
-    k_coldot<32><<<grid, 128, 0, st>>>((const bf16*)A, lda, (const bf16*)E, lde, (int)T, (int)K, rows_per_chunk,
-                                       (float*)part);
-  else
-    k_coldot<64><<<grid, 128, 0, st>>>((const bf16*)A, lda, (const bf16*)E, lde, (int)T, (int)K, rows_per_chunk,
-                                       (float*)part);
-  mx_note_launch();
-  if (int e = mx_launch_status("coldot")) return e;
+  auto go = [&](auto kern, int nj) -> int {
+    const size_t smem = cd_smem(nj);
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return mx_cuda_status(e, "coldot: set smem");
+    kern<<<grid, 160, smem, st>>>(ta, te, (int)K, rows_per_chunk, (int)T, (float*)part, mx_dev_error_ptr());
+    mx_note_launch();
+    return mx_launch_status("coldot");
+  };
+  int e = n == 16 ? go(k_coldot<16>, 16) : (n == 32 ? go(k_coldot<32>, 32) : go(k_coldot<64>, 64));
+  if (e) return e;
   const int64_t nn = K * n;
   k_sum_parts<<<grid_for(nn, 256), 256, 0, st>>>((const float*)part, chunks, nn, nn, 1.f, post, nullptr, (bf16*)out,
                                                  transpose_out ? K : 0, transpose_out ? n : 0);
@@ -1150,7 +1237,7 @@ extern "C" int mxm_coldot_noalloc(const void* A, int64_t lda, const void* E, int
   const int64_t max_chunks = (int64_t)MXM_NOALLOC_SCRATCH_BYTES / per_chunk;
   if (chunks > max_chunks) {  // fewer, taller row chunks so the partials fit the fixed scratch
     int64_t r = (T + max_chunks - 1) / max_chunks;
-    r = (r + 15) / 16 * 16;
+    r = (r + CD_ROWS - 1) / CD_ROWS * CD_ROWS;
     rpc = (int)r;
     chunks = (int)((T + r - 1) / r);
   }
