@@ -128,6 +128,13 @@ int mxm_mlp_bwd_reduce(const void* dxa_part, const void* dbg_part, const void* d
 int mxm_rowdot(const void* A, int64_t lda, const void* B, int64_t T, int64_t K, int n, float post, void* out,
                int64_t ldo, void* stream);
 
+/* The per-step bf16 forms of the LoRA matrices in one launch (the reference's casts in _MLP.forward /
+ * backward, scripts/fused_mlp.py:272-276,282,311,331).  Sources Ag, Au [r, H], Bg, Bu [N, r], Ad [r, N],
+ * Bd [H, r], contiguous, all fp32 (src_fp32 = 1) or all bf16.  out (bf16, r * (7H + 3N) elements) =
+ * S [2r, H] (= [Ag; Au]) | bg | bu | ad | bd | bds = bf16(bd * s_d) [H, r] | bd^T [r, H] | S^T [H, 2r]. */
+int mxm_lora_prep(const void* Ag, const void* Au, const void* Bg, const void* Bu, const void* Ad, const void* Bd,
+                  int src_fp32, int64_t H, int64_t N, int r, float s_d, void* out, void* stream);
+
 /* mxm_rowdot plus the row-wise MXFP8 quantization of A from the same read of A: q [T, K] (row stride ldq)
  * and s (blocked layout of a [ceil128(T), K] operand) are exactly mxm_quant_rows(A).  The reference
  * quantizes and multiplies in two passes (scripts/fused_mlp.py:277-278 for x, :307,311 for dy). */
@@ -138,12 +145,13 @@ int mxm_rowdot_quant(const void* A, int64_t lda, const void* B, int64_t T, int64
  * [T, K] operand. */
 int mxm_coldot_chunks(int64_t T, int64_t K, int* rows_per_chunk, int* chunks);
 
-/* out = bf16( bf16(A[T, K]^T E[T, n]) * post ), written [K, n] (or [n, K] when transpose_out).
+/* out = bf16( bf16(A[T, K]^T E[T, n]) * post ), written [K, n] (or [n, K] when transpose_out), as bf16, or
+ * with out_fp32 as the same (bf16-valued) numbers in fp32 -- the gradient in an fp32 parameter's dtype.
  * part: fp32 [chunks, K, n] scratch; rows_per_chunk a multiple of 64.  K % 64 == 0, n in {16, 32, 64},
  * lda and lde multiples of 8 (16-byte rows), A and E 16-byte aligned.
  * The LoRA weight gradients dA = dxa^T x and dB_down = s_d (dy^T xS_down) (scripts/fused_mlp.py:316-318,333). */
 int mxm_coldot(const void* A, int64_t lda, const void* E, int64_t lde, int64_t T, int64_t K, int n, float post,
-               int transpose_out, void* part, int rows_per_chunk, int chunks, void* out, void* stream);
+               int transpose_out, void* part, int rows_per_chunk, int chunks, void* out, int out_fp32, void* stream);
 
 /* Allocation-free variant of mxm_coldot, for callers that cannot allocate device memory: code running
  * inside a custom device allocator (a nested allocation would re-enter it) and services that reserve

@@ -843,23 +843,68 @@ __global__ void __launch_bounds__(160) k_coldot(const __grid_constant__ CUtensor
 }
 
 // out[i] = scale * sum_{p < nparts} src[p * stride + i]   (fixed order); bf16 or fp32 output,
-// optionally transposed: element i = (a, b) of an [A, B] matrix written at out[b * A + a].
+// optionally transposed: element i = (a, b) of an [A, B] matrix written at out[b * A + a].  With
+// `round_out` the value is rounded as for the bf16 output (bf16(bf16(v) * post)) and stored as fp32.
 __global__ void k_sum_parts(const float* __restrict__ src, int nparts, int64_t n, int64_t stride, float scale,
                             float post, float* __restrict__ out_f, bf16* __restrict__ out_h, int64_t tr_a,
-                            int64_t tr_b) {
+                            int64_t tr_b, int round_out) {
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
     float v = 0.f;
     for (int p = 0; p < nparts; ++p) v += src[p * stride + i];
     v *= scale;
     int64_t o = i;
     if (tr_a > 0) o = (i % tr_b) * tr_a + i / tr_b;
-    if (out_h) {
-      float r = bf16_round_f(v);
-      if (post != 1.0f) r = bf16_round_f(r * post);
-      out_h[o] = __float2bfloat16_rn(r);
-    } else {
-      out_f[o] = v;
+    if (out_h || round_out) {
+      v = bf16_round_f(v);
+      if (post != 1.0f) v = bf16_round_f(v * post);
     }
+    if (out_h)
+      out_h[o] = __float2bfloat16_rn(v);
+    else
+      out_f[o] = v;
+  }
+}
+
+// The per-step bf16 forms of the six LoRA matrices (the reference's _MLP.forward casts,
+// scripts/fused_mlp.py:272-276, and the transposed / scaled copies its backward makes, :282,311,331),
+// one launch: out = S [2r, H] | bg [N, r] | bu [N, r] | ad [r, N] | bd [H, r] | bds [H, r] | bdT [r, H] |
+// ST [H, 2r] with S = [Ag; Au], bds = bf16(bd * s_d).  Sources are fp32 (src_f32) or bf16, contiguous.
+struct LoraSrc {
+  const void* p[6];  // Ag, Au, Bg, Bu, Ad, Bd
+};
+__global__ void k_lora_prep(LoraSrc src, int src_f32, int H, int N, int r, float s_d, bf16* __restrict__ out) {
+  const int64_t nS = 2ll * r * H, nB = (int64_t)N * r, nD = (int64_t)H * r;
+  const int64_t o_bg = nS, o_bu = o_bg + nB, o_ad = o_bu + nB, o_bd = o_ad + nB, o_bds = o_bd + nD,
+                o_bdT = o_bds + nD, o_ST = o_bdT + nD, total = o_ST + nS;
+  auto ld = [&](int w, int64_t i) -> float {
+    return src_f32 ? reinterpret_cast<const float*>(src.p[w])[i]
+                   : __bfloat162float(reinterpret_cast<const bf16*>(src.p[w])[i]);
+  };
+  auto ldS = [&](int64_t i) -> float {  // S = [Ag; Au] flat [2r, H]
+    return i < (int64_t)r * H ? ld(0, i) : ld(1, i - (int64_t)r * H);
+  };
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    float v;
+    if (i < o_bg) {
+      v = ldS(i);
+    } else if (i < o_bu) {
+      v = ld(2, i - o_bg);
+    } else if (i < o_ad) {
+      v = ld(3, i - o_bu);
+    } else if (i < o_bd) {
+      v = ld(4, i - o_ad);
+    } else if (i < o_bds) {
+      v = ld(5, i - o_bd);
+    } else if (i < o_bdT) {
+      v = bf16_round_f(bf16_round_f(ld(5, i - o_bds)) * s_d);
+    } else if (i < o_ST) {  // bdT [r, H]: (j, h) <- Bd [H, r] (h, j)
+      const int64_t e = i - o_bdT, j = e / H, h = e % H;
+      v = ld(5, h * r + j);
+    } else {                // ST [H, 2r]: (h, j) <- S [2r, H] (j, h)
+      const int64_t e = i - o_ST, h = e / (2 * r), j = e % (2 * r);
+      v = ldS(j * H + h);
+    }
+    out[i] = __float2bfloat16_rn(v);
   }
 }
 
@@ -977,7 +1022,7 @@ extern "C" int mxm_mlp_fwd_epilogue(const void* gu, const void* xs, const void* 
   if (col_groups > 1) {
     const int64_t n = T * r;
     k_sum_parts<<<grid_for(n, 256), 256, 0, st>>>((const float*)xsd_part, col_groups, n, n, 1.0f, 1.0f, nullptr,
-                                                  (bf16*)xsd, 0, 0);
+                                                  (bf16*)xsd, 0, 0, 0);
     mx_note_launch();
     if (int e = mx_launch_status("mlp fwd xsd sum")) return e;
   }
@@ -1117,6 +1162,20 @@ extern "C" int mxm_rowdot(const void* A, int64_t lda, const void* B, int64_t T, 
   return mx_launch_status("rowdot");
 }
 
+extern "C" int mxm_lora_prep(const void* Ag, const void* Au, const void* Bg, const void* Bu, const void* Ad,
+                             const void* Bd, int src_fp32, int64_t H, int64_t N, int r, float s_d, void* out,
+                             void* stream) {
+  MX_CHECK_ARG(Ag && Au && Bg && Bu && Ad && Bd && out, "mxm_lora_prep: null pointer");
+  MX_CHECK_ARG(H >= 1 && N >= 1 && r >= 1 && r <= 256 && H < (1ll << 31) && N < (1ll << 31),
+               "mxm_lora_prep: bad shape");
+  LoraSrc src{{Ag, Au, Bg, Bu, Ad, Bd}};
+  const int64_t total = (int64_t)r * (7 * H + 3 * N);
+  k_lora_prep<<<grid_for(total, 256), 256, 0, (cudaStream_t)stream>>>(src, src_fp32, (int)H, (int)N, r, s_d,
+                                                                        (bf16*)out);
+  mx_note_launch();
+  return mx_launch_status("lora prep");
+}
+
 extern "C" int mxm_rowdot_quant(const void* A, int64_t lda, const void* B, int64_t T, int64_t K, int n, float post,
                                 void* out, int64_t ldo, void* q, int64_t ldq, void* s, void* stream) {
   MX_CHECK_ARG(A && B && out && q && s, "mxm_rowdot_quant: null pointer");
@@ -1155,10 +1214,11 @@ extern "C" int mxm_coldot_chunks(int64_t T, int64_t K, int* rows_per_chunk, int*
   return MXM_OK;
 }
 
-// out = bf16( bf16(sum_t A[t,k] E[t,j]) * post ), written [K, n] or transposed [n, K].
+// out = bf16( bf16(sum_t A[t,k] E[t,j]) * post ), written [K, n] or transposed [n, K], as bf16 or (out_fp32)
+// as the same values in fp32.
 extern "C" int mxm_coldot(const void* A, int64_t lda, const void* E, int64_t lde, int64_t T, int64_t K, int n,
                           float post, int transpose_out, void* part, int rows_per_chunk, int chunks, void* out,
-                          void* stream) {
+                          int out_fp32, void* stream) {
   MX_CHECK_ARG(A && E && part && out, "mxm_coldot: null pointer");
   MX_CHECK_ARG(T >= 1 && T < (1ll << 31) && K % 64 == 0 && (n == 16 || n == 32 || n == 64) &&
                    rows_per_chunk % CD_ROWS == 0 && rows_per_chunk > 0 && (int64_t)rows_per_chunk * chunks >= T,
@@ -1187,8 +1247,9 @@ extern "C" int mxm_coldot(const void* A, int64_t lda, const void* E, int64_t lde
   int e = n == 16 ? go(k_coldot<16>, 16) : (n == 32 ? go(k_coldot<32>, 32) : go(k_coldot<64>, 64));
   if (e) return e;
   const int64_t nn = K * n;
-  k_sum_parts<<<grid_for(nn, 256), 256, 0, st>>>((const float*)part, chunks, nn, nn, 1.f, post, nullptr, (bf16*)out,
-                                                 transpose_out ? K : 0, transpose_out ? n : 0);
+  k_sum_parts<<<grid_for(nn, 256), 256, 0, st>>>((const float*)part, chunks, nn, nn, 1.f, post,
+                                                 out_fp32 ? (float*)out : nullptr, out_fp32 ? nullptr : (bf16*)out,
+                                                 transpose_out ? K : 0, transpose_out ? n : 0, out_fp32 ? 1 : 0);
   mx_note_launch();
   return mx_launch_status("coldot sum");
 }
@@ -1244,5 +1305,5 @@ extern "C" int mxm_coldot_noalloc(const void* A, int64_t lda, const void* E, int
   float* scratch = nullptr;
   if (int e = noalloc_scratch(&scratch)) return e;
   // every partial the reduction reads is written by k_coldot first: nothing needs clearing
-  return mxm_coldot(A, lda, E, lde, T, K, n, post, transpose_out, scratch, rpc, chunks, out, stream);
+  return mxm_coldot(A, lda, E, lde, T, K, n, post, transpose_out, scratch, rpc, chunks, out, 0, stream);
 }

@@ -67,17 +67,41 @@ def rowdot_quant(A, B, post=1.0):
     return out, q, s.view(_E8)
 
 
-def coldot(A, E, post=1.0, transpose_out=False):
-    """bf16(bf16(A^T @ E) * post): A [T, K] bf16, E [T, n] bf16 (n in {16, 32}) -> [K, n] (or [n, K])."""
+def coldot(A, E, post=1.0, transpose_out=False, out_dtype=torch.bfloat16):
+    """bf16(bf16(A^T @ E) * post): A [T, K] bf16, E [T, n] bf16 (n in {16, 32, 64}) -> [K, n] (or [n, K]);
+    out_dtype float32 stores the same bf16-valued numbers in fp32 (a gradient for an fp32 parameter)."""
     T, K = A.shape
     n = E.shape[1]
+    assert out_dtype in (torch.bfloat16, torch.float32)
     rpc, nch = _i(0), _i(0)
     _nx.call("mxm_coldot_chunks", T, K, _nx.ctypes_ref(rpc), _nx.ctypes_ref(nch))
     part = torch.empty((nch.value, K, n), dtype=torch.float32, device=A.device)
-    out = torch.empty((n, K) if transpose_out else (K, n), dtype=torch.bfloat16, device=A.device)
+    out = torch.empty((n, K) if transpose_out else (K, n), dtype=out_dtype, device=A.device)
     _nx.call("mxm_coldot", _nx.ptr(A), A.stride(0), _nx.ptr(E), E.stride(0), T, K, n, float(post),
-             1 if transpose_out else 0, _nx.ptr(part), rpc.value, nch.value, _nx.ptr(out), _nx.stream_of(A))
+             1 if transpose_out else 0, _nx.ptr(part), rpc.value, nch.value, _nx.ptr(out),
+             1 if out_dtype == torch.float32 else 0, _nx.stream_of(A))
     return out
+
+
+def lora_prep(Ag, Au, Bg, Bu, Ad, Bd, s_d):
+    """The bf16 LoRA operands of one step in one launch: (S, bg, bu, ad, bd, bds, bdT, ST) with
+    S = [Ag; Au], bds = bf16(bd * s_d), bdT = bd^T, ST = S^T (all contiguous views of one buffer); None
+    when the parameters are not all contiguous fp32 or all contiguous bf16 on one device."""
+    ws = (Ag, Au, Bg, Bu, Ad, Bd)
+    dts = {w.dtype for w in ws}
+    if len(dts) != 1 or dts.pop() not in (torch.float32, torch.bfloat16) or \
+            not all(w.is_contiguous() and w.device == Ag.device for w in ws):
+        return None
+    r, H = Ag.shape
+    N = Bg.shape[0]
+    if Au.shape != (r, H) or Bg.shape != (N, r) or Bu.shape != (N, r) or Ad.shape != (r, N) or Bd.shape != (H, r):
+        return None
+    buf = torch.empty(r * (7 * H + 3 * N), dtype=torch.bfloat16, device=Ag.device)
+    _nx.call("mxm_lora_prep", _nx.ptr(Ag), _nx.ptr(Au), _nx.ptr(Bg), _nx.ptr(Bu), _nx.ptr(Ad), _nx.ptr(Bd),
+             1 if Ag.dtype == torch.float32 else 0, H, N, r, float(s_d), _nx.ptr(buf), _nx.stream_of(Ag))
+    sizes = [2 * r * H, N * r, N * r, r * N, H * r, H * r, r * H, H * 2 * r]
+    shapes = [(2 * r, H), (N, r), (N, r), (r, N), (H, r), (H, r), (r, H), (H, 2 * r)]
+    return tuple(p.view(sh) for p, sh in zip(torch.split(buf, sizes), shapes))
 
 
 def mx_mm_lora(a, b, scale_a, scale_b, L, Rm):
@@ -155,17 +179,25 @@ class _MLP(torch.autograd.Function):
         x2 = x.reshape(-1, K)
         if x2.dtype != dt or not x2.is_contiguous():
             x2 = x2.to(dt).contiguous()
-        S = _cast(((id(Ag), id(Au)), dt), lambda: torch.cat([Ag.detach().to(dt), Au.detach().to(dt)]))
-        bg = _cast((id(Bg), dt), lambda: Bg.detach().to(dt).contiguous())
-        bu = _cast((id(Bu), dt), lambda: Bu.detach().to(dt).contiguous())
-        ad = _cast(((id(Ad),), dt), lambda: torch.cat([Ad.detach().to(dt)]))
-        bd = _cast((id(Bd), dt), lambda: Bd.detach().to(dt).contiguous())
+        P = _cast(("prep", id(Ag), id(Au), id(Bg), id(Bu), id(Ad), id(Bd), s_d, dt),
+                  lambda: lora_prep(*(w.detach() for w in (Ag, Au, Bg, Bu, Ad, Bd)), s_d) if dt == torch.bfloat16
+                  else None)
+        if P is not None:
+            S, bg, bu, ad, bd, bds, bdT, ST = P
+        else:   # parameters in another dtype / layout: the reference's per-tensor casts
+            S = _cast(((id(Ag), id(Au)), dt), lambda: torch.cat([Ag.detach().to(dt), Au.detach().to(dt)]))
+            bg = _cast((id(Bg), dt), lambda: Bg.detach().to(dt).contiguous())
+            bu = _cast((id(Bu), dt), lambda: Bu.detach().to(dt).contiguous())
+            ad = _cast(((id(Ad),), dt), lambda: torch.cat([Ad.detach().to(dt)]))
+            bd = _cast((id(Bd), dt), lambda: Bd.detach().to(dt).contiguous())
+            bds = _cast(("s", id(Bd), s_d, dt), lambda: (bd.float() * s_d).to(dt).contiguous())
+            bdT = _cast(("T", id(bd)), lambda: bd.t().contiguous())
+            ST = _cast(("T", id(S)), lambda: S.t().contiguous())
         xs, q, sc = rowdot_quant(x2, S)                                  # [T, 2R] = xa_gate | xa_up; MXFP8(x)
         gu = mxfp8.mx_mm(q, hold.w.t(), sc, hold.ws)                     # [T, 2N] gate | up
         del q, sc
         if need_out:
             qh, sh, xsd = mlp_fwd(gu, xs, bg, bu, ad, s_g, s_u, True)
-            bds = _cast(("s", id(Bd), s_d, dt), lambda: (bd.float() * s_d).to(dt).contiguous())
             y = mx_mm_lora(qh, down._mx_w.t(), sh, down._mx_ws, xsd, bds)
             del qh, sh, xsd
         else:   # graph only (checkpoint recompute): nobody reads the output value
@@ -173,6 +205,8 @@ class _MLP(torch.autograd.Function):
             y = x2.new_empty(x2.shape[0], down.out_features)
         ctx.save_for_backward(x2, xs, gu, S, bg, bu, ad, bd)
         ctx.meta = (hold, down, (s_g, s_u, s_d), dt, lead, K, x.dtype)
+        ctx.tr = (bdT, ST)   # parameter-derived transposes (not activations)
+        ctx.gdt = tuple(w.dtype for w in (Ag, Au, Bd))
         return y.view(*lead, y.shape[-1])
 
     @staticmethod
@@ -187,7 +221,7 @@ class _MLP(torch.autograd.Function):
         if not dy2.is_contiguous():
             dy2 = dy2.contiguous()
         T, N = gu.shape[0], gu.shape[1] // 2
-        bdT = _cast(("T", id(bd)), lambda: bd.t().contiguous())
+        bdT, ST = ctx.tr
         dxd, qd, sd = rowdot_quant(dy2, bdT, post=s_d)                    # bf16(bf16(dy @ Bd) * s_d); MXFP8(dy)
         wt, wts = mxfp8.mx_wt(down)
         dhm = mxfp8.mx_mm(qd, wt.t(), sd, wts)                           # [T, N]
@@ -204,14 +238,15 @@ class _MLP(torch.autograd.Function):
                  float(s_g), float(s_u), sb, ncg, _nx.ptr(dxa), _nx.ptr(xsd), _nx.ptr(dB_g), _nx.ptr(dB_u),
                  _nx.ptr(dA_d), _nx.stream_of(gu))
         del dxa_p, dbg_p, dbu_p, dad_p
-        dB_d = coldot(dy2, xsd, post=s_d)                                # bf16(bf16(dy^T xS_down) * s_d) [H, R]
+        f32 = lambda k: torch.float32 if ctx.gdt[k] == torch.float32 else torch.bfloat16  # noqa: E731
+        dB_d = coldot(dy2, xsd, post=s_d, out_dtype=f32(2))              # bf16(bf16(dy^T xS_down) * s_d) [H, R]
         dx = None
         if need_x:
-            ST = _cast(("T", id(S)), lambda: S.t().contiguous())
             dx = mx_mm_lora(qg, hold.wt.t(), sg.view(_E8), hold.wts, dxa, ST)   # K = 2N: gate + up
             del qg, sg
             dx = dx.view(*lead, K).to(xdt)
-        dA = coldot(x2, dxa, transpose_out=True)                          # [2R, H]
+        dA = coldot(x2, dxa, transpose_out=True,
+                    out_dtype=f32(0) if ctx.gdt[0] == ctx.gdt[1] else torch.bfloat16)   # [2R, H]
         grads = [dA[:R], dB_g, dA[R:], dB_u, dA_d, dB_d]
         ws_in = ctx.needs_input_grad[3:]
         return (dx, None, None, *[g if ws_in[k] else None for k, g in enumerate(grads)])
