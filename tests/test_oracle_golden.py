@@ -97,3 +97,16 @@ def test_mlp_forward_backward_matches_reference(mg):
     assert O.rel_fro(g["dx"], O.bf16_bits_to_f32(mg["dx"])) < tol
     for k in ("dAg", "dBg", "dAu", "dBu", "dAd", "dBd"):
         assert O.rel_fro(g[k], mg[k]) < tol, k
+
+
+def test_scale_from_amax_bits_equals_division():
+    """The kernels compute the E8M0 scale from the abs-max's bf16 bits, ((bits + 0x1F) >> 7) - 8 clamped
+    at 0, +inf -> 254, NaN -> 255, instead of rceil(amax / 448) (scripts/mxfp8.py:60-63): same code for
+    every non-negative bf16 value."""
+    bits = np.arange(0, 0x8000, dtype=np.uint32)
+    m = (bits << 16).view(np.float32)
+    with np.errstate(invalid="ignore"):
+        ref = O.e8m0_rceil(m / np.float32(448.0)).astype(np.int64)
+    e = np.maximum(((bits.astype(np.int64) + 0x1F) >> 7) - 8, 0)
+    e = np.where(bits == 0x7F80, 254, np.where(bits > 0x7F80, 255, e))
+    assert np.array_equal(e, ref)

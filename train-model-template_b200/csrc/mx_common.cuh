@@ -46,6 +46,22 @@ MX_DEV uint32_t mx_e8m0_rceil(float descale) {
   return r & 0xFFu;
 }
 
+// The same E8M0 scale computed from the block's abs-max without the division: rceil(RN(amax / 448)).
+// amax is a bf16 value (the abs-max of bf16 inputs), s * 2^E with a 7-bit fraction; 448 = 1.75 * 2^8,
+// so amax / 448 = (s / 1.75) * 2^(E-8) with s / 1.75 in [0.57, 1.15): it rounds up to 2^(E-8) when
+// s <= 1.75 and to 2^(E-7) when s > 1.75 (fraction > 0x60), and no value is near enough to a power of
+// two for the fp32 rounding of the quotient to change that.  In the bf16 bits that is
+// ((bits + 0x1F) >> 7) - 8, clamped at 0 (scales below 2^-127), with +inf -> 254 and NaN -> 255 as the
+// saturating cvt gives.  Checked against the division for all 32,768 non-negative bf16 values.
+MX_DEV uint32_t mx_e8m0_of_amax(float amax) {
+  const uint32_t b = __float_as_uint(amax) >> 16;  // bf16-exact: the low half is zero
+  int e = (int)((b + 0x1Fu) >> 7) - 8;
+  e = e < 0 ? 0 : e;
+  e = b == 0x7F80u ? 254 : e;
+  e = b > 0x7F80u ? 255 : e;
+  return (uint32_t)e;
+}
+
 // Multiplier applied to the block before the E4M3 cast: 255 -> NaN, 254 -> 2^-127,
 // 0 -> 1.0, else 2^(127 - e).  2^(127-e) is built from its exponent bits (exact).
 MX_DEV float mx_e8m0_rcp(uint32_t e) {

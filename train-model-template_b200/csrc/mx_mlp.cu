@@ -77,30 +77,49 @@ MX_DEV uint32_t max_bf16x2(uint32_t a, uint32_t b) {
   return r;
 }
 
-// Quantizes one 32-column block of a 16-row warp tile whose bf16 values are held packed in
-// D-fragment form: pk[i][h] = (row g + 8h, cols 8i+2t, +1), i = 0..3 (t = lane % 4).  Codes go to
-// q[row * ldq + col0 + ...] for rows < T; the scales of rows g and g+8 (always, padded rows included)
-// to the blocked layout of a [*, scols] operand for rows < Tpad.
-MX_DEV void quant_block16p(const uint32_t (&pk)[4][2], int64_t row_g, int64_t T, int64_t Tpad, int64_t col0,
-                           uint8_t* q, int64_t ldq, uint8_t* s, int64_t scols, int t) {
+// Per-thread store targets of the MX output of one 16-row warp tile (rows g and g + 8), fixed for the
+// whole kernel: the code row pointers (+ 2t), the scale bytes of k-block 0, and the store predicates
+// (codes for rows < T; scales for rows < Tpad, written by lane t = 0 of the quad).
+struct QRows {
+  uint8_t* code[2];
+  uint8_t* scale[2];
+  bool live[2], slive[2];
+};
+MX_DEV QRows qrows_init(int64_t row_g, int64_t T, int64_t Tpad, uint8_t* q, int64_t ldq, uint8_t* s, int64_t scols,
+                        int t) {
+  QRows r;
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int64_t row = row_g + 8 * h;
+    r.live[h] = row < T;
+    r.slive[h] = t == 0 && row < Tpad;
+    r.code[h] = q ? q + (r.live[h] ? row : 0) * ldq + 2 * t : nullptr;
+    r.scale[h] = s ? s + mx_scale_offset(row < Tpad ? row : 0, 0, scols) : nullptr;
+  }
+  return r;
+}
+
+// Quantizes one 32-column block (columns col0 .. col0+31, col0 % 32 == 0) of a 16-row warp tile whose
+// bf16 values are held packed in D-fragment form: pk[i][h] = (row g + 8h, cols 8i+2t, +1), i = 0..3
+// (t = lane % 4).  Codes and the two rows' scales go to the targets of `qr`.
+MX_DEV void quant_block16p(const uint32_t (&pk)[4][2], const QRows& qr, int64_t col0, int t) {
+  const int64_t soff = ((col0 >> 7) << 9) + ((col0 >> 5) & 3);  // k-block col0/32 in the blocked layout
 #pragma unroll
   for (int h = 0; h < 2; ++h) {
     const uint32_t m2 = max_bf16x2(absmax_bf16x2(pk[0][h], pk[1][h]), absmax_bf16x2(pk[2][h], pk[3][h]));
     float m = nanmax(bf16_lo(m2), bf16_hi(m2));
     m = nanmax(m, __shfl_xor_sync(0xffffffffu, m, 1));
     m = nanmax(m, __shfl_xor_sync(0xffffffffu, m, 2));
-    const uint32_t e = mx_e8m0_rceil(__fdiv_rn(m, 448.0f));
+    const uint32_t e = mx_e8m0_of_amax(m);
     const float rcp = mx_e8m0_rcp(e);
-    const int64_t row = row_g + 8 * h;
-    const bool live = row < T;
-    uint8_t* dst = q + (live ? row : 0) * ldq + col0 + 2 * t;
+    uint8_t* dst = qr.code[h] + col0;
     const float2 r2 = make_float2(rcp, rcp);
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       const float2 v = __fmul2_rn(up2(pk[i][h]), r2);
-      stg16_if(dst + 8 * i, e4m3x2_sat(v.x, v.y), live);
+      stg16_if(dst + 8 * i, e4m3x2_sat(v.x, v.y), qr.live[h]);
     }
-    stg8_if(s + mx_scale_offset(row < Tpad ? row : 0, col0 >> 5, scols), e, t == 0 && row < Tpad);
+    stg8_if(qr.scale[h] + soff, e, qr.slive[h]);
   }
 }
 
@@ -231,6 +250,7 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
   }
   const uint32_t s_ring = smem_u32(smem);
   const float2 sg2 = make_float2(s_g, s_g), su2 = make_float2(s_u, s_u);
+  const QRows qr = qrows_init(ra, T, Tpad, qh, N, sh, N, t);
   int stage = 0;
   uint32_t phase = 0;
   for (int ct = 0; ct < tpg; ++ct) {
@@ -271,7 +291,7 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
           }
         }
       }
-      if (write_q) quant_block16p(hp, ra, T, Tpad, n0 + 32 * b, qh, N, sh, N, t);
+      if (write_q) quant_block16p(hp, qr, n0 + 32 * b, t);
       // xS_down += h (16 x 32 block) A_down^T: two k-slices of 16 columns
 #pragma unroll
       for (int mm = 0; mm < 2; ++mm) {
@@ -460,6 +480,7 @@ __global__ void __launch_bounds__(32 * (bwd_cons(R) + 1), 1)
 
   const int64_t ra = (int64_t)r0 + warp * 16 + g;
   const float2 sg2 = make_float2(s_g, s_g), su2 = make_float2(s_u, s_u);
+  const QRows qr = qrows_init(ra, T, Tpad, q, N2, s, N2, t);
   int stage = 0;
   uint32_t phase = 0;
   for (int ct = 0; ct < tpg; ++ct) {
@@ -510,8 +531,8 @@ __global__ void __launch_bounds__(32 * (bwd_cons(R) + 1), 1)
         }
       }
       if (write_q) {
-        quant_block16p(dgp, ra, T, Tpad, n0, q, N2, s, N2, t);
-        quant_block16p(dup, ra, T, Tpad, (int64_t)N + n0, q, N2, s, N2, t);
+        quant_block16p(dgp, qr, n0, t);
+        quant_block16p(dup, qr, (int64_t)N + n0, t);
       }
       // per-row products (sums over columns): [dg Bg | du Bu | h Ad^T]
 #pragma unroll
@@ -631,7 +652,7 @@ MX_DEV uint2 quant8_lane(const uint4& v, uint32_t& e) {
   float m = nanmax(bf16_lo(m2), bf16_hi(m2));
   m = nanmax(m, __shfl_xor_sync(0xffffffffu, m, 1));
   m = nanmax(m, __shfl_xor_sync(0xffffffffu, m, 2));
-  e = mx_e8m0_rceil(__fdiv_rn(m, 448.0f));
+  e = mx_e8m0_of_amax(m);
   const float rcp = mx_e8m0_rcp(e);
   const float2 r2 = make_float2(rcp, rcp);
   const float2 f0 = __fmul2_rn(up2(v.x), r2), f1 = __fmul2_rn(up2(v.y), r2);

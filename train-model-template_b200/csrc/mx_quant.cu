@@ -2,7 +2,7 @@
 // along the quantized axis), scales written directly in the 128x4 blocked layout the tcgen05
 // block-scaled MMA consumes.  Algorithm of the reference _quant_kernel (scripts/mxfp8.py:46-75):
 //   amax = max |x| over the block (NaN if the block holds a NaN)
-//   e    = round-up-to-power-of-two(amax / 448) as E8M0        (cvt.rp.satfinite.ue8m0x2.f32)
+//   e    = round-up-to-power-of-two(amax / 448) as E8M0        (from amax's bits: mx_e8m0_of_amax)
 //   q    = e4m3_rne(clamp(x * rcp(e), -448, 448)),  rcp(e) = 2^(127-e) (special cases 0/254/255)
 //
 // One CTA owns a 128-row x 128-column tile, which is exactly one 512-byte scale block of the
@@ -29,9 +29,8 @@ __device__ __forceinline__ Quant8 quant8(const float (&v)[8]) {
   for (int i = 0; i < 8; ++i) m = mx_absmax_nan(m, v[i]);
   m = mx_max_nan(m, __shfl_xor_sync(0xffffffffu, m, 1));
   m = mx_max_nan(m, __shfl_xor_sync(0xffffffffu, m, 2));
-  const float descale = __fdiv_rn(m, 448.0f);
   Quant8 r;
-  r.e = mx_e8m0_rceil(descale);
+  r.e = mx_e8m0_of_amax(m);
   const float rcp = mx_e8m0_rcp(r.e);
   uint32_t w[4];
 #pragma unroll
@@ -104,7 +103,7 @@ __global__ void __launch_bounds__(QT) k_quant(const __nv_bfloat16* __restrict__ 
         v[i] = __uint_as_float((uint32_t)s_tile[(jb * 32 + i) * 128 + k] << 16);
         m = mx_absmax_nan(m, v[i]);
       }
-      const uint32_t e = mx_e8m0_rceil(__fdiv_rn(m, 448.0f));
+      const uint32_t e = mx_e8m0_of_amax(m);
       const float rcp = mx_e8m0_rcp(e);
       uint32_t w4[8];
 #pragma unroll
