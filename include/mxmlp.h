@@ -128,6 +128,26 @@ int mxm_mlp_bwd_reduce(const void* dxa_part, const void* dbg_part, const void* d
 int mxm_rowdot(const void* A, int64_t lda, const void* B, int64_t T, int64_t K, int n, float post, void* out,
                int64_t ldo, void* stream);
 
+/* Row-wise MXFP8 of x [R, K] into columns col_tile_off*128 .. of a wider MX operand [ceil128(R), s_cols]:
+ * codes at q[r * ldq + col_tile_off*128 + c], scales in that operand's blocked layout.  The quantize-only
+ * mode of the reference's lora_bwd (scripts/mxfp8.py:219-246): one K-concatenated dy for a group's dx. */
+int mxm_quant_rows_into(const void* x, int64_t R, int64_t K, int64_t ldx, void* q, int64_t ldq, void* s,
+                        int64_t s_cols, int64_t col_tile_off, void* stream);
+
+/* The reference's lora_bwd for one LoRA branch (scripts/mxfp8.py:127-263): dxa_out [T, r] = bf16(scale *
+ * dy B) with Bt = B^T [r, N]; dB_out [N, r] fp32 = scale * dy^T xa; and, when q / s are given, the row-wise
+ * MXFP8 of dy into columns col_tile_off*128 .. of a [ceil128(T), s_cols] operand from the same read of dy.
+ * part: fp32 [chunks, N, r] scratch with mxm_coldot_chunks(T, N) chunking.  N % 128 == 0, r in {16, 32, 64}. */
+int mxm_lora_bwd(const void* dy, int64_t ldy, int64_t T, int64_t N, const void* xa, int64_t ldxa, const void* Bt,
+                 int r, float scale, void* q, int64_t ldq, void* s, int64_t s_cols, int64_t col_tile_off,
+                 void* dxa_out, int64_t ld_dxa, void* dB_out, void* part, int rows_per_chunk, int chunks,
+                 void* stream);
+
+/* out = bf16(x + bf16(y + scale * xa B^T)) for x, y, out [T, N] bf16 contiguous, xa [T, r] (row stride ldxa),
+ * B [N, r] contiguous (reference res_lora, scripts/mxfp8.py:265-296).  N % 64 == 0, r in {16, 32, 64}. */
+int mxm_res_lora(const void* x, const void* y, const void* xa, int64_t ldxa, const void* B, int64_t T, int64_t N,
+                 int r, float scale, void* out, void* stream);
+
 /* The per-step bf16 forms of the LoRA matrices in one launch (the reference's casts in _MLP.forward /
  * backward, scripts/fused_mlp.py:272-276,282,311,331).  Sources Ag, Au [r, H], Bg, Bu [N, r], Ad [r, N],
  * Bd [H, r], contiguous, all fp32 (src_fp32 = 1) or all bf16.  out (bf16, r * (7H + 3N) elements) =

@@ -45,6 +45,10 @@ _SIGS = {
     "mxm_rowdot_quant": [_vp, _i64, _vp, _i64, _i64, _int, ctypes.c_float, _vp, _i64, _vp, _i64, _vp, _vp],
     "mxm_coldot_chunks": [_i64, _i64, ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_int)],
     "mxm_coldot": [_vp, _i64, _vp, _i64, _i64, _i64, _int, ctypes.c_float, _int, _vp, _int, _int, _vp, _int, _vp],
+    "mxm_quant_rows_into": [_vp, _i64, _i64, _i64, _vp, _i64, _vp, _i64, _i64, _vp],
+    "mxm_lora_bwd": [_vp, _i64, _i64, _i64, _vp, _i64, _vp, _int, ctypes.c_float, _vp, _i64, _vp, _i64, _i64, _vp, _i64,
+                     _vp, _vp, _int, _int, _vp],
+    "mxm_res_lora": [_vp, _vp, _vp, _i64, _vp, _i64, _i64, _int, ctypes.c_float, _vp, _vp],
     "mxm_lora_prep": [_vp, _vp, _vp, _vp, _vp, _vp, _int, _i64, _i64, _int, ctypes.c_float, _vp, _vp],
     "mxm_coldot_noalloc": [_vp, _i64, _vp, _i64, _i64, _i64, _int, ctypes.c_float, _int, _vp, _vp],
 }

@@ -662,17 +662,19 @@ MX_DEV uint2 quant8_lane(const uint4& v, uint32_t& e) {
 }
 
 // out[t, j] = bf16( bf16(sum_k A[t, k] B[j, k]) * post ) for j < NJ (16, 32 or 64); post == 1 skips
-// the second rounding.  CTA = 16 rows; its 4 warps split K in four and their fp32 partials are summed
+// the second rounding; with round_once, bf16(sum * post) (one rounding).  CTA = 16 rows; its 4 warps split K in four and their fp32 partials are summed
 // through shared memory in a fixed order.  The reduction index k is permuted consistently in A and B so
 // each lane loads 16 contiguous bytes per row per 32 k; a group of 32-k steps (four for n <= 32, two
 // for n = 64) has all its A vectors and B fragments requested before any is used, so a group costs
 // one memory latency.  With QUANT the same registers are also quantized row-wise to MXFP8
-// (codes q [T, K], scales s in the blocked layout of a [Tpad, K] operand), since the 4 lanes holding a
-// row's 32 k are exactly one MX block: one read of A serves both.  The QUANT grid covers Tpad rows.
+// (codes q [T, K] at row stride ldq; scales in the blocked layout of a [Tpad, scols] operand from k-block
+// kb_off on), since the 4 lanes holding a row's 32 k are exactly one MX block: one read of A serves both.
+// The QUANT grid covers Tpad rows.
 template <int NJ, bool QUANT>
 __global__ void __launch_bounds__(128) k_rowdot(const bf16* __restrict__ A, int64_t lda, const bf16* __restrict__ B,
-                                                int T, int K, float post, bf16* __restrict__ out, int64_t ldo,
-                                                uint8_t* __restrict__ q, int64_t ldq, uint8_t* __restrict__ s) {
+                                                int T, int K, float post, int round_once, bf16* __restrict__ out,
+                                                int64_t ldo, uint8_t* __restrict__ q, int64_t ldq,
+                                                uint8_t* __restrict__ s, int64_t scols, int kb_off) {
   __shared__ float red[4][16][NJ + 1];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
   const int64_t r0 = (int64_t)blockIdx.x * 16;
@@ -694,8 +696,8 @@ __global__ void __launch_bounds__(128) k_rowdot(const bf16* __restrict__ A, int6
       if (va) *reinterpret_cast<uint2*>(q + ra * ldq + k0 + 8 * t) = ca;
       if (vb) *reinterpret_cast<uint2*>(q + rb * ldq + k0 + 8 * t) = cb;
       if (t == 0) {
-        s[mx_scale_offset(ra, k0 >> 5, K)] = (uint8_t)ea;
-        s[mx_scale_offset(rb, k0 >> 5, K)] = (uint8_t)eb;
+        s[mx_scale_offset(ra, kb_off + (k0 >> 5), scols)] = (uint8_t)ea;
+        s[mx_scale_offset(rb, kb_off + (k0 >> 5), scols)] = (uint8_t)eb;
       }
     }
     // fragment k slots (2t, 2t+1 | 2t+8, 2t+9) <- actual k (8t, 8t+1 | 8t+2, 8t+3), then (8t+4.. | 8t+6..)
@@ -746,8 +748,12 @@ __global__ void __launch_bounds__(128) k_rowdot(const bf16* __restrict__ A, int6
 #pragma unroll
     for (int e = 0; e < 2; ++e) {
       const float sum = (red[0][rr][c + e] + red[1][rr][c + e]) + (red[2][rr][c + e] + red[3][rr][c + e]);
-      v[e] = bf16_round_f(sum);
-      if (post != 1.0f) v[e] = bf16_round_f(v[e] * post);
+      if (round_once) {
+        v[e] = bf16_round_f(sum * post);
+      } else {
+        v[e] = bf16_round_f(sum);
+        if (post != 1.0f) v[e] = bf16_round_f(v[e] * post);
+      }
     }
     if (r0 + rr < T) *reinterpret_cast<uint32_t*>(out + (r0 + rr) * ldo + c) = pack_bf16x2(v[0], v[1]);
   }
@@ -860,6 +866,53 @@ __global__ void __launch_bounds__(160) k_coldot(const __grid_constant__ CUtensor
     const int j = 8 * jt + 2 * t;
     *reinterpret_cast<float2*>(P + (int64_t)k * NJ + j) = make_float2(acc[jt][0], acc[jt][1]);
     *reinterpret_cast<float2*>(P + (int64_t)(k + 8) * NJ + j) = make_float2(acc[jt][2], acc[jt][3]);
+  }
+}
+
+// out = bf16(x + bf16(y + scale * xa B^T)) for x, y [T, N] bf16, xa [T, R] (row stride ldxa), B [N, R]:
+// the residual add with the rank-R LoRA term of o_proj / out_proj computed in registers (reference
+// _res_lora_kernel, scripts/mxfp8.py:266-282).  Warp = 16 rows x 64 columns: xa and B fragments from
+// 4-byte loads, R/16 x 8 mma.sync, then the two roundings per element on the accumulator fragment.
+template <int R>
+__global__ void __launch_bounds__(128) k_res_lora(const bf16* __restrict__ x, const bf16* __restrict__ y,
+                                                  const bf16* __restrict__ xa, int64_t ldxa,
+                                                  const bf16* __restrict__ B, int T, int N, float scale,
+                                                  bf16* __restrict__ out) {
+  constexpr int KS = R / 16;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const int64_t ra = (int64_t)blockIdx.x * 64 + warp * 16 + g, rb = ra + 8;
+  const int c0 = blockIdx.y * 64;
+  const bool va = ra < T, vb = rb < T;
+  uint32_t a[KS][4];
+#pragma unroll
+  for (int kk = 0; kk < KS; ++kk) {
+    const bf16* pa = xa + ra * ldxa + 16 * kk + 2 * t;
+    const bf16* pb = xa + rb * ldxa + 16 * kk + 2 * t;
+    a[kk][0] = va ? ld32(pa) : 0u;
+    a[kk][1] = vb ? ld32(pb) : 0u;
+    a[kk][2] = va ? ld32(pa + 8) : 0u;
+    a[kk][3] = vb ? ld32(pb + 8) : 0u;
+  }
+  float acc[8][4];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+    const bf16* pB = B + (int64_t)(c0 + 8 * i + g) * R + 2 * t;   // B operand: (k = j, n = column)
+#pragma unroll
+    for (int kk = 0; kk < KS; ++kk) mma16816(acc[i], a[kk], ld32g(pB + 16 * kk), ld32g(pB + 16 * kk + 8));
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int c = c0 + 8 * i + 2 * t;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int64_t row = h ? rb : ra;
+      if (!(h ? vb : va)) continue;
+      const int64_t off = row * N + c;
+      const float2 yv = up2(ld32g(y + off)), xv = up2(ld32g(x + off));
+      const float2 tv = up2(rn2(make_float2(__fmaf_rn(scale, acc[i][2 * h], yv.x), __fmaf_rn(scale, acc[i][2 * h + 1], yv.y))));
+      *reinterpret_cast<uint32_t*>(out + off) = rn2(make_float2(xv.x + tv.x, xv.y + tv.y));
+    }
   }
 }
 
@@ -1170,8 +1223,8 @@ extern "C" int mxm_rowdot(const void* A, int64_t lda, const void* B, int64_t T, 
   const unsigned grid = (unsigned)((T + 15) / 16);
   cudaStream_t st = (cudaStream_t)stream;
   auto go = [&](auto kern) {
-    kern<<<grid, 128, 0, st>>>((const bf16*)A, lda, (const bf16*)B, (int)T, (int)K, post, (bf16*)out, ldo, nullptr, 0,
-                               nullptr);
+    kern<<<grid, 128, 0, st>>>((const bf16*)A, lda, (const bf16*)B, (int)T, (int)K, post, 0, (bf16*)out, ldo, nullptr,
+                               0, nullptr, K, 0);
   };
   if (n == 16)
     go(k_rowdot<16, false>);
@@ -1197,6 +1250,96 @@ extern "C" int mxm_lora_prep(const void* Ag, const void* Au, const void* Bg, con
   return mx_launch_status("lora prep");
 }
 
+// The reference's lora_bwd in its LoRA mode (scripts/mxfp8.py:219-263) for one branch:
+//   dxa_out [T, r] = bf16(scale * dy Bt^T)  (dy [T, N], Bt = B^T [r, N])      -- one rounding
+//   dB_out  [N, r] = scale * dy^T xa        (fp32, fixed-order partial sums)
+//   q / s (optional): row-wise MXFP8 of dy into columns col_tile_off*128 .. of a [ceil128(T), s_cols] operand,
+//   from the same read of dy as dxa.
+extern "C" int mxm_lora_bwd(const void* dy, int64_t ldy, int64_t T, int64_t N, const void* xa, int64_t ldxa,
+                            const void* Bt, int r, float scale, void* q, int64_t ldq, void* s, int64_t s_cols,
+                            int64_t col_tile_off, void* dxa_out, int64_t ld_dxa, void* dB_out, void* part,
+                            int rows_per_chunk, int chunks, void* stream) {
+  MX_CHECK_ARG(dy && xa && Bt && dxa_out && dB_out && part, "mxm_lora_bwd: null pointer");
+  MX_CHECK_ARG(T >= 1 && T < (1ll << 31) && N >= 128 && N % 128 == 0 && (r == 16 || r == 32 || r == 64) &&
+                   ldy % 8 == 0 && ldxa % 8 == 0 && ld_dxa % 2 == 0,
+               "mxm_lora_bwd: need N %% 128 == 0, r in {16, 32, 64}, ldy and ldxa multiples of 8");
+  MX_CHECK_ARG(mx_aligned(dy, 16) && mx_aligned(xa, 16) && mx_aligned(Bt, 16) && mx_aligned(dxa_out, 4),
+               "mxm_lora_bwd: alignment");
+  MX_CHECK_ARG((q == nullptr) == (s == nullptr), "mxm_lora_bwd: q and s go together");
+  if (q) {
+    MX_CHECK_ARG(s_cols % 128 == 0 && col_tile_off >= 0 && col_tile_off * 128 + N <= s_cols && ldq >= s_cols &&
+                     ldq % 8 == 0 && mx_aligned(q, 8),
+                 "mxm_lora_bwd: quantized columns outside the %lld-column operand", (long long)s_cols);
+  }
+  cudaStream_t st = (cudaStream_t)stream;
+  const unsigned grid = q ? (unsigned)((T + 127) / 128 * 8) : (unsigned)((T + 15) / 16);
+  uint8_t* qc = q ? (uint8_t*)q + col_tile_off * 128 : nullptr;
+  auto go = [&](auto kern) {
+    kern<<<grid, 128, 0, st>>>((const bf16*)dy, ldy, (const bf16*)Bt, (int)T, (int)N, scale, 1, (bf16*)dxa_out,
+                               ld_dxa, qc, ldq, (uint8_t*)s, s_cols, (int)(col_tile_off * 4));
+  };
+  if (q) {
+    if (r == 16) go(k_rowdot<16, true>);
+    else if (r == 32) go(k_rowdot<32, true>);
+    else go(k_rowdot<64, true>);
+  } else {
+    if (r == 16) go(k_rowdot<16, false>);
+    else if (r == 32) go(k_rowdot<32, false>);
+    else go(k_rowdot<64, false>);
+  }
+  mx_note_launch();
+  if (int e = mx_launch_status("lora bwd rowdot")) return e;
+  // dB = scale * dy^T xa: the coldot with an fp32, unrounded result
+  MX_CHECK_ARG(rows_per_chunk % CD_ROWS == 0 && rows_per_chunk > 0 && (int64_t)rows_per_chunk * chunks >= T,
+               "mxm_lora_bwd: bad chunking");
+  CUtensorMap ta, te;
+  if (int e = mx_make_tmap_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, dy, (uint64_t)N, (uint64_t)T, (uint64_t)(ldy * 2),
+                              CD_COLS, CD_ROWS, CU_TENSOR_MAP_SWIZZLE_128B))
+    return e;
+  if (int e = mx_make_tmap_2d(&te, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, xa, (uint64_t)r, (uint64_t)T,
+                              (uint64_t)(ldxa * 2), (uint32_t)r, CD_ROWS,
+                              r == 16 ? CU_TENSOR_MAP_SWIZZLE_32B
+                                      : (r == 32 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B)))
+    return e;
+  dim3 cgrid((unsigned)(N / CD_COLS), (unsigned)chunks);
+  auto goc = [&](auto kern, int nj) -> int {
+    const size_t smem = cd_smem(nj);
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return mx_cuda_status(e, "lora bwd: set smem");
+    kern<<<cgrid, 160, smem, st>>>(ta, te, (int)N, rows_per_chunk, (int)T, (float*)part, mx_dev_error_ptr());
+    mx_note_launch();
+    return mx_launch_status("lora bwd coldot");
+  };
+  if (int e = r == 16 ? goc(k_coldot<16>, 16) : (r == 32 ? goc(k_coldot<32>, 32) : goc(k_coldot<64>, 64))) return e;
+  const int64_t nn = N * r;
+  k_sum_parts<<<grid_for(nn, 256), 256, 0, st>>>((const float*)part, chunks, nn, nn, scale, 1.f, (float*)dB_out,
+                                                 nullptr, 0, 0, 0);
+  mx_note_launch();
+  return mx_launch_status("lora bwd sum");
+}
+
+// out = bf16(x + bf16(y + scale * xa B^T)), x / y / out [T, N] bf16 contiguous, xa [T, r] (row stride ldxa),
+// B [N, r] contiguous (reference res_lora, scripts/mxfp8.py:285-296).
+extern "C" int mxm_res_lora(const void* x, const void* y, const void* xa, int64_t ldxa, const void* B, int64_t T,
+                            int64_t N, int r, float scale, void* out, void* stream) {
+  MX_CHECK_ARG(x && y && xa && B && out, "mxm_res_lora: null pointer");
+  MX_CHECK_ARG(T >= 1 && T * N < (1ll << 31) && N % 64 == 0 && (r == 16 || r == 32 || r == 64) && ldxa % 2 == 0,
+               "mxm_res_lora: need N %% 64 == 0, r in {16, 32, 64}");
+  MX_CHECK_ARG(mx_aligned(x, 4) && mx_aligned(y, 4) && mx_aligned(out, 4) && mx_aligned(xa, 4) && mx_aligned(B, 4),
+               "mxm_res_lora: alignment");
+  dim3 grid((unsigned)((T + 63) / 64), (unsigned)(N / 64));
+  cudaStream_t st = (cudaStream_t)stream;
+  auto go = [&](auto kern) {
+    kern<<<grid, 128, 0, st>>>((const bf16*)x, (const bf16*)y, (const bf16*)xa, ldxa, (const bf16*)B, (int)T, (int)N,
+                               scale, (bf16*)out);
+  };
+  if (r == 16) go(k_res_lora<16>);
+  else if (r == 32) go(k_res_lora<32>);
+  else go(k_res_lora<64>);
+  mx_note_launch();
+  return mx_launch_status("res lora");
+}
+
 extern "C" int mxm_rowdot_quant(const void* A, int64_t lda, const void* B, int64_t T, int64_t K, int n, float post,
                                 void* out, int64_t ldo, void* q, int64_t ldq, void* s, void* stream) {
   MX_CHECK_ARG(A && B && out && q && s, "mxm_rowdot_quant: null pointer");
@@ -1208,8 +1351,8 @@ extern "C" int mxm_rowdot_quant(const void* A, int64_t lda, const void* B, int64
   const unsigned grid = (unsigned)((T + 127) / 128 * 8);  // 16-row CTAs over the padded rows
   cudaStream_t st = (cudaStream_t)stream;
   auto go = [&](auto kern) {
-    kern<<<grid, 128, 0, st>>>((const bf16*)A, lda, (const bf16*)B, (int)T, (int)K, post, (bf16*)out, ldo,
-                               (uint8_t*)q, ldq, (uint8_t*)s);
+    kern<<<grid, 128, 0, st>>>((const bf16*)A, lda, (const bf16*)B, (int)T, (int)K, post, 0, (bf16*)out, ldo,
+                               (uint8_t*)q, ldq, (uint8_t*)s, K, 0);
   };
   if (n == 16)
     go(k_rowdot<16, true>);

@@ -53,7 +53,8 @@ __device__ __forceinline__ void unpack8(const uint4& u, float (&v)[8]) {
 template <bool ROWS, bool COLS>
 __global__ void __launch_bounds__(QT) k_quant(const __nv_bfloat16* __restrict__ x, int64_t R, int64_t K, int64_t ldx,
                                              uint8_t* __restrict__ q, int64_t ldq, uint8_t* __restrict__ s,
-                                             uint8_t* __restrict__ qt, uint8_t* __restrict__ st) {
+                                             uint8_t* __restrict__ qt, uint8_t* __restrict__ st, int64_t s_tiles,
+                                             int64_t tile_off) {
   __shared__ __align__(16) uint8_t s_rows[512];
   __shared__ __align__(16) uint8_t s_cols[512];
   extern __shared__ __align__(16) uint16_t s_tile[];  // [128][128] bf16 bits (COLS only)
@@ -121,7 +122,7 @@ __global__ void __launch_bounds__(QT) k_quant(const __nv_bfloat16* __restrict__ 
   __syncthreads();
   if (tid < 32) {
     if (ROWS) {
-      uint8_t* dst = s + ((int64_t)blockIdx.x * (K >> 7) + blockIdx.y) * 512;
+      uint8_t* dst = s + ((int64_t)blockIdx.x * s_tiles + tile_off + blockIdx.y) * 512;
       reinterpret_cast<uint4*>(dst)[tid] = reinterpret_cast<const uint4*>(s_rows)[tid];
     }
   } else if (tid < 64) {
@@ -142,9 +143,12 @@ int check_common(const void* x, int64_t R, int64_t K, int64_t ldx, const char* f
   return MXM_OK;
 }
 
+// s_tiles / tile_off: the row-wise scales go to 128-column tiles tile_off .. of the blocked layout of an
+// operand s_tiles * 128 columns wide (the codes' columns are placed by the caller through q).
 template <bool ROWS, bool COLS>
 int launch(const void* x, int64_t R, int64_t K, int64_t ldx, void* q, int64_t ldq, void* s, void* qt, void* st,
-           void* stream) {
+           void* stream, int64_t s_tiles = -1, int64_t tile_off = 0) {
+  if (s_tiles < 0) s_tiles = K >> 7;
   const size_t smem = COLS ? 128 * 128 * sizeof(uint16_t) : 0;
   if (COLS) {
     cudaError_t e = cudaFuncSetAttribute(k_quant<ROWS, COLS>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -152,7 +156,7 @@ int launch(const void* x, int64_t R, int64_t K, int64_t ldx, void* q, int64_t ld
   }
   dim3 grid((unsigned)((R + 127) / 128), (unsigned)(K / 128));
   k_quant<ROWS, COLS><<<grid, QT, smem, (cudaStream_t)stream>>>(
-      (const __nv_bfloat16*)x, R, K, ldx, (uint8_t*)q, ldq, (uint8_t*)s, (uint8_t*)qt, (uint8_t*)st);
+      (const __nv_bfloat16*)x, R, K, ldx, (uint8_t*)q, ldq, (uint8_t*)s, (uint8_t*)qt, (uint8_t*)st, s_tiles, tile_off);
   mx_note_launch();
   return mx_launch_status("quant kernel launch");
 }
@@ -166,6 +170,21 @@ extern "C" int mxm_quant_rows(const void* x, int64_t R, int64_t K, int64_t ldx, 
   MX_CHECK_ARG(ldq >= K && ldq % 8 == 0 && mx_aligned(q, 8), "mxm_quant_rows: bad code buffer stride/alignment");
   MX_CHECK_ARG(mx_aligned(s, 16), "mxm_quant_rows: scale buffer not 16-byte aligned");
   return launch<true, false>(x, R, K, ldx, q, ldq, s, nullptr, nullptr, stream);
+}
+
+// Row-wise MXFP8 of x [R, K] into columns col_tile_off*128 .. of a wider MX operand [R, s_cols]: codes at
+// q[r * ldq + col_tile_off*128 + c], scales in that operand's blocked layout (reference lora_bwd's
+// quantize-only mode, scripts/mxfp8.py:219-246, used to build one K-concatenated dy for a group's dx).
+extern "C" int mxm_quant_rows_into(const void* x, int64_t R, int64_t K, int64_t ldx, void* q, int64_t ldq, void* s,
+                                   int64_t s_cols, int64_t col_tile_off, void* stream) {
+  if (int st = check_common(x, R, K, ldx, "mxm_quant_rows_into")) return st;
+  MX_CHECK_ARG(q && s, "mxm_quant_rows_into: null output");
+  MX_CHECK_ARG(s_cols % 128 == 0 && col_tile_off >= 0 && (col_tile_off * 128 + K) <= s_cols && ldq >= s_cols &&
+                   ldq % 8 == 0 && mx_aligned(q, 8) && mx_aligned(s, 16),
+               "mxm_quant_rows_into: columns [%lld, %lld) outside the %lld-column operand or bad buffers",
+               (long long)(col_tile_off * 128), (long long)(col_tile_off * 128 + K), (long long)s_cols);
+  return launch<true, false>(x, R, K, ldx, (uint8_t*)q + col_tile_off * 128, ldq, s, nullptr, nullptr, stream,
+                             s_cols >> 7, col_tile_off);
 }
 
 extern "C" int mxm_quant_cols(const void* x, int64_t R, int64_t K, int64_t ldx, void* qt, void* st, void* stream) {

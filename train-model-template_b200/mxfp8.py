@@ -14,7 +14,11 @@ on B200 (sm_100a) kernels.  Drop-in for the reference module of the same name
 * ``enable_mxfp8`` / ``disable_mxfp8`` / ``is_mx`` / ``mx_wt`` / ``wt_of`` / ``group_wt`` -- the frozen
   weight layout builder (scripts/mxfp8.py:398-509), including the shared gate|up pair that
   ``fused_mlp`` consumes.
+* ``lora_bwd`` / ``res_lora`` -- the LoRA backward of an MX linear from one read of dy (MXFP8 of dy into a
+  K-concatenated buffer + d(xa) + dB) and the residual add with the LoRA term, used by ``fused_linear``
+  (scripts/mxfp8.py:88-296).
 """
+import ctypes
 import os
 import types
 import weakref
@@ -102,6 +106,71 @@ def mx_mm(a, b, scale_a, scale_b, out=None):
     _nx.call("mxm_gemm", _nx.ptr(a), a.stride(0), _nx.ptr(scale_a), _nx.ptr(bt), bt.stride(0), _nx.ptr(scale_b),
              M, N, K, _nx.ptr(out), out.stride(0), _nx.stream_of(a))
     return out
+
+
+# ---------------------------------------------------------------------------------------------- LoRA backward
+_rowdot_ns = (16, 32, 64)
+
+
+def _native_lora_ok(dy, xa, B, R):
+    return (R in _rowdot_ns and dy.stride(0) % 8 == 0 and xa.stride(0) % 8 == 0 and xa.data_ptr() % 16 == 0
+            and dy.data_ptr() % 16 == 0 and B.data_ptr() % 16 == 0)
+
+
+def lora_bwd(dy, xa=None, B=None, scale=1.0, q=None, s=None, col_tile_off=0, dxa_out=None):
+    """One read of dy [T, N] bf16 (rows contiguous) for a LoRA branch over an MX base weight
+    (scripts/mxfp8.py:219-263): with q / s, dy's row-wise MXFP8 goes into columns col_tile_off*128 .. of the
+    K-concatenated q [T, sum N] (scales in q's blocked layout, byte-identical to mx_quant(dy)); with a
+    LoRA branch (xa [T, r] = its columns of x S^T, B [N, r] bf16 contiguous) scale * dy @ B is written,
+    rounded once to bf16, into dxa_out [T, r] and dB = scale * dy^T @ xa is returned in fp32."""
+    T, N = dy.shape
+    assert dy.dtype == torch.bfloat16 and dy.stride(1) == 1 and N % 128 == 0, (dy.dtype, dy.shape, dy.stride())
+    has_lora, do_q = xa is not None, q is not None
+    if not (has_lora or do_q):
+        return None
+    assert T * max(dy.stride(0), q.shape[1] if do_q else 0) < 2**31
+    if do_q:
+        assert q.shape[0] == T and q.shape[1] % 128 == 0 and q.stride(1) == 1, (q.shape, q.stride())
+        assert s.numel() == scale_numel(T, q.shape[1]), (s.numel(), T, q.shape)
+    if not has_lora:
+        _nx.call("mxm_quant_rows_into", _nx.ptr(dy), T, N, dy.stride(0), _nx.ptr(q), q.stride(0), _nx.ptr(s),
+                 q.shape[1], col_tile_off, _nx.stream_of(dy))
+        return None
+    R = xa.shape[1]
+    assert xa.stride(1) == 1 and B.is_contiguous() and B.shape == (N, R) and B.dtype == torch.bfloat16
+    assert dxa_out.shape == (T, R) and dxa_out.stride(1) == 1
+    if not _native_lora_ok(dy, xa, B, R):
+        # ranks / layouts the kernels do not take: the same products with torch GEMMs (fp32 accumulate)
+        if do_q:
+            lora_bwd(dy, q=q, s=s, col_tile_off=col_tile_off)
+        dxa_out.copy_(((dy.float() @ B.float()) * scale).to(dxa_out.dtype))
+        return (dy.t().float() @ xa.float()) * scale
+    Bt = B.t().contiguous()                                            # [r, N]: rows of the rowdot operand
+    rpc, nch = ctypes.c_int(0), ctypes.c_int(0)
+    _nx.call("mxm_coldot_chunks", T, N, _nx.ctypes_ref(rpc), _nx.ctypes_ref(nch))
+    part = torch.empty((nch.value, N, R), dtype=torch.float32, device=dy.device)
+    dB = torch.empty((N, R), dtype=torch.float32, device=dy.device)
+    _nx.call("mxm_lora_bwd", _nx.ptr(dy), dy.stride(0), T, N, _nx.ptr(xa), xa.stride(0), _nx.ptr(Bt), R,
+             float(scale), _nx.ptr(q) if do_q else None, q.stride(0) if do_q else 0, _nx.ptr(s) if do_q else None,
+             q.shape[1] if do_q else 0, col_tile_off, _nx.ptr(dxa_out), dxa_out.stride(0), _nx.ptr(dB),
+             _nx.ptr(part), rpc.value, nch.value, _nx.stream_of(dy))
+    return dB
+
+
+def res_lora(x, y, xa, B, scale):
+    """x + (y + scale * xa @ B^T) with the reference's two bf16 roundings (addmm, then the residual add), for
+    x, y [T, N] bf16 contiguous, xa [T, r] (any row stride), B [N, r] contiguous -- scripts/mxfp8.py:285-296."""
+    T, N = x.shape
+    assert T * N < 2**31 and N % 128 == 0
+    out = torch.empty_like(x)
+    R = xa.shape[1]
+    if (R in _rowdot_ns and xa.stride(1) == 1 and xa.stride(0) % 2 == 0 and x.is_contiguous() and y.is_contiguous()
+            and B.is_contiguous() and x.dtype == y.dtype == B.dtype == xa.dtype == torch.bfloat16):
+        _nx.call("mxm_res_lora", _nx.ptr(x), _nx.ptr(y), _nx.ptr(xa), xa.stride(0), _nx.ptr(B), T, N, R,
+                 float(scale), _nx.ptr(out), _nx.stream_of(x))
+        return out
+    t = (y.float() + scale * (xa.float() @ B.float().t())).to(torch.bfloat16)
+    return out.copy_((x.float() + t.float()).to(x.dtype))
 
 
 # ---------------------------------------------------------------------------------------------- MX linears
