@@ -101,6 +101,17 @@ int mxm_mlp_fwd_epilogue(const void* gu, const void* xs, const void* bg, const v
                          int64_t N, int r, float s_g, float s_u, void* qh, void* sh, void* xsd, void* xsd_part,
                          int col_groups, void* stream);
 
+/* The gate|up GEMM with the forward epilogue fused in (reference gu GEMM + _fwd_kernel, scripts/fused_mlp.py:
+ * 279-282 and :81-109): gu [M, 2N] bf16 = [x W_gate^T | x W_up^T] from MX codes qa [M, K] and qb = W_gu [2N, K]
+ * (rows: gate then up) with their blocked scales; and from the same tiles qh / sh = MXFP8(h) [M, N],
+ * h = bf16(silu(g) u), g = bf16(gu_gate + s_g xs_g bg^T), u likewise, and xsd [M, r] bf16 = bf16(h ad^T).
+ * xs [M, 2r] bf16 contiguous, bg / bu [N, r], ad [r, N] bf16 contiguous; r = 16; N % 128 == 0.
+ * xsd_part: fp32 scratch of slots * M * r elements (mxm_gemm_glu_partition). */
+int mxm_gemm_glu_partition(int64_t M, int64_t N, int* per, int* grid, int* slots);
+int mxm_gemm_glu(const void* qa, int64_t lda, const void* sa, const void* qb, int64_t ldb, const void* sb, int64_t M,
+                 int64_t N, int64_t K, void* gu, const void* xs, const void* bg, const void* bu, const void* ad, int r,
+                 float s_g, float s_u, void* qh, void* sh, void* xsd_part, void* xsd, void* stream);
+
 /* Super-block rows and column-group count for the backward epilogue (reference _bwd_grid,
  * scripts/fused_mlp.py:218-232). */
 int mxm_mlp_bwd_partitions(int64_t T, int64_t N, int r, int* super_block, int* col_groups);

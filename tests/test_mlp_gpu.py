@@ -135,3 +135,35 @@ def test_need_out_false_and_determinism():
     _, dx3, g3 = _run(*case, s, need_out=False)
     assert torch.equal(dx1, dx3)
     assert all(torch.equal(a, b) for a, b in zip(g1, g3))
+
+
+@pytest.mark.parametrize("T,H,N", [(1, 1024, 3584), (77, 1024, 3584), (1000, 2048, 6144), (2049, 1024, 3584),
+                                   (4096, 2048, 6144)])
+def test_gemm_glu_matches_two_passes(T, H, N):
+    """The gate|up GEMM with the fused forward epilogue gives the same gu and the same MXFP8(h) bytes as the
+    GEMM followed by the separate epilogue kernel; xS_down differs only by the fp32 summation order."""
+    import fused_mlp
+    import mxfp8
+    g = torch.Generator().manual_seed(T + N)
+    dev = torch.device("cuda")
+    x = torch.randn(T, H, generator=g).to(torch.bfloat16).to(dev)
+    w = (torch.randn(2 * N, H, generator=g) * 0.02).to(torch.bfloat16).to(dev)
+    r = 16
+    xs = (torch.randn(T, 2 * r, generator=g) * 0.5).to(torch.bfloat16).to(dev)
+    bg = (torch.randn(N, r, generator=g) * 0.05).to(torch.bfloat16).to(dev)
+    bu = (torch.randn(N, r, generator=g) * 0.05).to(torch.bfloat16).to(dev)
+    ad = (torch.randn(r, N, generator=g) * 0.05).to(torch.bfloat16).to(dev)
+    q, sc = mxfp8.mx_quant(x)
+    qw, sw = mxfp8.mx_quant(w)
+    gu, qh, sh, xsd = fused_mlp.gemm_glu(q, sc, qw, sw, xs, bg, bu, ad, 2.0, 2.0)
+    gu0 = mxfp8.mx_mm(q, qw.t(), sc, sw)
+    qh0, sh0, xsd0 = fused_mlp.mlp_fwd(gu0, xs, bg, bu, ad, 2.0, 2.0, True)
+    torch.cuda.synchronize()
+    import _mxlib
+    assert _mxlib.device_error() == 0
+    assert torch.equal(gu, gu0)
+    assert torch.equal(qh.view(torch.uint8), qh0.view(torch.uint8))
+    assert torch.equal(sh.view(torch.uint8), sh0.view(torch.uint8))
+    d = (xsd.float() - xsd0.float()).abs()
+    assert float(d.max()) <= float(xsd0.float().abs().max()) * 2.0 ** -7 + 1e-6
+    assert float((xsd != xsd0).float().mean()) < 0.01

@@ -33,6 +33,10 @@ _SIGS = {
     "mxm_quant_both": [_vp, _i64, _i64, _i64, _vp, _vp, _vp, _vp, _vp],
     "mxm_gemm": [_vp, _i64, _vp, _vp, _i64, _vp, _i64, _i64, _i64, _vp, _i64, _vp],
     "mxm_gemm_lora": [_vp, _i64, _vp, _vp, _i64, _vp, _i64, _i64, _i64, _vp, _i64, _vp, _int, _vp, _i64, _vp],
+    "mxm_gemm_glu_partition": [_i64, _i64, ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_int),
+                               ctypes.POINTER(ctypes.c_int)],
+    "mxm_gemm_glu": [_vp, _i64, _vp, _vp, _i64, _vp, _i64, _i64, _i64, _vp, _vp, _vp, _vp, _vp, _int, ctypes.c_float,
+                     ctypes.c_float, _vp, _vp, _vp, _vp, _vp],
     "mxm_mlp_fwd_partitions": [_i64, _i64, _int, ctypes.POINTER(ctypes.c_int)],
     "mxm_mlp_fwd_epilogue": [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _int, ctypes.c_float, ctypes.c_float, _vp, _vp,
                              _vp, _vp, _int, _vp],

@@ -1,0 +1,123 @@
+// Element-wise helpers shared by the memory-bound MLP epilogues (csrc/mx_mlp.cu) and the GEMM with the
+// fused SwiGLU epilogue (csrc/mx_gemm.cu): packed f32x2 / bf16x2 arithmetic, the MXFP8 quantization of a
+// warp tile held in mma D-fragment form, predicated stores, and the shared-memory swizzle of TMA tiles.
+#pragma once
+#include "mx_mma.cuh"
+
+MX_DEV float nanmax(float a, float b) {
+  float r;
+  asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+  return r;
+}
+// Two floats -> two E4M3 codes (RNE, saturating: |v| <= 448 after the power-of-two block scaling,
+// and +-inf saturates to +-448 exactly as the reference's clamp does).
+MX_DEV uint32_t e4m3x2_sat(float lo, float hi) {
+  uint16_t r;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
+// Predicated global stores (no branch around them).
+MX_DEV void stg16_if(void* p, uint32_t v, bool pred) {
+  asm volatile("{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %2, 0;\n\t@q st.global.b16 [%0], %1;\n\t}" ::"l"(p),
+               "h"((uint16_t)v), "r"((int)pred));
+}
+MX_DEV void stg8_if(void* p, uint32_t v, bool pred) {
+  asm volatile("{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %2, 0;\n\t@q st.global.b8 [%0], %1;\n\t}" ::"l"(p),
+               "h"((uint16_t)v), "r"((int)pred));
+}
+
+// ---- packed helpers: two values per instruction (Blackwell f32x2 ALU ops, bf16x2 conversions)
+MX_DEV float2 up2(uint32_t p) { return make_float2(bf16_lo(p), bf16_hi(p)); }
+MX_DEV uint32_t rn2(float2 v) { return pack_bf16x2(v.x, v.y); }   // round both to bf16 (RNE)
+MX_DEV float ex2a(float x) {
+  float r;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
+MX_DEV float rcpa(float x) {
+  float r;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
+// sigmoid(g) = 1 / (1 + exp(-g)) for a pair (exp via ex2 of -g*log2(e))
+MX_DEV float2 sigmoid2(float2 g) {
+  const float2 t = __fmul2_rn(g, make_float2(-1.4426950408889634f, -1.4426950408889634f));
+  return make_float2(rcpa(ex2a(t.x) + 1.0f), rcpa(ex2a(t.y) + 1.0f));
+}
+MX_DEV uint32_t absmax_bf16x2(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("{\n\t.reg .b32 x, y;\n\tabs.bf16x2 x, %1;\n\tabs.bf16x2 y, %2;\n\tmax.NaN.bf16x2 %0, x, y;\n\t}"
+      : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+MX_DEV uint32_t max_bf16x2(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("max.NaN.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+
+// Per-thread store targets of the MX output of one 16-row warp tile (rows g and g + 8), fixed for the
+// whole kernel: the code row pointers (+ 2t), the scale bytes of k-block 0, and the store predicates
+// (codes for rows < T; scales for rows < Tpad, written by lane t = 0 of the quad).
+struct QRows {
+  uint8_t* code[2];
+  uint8_t* scale[2];
+  bool live[2], slive[2];
+};
+MX_DEV QRows qrows_init(int64_t row_g, int64_t T, int64_t Tpad, uint8_t* q, int64_t ldq, uint8_t* s, int64_t scols,
+                        int t) {
+  QRows r;
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int64_t row = row_g + 8 * h;
+    r.live[h] = row < T;
+    r.slive[h] = t == 0 && row < Tpad;
+    r.code[h] = q ? q + (r.live[h] ? row : 0) * ldq + 2 * t : nullptr;
+    r.scale[h] = s ? s + mx_scale_offset(row < Tpad ? row : 0, 0, scols) : nullptr;
+  }
+  return r;
+}
+
+// Quantizes one 32-column block (columns col0 .. col0+31, col0 % 32 == 0) of a 16-row warp tile whose
+// bf16 values are held packed in D-fragment form: pk[i][h] = (row g + 8h, cols 8i+2t, +1), i = 0..3
+// (t = lane % 4).  Codes and the two rows' scales go to the targets of `qr`.
+MX_DEV void quant_block16p(const uint32_t (&pk)[4][2], const QRows& qr, int64_t col0, int t) {
+  const int64_t soff = ((col0 >> 7) << 9) + ((col0 >> 5) & 3);  // k-block col0/32 in the blocked layout
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const uint32_t m2 = max_bf16x2(absmax_bf16x2(pk[0][h], pk[1][h]), absmax_bf16x2(pk[2][h], pk[3][h]));
+    float m = nanmax(bf16_lo(m2), bf16_hi(m2));
+    m = nanmax(m, __shfl_xor_sync(0xffffffffu, m, 1));
+    m = nanmax(m, __shfl_xor_sync(0xffffffffu, m, 2));
+    const uint32_t e = mx_e8m0_of_amax(m);
+    const float rcp = mx_e8m0_rcp(e);
+    uint8_t* dst = qr.code[h] + col0;
+    const float2 r2 = make_float2(rcp, rcp);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 v = __fmul2_rn(up2(pk[i][h]), r2);
+      stg16_if(dst + 8 * i, e4m3x2_sat(v.x, v.y), qr.live[h]);
+    }
+    stg8_if(qr.scale[h] + soff, e, qr.slive[h]);
+  }
+}
+
+// Byte offset of 16-byte chunk `chunk` of row `row` in a tile with RB-byte rows stored by TMA with the
+// matching RB-byte swizzle (RB = 32, 64, 128): chunk bits [4, 4+b) are XORed with address bits [7, 7+b).
+template <int RB>
+MX_DEV uint32_t swz(uint32_t row, uint32_t chunk) {
+  constexpr uint32_t SH = RB == 128 ? 0 : (RB == 64 ? 1 : 2), MK = RB / 16 - 1;
+  return row * RB + ((chunk ^ ((row >> SH) & MK)) << 4);
+}
+template <int RB>
+__host__ __device__ constexpr CUtensorMapSwizzle swz_mode() {
+  return RB == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : (RB == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B);
+}
+
+// Rounds a pointer into dynamic shared memory up to 1024 bytes by pointer arithmetic, so the result
+// keeps the shared state space (and the compiler keeps emitting shared-memory instructions for it).
+MX_DEV uint8_t* align1024(uint8_t* p) { return p + ((1024u - (smem_u32(p) & 1023u)) & 1023u); }
+
+
+

@@ -23,7 +23,10 @@
 //               rest), then converts to bf16 and stores 16-byte vectors.
 // Every mbarrier wait is bounded (see mbar_wait): on a timeout the kernel records an error code in the
 // device flag and all roles fall through to the TMEM release and exit.
+#include <algorithm>
+
 #include "mx_common.cuh"
+#include "mx_epi.cuh"
 #include "mx_runtime.h"
 
 namespace {
@@ -243,6 +246,342 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   if (warp == 2) tmem_dealloc(tmem, TMEM_COLS);
 }
 
+// ------------------------------------------------------------------------------------------------
+// Gate|up GEMM with the SwiGLU-LoRA forward epilogue fused in (the reference's gu GEMM and _fwd_kernel,
+// scripts/fused_mlp.py:279-282 and :81-109).  A 128 x 256 tile pairs gate columns [128 tn, +128) with the
+// up columns N + 128 tn .. of the same 128 outputs: its B stage is two TMA boxes of W_gu rows (gate, up)
+// and its two B scale blocks are the matching ones, so one tcgen05 accumulator holds both halves of 128
+// (g, u) column pairs.  Producer / MMA warps as in k_mx_gemm (3 stages).  The 8 epilogue warps drain the
+// accumulator (warp q|h: lanes 32q.., half h = gate / up), hand it back, store gu (bf16; the backward
+// reads it) and stage the same bf16 tile in shared memory; after one named barrier each warp runs the
+// forward epilogue on 16 rows x 128 pairs of the staged tile -- the LoRA-B terms with mma.sync, SwiGLU,
+// the MXFP8 codes of h, and the per-row xS_down = h A_down^T accumulated in registers -- while the MMAs
+// of the next tile proceed.  A CTA works through a contiguous range of tiles (column tiles fastest), so
+// xS_down accumulates over the columns of a row block and is written as one fp32 partial per (row block,
+// CTA); a fixed-order reduction sums them.  Rank 16 only (the rank-32 slices do not fit shared memory).
+constexpr int GLU_STAGES = 3;
+constexpr int GLU_B_BYTES = 256 * BK;
+constexpr int GLU_STAGING = 2 * 2 * 128 * 128;   // g | u halves, two [128 x 64] bf16 sub-tiles each
+__host__ __device__ constexpr int glu_slices(int R) { return 2 * 128 * R * 2 + R * 128 * 2; }
+__host__ __device__ constexpr size_t glu_ring() {
+  return ((size_t)GLU_STAGES * (A_BYTES + GLU_B_BYTES + SFA_BYTES + SFB_BYTES) + 1023) / 1024 * 1024;
+}
+__host__ __device__ constexpr size_t glu_smem(int R) { return 1024 + glu_ring() + GLU_STAGING + glu_slices(R) + 256; }
+
+MX_DEV void epi_sync() { asm volatile("bar.sync 1, %0;" ::"r"(EPI_THREADS) : "memory"); }
+
+template <int R>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    k_mx_gemm_glu(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                  const uint8_t* __restrict__ sa, const uint8_t* __restrict__ sb, int M, int N, int K,
+                  __nv_bfloat16* __restrict__ gu, const __nv_bfloat16* __restrict__ xs,
+                  const __nv_bfloat16* __restrict__ bg, const __nv_bfloat16* __restrict__ bu,
+                  const __nv_bfloat16* __restrict__ ad, float s_g, float s_u, uint8_t* __restrict__ qh,
+                  uint8_t* __restrict__ sh, float* __restrict__ xsd_part, int per, int* err) {
+  constexpr int STAGES = GLU_STAGES, KS = R / 16;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = sA + STAGES * A_BYTES;
+  uint8_t* sSFA = sB + STAGES * GLU_B_BYTES;
+  uint8_t* sSFB = sSFA + STAGES * SFA_BYTES;
+  uint8_t* stg = smem + glu_ring();          // [g | u][2 sub-tiles][128 rows x 128 B], 128-byte swizzle
+  uint8_t* sl = stg + GLU_STAGING;           // Bg, Bu [128 x R] (2R-byte swizzle), Ad [2][R x 128 B]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sl + glu_slices(R));
+  uint64_t* full = bars;
+  uint64_t* empty = bars + STAGES;
+  uint64_t* tmem_full = bars + 2 * STAGES;
+  uint64_t* tmem_empty = tmem_full + 1;
+  uint32_t* tmem_base = reinterpret_cast<uint32_t*>(tmem_full + 2);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int num_m = (M + BM - 1) / BM;
+  const int num_n = N / 128;
+  const int num_tiles = num_m * num_n;
+  const int KT = K / BK;
+  const int t_lo = blockIdx.x * per, t_hi = min(t_lo + per, num_tiles);
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < STAGES; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    mbar_init(tmem_full, 1);
+    mbar_init(tmem_empty, EPI_THREADS);
+    fence_barrier_init();
+  }
+  if (warp == 2) tmem_alloc(tmem_base, TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_base;
+  constexpr int SFA_COL = 256, SFB_COL = 260;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      prefetch_tmap(&tmA);
+      prefetch_tmap(&tmB);
+    }
+    int stage = 0;
+    uint32_t phase = 0;
+    bool ok = true;
+    for (int tile = t_lo; tile < t_hi && ok; ++tile) {
+      const int tm = tile / num_n, tn = tile % num_n;
+      for (int kt = 0; kt < KT; ++kt) {
+        if (!mbar_wait(&empty[stage], phase ^ 1, err, MX_DEV_TIMEOUT_PRODUCER)) {
+          ok = false;
+          break;
+        }
+        if (lane == 0) {
+          uint64_t* fb = &full[stage];
+          mbar_arrive_expect_tx(fb, A_BYTES + GLU_B_BYTES + SFA_BYTES + SFB_BYTES);
+          tma_load_2d(sA + stage * A_BYTES, &tmA, fb, kt * BK, tm * BM);
+          tma_load_2d(sB + stage * GLU_B_BYTES, &tmB, fb, kt * BK, tn * 128);             // gate rows
+          tma_load_2d(sB + stage * GLU_B_BYTES + 128 * BK, &tmB, fb, kt * BK, N + tn * 128); // up rows
+          bulk_load(sSFA + stage * SFA_BYTES, sa + ((int64_t)tm * KT + kt) * 512, 512, fb);
+          bulk_load(sSFB + stage * SFB_BYTES, sb + ((int64_t)tn * KT + kt) * 512, 512, fb);
+          bulk_load(sSFB + stage * SFB_BYTES + 512, sb + ((int64_t)(num_n + tn) * KT + kt) * 512, 512, fb);
+        }
+        __syncwarp();
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+    }
+  } else if (warp == 1) {
+    int stage = 0;
+    uint32_t phase = 0, acc_phase = 0;
+    bool ok = true;
+    for (int tile = t_lo; tile < t_hi && ok; ++tile) {
+      if (!mbar_wait(tmem_empty, acc_phase ^ 1, err, MX_DEV_TIMEOUT_MMA_TMEM)) break;
+      tc_fence_after();
+      for (int kt = 0; kt < KT; ++kt) {
+        if (!mbar_wait(&full[stage], phase, err, MX_DEV_TIMEOUT_MMA)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        if (lane == 0) {
+          const uint32_t sfa = smem_u32(sSFA + stage * SFA_BYTES);
+          const uint32_t sfb = smem_u32(sSFB + stage * SFB_BYTES);
+          tmem_cp_32x128b_x4(tmem + SFA_COL, make_sdesc(sfa, 0, 128, 0));
+          tmem_cp_32x128b_x4(tmem + SFB_COL, make_sdesc(sfb, 0, 128, 0));
+          tmem_cp_32x128b_x4(tmem + SFB_COL + 4, make_sdesc(sfb + 512, 0, 128, 0));
+          const uint32_t a0 = smem_u32(sA + stage * A_BYTES);
+          const uint32_t b0 = smem_u32(sB + stage * GLU_B_BYTES);
+#pragma unroll
+          for (int k = 0; k < BK / 32; ++k) {
+            const uint64_t adsc = make_sdesc(a0 + k * 32, 0, 1024, 2);
+            const uint64_t bdsc = make_sdesc(b0 + k * 32, 0, 1024, 2);
+            umma_mxf8(tmem, adsc, bdsc, mx_idesc(BM, 256, k, k), tmem + SFA_COL, tmem + SFB_COL, (kt | k) != 0);
+          }
+          umma_commit(&empty[stage]);
+        }
+        __syncwarp();
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+      if (!ok) break;
+      if (lane == 0) umma_commit(tmem_full);
+      __syncwarp();
+      acc_phase ^= 1;
+    }
+  } else if (warp >= EPI_WARP0) {
+    const int e = warp - EPI_WARP0;            // SwiGLU rows 16e .. 16e+15 of a tile
+    const int q = warp & 3, h = e >> 2;        // drain: TMEM lanes 32q .., accumulator half h (0 gate, 1 up)
+    const int g = lane >> 2, t = lane & 3, mi = lane >> 3, lr = lane & 7;
+    const int et = e * 32 + lane;              // 0 .. 255
+    const int64_t Tpad = (int64_t)num_m * BM;
+    const int lrow = e * 16 + (mi & 1) * 8 + lr;
+    uint32_t o_gu[4], o_b[4][KS], o_ad[4][KS];
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+      o_gu[p] = swz<128>((uint32_t)lrow, (uint32_t)(2 * p + (mi >> 1)));
+#pragma unroll
+      for (int kk = 0; kk < KS; ++kk) {
+        o_b[p][kk] = swz<2 * R>((uint32_t)(8 * (2 * p + (mi >> 1)) + lr), (uint32_t)(2 * kk + (mi & 1)));
+        o_ad[p][kk] = swz<128>((uint32_t)(16 * kk + 8 * (mi >> 1) + lr), (uint32_t)(2 * p + (mi & 1)));
+      }
+    }
+    const uint32_t s_stg = smem_u32(stg), s_bg = smem_u32(sl), s_bu = s_bg + 128 * R * 2, s_ad = s_bu + 128 * R * 2;
+    const float2 sg2 = make_float2(s_g, s_g), su2 = make_float2(s_u, s_u);
+    float accx[R / 8][4];
+    uint32_t axg[KS][4], axu[KS][4];
+    QRows qr{};
+    int cur_tm = -1;
+    int64_t ra = 0, rb = 0;
+    auto flush = [&](int tm_done) {   // this CTA's partial of xS_down for its rows of row block tm_done
+      const int slot = (int)blockIdx.x - (tm_done * num_n) / per;
+      float* P = xsd_part + (int64_t)slot * M * R;
+#pragma unroll
+      for (int jt = 0; jt < R / 8; ++jt) {
+        const int c = 8 * jt + 2 * t;
+        if (ra < M) *reinterpret_cast<float2*>(P + ra * R + c) = make_float2(accx[jt][0], accx[jt][1]);
+        if (rb < M) *reinterpret_cast<float2*>(P + rb * R + c) = make_float2(accx[jt][2], accx[jt][3]);
+      }
+    };
+    uint32_t acc_phase = 0;
+    for (int tile = t_lo; tile < t_hi; ++tile) {
+      const int tm = tile / num_n, tn = tile % num_n;
+      if (tm != cur_tm) {
+        if (cur_tm >= 0) flush(cur_tm);
+        cur_tm = tm;
+        ra = (int64_t)tm * BM + e * 16 + g;
+        rb = ra + 8;
+        const bool va = ra < M, vb = rb < M;
+#pragma unroll
+        for (int kk = 0; kk < KS; ++kk) {
+          const __nv_bfloat16* pa = xs + ra * (2 * R) + 16 * kk + 2 * t;
+          const __nv_bfloat16* pb = xs + rb * (2 * R) + 16 * kk + 2 * t;
+          axg[kk][0] = va ? ld32(pa) : 0u;
+          axg[kk][1] = vb ? ld32(pb) : 0u;
+          axg[kk][2] = va ? ld32(pa + 8) : 0u;
+          axg[kk][3] = vb ? ld32(pb + 8) : 0u;
+          axu[kk][0] = va ? ld32(pa + R) : 0u;
+          axu[kk][1] = vb ? ld32(pb + R) : 0u;
+          axu[kk][2] = va ? ld32(pa + R + 8) : 0u;
+          axu[kk][3] = vb ? ld32(pb + R + 8) : 0u;
+        }
+#pragma unroll
+        for (int j = 0; j < R / 8; ++j) accx[j][0] = accx[j][1] = accx[j][2] = accx[j][3] = 0.f;
+        qr = qrows_init(ra, M, Tpad, qh, N, sh, N, t);
+      }
+      // 1. drain the accumulator, hand it back, store gu and stage the bf16 tile
+      if (!mbar_wait(tmem_full, acc_phase, err, MX_DEV_TIMEOUT_EPILOGUE)) break;
+      tc_fence_after();
+      {
+        const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + h * 128;
+        const int rl = q * 32 + lane;
+        const int64_t row = (int64_t)tm * BM + rl;
+        uint4* dst = reinterpret_cast<uint4*>(gu + row * (2 * (int64_t)N) + (h ? N : 0) + (int64_t)tn * 128);
+        const uint32_t sbase = s_stg + (uint32_t)h * (2 * 128 * 128);
+#pragma unroll
+        for (int c2 = 0; c2 < 2; ++c2) {   // 64 columns at a time (one staged sub-tile)
+          uint32_t r[2][32];
+          tmem_ld32(taddr + c2 * 64, r[0]);
+          tmem_ld32(taddr + c2 * 64 + 32, r[1]);
+          tmem_ld_wait();
+          if (c2 == 1) {
+            tc_fence_before();
+            mbar_arrive(tmem_empty);   // the MMAs of the next tile start now
+          }
+#pragma unroll
+          for (int c = 0; c < 2; ++c)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              uint4 o;
+              o.x = pack_bf16x2(__uint_as_float(r[c][8 * j + 0]), __uint_as_float(r[c][8 * j + 1]));
+              o.y = pack_bf16x2(__uint_as_float(r[c][8 * j + 2]), __uint_as_float(r[c][8 * j + 3]));
+              o.z = pack_bf16x2(__uint_as_float(r[c][8 * j + 4]), __uint_as_float(r[c][8 * j + 5]));
+              o.w = pack_bf16x2(__uint_as_float(r[c][8 * j + 6]), __uint_as_float(r[c][8 * j + 7]));
+              if (row < M) dst[8 * c2 + 4 * c + j] = o;
+              // column 64 c2 + 32 c + 8 j of the half: sub-tile c2, chunk 4 c + j
+              const uint32_t a = sbase + (uint32_t)c2 * (128 * 128) + swz<128>((uint32_t)rl, (uint32_t)(4 * c + j));
+              asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(o.x), "r"(o.y), "r"(o.z),
+                           "r"(o.w) : "memory");
+            }
+        }
+        acc_phase ^= 1;
+      }
+      // 2. this tile's B_gate / B_up rows and A_down columns into shared memory
+      for (int i = et; i < 128 * (R / 8); i += EPI_THREADS) {
+        const int n = i / (R / 8), c = i % (R / 8);
+        const uint4 vg = __ldg(reinterpret_cast<const uint4*>(bg + ((int64_t)tn * 128 + n) * R + 8 * c));
+        const uint4 vu = __ldg(reinterpret_cast<const uint4*>(bu + ((int64_t)tn * 128 + n) * R + 8 * c));
+        const uint32_t o = swz<2 * R>((uint32_t)n, (uint32_t)c);
+        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(s_bg + o), "r"(vg.x), "r"(vg.y), "r"(vg.z),
+                     "r"(vg.w) : "memory");
+        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(s_bu + o), "r"(vu.x), "r"(vu.y), "r"(vu.z),
+                     "r"(vu.w) : "memory");
+      }
+      for (int i = et; i < R * 16; i += EPI_THREADS) {
+        const int j = i / 16, c8 = i % 16;
+        const uint4 v = __ldg(reinterpret_cast<const uint4*>(ad + (int64_t)j * N + (int64_t)tn * 128 + 8 * c8));
+        const uint32_t a = s_ad + (uint32_t)(c8 >> 3) * (R * 128) + swz<128>((uint32_t)j, (uint32_t)(c8 & 7));
+        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+                     : "memory");
+      }
+      epi_sync();
+      // 3. the forward epilogue on rows 16e .. 16e+15, two 64-column sub-tiles
+#pragma unroll 1
+      for (int sbk = 0; sbk < 2; ++sbk) {
+        const uint32_t tg = s_stg + sbk * (128 * 128), tu = tg + 2 * 128 * 128;
+        const uint32_t tbg = s_bg + sbk * (64 * R * 2), tbu = s_bu + sbk * (64 * R * 2), tad = s_ad + sbk * (R * 128);
+#pragma unroll
+        for (int b = 0; b < 2; ++b) {
+          uint32_t hp[4][2];
+#pragma unroll
+          for (int pp = 0; pp < 2; ++pp) {
+            const int p = 2 * b + pp;
+            uint32_t G[4], U[4];
+            ldsm4(G, tg + o_gu[p]);
+            ldsm4(U, tu + o_gu[p]);
+            float dg0[4] = {0.f, 0.f, 0.f, 0.f}, dg1[4] = {0.f, 0.f, 0.f, 0.f};
+            float du0[4] = {0.f, 0.f, 0.f, 0.f}, du1[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+            for (int kk = 0; kk < KS; ++kk) {
+              uint32_t BG[4], BU[4];
+              ldsm4(BG, tbg + o_b[p][kk]);
+              ldsm4(BU, tbu + o_b[p][kk]);
+              mma16816(dg0, axg[kk], BG[0], BG[1]);
+              mma16816(dg1, axg[kk], BG[2], BG[3]);
+              mma16816(du0, axu[kk], BU[0], BU[1]);
+              mma16816(du1, axu[kk], BU[2], BU[3]);
+            }
+#pragma unroll
+            for (int qq = 0; qq < 2; ++qq) {
+              const float* dgv = qq ? dg1 : dg0;
+              const float* duv = qq ? du1 : du0;
+#pragma unroll
+              for (int hh = 0; hh < 2; ++hh) {
+                const float2 gg = up2(rn2(__ffma2_rn(sg2, make_float2(dgv[2 * hh], dgv[2 * hh + 1]), up2(G[2 * qq + hh]))));
+                const float2 uu = up2(rn2(__ffma2_rn(su2, make_float2(duv[2 * hh], duv[2 * hh + 1]), up2(U[2 * qq + hh]))));
+                hp[2 * pp + qq][hh] = rn2(__fmul2_rn(__fmul2_rn(gg, sigmoid2(gg)), uu));
+              }
+            }
+          }
+          quant_block16p(hp, qr, (int64_t)tn * 128 + sbk * 64 + 32 * b, t);
+#pragma unroll
+          for (int mm = 0; mm < 2; ++mm) {
+            const uint32_t a4[4] = {hp[2 * mm][0], hp[2 * mm][1], hp[2 * mm + 1][0], hp[2 * mm + 1][1]};
+#pragma unroll
+            for (int jp = 0; jp < KS; ++jp) {
+              uint32_t AD[4];
+              ldsm4(AD, tad + o_ad[2 * b + mm][jp]);
+              mma16816(accx[2 * jp], a4, AD[0], AD[1]);
+              mma16816(accx[2 * jp + 1], a4, AD[2], AD[3]);
+            }
+          }
+        }
+      }
+      epi_sync();   // staged tile and slices are free for the next tile
+    }
+    if (cur_tm >= 0) flush(cur_tm);
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 2) tmem_dealloc(tmem, TMEM_COLS);
+}
+
+// xsd [M, R] bf16 = the fixed-order sum of the CTAs' partials of each row block (k_mx_gemm_glu).
+__global__ void k_glu_xsd_reduce(const float* __restrict__ part, int M, int R, int num_n, int per,
+                                 __nv_bfloat16* __restrict__ xsd) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < (int64_t)M * R; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t row = i / R;
+    const int tm = (int)(row / BM);
+    const int c_lo = (tm * num_n) / per, c_hi = ((tm + 1) * num_n - 1) / per;
+    float v = 0.f;
+    for (int c = 0; c <= c_hi - c_lo; ++c) v += part[(int64_t)c * M * R + i];
+    xsd[i] = __float2bfloat16_rn(v);
+  }
+}
+
 CUtensorMapSwizzle lora_swizzle(int kr) {
   return kr == 16 ? CU_TENSOR_MAP_SWIZZLE_32B : (kr == 32 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B);
 }
@@ -324,4 +663,63 @@ extern "C" int mxm_gemm_lora(const void* qa, int64_t lda, const void* sa, const 
                              int64_t M, int64_t N, int64_t K, const void* L, int64_t ldl, const void* Rm, int kr,
                              void* d, int64_t ldd, void* stream) {
   return gemm_launch(qa, lda, sa, qb, ldb, sb, M, N, K, d, ldd, L, ldl, Rm, kr, stream, "mxm_gemm_lora");
+}
+
+// ------------------------------------------------------------------------------------------------ fused gate|up
+extern "C" int mxm_gemm_glu_partition(int64_t M, int64_t N, int* per, int* grid, int* slots) {
+  MX_CHECK_ARG(M >= 1 && N >= 128 && N % 128 == 0 && per && grid && slots, "mxm_gemm_glu_partition: bad args");
+  const int64_t num_n = N / 128, tiles = ((M + BM - 1) / BM) * num_n;
+  int64_t g = tiles < mxm_num_sms() ? tiles : mxm_num_sms();
+  const int64_t p = (tiles + g - 1) / g;
+  g = (tiles + p - 1) / p;
+  *per = (int)p;
+  *grid = (int)g;
+  *slots = (int)((num_n + p - 1) / p + 1);   // CTAs that can touch one row block
+  return MXM_OK;
+}
+
+extern "C" int mxm_gemm_glu(const void* qa, int64_t lda, const void* sa, const void* qb, int64_t ldb, const void* sb,
+                            int64_t M, int64_t N, int64_t K, void* gu, const void* xs, const void* bg, const void* bu,
+                            const void* ad, int r, float s_g, float s_u, void* qh, void* sh, void* xsd_part, void* xsd,
+                            void* stream) {
+  MX_CHECK_ARG(qa && sa && qb && sb && gu && xs && bg && bu && ad && qh && sh && xsd_part && xsd,
+               "mxm_gemm_glu: null pointer");
+  MX_CHECK_ARG(r == 16, "mxm_gemm_glu: LoRA rank %d not supported (16 only)", r);
+  MX_CHECK_ARG(M >= 1 && M < (1ll << 31) && N >= 128 && N % 128 == 0 && 2 * N * M < (1ll << 31) && K >= BK &&
+                   K % BK == 0 && lda >= K && ldb >= K && lda % 16 == 0 && ldb % 16 == 0,
+               "mxm_gemm_glu: need N %% 128 == 0, K %% 128 == 0, 2N * M < 2^31");
+  MX_CHECK_ARG(mx_aligned(gu, 16) && mx_aligned(xs, 4) && mx_aligned(bg, 16) && mx_aligned(bu, 16) &&
+                   mx_aligned(ad, 16) && mx_aligned(sa, 16) && mx_aligned(sb, 16) && mx_aligned(qh, 8),
+               "mxm_gemm_glu: alignment");
+  int per = 0, grid = 0, slots = 0;
+  if (int e = mxm_gemm_glu_partition(M, N, &per, &grid, &slots)) return e;
+  CUtensorMap tmA, tmB;
+  if (int st = mx_make_tmap_2d(&tmA, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, qa, (uint64_t)K, (uint64_t)M, (uint64_t)lda, BK,
+                               BM, CU_TENSOR_MAP_SWIZZLE_128B))
+    return st;
+  if (int st = mx_make_tmap_2d(&tmB, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, qb, (uint64_t)K, (uint64_t)(2 * N),
+                               (uint64_t)ldb, BK, 128, CU_TENSOR_MAP_SWIZZLE_128B))
+    return st;
+  static bool attr_done[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const size_t smem = glu_smem(16);
+  if (dev >= 0 && dev < 64 && !attr_done[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(k_mx_gemm_glu<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return mx_cuda_status(e, "gemm glu: set smem");
+    attr_done[dev] = true;
+  }
+  cudaStream_t st = (cudaStream_t)stream;
+  k_mx_gemm_glu<16><<<grid, NUM_THREADS, smem, st>>>(tmA, tmB, (const uint8_t*)sa, (const uint8_t*)sb, (int)M, (int)N,
+                                                     (int)K, (__nv_bfloat16*)gu, (const __nv_bfloat16*)xs,
+                                                     (const __nv_bfloat16*)bg, (const __nv_bfloat16*)bu,
+                                                     (const __nv_bfloat16*)ad, s_g, s_u, (uint8_t*)qh, (uint8_t*)sh,
+                                                     (float*)xsd_part, per, mx_dev_error_ptr());
+  mx_note_launch();
+  if (int e = mx_launch_status("gemm glu")) return e;
+  const int64_t n = M * r;
+  const int rg = (int)std::min<int64_t>((n + 255) / 256, (int64_t)mxm_num_sms() * 8);
+  k_glu_xsd_reduce<<<rg, 256, 0, st>>>((const float*)xsd_part, (int)M, r, (int)(N / 128), per, (__nv_bfloat16*)xsd);
+  mx_note_launch();
+  return mx_launch_status("gemm glu xsd reduce");
 }

@@ -6,8 +6,8 @@ need_out)``, ``_MLP`` autograd contract (9 inputs, 9 gradients, the same saved t
 
 Per layer call (T tokens, H hidden, N intermediate, r LoRA rank):
   forward : xs = x S^T (rank-2r, tensor-core rowdot) and q, s = MXFP8(x) from one read of x
-            gu = [x W_gate^T | x W_up^T]          -- tcgen05 block-scaled GEMM, K = H
-            q_h, s_h, xS_down = epilogue(gu)       -- LoRA-B add, SwiGLU, MX quantize h
+            gu = [x W_gate^T | x W_up^T]          -- tcgen05 block-scaled GEMM, K = H, and in the same
+            q_h, s_h, xS_down = epilogue(gu)          kernel (rank 16) the LoRA-B add, SwiGLU, MX quantize h
             y = h W_down^T + xS_down (s_d B_down)^T -- tcgen05 GEMM; the LoRA term is a bf16 tcgen05 MMA
                                                        into the same TMEM accumulator
   backward: q, s = MXFP8(dy) and dxd = s_d dy B_down from one read of dy; dh_mx = dy W_down (tcgen05)
@@ -139,6 +139,30 @@ def mlp_fwd(gu, xs, bg, bu, ad, s_g, s_u, write_q):
     return (q, s.view(_E8), xsd) if write_q else (None, None, xsd)
 
 
+def gemm_glu(q, sc, w, ws, xs, bg, bu, ad, s_g, s_u):
+    """gu = [x W_gate^T | x W_up^T] and, from the same GEMM tiles, the forward epilogue (MXFP8(h), xS_down):
+    mx_mm + mlp_fwd in one kernel.  q / sc: MXFP8(x) [T, H]; w / ws: W_gu codes [2N, H] and scales.
+    -> (gu [T, 2N] bf16, q_h [T, N] fp8, s_h, xS_down [T, r] bf16).  Rank 16 only."""
+    T, H = q.shape
+    N2 = w.shape[0]
+    N, R = N2 // 2, ad.shape[0]
+    dev = q.device
+    per, grid, slots = _i(0), _i(0), _i(0)
+    _nx.call("mxm_gemm_glu_partition", T, N, _nx.ctypes_ref(per), _nx.ctypes_ref(grid), _nx.ctypes_ref(slots))
+    gu = torch.empty((T, N2), dtype=torch.bfloat16, device=dev)
+    qh = torch.empty((T, N), dtype=_F8, device=dev)
+    sh = torch.empty(_cdiv(T, 128) * (N // 128) * 512, dtype=torch.uint8, device=dev)
+    part = torch.empty((slots.value, T, R), dtype=torch.float32, device=dev)
+    xsd = torch.empty((T, R), dtype=torch.bfloat16, device=dev)
+    _nx.call("mxm_gemm_glu", _nx.ptr(q), q.stride(0), _nx.ptr(sc), _nx.ptr(w), w.stride(0), _nx.ptr(ws), T, N, H,
+             _nx.ptr(gu), _nx.ptr(xs), _nx.ptr(bg), _nx.ptr(bu), _nx.ptr(ad), R, float(s_g), float(s_u),
+             _nx.ptr(qh), _nx.ptr(sh), _nx.ptr(part), _nx.ptr(xsd), _nx.stream_of(q))
+    return gu, qh, sh.view(_E8), xsd
+
+
+FUSE_GLU = [True]   # gate|up GEMM + forward epilogue in one kernel (rank 16); False: two passes
+
+
 def _bwd_launch(gu, xs, dhm, dxd, bg, bu, ad, s_g, s_u, need_q):
     T, N2 = gu.shape
     N, R = N2 // 2, ad.shape[0]
@@ -194,10 +218,15 @@ class _MLP(torch.autograd.Function):
             bdT = _cast(("T", id(bd)), lambda: bd.t().contiguous())
             ST = _cast(("T", id(S)), lambda: S.t().contiguous())
         xs, q, sc = rowdot_quant(x2, S)                                  # [T, 2R] = xa_gate | xa_up; MXFP8(x)
-        gu = mxfp8.mx_mm(q, hold.w.t(), sc, hold.ws)                     # [T, 2N] gate | up
-        del q, sc
+        if need_out and FUSE_GLU[0] and ad.shape[0] == 16 and hold.w.is_contiguous():
+            gu, qh, sh, xsd = gemm_glu(q, sc, hold.w, hold.ws, xs, bg, bu, ad, s_g, s_u)   # one pass over gu
+            del q, sc
+        else:
+            gu = mxfp8.mx_mm(q, hold.w.t(), sc, hold.ws)                 # [T, 2N] gate | up
+            del q, sc
+            if need_out:
+                qh, sh, xsd = mlp_fwd(gu, xs, bg, bu, ad, s_g, s_u, True)
         if need_out:
-            qh, sh, xsd = mlp_fwd(gu, xs, bg, bu, ad, s_g, s_u, True)
             y = mx_mm_lora(qh, down._mx_w.t(), sh, down._mx_ws, xsd, bds)
             del qh, sh, xsd
         else:   # graph only (checkpoint recompute): nobody reads the output value
