@@ -226,7 +226,8 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
 // is deterministic.
 constexpr int BWD_BN = 32, BWD_ST = 3;
 // consumer warps: 16 warps in all (4 per scheduler, 128 registers) for r = 16; 12 (3 per scheduler,
-// 168 registers) for r = 32, whose per-row sums and fragments need more registers
+// 168 registers) for r = 32, whose per-row sums and fragments need more registers.  (14 consumers, so
+// that 16,384 tokens fill exactly 148 CTAs, measured slower: the fourth warp per scheduler matters more.)
 __host__ __device__ constexpr int bwd_cons(int R) { return R == 16 ? 15 : 11; }
 __host__ __device__ constexpr int bwd_rows(int R) { return 16 * bwd_cons(R); }   // rows per CTA
 __host__ __device__ constexpr int bwd_tile(int R) { return bwd_rows(R) * BWD_BN * 2; }
