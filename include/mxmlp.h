@@ -112,14 +112,15 @@ int mxm_gemm_glu(const void* qa, int64_t lda, const void* sa, const void* qb, in
                  int64_t N, int64_t K, void* gu, const void* xs, const void* bg, const void* bu, const void* ad, int r,
                  float s_g, float s_u, void* qh, void* sh, void* xsd_part, void* xsd, void* stream);
 
-/* Super-block rows and column-group count for the backward epilogue (reference _bwd_grid,
- * scripts/fused_mlp.py:218-232). */
+/* Row-block size and dxa partial-slot count for the backward epilogue (reference _bwd_grid,
+ * scripts/fused_mlp.py:218-232): col_groups = the number of [T, 3r] fp32 slots dxa_part needs. */
 int mxm_mlp_bwd_partitions(int64_t T, int64_t N, int r, int* super_block, int* col_groups);
 
 /* Backward epilogue of the fused MLP (reference mlp_bwd / _bwd_kernel, scripts/fused_mlp.py:112-175,235-259).
  * Recomputes g, u, h from gu; dh = bf16(dhm + dxd ad); du = bf16(dh silu(g)); dg = bf16(dh u sig (g (1-sig) + 1));
  * q / s = MXFP8([dg | du]) [T, 2N] (skipped when q is NULL).  Partial sums (fp32, fixed-order reduction in
- * mxm_mlp_bwd_reduce): dxa_part [col_groups, T, 3r] = [dg bg | du bu | h ad^T];
+ * mxm_mlp_bwd_reduce): dxa_part [col_groups, T, 3r] = [dg bg | du bu | h ad^T], one slot per CTA that
+ * worked on a row block (slots a row block does not use are left unwritten);
  * dbg_part / dbu_part [n_super, N, r] = dg^T xa_g / du^T xa_u; dad_part [n_super, r, N] = dxd^T h,
  * n_super = ceil(ceil128(T) / super_block). */
 int mxm_mlp_bwd_epilogue(const void* gu, const void* xs, const void* dhm, const void* dxd, const void* bg,

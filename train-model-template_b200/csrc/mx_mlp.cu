@@ -210,12 +210,15 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
 }
 
 // ------------------------------------------------------------------------------------------------ backward
-// CTA = one block of SB = 16 x CONS rows x one column group of `tpg` 32-column tiles.  Warp CONS streams,
-// per column tile, the [SB x 32] bf16 tiles of g, u and dh (64-byte swizzle) plus the tile's slices of
-// B_gate, B_up ([32 x r]) and A_down ([r x 32]) into a 3-stage ring with TMA; the block's xs and dxd
-// rows are loaded once.  Consumer warps 0 .. CONS-1 each own 16 rows:
+// Persistent CTAs, one per SM, each walking a contiguous run of `per` work items (row block of
+// SB = 16 x CONS rows, 32-column tile), column tile fastest.  Warp CONS streams, per item, the [SB x 32]
+// bf16 tiles of g, u and dh (64-byte swizzle) plus the tile's slices of B_gate, B_up ([32 x r]) and
+// A_down ([r x 32]) into a 3-stage ring with TMA, and, when the run enters a row block, the block's xs
+// and dxd rows (once the consumers release the previous block's: rows_empty).  Consumer warps
+// 0 .. CONS-1 each own 16 rows of the current block:
 //   * dg, du, h of the tile are computed in registers, quantized, and multiplied by the B slices into
-//     the per-row sums dxa_gate, dxa_up, xS_down, which stay in registers over all of the group's tiles;
+//     the per-row sums dxa_gate, dxa_up, xS_down, which stay in registers while the run stays in the
+//     row block and are then stored into this CTA's slot of the fp32 partials;
 //   * dg, du, h are also stored (bf16, the same swizzle) into a shared operand tile.  When every warp has
 //     stored its rows (mbarrier op_full), the 6 (r = 16) or 12 (r = 32) 16 x 16 blocks of dB_gate^T,
 //     dB_up^T and dA_down -- dealt out to the warps in turn, a different set each tile -- are each
@@ -226,8 +229,8 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
 // is deterministic.
 constexpr int BWD_BN = 32, BWD_ST = 3;
 // consumer warps: 16 warps in all (4 per scheduler, 128 registers) for r = 16; 12 (3 per scheduler,
-// 168 registers) for r = 32, whose per-row sums and fragments need more registers.  (14 consumers, so
-// that 16,384 tokens fill exactly 148 CTAs, measured slower: the fourth warp per scheduler matters more.)
+// 168 registers) for r = 32, whose per-row sums and fragments need more registers.  (14 consumers
+// measured slower: the fourth warp per scheduler matters more than the block height.)
 __host__ __device__ constexpr int bwd_cons(int R) { return R == 16 ? 15 : 11; }
 __host__ __device__ constexpr int bwd_rows(int R) { return 16 * bwd_cons(R); }   // rows per CTA
 __host__ __device__ constexpr int bwd_tile(int R) { return bwd_rows(R) * BWD_BN * 2; }
@@ -236,7 +239,7 @@ __host__ __device__ constexpr int bwd_stage(int R) { return 3 * bwd_tile(R) + 3 
 __host__ __device__ constexpr size_t bwd_rowbuf(int R) { return ((size_t)bwd_rows(R) * 3 * R * 2 + 1023) / 1024 * 1024; }
 __host__ __device__ constexpr size_t bwd_smem(int R) {
   return 1024 + (size_t)BWD_ST * bwd_stage(R) + bwd_rowbuf(R) + 3 * (size_t)bwd_tile(R) +
-         (2 * BWD_ST + 3) * sizeof(uint64_t);
+         (2 * BWD_ST + 4) * sizeof(uint64_t);
 }
 
 template <int R>
@@ -246,7 +249,7 @@ __global__ void __launch_bounds__(32 * (bwd_cons(R) + 1), 1)
               const __grid_constant__ CUtensorMap tm_ad, const __grid_constant__ CUtensorMap tm_xs,
               const __grid_constant__ CUtensorMap tm_dxd, uint8_t* __restrict__ q, uint8_t* __restrict__ s,
               float* __restrict__ dxa_part, float* __restrict__ dbg_part, float* __restrict__ dbu_part,
-              float* __restrict__ dad_part, int T, int Tpad, int N, float s_g, float s_u, int tpg, int write_q,
+              float* __restrict__ dad_part, int T, int Tpad, int N, float s_g, float s_u, int per, int write_q,
               int* err) {
   constexpr int CONS = bwd_cons(R), SB = bwd_rows(R), KS = R / 16, NT = BWD_BN / 8, R3 = 3 * R;
   constexpr int TILE = bwd_tile(R), BT = bwd_btile(R), STG = bwd_stage(R);
@@ -261,8 +264,11 @@ __global__ void __launch_bounds__(32 * (bwd_cons(R) + 1), 1)
   uint64_t* rows_full = empty + BWD_ST;
   uint64_t* op_full = rows_full + 1;   // all consumer warps stored the tile's dg | du | h
   uint64_t* op_empty = op_full + 1;    // all column-product blocks of the tile were read
+  uint64_t* rows_empty = op_empty + 1; // all consumer warps are done with the row block in rows_xs / rows_dxd
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int cg = blockIdx.y, r0 = blockIdx.x * SB;
+  const int nt = N / BWD_BN;                                   // column tiles per row block
+  const int items = ((Tpad + SB - 1) / SB) * nt;               // (row block, column tile), column fastest
+  const int it_lo = blockIdx.x * per, it_hi = min(it_lo + per, items);
   const int64_t N2 = 2 * (int64_t)N;
   if (threadIdx.x == 0) {
     for (int i = 0; i < BWD_ST; ++i) {
@@ -270,6 +276,7 @@ __global__ void __launch_bounds__(32 * (bwd_cons(R) + 1), 1)
       mbar_init(&empty[i], CONS);
     }
     mbar_init(rows_full, 1);
+    mbar_init(rows_empty, CONS);
     mbar_init(op_full, CONS);
     mbar_init(op_empty, TASKS);
     fence_barrier_init();
@@ -283,15 +290,12 @@ __global__ void __launch_bounds__(32 * (bwd_cons(R) + 1), 1)
       prefetch_tmap(&tm_bg);
       prefetch_tmap(&tm_bu);
       prefetch_tmap(&tm_ad);
-      mbar_arrive_expect_tx(rows_full, (uint32_t)(SB * 3 * R * 2));
-      tma_load_2d(rows_xs, &tm_xs, rows_full, 0, r0);
-      tma_load_2d(rows_dxd, &tm_dxd, rows_full, 0, r0);
     }
     int stage = 0;
     uint32_t phase = 0;
-    int issued = 0;
-    for (int ct = 0; ct < tpg; ++ct) {
-      const int n0 = (cg * tpg + ct) * BWD_BN;
+    int issued = 0, row_loads = 0, cur_sbi = -1;
+    for (int it = it_lo; it < it_hi; ++it) {
+      const int sbi = it / nt, n0 = (it % nt) * BWD_BN, r0 = sbi * SB;
       if (!mbar_wait(&empty[stage], phase ^ 1, err, MX_DEV_TIMEOUT_PRODUCER)) break;
       if (lane == 0) {
         uint8_t* dst = smem + stage * STG;
@@ -310,19 +314,32 @@ __global__ void __launch_bounds__(32 * (bwd_cons(R) + 1), 1)
         stage = 0;
         phase ^= 1;
       }
+      // a new row block: its xs / dxd rows, once the consumers are done with the last block's (the
+      // block's first tile is already on its way)
+      if (sbi != cur_sbi) {
+        if (cur_sbi >= 0 && !mbar_wait(rows_empty, (uint32_t)((row_loads - 1) & 1), err, MX_DEV_TIMEOUT_PRODUCER))
+          break;
+        if (lane == 0) {
+          mbar_arrive_expect_tx(rows_full, (uint32_t)(SB * 3 * R * 2));
+          tma_load_2d(rows_xs, &tm_xs, rows_full, 0, r0);
+          tma_load_2d(rows_dxd, &tm_dxd, rows_full, 0, r0);
+        }
+        __syncwarp();
+        ++row_loads;
+        cur_sbi = sbi;
+      }
     }
     // leave no copy in flight: wait (bounded) for the last load of every stage that was used
     for (int k = 0; k < BWD_ST && k < issued; ++k) {
       const int i = issued - 1 - k, st = i % BWD_ST;
       mbar_wait(&full[st], (uint32_t)((i / BWD_ST) & 1), err, MX_DEV_TIMEOUT_PRODUCER);
     }
-    mbar_wait(rows_full, 0, err, MX_DEV_TIMEOUT_PRODUCER);
+    if (row_loads > 0) mbar_wait(rows_full, (uint32_t)((row_loads - 1) & 1), err, MX_DEV_TIMEOUT_PRODUCER);
     return;
   }
 
   const int g = lane >> 2, t = lane & 3;
   const int mi = lane >> 3, lr = lane & 7;
-  if (!mbar_wait(rows_full, 0, err, MX_DEV_TIMEOUT_EPILOGUE)) return;
 
   // Per-lane shared-memory offsets, fixed for the whole kernel (the swizzles make them non-affine).
   // g / u / dh tiles and the dg / du / h operand tile (64-byte rows, 64-byte swizzle): matrices
@@ -348,27 +365,53 @@ __global__ void __launch_bounds__(32 * (bwd_cons(R) + 1), 1)
   }
   const uint32_t s_xs = smem_u32(rows_xs), s_dxd = smem_u32(rows_dxd), s_ring = smem_u32(smem);
   const uint32_t ob = smem_u32(opbuf);
-  // this warp's rows of xa_gate | xa_up | dxd as MMA A fragments, for the whole kernel
-  uint32_t axg[KS][4], axu[KS][4], axd[KS][4];
+  uint32_t axg[KS][4], axu[KS][4], axd[KS][4];     // this warp's rows of xa_gate | xa_up | dxd (A fragments)
+  float rg[R / 8][4], ru[R / 8][4], rx[R / 8][4];  // per-row sums over this CTA's columns of the row block
+  QRows qr{};
+  uint32_t rows_ph = 0;
+  // this CTA's partial of the row block's per-row products [dg Bg | du Bu | h Ad^T]: one slot per CTA
+  // that works on the block, in CTA order
+  auto flush_rows = [&](int sbi) {
+    const int slot = (int)blockIdx.x - (sbi * nt) / per;
+    float* P = dxa_part + (int64_t)slot * T * R3;
+    const int64_t ra = (int64_t)sbi * SB + warp * 16 + g;
 #pragma unroll
-  for (int kk = 0; kk < KS; ++kk) {
-    ldsm4(axg[kk], s_xs + swz<4 * R>((uint32_t)lrow, (uint32_t)(2 * kk + (mi >> 1))));
-    ldsm4(axu[kk], s_xs + swz<4 * R>((uint32_t)lrow, (uint32_t)(2 * KS + 2 * kk + (mi >> 1))));
-    ldsm4(axd[kk], s_dxd + swz<2 * R>((uint32_t)lrow, (uint32_t)(2 * kk + (mi >> 1))));
-  }
-  float rg[R / 8][4], ru[R / 8][4], rx[R / 8][4];  // per-row sums over the group's columns
-#pragma unroll
-  for (int j = 0; j < R / 8; ++j)
-#pragma unroll
-    for (int e = 0; e < 4; ++e) rg[j][e] = ru[j][e] = rx[j][e] = 0.f;
+    for (int jt = 0; jt < R / 8; ++jt) {
+      const int c = 8 * jt + 2 * t;
+      if (ra < T) {
+        *reinterpret_cast<float2*>(P + ra * R3 + c) = make_float2(rg[jt][0], rg[jt][1]);
+        *reinterpret_cast<float2*>(P + ra * R3 + R + c) = make_float2(ru[jt][0], ru[jt][1]);
+        *reinterpret_cast<float2*>(P + ra * R3 + 2 * R + c) = make_float2(rx[jt][0], rx[jt][1]);
+      }
+      if (ra + 8 < T) {
+        *reinterpret_cast<float2*>(P + (ra + 8) * R3 + c) = make_float2(rg[jt][2], rg[jt][3]);
+        *reinterpret_cast<float2*>(P + (ra + 8) * R3 + R + c) = make_float2(ru[jt][2], ru[jt][3]);
+        *reinterpret_cast<float2*>(P + (ra + 8) * R3 + 2 * R + c) = make_float2(rx[jt][2], rx[jt][3]);
+      }
+    }
+  };
 
-  const int64_t ra = (int64_t)r0 + warp * 16 + g;
   const float2 sg2 = make_float2(s_g, s_g), su2 = make_float2(s_u, s_u);
-  const QRows qr = qrows_init(ra, T, Tpad, q, N2, s, N2, t);
   int stage = 0;
   uint32_t phase = 0;
-  for (int ct = 0; ct < tpg; ++ct) {
-    const int n0 = (cg * tpg + ct) * BWD_BN;
+  int sbi = it_lo / nt, n0 = (it_lo % nt) * BWD_BN;
+  const int cnt = it_hi - it_lo;
+  for (int ct = 0; ct < cnt; ++ct) {   // ct: this CTA's tile count, for the hand-off parities
+    if (ct == 0 || n0 == 0) {          // entering a row block
+      if (!mbar_wait(rows_full, rows_ph, err, MX_DEV_TIMEOUT_EPILOGUE)) break;
+      rows_ph ^= 1;
+#pragma unroll
+      for (int kk = 0; kk < KS; ++kk) {
+        ldsm4(axg[kk], s_xs + swz<4 * R>((uint32_t)lrow, (uint32_t)(2 * kk + (mi >> 1))));
+        ldsm4(axu[kk], s_xs + swz<4 * R>((uint32_t)lrow, (uint32_t)(2 * KS + 2 * kk + (mi >> 1))));
+        ldsm4(axd[kk], s_dxd + swz<2 * R>((uint32_t)lrow, (uint32_t)(2 * kk + (mi >> 1))));
+      }
+#pragma unroll
+      for (int j = 0; j < R / 8; ++j)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) rg[j][e] = ru[j][e] = rx[j][e] = 0.f;
+      qr = qrows_init((int64_t)sbi * SB + warp * 16 + g, T, Tpad, q, N2, s, N2, t);
+    }
     if (!mbar_wait(&full[stage], phase, err, MX_DEV_TIMEOUT_EPILOGUE)) break;
     {
       const uint32_t sb = s_ring + (uint32_t)stage * STG;
@@ -487,13 +530,13 @@ __global__ void __launch_bounds__(32 * (bwd_cons(R) + 1), 1)
       for (int h = 0; h < 2; ++h) {
         const int n = n0 + 16 * nh + 8 * h + 2 * t;
         if (prod < 2) {   // [n_blocks, N, r]: element (n, j)
-          float* P = (prod == 0 ? dbg_part : dbu_part) + ((int64_t)blockIdx.x * N + n) * R + j;
+          float* P = (prod == 0 ? dbg_part : dbu_part) + ((int64_t)sbi * N + n) * R + j;
           P[0] = acc[h][0];
           P[R] = acc[h][1];
           P[8] = acc[h][2];
           P[R + 8] = acc[h][3];
         } else {          // [n_blocks, r, N]: element (j, n)
-          float* P = dad_part + ((int64_t)blockIdx.x * R + j) * N + n;
+          float* P = dad_part + ((int64_t)sbi * R + j) * N + n;
           *reinterpret_cast<float2*>(P) = make_float2(acc[h][0], acc[h][1]);
           *reinterpret_cast<float2*>(P + 8 * (int64_t)N) = make_float2(acc[h][2], acc[h][3]);
         }
@@ -502,21 +545,15 @@ __global__ void __launch_bounds__(32 * (bwd_cons(R) + 1), 1)
       if (lane == 0) mbar_arrive(op_empty);
     }
     if (!ok) break;
-  }
-  // the group's partial of the per-row products
-  float* P = dxa_part + (int64_t)cg * T * R3;
-#pragma unroll
-  for (int jt = 0; jt < R / 8; ++jt) {
-    const int c = 8 * jt + 2 * t;
-    if (ra < T) {
-      *reinterpret_cast<float2*>(P + ra * R3 + c) = make_float2(rg[jt][0], rg[jt][1]);
-      *reinterpret_cast<float2*>(P + ra * R3 + R + c) = make_float2(ru[jt][0], ru[jt][1]);
-      *reinterpret_cast<float2*>(P + ra * R3 + 2 * R + c) = make_float2(rx[jt][0], rx[jt][1]);
-    }
-    if (ra + 8 < T) {
-      *reinterpret_cast<float2*>(P + (ra + 8) * R3 + c) = make_float2(rg[jt][2], rg[jt][3]);
-      *reinterpret_cast<float2*>(P + (ra + 8) * R3 + R + c) = make_float2(ru[jt][2], ru[jt][3]);
-      *reinterpret_cast<float2*>(P + (ra + 8) * R3 + 2 * R + c) = make_float2(rx[jt][2], rx[jt][3]);
+    const bool last = ct + 1 == cnt;
+    if ((n0 += BWD_BN) == N || last) {   // leaving the row block
+      flush_rows(sbi);
+      if (!last) {
+        __syncwarp();
+        if (lane == 0) mbar_arrive(rows_empty);
+      }
+      n0 = 0;
+      ++sbi;
     }
   }
 }
@@ -893,16 +930,20 @@ __global__ void __launch_bounds__(256) k_sum_parts4(SumJobs jobs, int nparts, in
   }
 }
 
-// dxa partials [nparts, T, 3R] -> dxa bf16 [T, 2R] (gate part x s_g, up part x s_u) and xS_down bf16 [T, R].
-__global__ void k_reduce_dxa(const float* __restrict__ src, int nparts, int T, int R, float s_g, float s_u,
-                             bf16* __restrict__ dxa, bf16* __restrict__ xsd) {
+// dxa partials [slots, T, 3R] -> dxa bf16 [T, 2R] (gate part x s_g, up part x s_u) and xS_down bf16 [T, R].
+// Row block sbi (rows sb * sbi ..) was worked on by CTAs c_lo .. c_hi of the backward epilogue, whose
+// partials sit in slots 0 .. c_hi - c_lo; they are added in slot order.
+__global__ void k_reduce_dxa(const float* __restrict__ src, int sb, int nt, int per, int T, int R, float s_g,
+                             float s_u, bf16* __restrict__ dxa, bf16* __restrict__ xsd) {
   const int64_t n = (int64_t)T * 3 * R;
   const int64_t stride = n;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
-    float v = 0.f;
-    for (int p = 0; p < nparts; ++p) v += src[p * stride + i];
     const int64_t row = i / (3 * R);
     const int c = (int)(i % (3 * R));
+    const int sbi = (int)(row / sb);
+    const int nparts = ((sbi + 1) * nt - 1) / per - (sbi * nt) / per + 1;
+    float v = 0.f;
+    for (int p = 0; p < nparts; ++p) v += src[p * stride + i];
     if (c < R)
       dxa[row * 2 * R + c] = __float2bfloat16_rn(v * s_g);
     else if (c < 2 * R)
@@ -987,33 +1028,40 @@ extern "C" int mxm_mlp_fwd_epilogue(const void* gu, const void* xs, const void* 
   return MXM_OK;
 }
 
-// Backward partition: row blocks of SB = 16 x (consumer warps) rows (fixed by the kernel) and the
-// column-group count.  One CTA fits per SM, so the time is about (waves) x (tiles per CTA); each extra
-// group adds a [T, 3r] fp32 partial of the row sums that is written and read once more, charged as
-// the fraction of a tile time those bytes take.  The reference's _bwd_grid
-// (scripts/fused_mlp.py:218-232) makes the same partial-bytes / parallelism trade-off.
-extern "C" int mxm_mlp_bwd_partitions(int64_t T, int64_t N, int r, int* super_block, int* col_groups) {
-  MX_CHECK_ARG(T >= 1 && N >= 128 && N % 128 == 0 && (r == 16 || r == 32) && super_block && col_groups,
-               "mxm_mlp_bwd_partitions: bad args");
-  const int sb = r == 16 ? bwd_rows(16) : bwd_rows(32);
+// Backward partition.  Work items are (row block of SB = 16 x consumer-warps rows, 32-column tile), the
+// column tile fastest; each CTA (one per SM) takes a contiguous run of `per` items, so every SM gets the
+// same number of tiles whatever T is, and a row block is shared by at most ceil(nt / per) + 1 CTAs, each
+// writing its per-row sums into its own slot of dxa_part.  The reference's _bwd_grid
+// (scripts/fused_mlp.py:218-232) splits the columns into groups for the same reason: enough CTAs for the
+// GPU, at the cost of [T, 3r] fp32 partials per extra group.
+namespace {
+struct BwdPlan {
+  int sb, nt, nsb, items, per, grid, slots;
+};
+BwdPlan bwd_plan(int64_t T, int64_t N, int r) {
+  BwdPlan p;
+  p.sb = r == 16 ? bwd_rows(16) : bwd_rows(32);
   const int64_t tpad = (T + 127) / 128 * 128;
-  const int64_t nsb = (tpad + sb - 1) / sb;
-  const int nt = (int)(N / BWD_BN);
-  const int64_t nsm = mxm_num_sms();
-  const double group_cost = 1.1e-6 * (double)T * r;
-  int best = 1;
-  double best_cost = 1e300;
-  for (int ncg = 1; ncg <= nt; ++ncg) {
-    if (nt % ncg) continue;
-    const int64_t waves = (nsb * ncg + nsm - 1) / nsm;
-    const double cost = (double)waves * (nt / ncg) + group_cost * ncg;
-    if (cost < best_cost) {
-      best_cost = cost;
-      best = ncg;
-    }
-  }
-  *super_block = sb;
-  *col_groups = best;
+  p.nsb = (int)((tpad + p.sb - 1) / p.sb);
+  p.nt = (int)(N / BWD_BN);
+  p.items = p.nsb * p.nt;
+  const int nsm = mxm_num_sms();
+  p.per = (p.items + nsm - 1) / nsm;
+  p.grid = (p.items + p.per - 1) / p.per;
+  p.slots = 1;
+  for (int b = 0; b < p.nsb; ++b)
+    p.slots = std::max(p.slots, ((b + 1) * p.nt - 1) / p.per - (b * p.nt) / p.per + 1);
+  return p;
+}
+}  // namespace
+
+extern "C" int mxm_mlp_bwd_partitions(int64_t T, int64_t N, int r, int* super_block, int* col_groups) {
+  MX_CHECK_ARG(T >= 1 && T < (1ll << 31) && N >= 128 && N % 128 == 0 && (r == 16 || r == 32) && super_block &&
+                   col_groups,
+               "mxm_mlp_bwd_partitions: bad args");
+  const BwdPlan p = bwd_plan(T, N, r);
+  *super_block = p.sb;
+  *col_groups = p.slots;
   return MXM_OK;
 }
 
@@ -1026,9 +1074,9 @@ extern "C" int mxm_mlp_bwd_epilogue(const void* gu, const void* xs, const void* 
   MX_CHECK_ARG(T >= 1 && T < (1ll << 31) && N >= 128 && N % 128 == 0 && (r == 16 || r == 32),
                "mxm_mlp_bwd_epilogue: need T >= 1, N %% 128 == 0, r in {16, 32}");
   MX_CHECK_ARG((q == nullptr) == (s == nullptr), "mxm_mlp_bwd_epilogue: q and s go together");
-  const int nt = (int)(N / BWD_BN);
-  MX_CHECK_ARG(col_groups >= 1 && nt % col_groups == 0 && super_block == (r == 16 ? bwd_rows(16) : bwd_rows(32)),
-               "mxm_mlp_bwd_epilogue: bad partition (%d, %d)", super_block, col_groups);
+  const BwdPlan p = bwd_plan(T, N, r);
+  MX_CHECK_ARG(col_groups >= p.slots && super_block == p.sb,
+               "mxm_mlp_bwd_epilogue: bad partition (%d, %d): use mxm_mlp_bwd_partitions", super_block, col_groups);
   MX_CHECK_ARG(mx_aligned(gu, 16) && mx_aligned(dhm, 16) && mx_aligned(bg, 16) && mx_aligned(bu, 16) &&
                    mx_aligned(ad, 16),
                "mxm_mlp_bwd_epilogue: gu / dhm / bg / bu / ad must be 16-byte aligned");
@@ -1056,18 +1104,15 @@ extern "C" int mxm_mlp_bwd_epilogue(const void* gu, const void* xs, const void* 
                               (uint64_t)(2 * r), r, super_block, r == 16 ? CU_TENSOR_MAP_SWIZZLE_32B : CU_TENSOR_MAP_SWIZZLE_64B))
     return e;
   const int64_t tpad = (T + 127) / 128 * 128;
-  const int nsb = (int)((tpad + super_block - 1) / super_block);
-  dim3 grid((unsigned)nsb, (unsigned)col_groups);
   const size_t smem = bwd_smem(r);
   cudaStream_t st = (cudaStream_t)stream;
-  const int tpg = nt / col_groups;
   auto go = [&](auto kern) -> int {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return mx_cuda_status(e, "mlp bwd epilogue: set smem");
-    kern<<<grid, 32 * (bwd_cons(r) + 1), smem, st>>>(tgu, tdh, tbg, tbu, tad, txs, tdxd, (uint8_t*)q, (uint8_t*)s,
-                                                     (float*)dxa_part, (float*)dbg_part, (float*)dbu_part,
-                                                     (float*)dad_part, (int)T, (int)tpad, (int)N, s_g, s_u, tpg,
-                                                     q != nullptr, mx_dev_error_ptr());
+    kern<<<p.grid, 32 * (bwd_cons(r) + 1), smem, st>>>(tgu, tdh, tbg, tbu, tad, txs, tdxd, (uint8_t*)q, (uint8_t*)s,
+                                                       (float*)dxa_part, (float*)dbg_part, (float*)dbu_part,
+                                                       (float*)dad_part, (int)T, (int)tpad, (int)N, s_g, s_u, p.per,
+                                                       q != nullptr, mx_dev_error_ptr());
     mx_note_launch();
     return mx_launch_status("mlp bwd epilogue");
   };
@@ -1080,12 +1125,16 @@ extern "C" int mxm_mlp_bwd_reduce(const void* dxa_part, const void* dbg_part, co
                                   void* dAd, void* stream) {
   MX_CHECK_ARG(dxa_part && dbg_part && dbu_part && dad_part && dxa && xsd && dBg && dBu && dAd,
                "mxm_mlp_bwd_reduce: null pointer");
-  const int64_t tpad = (T + 127) / 128 * 128;
-  const int nsb = (int)((tpad + super_block - 1) / super_block);
+  MX_CHECK_ARG(T >= 1 && T < (1ll << 31) && N >= 128 && N % 128 == 0 && (r == 16 || r == 32),
+               "mxm_mlp_bwd_reduce: need T >= 1, N %% 128 == 0, r in {16, 32}");
+  const BwdPlan p = bwd_plan(T, N, r);
+  MX_CHECK_ARG(col_groups >= p.slots && super_block == p.sb,
+               "mxm_mlp_bwd_reduce: bad partition (%d, %d): use mxm_mlp_bwd_partitions", super_block, col_groups);
+  const int nsb = p.nsb;
   cudaStream_t st = (cudaStream_t)stream;
   const int64_t nd = T * 3 * r;
-  k_reduce_dxa<<<grid_for(nd, 256), 256, 0, st>>>((const float*)dxa_part, col_groups, (int)T, r, s_g, s_u, (bf16*)dxa,
-                                                  (bf16*)xsd);
+  k_reduce_dxa<<<grid_for(nd, 256), 256, 0, st>>>((const float*)dxa_part, p.sb, p.nt, p.per, (int)T, r, s_g, s_u,
+                                                  (bf16*)dxa, (bf16*)xsd);
   mx_note_launch();
   const int64_t nb4 = N * r / 4;  // N % 128 == 0
   SumJobs jobs;

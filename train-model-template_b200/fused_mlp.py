@@ -163,7 +163,7 @@ def gemm_glu(q, sc, w, ws, xs, bg, bu, ad, s_g, s_u):
 FUSE_GLU = [True]   # gate|up GEMM + forward epilogue in one kernel (rank 16); False: two passes
 
 
-def _bwd_launch(gu, xs, dhm, dxd, bg, bu, ad, s_g, s_u, need_q):
+def _bwd_launch(gu, xs, dhm, dxd, bg, bu, ad, s_g, s_u, need_q, zero_slots=False):
     T, N2 = gu.shape
     N, R = N2 // 2, ad.shape[0]
     dev = gu.device
@@ -175,7 +175,8 @@ def _bwd_launch(gu, xs, dhm, dxd, bg, bu, ad, s_g, s_u, need_q):
     if need_q:
         q = torch.empty((T, N2), dtype=_F8, device=dev)
         s = torch.empty(_cdiv(T, 128) * (N2 // 128) * 512, dtype=torch.uint8, device=dev)
-    dxa = torch.empty((ncg, T, 3 * R), dtype=torch.float32, device=dev)
+    # per-row partial slots: a row block fills only the slots of the CTAs that worked on it
+    dxa = (torch.zeros if zero_slots else torch.empty)((ncg, T, 3 * R), dtype=torch.float32, device=dev)
     dbg = torch.empty((nsb, N, R), dtype=torch.float32, device=dev)
     dbu = torch.empty((nsb, N, R), dtype=torch.float32, device=dev)
     dad = torch.empty((nsb, R, N), dtype=torch.float32, device=dev)
@@ -188,7 +189,7 @@ def _bwd_launch(gu, xs, dhm, dxd, bg, bu, ad, s_g, s_u, need_q):
 def mlp_bwd(gu, xs, dhm, dxd, bg, bu, ad, s_g, s_u, need_q):
     """-> (q_dgu [T, 2N] fp8, s_dgu, [dxa_gate | dxa_up | xS_down] [T, 3R] fp32 (dxa not yet scaled by s),
     dBg, dBu [N, R] fp32 (not scaled), dAd [R, N]) -- scripts/fused_mlp.py:235-259."""
-    q, s, (dxa, dbg, dbu, dad, sb, ncg) = _bwd_launch(gu, xs, dhm, dxd, bg, bu, ad, s_g, s_u, need_q)
+    q, s, (dxa, dbg, dbu, dad, sb, ncg) = _bwd_launch(gu, xs, dhm, dxd, bg, bu, ad, s_g, s_u, need_q, True)
     red = lambda p: p[0] if p.shape[0] == 1 else p.sum(0)  # noqa: E731  (fixed order on one device)
     return (q, s.view(_E8) if need_q else None, red(dxa), red(dbg), red(dbu), red(dad))
 
