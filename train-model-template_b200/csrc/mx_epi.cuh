@@ -22,6 +22,10 @@ MX_DEV void stg16_if(void* p, uint32_t v, bool pred) {
   asm volatile("{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %2, 0;\n\t@q st.global.b16 [%0], %1;\n\t}" ::"l"(p),
                "h"((uint16_t)v), "r"((int)pred));
 }
+MX_DEV void stg64_if(void* p, uint32_t lo, uint32_t hi, bool pred) {
+  asm volatile("{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %3, 0;\n\t@q st.global.v2.b32 [%0], {%1, %2};\n\t}" ::"l"(p),
+               "r"(lo), "r"(hi), "r"((int)pred));
+}
 MX_DEV void stg8_if(void* p, uint32_t v, bool pred) {
   asm volatile("{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %2, 0;\n\t@q st.global.b8 [%0], %1;\n\t}" ::"l"(p),
                "h"((uint16_t)v), "r"((int)pred));
@@ -79,9 +83,24 @@ MX_DEV QRows qrows_init(int64_t row_g, int64_t T, int64_t Tpad, uint8_t* q, int6
   return r;
 }
 
+// Quad transpose of 16-bit pairs: lane t of each quad holds c[i] (the codes of columns 8i+2t, +1,
+// i = 0..3) as r0 = c0 | c1 << 16, r1 = c2 | c3 << 16; afterwards it holds the codes of its own 8
+// columns 8t .. 8t+7 in order (r0 = columns 8t .. 8t+3, r1 = 8t+4 .. 8t+7).  Two steps: swap the
+// off-diagonal 2 x 2 blocks between lanes t and t ^ 2, then transpose each 2 x 2 block between t, t ^ 1.
+MX_DEV void quad_transpose16(uint32_t& r0, uint32_t& r1, int t) {
+  const bool lo = t < 2;
+  const uint32_t got = __shfl_xor_sync(0xffffffffu, lo ? r1 : r0, 2);
+  if (lo) r1 = got; else r0 = got;
+  const uint32_t o0 = __shfl_xor_sync(0xffffffffu, r0, 1), o1 = __shfl_xor_sync(0xffffffffu, r1, 1);
+  const bool even = (t & 1) == 0;
+  r0 = even ? __byte_perm(r0, o0, 0x5410) : __byte_perm(o0, r0, 0x7632);
+  r1 = even ? __byte_perm(r1, o1, 0x5410) : __byte_perm(o1, r1, 0x7632);
+}
+
 // Quantizes one 32-column block (columns col0 .. col0+31, col0 % 32 == 0) of a 16-row warp tile whose
 // bf16 values are held packed in D-fragment form: pk[i][h] = (row g + 8h, cols 8i+2t, +1), i = 0..3
-// (t = lane % 4).  Codes and the two rows' scales go to the targets of `qr`.
+// (t = lane % 4).  Codes and the two rows' scales go to the targets of `qr`; after a quad transpose
+// each lane writes 8 consecutive codes, so a quad fills the row's 32-byte sector in one store.
 MX_DEV void quant_block16p(const uint32_t (&pk)[4][2], const QRows& qr, int64_t col0, int t) {
   const int64_t soff = ((col0 >> 7) << 9) + ((col0 >> 5) & 3);  // k-block col0/32 in the blocked layout
 #pragma unroll
@@ -92,13 +111,16 @@ MX_DEV void quant_block16p(const uint32_t (&pk)[4][2], const QRows& qr, int64_t 
     m = nanmax(m, __shfl_xor_sync(0xffffffffu, m, 2));
     const uint32_t e = mx_e8m0_of_amax(m);
     const float rcp = mx_e8m0_rcp(e);
-    uint8_t* dst = qr.code[h] + col0;
     const float2 r2 = make_float2(rcp, rcp);
+    uint32_t c[4];
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       const float2 v = __fmul2_rn(up2(pk[i][h]), r2);
-      stg16_if(dst + 8 * i, e4m3x2_sat(v.x, v.y), qr.live[h]);
+      c[i] = e4m3x2_sat(v.x, v.y);
     }
+    uint32_t r0 = __byte_perm(c[0], c[1], 0x5410), r1 = __byte_perm(c[2], c[3], 0x5410);
+    quad_transpose16(r0, r1, t);
+    stg64_if(qr.code[h] + col0 + 6 * t, r0, r1, qr.live[h]);   // code[h] already points at column 2t
     stg8_if(qr.scale[h] + soff, e, qr.slive[h]);
   }
 }
