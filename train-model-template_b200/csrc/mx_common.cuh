@@ -134,6 +134,15 @@ MX_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Non-blocking test of the phase with the given parity (for a warp that polls more than one barrier).
+MX_DEV bool mbar_test(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tmbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity) : "memory");
+  return ok != 0;
+}
+
 // Waits for the phase with the given parity to complete.  Gives up after `limit_ns` of wall
 // time (globaltimer), records `err` and returns false: no wait in these kernels is unbounded.
 #ifndef MX_WAIT_LIMIT_NS

@@ -214,19 +214,17 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
 // SB = 16 x CONS rows, 32-column tile), column tile fastest.  Warp CONS streams, per item, the [SB x 32]
 // bf16 tiles of g, u and dh (64-byte swizzle) plus the tile's slices of B_gate, B_up ([32 x r]) and
 // A_down ([r x 32]) into a 3-stage ring with TMA, and, when the run enters a row block, the block's xs
-// and dxd rows (once the consumers release the previous block's: rows_empty).  Consumer warps
-// 0 .. CONS-1 each own 16 rows of the current block:
+// and dxd rows.  Consumer warps 0 .. CONS-1 each own 16 rows of the current block:
 //   * dg, du, h of the tile are computed in registers, quantized, and multiplied by the B slices into
 //     the per-row sums dxa_gate, dxa_up, xS_down, which stay in registers while the run stays in the
 //     row block and are then stored into this CTA's slot of the fp32 partials;
-//   * dg, du, h are also stored (bf16, the same swizzle) into a shared operand tile.  When every warp has
-//     stored its rows (mbarrier op_full), the 6 (r = 16) or 12 (r = 32) 16 x 16 blocks of dB_gate^T,
-//     dB_up^T and dA_down -- dealt out to the warps in turn, a different set each tile -- are each
-//     reduced over the block's SB rows with mma (xa^T from the row buffer) and stored as the block's
-//     partial; the operand tile is released (op_empty) for the next tile's stores.  Warps without a
-//     block go straight on to the next tile.
-// Four warps per scheduler (r = 16) hide the latency of the per-element chains.  No atomics: the result
-// is deterministic.
+//   * dg, du, h are also stored (bf16, the same swizzle) into a shared operand tile (op_full when every
+//     consumer warp has stored its rows).
+// Warp CONS also reduces the operand tile over the block's SB rows into the column products dB_gate^T,
+// dB_up^T and dA_down (mma, xa^T from the row buffer) while the consumers go on to the next tile, and
+// then releases it (op_empty): the consumers never wait on those reductions unless they run a whole
+// tile ahead.  Four warps per scheduler (r = 16) hide the latency of the per-element chains.  No
+// atomics: the result is deterministic.
 constexpr int BWD_BN = 32, BWD_ST = 3;
 // consumer warps: 16 warps in all (4 per scheduler, 128 registers) for r = 16; 12 (3 per scheduler,
 // 168 registers) for r = 32, whose per-row sums and fragments need more registers.  (14 consumers
@@ -253,7 +251,6 @@ __global__ void __launch_bounds__(32 * (bwd_cons(R) + 1), 1)
               int* err) {
   constexpr int CONS = bwd_cons(R), SB = bwd_rows(R), KS = R / 16, NT = BWD_BN / 8, R3 = 3 * R;
   constexpr int TILE = bwd_tile(R), BT = bwd_btile(R), STG = bwd_stage(R);
-  constexpr int TASKS = 3 * 2 * KS;  // column-product blocks: {dBg, dBu, dAd} x (r / 16) x 2 column halves
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
   uint8_t* rows_xs = smem + BWD_ST * STG;             // [SB][2r] bf16, TMA-swizzled
@@ -278,12 +275,12 @@ __global__ void __launch_bounds__(32 * (bwd_cons(R) + 1), 1)
     mbar_init(rows_full, 1);
     mbar_init(rows_empty, CONS);
     mbar_init(op_full, CONS);
-    mbar_init(op_empty, TASKS);
+    mbar_init(op_empty, 1);
     fence_barrier_init();
   }
   __syncthreads();
 
-  if (warp == CONS) {  // TMA producer
+  if (warp == CONS) {  // TMA producer and column products
     if (lane == 0) {
       prefetch_tmap(&tm_gu);
       prefetch_tmap(&tm_dh);
@@ -291,42 +288,138 @@ __global__ void __launch_bounds__(32 * (bwd_cons(R) + 1), 1)
       prefetch_tmap(&tm_bu);
       prefetch_tmap(&tm_ad);
     }
+    const int g = lane >> 2, t = lane & 3, mi = lane >> 3, lr = lane & 7;
+    const uint32_t s_xs = smem_u32(rows_xs), s_dxd = smem_u32(rows_dxd), ob = smem_u32(opbuf);
+    // Column products of one stored tile: dB_gate^T = xa_gate^T dg, dB_up^T = xa_up^T du and
+    // dA_down = dxd^T h, each reduced over the block's SB rows with mma (A = xa^T from the row buffer,
+    // B = the operand tile, both through ldmatrix.trans; the offsets advance by 16 rows per k-step, the
+    // swizzles only use row bits 0-2) and stored as the block's partial.  Three (product, 16-row block
+    // of r) pairs per pass, both 16-column halves of the tile: 12 independent accumulator chains.
+    auto column_products = [&](int sbi, int n0) {
+      constexpr int PM = 3 * KS, BATCH = 3;
+#pragma unroll
+      for (int pm0 = 0; pm0 < PM; pm0 += BATCH) {
+        float acc[BATCH][2][2][4] = {};
+        uint32_t pa[BATCH], pb[BATCH][2];
+#pragma unroll
+        for (int b = 0; b < BATCH; ++b) {
+          const int prod = (pm0 + b) / KS, mt = (pm0 + b) % KS;
+          const uint32_t arow = (uint32_t)((mi >> 1) * 8 + lr);
+          pa[b] = prod < 2 ? s_xs + swz<4 * R>(arow, (uint32_t)(prod * 2 * KS + 2 * mt + (mi & 1)))
+                           : s_dxd + swz<2 * R>(arow, (uint32_t)(2 * mt + (mi & 1)));
+#pragma unroll
+          for (int nh = 0; nh < 2; ++nh)
+            pb[b][nh] = ob + (uint32_t)prod * TILE + swz<64>((uint32_t)((mi & 1) * 8 + lr), (uint32_t)(2 * nh + (mi >> 1)));
+        }
+#pragma unroll 5
+        for (int kk = 0; kk < CONS; ++kk) {
+#pragma unroll
+          for (int b = 0; b < BATCH; ++b) {
+            const int prod = (pm0 + b) / KS;
+            uint32_t A[4];
+            ldsm4t(A, pa[b]);
+            pa[b] += prod < 2 ? 16u * 4u * R : 16u * 2u * R;
+#pragma unroll
+            for (int nh = 0; nh < 2; ++nh) {
+              uint32_t B[4];
+              ldsm4t(B, pb[b][nh]);
+              pb[b][nh] += 16u * 64u;
+              mma16816(acc[b][nh][0], A, B[0], B[1]);
+              mma16816(acc[b][nh][1], A, B[2], B[3]);
+            }
+          }
+        }
+#pragma unroll
+        for (int b = 0; b < BATCH; ++b) {
+          const int prod = (pm0 + b) / KS, mt = (pm0 + b) % KS, j = 16 * mt + g;
+#pragma unroll
+          for (int nh = 0; nh < 2; ++nh)
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              const int n = n0 + 16 * nh + 8 * h + 2 * t;
+              const float* a = acc[b][nh][h];
+              if (prod < 2) {   // [n_blocks, N, r]: element (n, j)
+                float* P = (prod == 0 ? dbg_part : dbu_part) + ((int64_t)sbi * N + n) * R + j;
+                P[0] = a[0];
+                P[R] = a[1];
+                P[8] = a[2];
+                P[R + 8] = a[3];
+              } else {          // [n_blocks, r, N]: element (j, n)
+                float* P = dad_part + ((int64_t)sbi * R + j) * N + n;
+                *reinterpret_cast<float2*>(P) = make_float2(a[0], a[1]);
+                *reinterpret_cast<float2*>(P + 8 * (int64_t)N) = make_float2(a[2], a[3]);
+              }
+            }
+        }
+      }
+    };
+    // Three queues, polled in turn (lane 0 tests, the warp follows): the next row block's xs / dxd rows
+    // (once the consumers have their fragments of the current block and this warp's column products of
+    // the block are done), the next tile's loads (once its ring stage is free), and the column products
+    // of the oldest stored tile (once every consumer warp stored it: op_full).
+    const int cnt = it_hi - it_lo;
     int stage = 0;
     uint32_t phase = 0;
-    int issued = 0, row_loads = 0, cur_sbi = -1;
-    for (int it = it_lo; it < it_hi; ++it) {
-      const int sbi = it / nt, n0 = (it % nt) * BWD_BN, r0 = sbi * SB;
-      if (!mbar_wait(&empty[stage], phase ^ 1, err, MX_DEV_TIMEOUT_PRODUCER)) break;
-      if (lane == 0) {
-        uint8_t* dst = smem + stage * STG;
-        uint64_t* fb = &full[stage];
-        mbar_arrive_expect_tx(fb, STG);
-        tma_load_2d(dst, &tm_gu, fb, n0, r0);
-        tma_load_2d(dst + TILE, &tm_gu, fb, N + n0, r0);
-        tma_load_2d(dst + 2 * TILE, &tm_dh, fb, n0, r0);
-        tma_load_2d(dst + 3 * TILE, &tm_bg, fb, 0, n0);
-        tma_load_2d(dst + 3 * TILE + BT, &tm_bu, fb, 0, n0);
-        tma_load_2d(dst + 3 * TILE + 2 * BT, &tm_ad, fb, n0, 0);
+    int issued = 0, tasked = 0, row_loads = 0, rows_at = 0;   // rows_at: first item of the next row block
+    uint64_t t0 = mx_globaltimer();
+    while (tasked < cnt) {
+      bool prog = false;
+      if (rows_at < cnt && tasked == rows_at) {
+        const bool rdy = row_loads == 0 ||
+                         __shfl_sync(0xffffffffu, lane == 0 ? (int)mbar_test(rows_empty, (uint32_t)((row_loads - 1) & 1)) : 0, 0);
+        if (rdy) {
+          const int sbr = (it_lo + rows_at) / nt;
+          if (lane == 0) {
+            mbar_arrive_expect_tx(rows_full, (uint32_t)(SB * 3 * R * 2));
+            tma_load_2d(rows_xs, &tm_xs, rows_full, 0, sbr * SB);
+            tma_load_2d(rows_dxd, &tm_dxd, rows_full, 0, sbr * SB);
+          }
+          __syncwarp();
+          ++row_loads;
+          rows_at = (sbr + 1) * nt - it_lo;
+          prog = true;
+        }
       }
-      __syncwarp();
-      ++issued;
-      if (++stage == BWD_ST) {
-        stage = 0;
-        phase ^= 1;
-      }
-      // a new row block: its xs / dxd rows, once the consumers are done with the last block's (the
-      // block's first tile is already on its way)
-      if (sbi != cur_sbi) {
-        if (cur_sbi >= 0 && !mbar_wait(rows_empty, (uint32_t)((row_loads - 1) & 1), err, MX_DEV_TIMEOUT_PRODUCER))
-          break;
+      if (issued < cnt && __shfl_sync(0xffffffffu, lane == 0 ? (int)mbar_test(&empty[stage], phase ^ 1) : 0, 0)) {
+        const int it = it_lo + issued;
+        const int n0 = (it % nt) * BWD_BN, r0 = (it / nt) * SB;
         if (lane == 0) {
-          mbar_arrive_expect_tx(rows_full, (uint32_t)(SB * 3 * R * 2));
-          tma_load_2d(rows_xs, &tm_xs, rows_full, 0, r0);
-          tma_load_2d(rows_dxd, &tm_dxd, rows_full, 0, r0);
+          uint8_t* dst = smem + stage * STG;
+          uint64_t* fb = &full[stage];
+          mbar_arrive_expect_tx(fb, STG);
+          tma_load_2d(dst, &tm_gu, fb, n0, r0);
+          tma_load_2d(dst + TILE, &tm_gu, fb, N + n0, r0);
+          tma_load_2d(dst + 2 * TILE, &tm_dh, fb, n0, r0);
+          tma_load_2d(dst + 3 * TILE, &tm_bg, fb, 0, n0);
+          tma_load_2d(dst + 3 * TILE + BT, &tm_bu, fb, 0, n0);
+          tma_load_2d(dst + 3 * TILE + 2 * BT, &tm_ad, fb, n0, 0);
         }
         __syncwarp();
-        ++row_loads;
-        cur_sbi = sbi;
+        ++issued;
+        if (++stage == BWD_ST) {
+          stage = 0;
+          phase ^= 1;
+        }
+        prog = true;
+      }
+      if (tasked < issued &&
+          __shfl_sync(0xffffffffu, lane == 0 ? (int)mbar_test(op_full, (uint32_t)(tasked & 1)) : 0, 0)) {
+        mbar_wait(op_full, (uint32_t)(tasked & 1), err, MX_DEV_TIMEOUT_PRODUCER);   // complete: acquire, every lane
+        const int it = it_lo + tasked;
+        column_products(it / nt, (it % nt) * BWD_BN);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(op_empty);
+        ++tasked;
+        prog = true;
+      }
+      if (prog) {
+        t0 = mx_globaltimer();
+      } else {
+        if (mx_globaltimer() - t0 > MX_WAIT_LIMIT_NS) {
+          if (lane == 0) mx_set_error(err, MX_DEV_TIMEOUT_PRODUCER);
+          break;
+        }
+        __nanosleep(64);
       }
     }
     // leave no copy in flight: wait (bounded) for the last load of every stage that was used
@@ -406,6 +499,8 @@ __global__ void __launch_bounds__(32 * (bwd_cons(R) + 1), 1)
         ldsm4(axu[kk], s_xs + swz<4 * R>((uint32_t)lrow, (uint32_t)(2 * KS + 2 * kk + (mi >> 1))));
         ldsm4(axd[kk], s_dxd + swz<2 * R>((uint32_t)lrow, (uint32_t)(2 * kk + (mi >> 1))));
       }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(rows_empty);   // the block's rows are in registers now
 #pragma unroll
       for (int j = 0; j < R / 8; ++j)
 #pragma unroll
@@ -498,60 +593,9 @@ __global__ void __launch_bounds__(32 * (bwd_cons(R) + 1), 1)
       stage = 0;
       phase ^= 1;
     }
-    // column-product blocks: task -> product prod (0: dB_gate^T = xa_gate^T dg, 1: dB_up^T = xa_up^T du,
-    // 2: dA_down = dxd^T h), rows j 16 mt .. +15, tile columns 16 nh .. +15.  A = xa^T through
-    // ldmatrix.trans of the row buffer, B = the operand tile through ldmatrix.trans; both offsets
-    // advance by 16 rows per k-step (the swizzles only use row bits 0-2).
-    bool ok = true;
-    for (int task = (warp + CONS - (ct * TASKS) % CONS) % CONS; task < TASKS; task += CONS) {
-      if (!mbar_wait(op_full, (uint32_t)(ct & 1), err, MX_DEV_TIMEOUT_EPILOGUE)) {
-        ok = false;
-        break;
-      }
-      const int prod = task / (2 * KS), mt = (task >> 1) % KS, nh = task & 1;
-      const uint32_t arow = (uint32_t)((mi >> 1) * 8 + lr);
-      uint32_t pa = prod < 2 ? s_xs + swz<4 * R>(arow, (uint32_t)(prod * 2 * KS + 2 * mt + (mi & 1)))
-                             : s_dxd + swz<2 * R>(arow, (uint32_t)(2 * mt + (mi & 1)));
-      const uint32_t a_step = prod < 2 ? 16u * 4u * R : 16u * 2u * R;
-      uint32_t pb = ob + (uint32_t)prod * TILE + swz<64>((uint32_t)((mi & 1) * 8 + lr), (uint32_t)(2 * nh + (mi >> 1)));
-      float acc[2][4] = {};
-#pragma unroll 4
-      for (int kk = 0; kk < CONS; ++kk) {
-        uint32_t A[4], B[4];
-        ldsm4t(A, pa);
-        ldsm4t(B, pb);
-        mma16816(acc[0], A, B[0], B[1]);
-        mma16816(acc[1], A, B[2], B[3]);
-        pa += a_step;
-        pb += 16u * 64u;
-      }
-      const int j = 16 * mt + g;
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const int n = n0 + 16 * nh + 8 * h + 2 * t;
-        if (prod < 2) {   // [n_blocks, N, r]: element (n, j)
-          float* P = (prod == 0 ? dbg_part : dbu_part) + ((int64_t)sbi * N + n) * R + j;
-          P[0] = acc[h][0];
-          P[R] = acc[h][1];
-          P[8] = acc[h][2];
-          P[R + 8] = acc[h][3];
-        } else {          // [n_blocks, r, N]: element (j, n)
-          float* P = dad_part + ((int64_t)sbi * R + j) * N + n;
-          *reinterpret_cast<float2*>(P) = make_float2(acc[h][0], acc[h][1]);
-          *reinterpret_cast<float2*>(P + 8 * (int64_t)N) = make_float2(acc[h][2], acc[h][3]);
-        }
-      }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(op_empty);
-    }
-    if (!ok) break;
     const bool last = ct + 1 == cnt;
     if ((n0 += BWD_BN) == N || last) {   // leaving the row block
       flush_rows(sbi);
-      if (!last) {
-        __syncwarp();
-        if (lane == 0) mbar_arrive(rows_empty);
-      }
       n0 = 0;
       ++sbi;
     }
