@@ -173,6 +173,16 @@ MX_DEV void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar)
   asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
                ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar)) : "memory");
 }
+// Tiled store shared -> global (bulk-group completion): x = innermost coordinate (elements), y = row.
+MX_DEV void tma_store_2d(const CUtensorMap* map, const void* src, int32_t x, int32_t y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];"
+               ::"l"(map), "r"(x), "r"(y), "r"(smem_u32(src)) : "memory");
+}
+MX_DEV void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// The shared-memory sources of this thread's committed bulk stores have been read.
+MX_DEV void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// This thread's committed bulk stores are complete.
+MX_DEV void bulk_wait0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 MX_DEV void prefetch_tmap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
 }

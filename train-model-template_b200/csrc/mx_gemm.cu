@@ -252,8 +252,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 // up columns N + 128 tn .. of the same 128 outputs: its B stage is two TMA boxes of W_gu rows (gate, up)
 // and its two B scale blocks are the matching ones, so one tcgen05 accumulator holds both halves of 128
 // (g, u) column pairs.  Producer / MMA warps as in k_mx_gemm (3 stages).  The 8 epilogue warps drain the
-// accumulator (warp q|h: lanes 32q.., half h = gate / up), hand it back, store gu (bf16; the backward
-// reads it) and stage the same bf16 tile in shared memory; after one named barrier each warp runs the
+// accumulator (warp q|h: lanes 32q.., half h = gate / up), hand it back and stage the bf16 tile in
+// shared memory (128-byte swizzle), from which four TMA stores write gu (the backward reads it) in full
+// 128-byte rows; after one named barrier each warp runs the
 // forward epilogue on 16 rows x 128 pairs of the staged tile -- the LoRA-B terms with mma.sync, SwiGLU,
 // the MXFP8 codes of h, and the per-row xS_down = h A_down^T accumulated in registers -- while the MMAs
 // of the next tile proceed.  A CTA works through a contiguous range of tiles (column tiles fastest), so
@@ -273,8 +274,9 @@ MX_DEV void epi_sync() { asm volatile("bar.sync 1, %0;" ::"r"(EPI_THREADS) : "me
 template <int R>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     k_mx_gemm_glu(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                  const uint8_t* __restrict__ sa, const uint8_t* __restrict__ sb, int M, int N, int K,
-                  __nv_bfloat16* __restrict__ gu, const __nv_bfloat16* __restrict__ xs,
+                  const __grid_constant__ CUtensorMap tmG, const uint8_t* __restrict__ sa,
+                  const uint8_t* __restrict__ sb, int M, int N, int K,
+                  const __nv_bfloat16* __restrict__ xs,
                   const __nv_bfloat16* __restrict__ bg, const __nv_bfloat16* __restrict__ bu,
                   const __nv_bfloat16* __restrict__ ad, float s_g, float s_u, uint8_t* __restrict__ qh,
                   uint8_t* __restrict__ sh, float* __restrict__ xsd_part, int per, int* err) {
@@ -456,8 +458,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       {
         const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + h * 128;
         const int rl = q * 32 + lane;
-        const int64_t row = (int64_t)tm * BM + rl;
-        uint4* dst = reinterpret_cast<uint4*>(gu + row * (2 * (int64_t)N) + (h ? N : 0) + (int64_t)tn * 128);
         const uint32_t sbase = s_stg + (uint32_t)h * (2 * 128 * 128);
 #pragma unroll
         for (int c2 = 0; c2 < 2; ++c2) {   // 64 columns at a time (one staged sub-tile)
@@ -478,7 +478,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
               o.y = pack_bf16x2(__uint_as_float(r[c][8 * j + 2]), __uint_as_float(r[c][8 * j + 3]));
               o.z = pack_bf16x2(__uint_as_float(r[c][8 * j + 4]), __uint_as_float(r[c][8 * j + 5]));
               o.w = pack_bf16x2(__uint_as_float(r[c][8 * j + 6]), __uint_as_float(r[c][8 * j + 7]));
-              if (row < M) dst[8 * c2 + 4 * c + j] = o;
               // column 64 c2 + 32 c + 8 j of the half: sub-tile c2, chunk 4 c + j
               const uint32_t a = sbase + (uint32_t)c2 * (128 * 128) + swz<128>((uint32_t)rl, (uint32_t)(4 * c + j));
               asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(o.x), "r"(o.y), "r"(o.z),
@@ -486,6 +485,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             }
         }
         acc_phase ^= 1;
+        fence_proxy_async();   // the staged tile is read by the TMA stores below
       }
       // 2. this tile's B_gate / B_up rows and A_down columns into shared memory
       for (int i = et; i < 128 * (R / 8); i += EPI_THREADS) {
@@ -506,6 +506,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                      : "memory");
       }
       epi_sync();
+      // gu leaves from the staged tile: four [128 x 64] boxes (gate, up) x (sub-tile), rows >= M clipped
+      if (et == 0) {
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh)
+#pragma unroll
+          for (int c2 = 0; c2 < 2; ++c2)
+            tma_store_2d(&tmG, stg + (hh * 2 + c2) * (128 * 128), hh * N + tn * 128 + c2 * 64, tm * BM);
+        bulk_commit();
+      }
       // 3. the forward epilogue on rows 16e .. 16e+15, two 64-column sub-tiles
 #pragma unroll 1
       for (int sbk = 0; sbk < 2; ++sbk) {
@@ -558,8 +567,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           }
         }
       }
+      if (et == 0) bulk_wait_read0();   // the gu stores have read the staged tile
       epi_sync();   // staged tile and slices are free for the next tile
     }
+    if (et == 0) bulk_wait0();
     if (cur_tm >= 0) flush(cur_tm);
   }
 
@@ -693,12 +704,15 @@ extern "C" int mxm_gemm_glu(const void* qa, int64_t lda, const void* sa, const v
                "mxm_gemm_glu: alignment");
   int per = 0, grid = 0, slots = 0;
   if (int e = mxm_gemm_glu_partition(M, N, &per, &grid, &slots)) return e;
-  CUtensorMap tmA, tmB;
+  CUtensorMap tmA, tmB, tmG;
   if (int st = mx_make_tmap_2d(&tmA, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, qa, (uint64_t)K, (uint64_t)M, (uint64_t)lda, BK,
                                BM, CU_TENSOR_MAP_SWIZZLE_128B))
     return st;
   if (int st = mx_make_tmap_2d(&tmB, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, qb, (uint64_t)K, (uint64_t)(2 * N),
                                (uint64_t)ldb, BK, 128, CU_TENSOR_MAP_SWIZZLE_128B))
+    return st;
+  if (int st = mx_make_tmap_2d(&tmG, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, gu, (uint64_t)(2 * N), (uint64_t)M,
+                               (uint64_t)(4 * N), 64, BM, CU_TENSOR_MAP_SWIZZLE_128B))
     return st;
   static bool attr_done[64] = {};
   int dev = 0;
@@ -710,8 +724,8 @@ extern "C" int mxm_gemm_glu(const void* qa, int64_t lda, const void* sa, const v
     attr_done[dev] = true;
   }
   cudaStream_t st = (cudaStream_t)stream;
-  k_mx_gemm_glu<16><<<grid, NUM_THREADS, smem, st>>>(tmA, tmB, (const uint8_t*)sa, (const uint8_t*)sb, (int)M, (int)N,
-                                                     (int)K, (__nv_bfloat16*)gu, (const __nv_bfloat16*)xs,
+  k_mx_gemm_glu<16><<<grid, NUM_THREADS, smem, st>>>(tmA, tmB, tmG, (const uint8_t*)sa, (const uint8_t*)sb, (int)M, (int)N,
+                                                     (int)K, (const __nv_bfloat16*)xs,
                                                      (const __nv_bfloat16*)bg, (const __nv_bfloat16*)bu,
                                                      (const __nv_bfloat16*)ad, s_g, s_u, (uint8_t*)qh, (uint8_t*)sh,
                                                      (float*)xsd_part, per, mx_dev_error_ptr());
