@@ -26,6 +26,10 @@ MX_DEV void stg64_if(void* p, uint32_t lo, uint32_t hi, bool pred) {
   asm volatile("{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %3, 0;\n\t@q st.global.v2.b32 [%0], {%1, %2};\n\t}" ::"l"(p),
                "r"(lo), "r"(hi), "r"((int)pred));
 }
+MX_DEV void stg128_if(void* p, uint32_t a, uint32_t b, uint32_t c, uint32_t d, bool pred) {
+  asm volatile("{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %5, 0;\n\t@q st.global.v4.b32 [%0], {%1, %2, %3, %4};\n\t}" ::"l"(p),
+               "r"(a), "r"(b), "r"(c), "r"(d), "r"((int)pred));
+}
 MX_DEV void stg8_if(void* p, uint32_t v, bool pred) {
   asm volatile("{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %2, 0;\n\t@q st.global.b8 [%0], %1;\n\t}" ::"l"(p),
                "h"((uint16_t)v), "r"((int)pred));

@@ -724,6 +724,204 @@ __global__ void __launch_bounds__(128) k_rowdot(const bf16* __restrict__ A, int6
   }
 }
 
+// The same products with TMA, for B small enough to stay in shared memory (NJ x K x 2 bytes <= RD_B_MAX):
+// CTA = 128-row blocks (persistent, stride gridDim.x); warp 8 streams [128 rows x 64 k] boxes of A
+// (128-byte swizzle) into an RD_ST-stage ring, and during the CTA's first row block also the matching
+// [NJ x 64 k] boxes of B into a buffer that then serves every later block.  Consumer warps 0-7 each own
+// 16 rows for the whole K: mma A fragments by ldmatrix from the ring, B fragments from the B buffer, fp32
+// sums in registers, so no cross-warp reduction.  With QUANT the warp also quantizes its rows of each
+// box straight from the ring, two lanes per 32-k block (the same arithmetic as quant8_lane), each lane
+// storing 16 codes so that one store instruction covers 8 rows x 64 contiguous bytes.
+constexpr int RD_ROWS = 128, RD_KB = 64, RD_CONS = 8;
+constexpr int RD_A_BYTES = RD_ROWS * RD_KB * 2;   // 16 KB
+constexpr size_t RD_SMEM_MAX = 220 * 1024, RD_B_MAX = RD_SMEM_MAX - 1024 - 2 * RD_A_BYTES - 256;
+__host__ __device__ inline int rd_stages(int64_t b_bytes) {
+  const int64_t st = ((int64_t)RD_SMEM_MAX - 1024 - 256 - b_bytes) / RD_A_BYTES;
+  return st > 6 ? 6 : (int)st;
+}
+__host__ __device__ inline size_t rd_smem(int64_t b_bytes, int st) { return 1024 + (size_t)b_bytes + (size_t)st * RD_A_BYTES + 256; }
+
+template <int NJ, bool QUANT>
+__global__ void __launch_bounds__(32 * (RD_CONS + 1), 1)
+    k_rowdot_tma(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b, int T, int K,
+                 int nrb, int stages, float post, int round_once, bf16* __restrict__ out, int64_t ldo,
+                 uint8_t* __restrict__ q, int64_t ldq, uint8_t* __restrict__ s, int64_t scols, int kb_off, int* err) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align1024(smem_raw);
+  const int nkb = K / RD_KB;
+  uint8_t* sB = smem;                                            // [nkb][NJ rows x 128 B]
+  uint8_t* sA = sB + (size_t)nkb * NJ * 128;                     // [stages][128 rows x 128 B]
+  uint64_t* full = reinterpret_cast<uint64_t*>(sA + (size_t)stages * RD_A_BYTES);
+  uint64_t* empty = full + stages;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < stages; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], RD_CONS);
+    }
+    fence_barrier_init();
+  }
+  __syncthreads();
+
+  if (warp == RD_CONS) {   // TMA producer
+    int stage = 0, issued = 0;
+    uint32_t phase = 0;
+    bool ok = true;
+    for (int rb = blockIdx.x, first = 1; rb < nrb && ok; rb += gridDim.x, first = 0) {
+      for (int kb = 0; kb < nkb; ++kb) {
+        if (!mbar_wait(&empty[stage], phase ^ 1, err, MX_DEV_TIMEOUT_PRODUCER)) {
+          ok = false;
+          break;
+        }
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&full[stage], RD_A_BYTES + (first ? NJ * 128 : 0));
+          tma_load_2d(sA + (size_t)stage * RD_A_BYTES, &tm_a, &full[stage], kb * RD_KB, rb * RD_ROWS);
+          if (first) tma_load_2d(sB + (size_t)kb * NJ * 128, &tm_b, &full[stage], kb * RD_KB, 0);
+        }
+        __syncwarp();
+        ++issued;
+        if (++stage == stages) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+    }
+    for (int k = 0; k < stages && k < issued; ++k) {   // no copy left in flight
+      const int i = issued - 1 - k;
+      mbar_wait(&full[i % stages], (uint32_t)((i / stages) & 1), err, MX_DEV_TIMEOUT_PRODUCER);
+    }
+    return;
+  }
+
+  const int g = lane >> 2, t = lane & 3, mi = lane >> 3, lr = lane & 7;
+  // ldmatrix offsets within a box: A rows 16 warp + 8 (mi & 1) + lr, k-chunk 2 kk + (mi >> 1);
+  // B rows (n) 8 (2 jp + (mi >> 1)) + lr, k-chunk 2 kk + (mi & 1)
+  const uint32_t arow = (uint32_t)(warp * 16 + (mi & 1) * 8 + lr);
+  const uint32_t s_a = smem_u32(sA), s_b = smem_u32(sB);
+  int stage = 0;
+  uint32_t phase = 0;
+  for (int rb = blockIdx.x; rb < nrb; rb += gridDim.x) {
+    float acc[NJ / 8][4];
+#pragma unroll
+    for (int j = 0; j < NJ / 8; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
+    bool ok = true;
+    for (int kb = 0; kb < nkb; ++kb) {
+      if (!mbar_wait(&full[stage], phase, err, MX_DEV_TIMEOUT_EPILOGUE)) {
+        ok = false;
+        break;
+      }
+      const uint32_t ab = s_a + (uint32_t)stage * RD_A_BYTES, bb = s_b + (uint32_t)kb * NJ * 128;
+#pragma unroll
+      for (int kk = 0; kk < RD_KB / 16; ++kk) {
+        uint32_t A[4];
+        ldsm4(A, ab + swz<128>(arow, (uint32_t)(2 * kk + (mi >> 1))));
+#pragma unroll
+        for (int jp = 0; jp < NJ / 16; ++jp) {
+          uint32_t B[4];
+          ldsm4(B, bb + swz<128>((uint32_t)(8 * (2 * jp + (mi >> 1)) + lr), (uint32_t)(2 * kk + (mi & 1))));
+          mma16816(acc[2 * jp], A, B[0], B[1]);
+          mma16816(acc[2 * jp + 1], A, B[2], B[3]);
+        }
+      }
+      if (QUANT) {
+        // two passes of 8 rows: lanes 4i .. 4i+3 hold row 8 pass + i of the warp's 16 -- (block 0 | 1) x
+        // (16-element half 0 | 1) -- so each store instruction writes 8 rows x 64 contiguous bytes
+#pragma unroll
+        for (int pass = 0; pass < 2; ++pass) {
+          const uint32_t row = (uint32_t)(warp * 16 + 8 * pass + (lane >> 2));
+          const uint32_t blk = (uint32_t)((lane >> 1) & 1), half = (uint32_t)(lane & 1);
+          uint32_t v[8];
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            const uint32_t a = ab + swz<128>(row, 4 * blk + 2 * half + (uint32_t)c);
+            asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                         : "=r"(v[4 * c]), "=r"(v[4 * c + 1]), "=r"(v[4 * c + 2]), "=r"(v[4 * c + 3]) : "r"(a));
+          }
+          const uint32_t m4 = max_bf16x2(max_bf16x2(absmax_bf16x2(v[0], v[1]), absmax_bf16x2(v[2], v[3])),
+                                         max_bf16x2(absmax_bf16x2(v[4], v[5]), absmax_bf16x2(v[6], v[7])));
+          float m = nanmax(bf16_lo(m4), bf16_hi(m4));
+          m = nanmax(m, __shfl_xor_sync(0xffffffffu, m, 1));   // the other half of the 32-k block
+          const uint32_t e = mx_e8m0_of_amax(m);
+          const float rcp = mx_e8m0_rcp(e);
+          const float2 r2 = make_float2(rcp, rcp);
+          uint32_t w[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float2 x0 = __fmul2_rn(up2(v[2 * i]), r2), x1 = __fmul2_rn(up2(v[2 * i + 1]), r2);
+            w[i] = nan_canon4(e4m3x2_sat(x0.x, x0.y) | (e4m3x2_sat(x1.x, x1.y) << 16));
+          }
+          const int64_t rg_ = (int64_t)rb * RD_ROWS + row;
+          const bool live = rg_ < T;
+          const int64_t k0 = (int64_t)kb * RD_KB;
+          stg128_if(q + (live ? rg_ : 0) * ldq + k0 + 32 * blk + 16 * half, w[0], w[1], w[2], w[3], live);
+          // the row's two scale bytes (k-blocks 2 kb, 2 kb + 1: adjacent in the blocked layout)
+          const uint32_t e1 = __shfl_xor_sync(0xffffffffu, e, 2);
+          if ((lane & 3) == 0)
+            *reinterpret_cast<uint16_t*>(s + mx_scale_offset(rg_, kb_off + (k0 >> 5), scols)) = (uint16_t)(e | (e1 << 8));
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[stage]);
+      if (++stage == stages) {
+        stage = 0;
+        phase ^= 1;
+      }
+    }
+    if (!ok) break;
+    const int64_t r0 = (int64_t)rb * RD_ROWS + warp * 16 + g;
+#pragma unroll
+    for (int jt = 0; jt < NJ / 8; ++jt) {
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        float v[2];
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const float sum = acc[jt][2 * h + e];
+          if (round_once) {
+            v[e] = bf16_round_f(sum * post);
+          } else {
+            v[e] = bf16_round_f(sum);
+            if (post != 1.0f) v[e] = bf16_round_f(v[e] * post);
+          }
+        }
+        const int64_t row = r0 + 8 * h;
+        if (row < T) *reinterpret_cast<uint32_t*>(out + row * ldo + 8 * jt + 2 * t) = pack_bf16x2(v[0], v[1]);
+      }
+    }
+  }
+}
+
+// Launches the TMA row-product kernel when B fits in shared memory and the code rows allow 16-byte
+// stores; returns -1 (nothing launched) otherwise, so the caller can fall back to k_rowdot.
+int rowdot_tma(const void* A, int64_t lda, const void* B, int64_t T, int64_t K, int n, float post, int round_once,
+               void* out, int64_t ldo, uint8_t* q, int64_t ldq, uint8_t* s, int64_t scols, int kb_off,
+               cudaStream_t st) {
+  const int64_t b_bytes = (int64_t)n * K * 2;
+  if (b_bytes > (int64_t)RD_B_MAX || K % RD_KB != 0 || T >= (1ll << 31)) return -1;
+  if (q && (ldq % 16 != 0 || !mx_aligned(q, 16) || !mx_aligned(s, 2) || kb_off % 2 != 0)) return -1;
+  CUtensorMap ta, tb;
+  if (mx_make_tmap_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, A, (uint64_t)K, (uint64_t)T, (uint64_t)(lda * 2), RD_KB,
+                      RD_ROWS, CU_TENSOR_MAP_SWIZZLE_128B))
+    return -1;
+  if (mx_make_tmap_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, B, (uint64_t)K, (uint64_t)n, (uint64_t)(K * 2), RD_KB,
+                      (uint32_t)n, CU_TENSOR_MAP_SWIZZLE_128B))
+    return -1;
+  const int stages = rd_stages(b_bytes);
+  const size_t smem = rd_smem(b_bytes, stages);
+  const int nrb = (int)((T + RD_ROWS - 1) / RD_ROWS);
+  const int grid = std::min(nrb, mxm_num_sms());
+  auto go = [&](auto kern) -> int {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return mx_cuda_status(e, "rowdot tma: set smem");
+    kern<<<grid, 32 * (RD_CONS + 1), smem, st>>>(ta, tb, (int)T, (int)K, nrb, stages, post, round_once, (bf16*)out,
+                                                  ldo, q, ldq, s, scols, kb_off, mx_dev_error_ptr());
+    mx_note_launch();
+    return mx_launch_status("rowdot tma");
+  };
+  if (q) return n == 16 ? go(k_rowdot_tma<16, true>) : (n == 32 ? go(k_rowdot_tma<32, true>) : go(k_rowdot_tma<64, true>));
+  return n == 16 ? go(k_rowdot_tma<16, false>) : (n == 32 ? go(k_rowdot_tma<32, false>) : go(k_rowdot_tma<64, false>));
+}
+
 // part[chunk, k, j] = sum over the chunk's rows t of A[t, k] E[t, j]   (k < K, j < NJ)
 // CTA = 64 columns k of one row chunk: warp 4 streams [64 rows x 64 k] tiles of A (128-byte swizzle)
 // and the matching [64 rows x NJ] rows of E into a 5-stage ring with TMA; warps 0-3 each own 16
@@ -1197,8 +1395,10 @@ extern "C" int mxm_rowdot(const void* A, int64_t lda, const void* B, int64_t T, 
   MX_CHECK_ARG(T >= 1 && K >= 128 && K % 128 == 0 && (n == 16 || n == 32 || n == 64) && lda % 8 == 0 && ldo % 2 == 0,
                "mxm_rowdot: need K %% 128 == 0, n in {16, 32, 64}, lda %% 8 == 0");
   MX_CHECK_ARG(mx_aligned(A, 16) && mx_aligned(B, 16) && mx_aligned(out, 4), "mxm_rowdot: alignment");
-  const unsigned grid = (unsigned)((T + 15) / 16);
   cudaStream_t st = (cudaStream_t)stream;
+  const int e = rowdot_tma(A, lda, B, T, K, n, post, 0, out, ldo, nullptr, 0, nullptr, K, 0, st);
+  if (e >= 0) return e;
+  const unsigned grid = (unsigned)((T + 15) / 16);
   auto go = [&](auto kern) {
     kern<<<grid, 128, 0, st>>>((const bf16*)A, lda, (const bf16*)B, (int)T, (int)K, post, 0, (bf16*)out, ldo, nullptr,
                                0, nullptr, K, 0);
@@ -1251,21 +1451,26 @@ extern "C" int mxm_lora_bwd(const void* dy, int64_t ldy, int64_t T, int64_t N, c
   cudaStream_t st = (cudaStream_t)stream;
   const unsigned grid = q ? (unsigned)((T + 127) / 128 * 8) : (unsigned)((T + 15) / 16);
   uint8_t* qc = q ? (uint8_t*)q + col_tile_off * 128 : nullptr;
-  auto go = [&](auto kern) {
-    kern<<<grid, 128, 0, st>>>((const bf16*)dy, ldy, (const bf16*)Bt, (int)T, (int)N, scale, 1, (bf16*)dxa_out,
-                               ld_dxa, qc, ldq, (uint8_t*)s, s_cols, (int)(col_tile_off * 4));
-  };
-  if (q) {
-    if (r == 16) go(k_rowdot<16, true>);
-    else if (r == 32) go(k_rowdot<32, true>);
-    else go(k_rowdot<64, true>);
-  } else {
-    if (r == 16) go(k_rowdot<16, false>);
-    else if (r == 32) go(k_rowdot<32, false>);
-    else go(k_rowdot<64, false>);
+  const int et = rowdot_tma(dy, ldy, Bt, T, N, r, scale, 1, dxa_out, ld_dxa, qc, ldq, (uint8_t*)s, s_cols,
+                            (int)(col_tile_off * 4), st);
+  if (et > 0) return et;
+  if (et < 0) {
+    auto go = [&](auto kern) {
+      kern<<<grid, 128, 0, st>>>((const bf16*)dy, ldy, (const bf16*)Bt, (int)T, (int)N, scale, 1, (bf16*)dxa_out,
+                                 ld_dxa, qc, ldq, (uint8_t*)s, s_cols, (int)(col_tile_off * 4));
+    };
+    if (q) {
+      if (r == 16) go(k_rowdot<16, true>);
+      else if (r == 32) go(k_rowdot<32, true>);
+      else go(k_rowdot<64, true>);
+    } else {
+      if (r == 16) go(k_rowdot<16, false>);
+      else if (r == 32) go(k_rowdot<32, false>);
+      else go(k_rowdot<64, false>);
+    }
+    mx_note_launch();
+    if (int e = mx_launch_status("lora bwd rowdot")) return e;
   }
-  mx_note_launch();
-  if (int e = mx_launch_status("lora bwd rowdot")) return e;
   // dB = scale * dy^T xa: the coldot with an fp32, unrounded result
   MX_CHECK_ARG(rows_per_chunk % CD_ROWS == 0 && rows_per_chunk > 0 && (int64_t)rows_per_chunk * chunks >= T,
                "mxm_lora_bwd: bad chunking");
@@ -1325,8 +1530,10 @@ extern "C" int mxm_rowdot_quant(const void* A, int64_t lda, const void* B, int64
                "mxm_rowdot_quant: need K %% 128 == 0, n in {16, 32, 64}, lda %% 8 == 0, ldq >= K, ldq %% 8 == 0");
   MX_CHECK_ARG(mx_aligned(A, 16) && mx_aligned(B, 16) && mx_aligned(out, 4) && mx_aligned(q, 8),
                "mxm_rowdot_quant: alignment");
-  const unsigned grid = (unsigned)((T + 127) / 128 * 8);  // 16-row CTAs over the padded rows
   cudaStream_t st = (cudaStream_t)stream;
+  const int e = rowdot_tma(A, lda, B, T, K, n, post, 0, out, ldo, (uint8_t*)q, ldq, (uint8_t*)s, K, 0, st);
+  if (e >= 0) return e;
+  const unsigned grid = (unsigned)((T + 127) / 128 * 8);  // 16-row CTAs over the padded rows
   auto go = [&](auto kern) {
     kern<<<grid, 128, 0, st>>>((const bf16*)A, lda, (const bf16*)B, (int)T, (int)K, post, 0, (bf16*)out, ldo,
                                (uint8_t*)q, ldq, (uint8_t*)s, K, 0);
