@@ -1158,40 +1158,61 @@ struct SumJobs {
 __global__ void __launch_bounds__(256) k_sum_parts4(SumJobs jobs, int nparts, int64_t n4, int64_t stride4) {
   const SumJob jb = blockIdx.y == 0 ? jobs.j[0] : (blockIdx.y == 1 ? jobs.j[1] : jobs.j[2]);
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (int64_t)gridDim.x * blockDim.x) {
-    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    // partials in order, 16 loads in flight: even parts into v, odd parts into w, then v + w
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f), w = v;
     const float4* p = jb.src + i;
-#pragma unroll 8
-    for (int k = 0; k < nparts; ++k) {
-      const float4 x = __ldg(p + k * stride4);
-      v.x += x.x;
-      v.y += x.y;
-      v.z += x.z;
-      v.w += x.w;
+    int k = 0;
+    for (; k + 16 <= nparts; k += 16) {
+      float4 x[16];
+#pragma unroll
+      for (int u = 0; u < 16; ++u) x[u] = __ldg(p + (int64_t)(k + u) * stride4);
+#pragma unroll
+      for (int u = 0; u < 16; u += 2) {
+        v.x += x[u].x; v.y += x[u].y; v.z += x[u].z; v.w += x[u].w;
+        w.x += x[u + 1].x; w.y += x[u + 1].y; w.z += x[u + 1].z; w.w += x[u + 1].w;
+      }
     }
-    jb.out[i] = make_float4(v.x * jb.scale, v.y * jb.scale, v.z * jb.scale, v.w * jb.scale);
+    for (; k < nparts; ++k) {
+      const float4 x = __ldg(p + (int64_t)k * stride4);
+      if (k & 1) {
+        w.x += x.x; w.y += x.y; w.z += x.z; w.w += x.w;
+      } else {
+        v.x += x.x; v.y += x.y; v.z += x.z; v.w += x.w;
+      }
+    }
+    jb.out[i] = make_float4((v.x + w.x) * jb.scale, (v.y + w.y) * jb.scale, (v.z + w.z) * jb.scale,
+                            (v.w + w.w) * jb.scale);
   }
 }
 
 // dxa partials [slots, T, 3R] -> dxa bf16 [T, 2R] (gate part x s_g, up part x s_u) and xS_down bf16 [T, R].
 // Row block sbi (rows sb * sbi ..) was worked on by CTAs c_lo .. c_hi of the backward epilogue, whose
-// partials sit in slots 0 .. c_hi - c_lo; they are added in slot order.
-__global__ void k_reduce_dxa(const float* __restrict__ src, int sb, int nt, int per, int T, int R, float s_g,
-                             float s_u, bf16* __restrict__ dxa, bf16* __restrict__ xsd) {
-  const int64_t n = (int64_t)T * 3 * R;
-  const int64_t stride = n;
+// partials sit in slots 0 .. c_hi - c_lo; they are added in slot order.  Four values per thread.
+template <int R>
+__global__ void k_reduce_dxa(const float* __restrict__ src, int sb, int nt, int per, int T, float s_g, float s_u,
+                             bf16* __restrict__ dxa, bf16* __restrict__ xsd) {
+  constexpr int Q = 3 * R / 4;   // float4s per row
+  const int64_t n = (int64_t)T * Q;
+  const int64_t stride = (int64_t)T * Q;
+  const float4* s4 = reinterpret_cast<const float4*>(src);
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t row = i / (3 * R);
-    const int c = (int)(i % (3 * R));
+    const int64_t row = i / Q;
+    const int c = 4 * (int)(i - row * Q);
     const int sbi = (int)(row / sb);
     const int nparts = ((sbi + 1) * nt - 1) / per - (sbi * nt) / per + 1;
-    float v = 0.f;
-    for (int p = 0; p < nparts; ++p) v += src[p * stride + i];
-    if (c < R)
-      dxa[row * 2 * R + c] = __float2bfloat16_rn(v * s_g);
-    else if (c < 2 * R)
-      dxa[row * 2 * R + c] = __float2bfloat16_rn(v * s_u);
+    float4 v = __ldg(s4 + i);
+    for (int p = 1; p < nparts; ++p) {
+      const float4 x = __ldg(s4 + p * stride + i);
+      v.x += x.x; v.y += x.y; v.z += x.z; v.w += x.w;
+    }
+    const float sc = c < R ? s_g : (c < 2 * R ? s_u : 1.f);
+    uint2 o;
+    o.x = pack_bf16x2(v.x * sc, v.y * sc);
+    o.y = pack_bf16x2(v.z * sc, v.w * sc);
+    if (c < 2 * R)
+      *reinterpret_cast<uint2*>(dxa + row * 2 * R + c) = o;
     else
-      xsd[row * R + c - 2 * R] = __float2bfloat16_rn(v);
+      *reinterpret_cast<uint2*>(xsd + row * R + c - 2 * R) = o;
   }
 }
 
@@ -1374,9 +1395,13 @@ extern "C" int mxm_mlp_bwd_reduce(const void* dxa_part, const void* dbg_part, co
                "mxm_mlp_bwd_reduce: bad partition (%d, %d): use mxm_mlp_bwd_partitions", super_block, col_groups);
   const int nsb = p.nsb;
   cudaStream_t st = (cudaStream_t)stream;
-  const int64_t nd = T * 3 * r;
-  k_reduce_dxa<<<grid_for(nd, 256), 256, 0, st>>>((const float*)dxa_part, p.sb, p.nt, p.per, (int)T, r, s_g, s_u,
-                                                  (bf16*)dxa, (bf16*)xsd);
+  const int64_t nd = T * 3 * r / 4;
+  if (r == 16)
+    k_reduce_dxa<16><<<grid_for(nd, 256), 256, 0, st>>>((const float*)dxa_part, p.sb, p.nt, p.per, (int)T, s_g, s_u,
+                                                        (bf16*)dxa, (bf16*)xsd);
+  else
+    k_reduce_dxa<32><<<grid_for(nd, 256), 256, 0, st>>>((const float*)dxa_part, p.sb, p.nt, p.per, (int)T, s_g, s_u,
+                                                        (bf16*)dxa, (bf16*)xsd);
   mx_note_launch();
   const int64_t nb4 = N * r / 4;  // N % 128 == 0
   SumJobs jobs;
