@@ -62,18 +62,57 @@ def _args():
 
 # ----------------------------------------------------------------------------------------------- clocks
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms while the timed region runs."""
+    """SM clock, power and throttle reasons sampled while the timed region runs (read-only queries).
+
+    NVML from a thread every 5 ms (a timed region of a few tens of milliseconds still gets samples);
+    `nvidia-smi -lms 200` when NVML is not importable."""
 
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
          "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
          "clocks_event_reasons.sw_power_cap")
+    NAMES = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+    BITS = (0x8, 0x40, 0x20, 0x4)   # NVML clocks-event-reason bits of NAMES
 
     def __init__(self, index):
         self.index = index
         self.proc = None
         self.path = None
+        self.thread = None
+        self.rows = []
+
+    def _nvml_handle(self, nv):
+        try:
+            import torch
+            p = torch.cuda.get_device_properties(self.index)
+            bus = f"{p.pci_domain_id:08X}:{p.pci_bus_id:02X}:{p.pci_device_id:02X}.0"
+            return nv.nvmlDeviceGetHandleByPciBusId(bus)
+        except Exception:
+            return nv.nvmlDeviceGetHandleByIndex(self.index)
 
     def start(self):
+        try:
+            import threading
+            import pynvml as nv
+            nv.nvmlInit()
+            h = self._nvml_handle(nv)
+            reasons = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                nv.nvmlDeviceGetCurrentClocksThrottleReasons
+            self.max_mhz = float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM))
+            self.stop_ev = threading.Event()
+
+            def run():
+                while True:
+                    try:
+                        self.rows.append((float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)), int(reasons(h))))
+                    except Exception:
+                        pass
+                    if self.stop_ev.wait(0.005):
+                        break
+            self.thread = threading.Thread(target=run, daemon=True)
+            self.thread.start()
+            return
+        except Exception:
+            self.thread = None
         try:
             fd, self.path = tempfile.mkstemp(suffix=".csv")
             os.close(fd)
@@ -84,6 +123,14 @@ class ClockSampler:
             self.proc = None
 
     def stop(self):
+        if self.thread is not None:
+            self.stop_ev.set()
+            self.thread.join(timeout=5)
+            if not self.rows:
+                return None
+            reasons = sorted({n for _, m in self.rows for n, b in zip(self.NAMES, self.BITS) if m & b})
+            return {"sm_mhz": statistics.median(c for c, _ in self.rows), "sm_max_mhz": self.max_mhz,
+                    "reasons": reasons, "samples": len(self.rows), "source": "nvml"}
         if self.proc is None:
             return None
         self.proc.terminate()
@@ -101,10 +148,9 @@ class ClockSampler:
             return None
         sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
         mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
-        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
-        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower().startswith("active")})
+        reasons = sorted({n for r in rows for n, v in zip(self.NAMES, r[5:9]) if v.lower().startswith("active")})
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(rows)}
+                "reasons": reasons, "samples": len(rows), "source": "nvidia-smi"}
 
 
 # ----------------------------------------------------------------------------------------------- our arm
