@@ -52,7 +52,9 @@ def _args():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    ap.add_argument("--workload", choices=("layer", "stack"), default="layer")
+    ap.add_argument("--workload", choices=("layer", "stack", "quant", "ragged"), default="layer",
+                    help="layer: configs[1] (default); stack: configs[3]; quant: the configs[2] quantizer sweep "
+                         "(HBM GB/s); ragged: configs[4] small-M latency at the 0.8B shape")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end (host buffers) measurement")
     ap.add_argument("--tokens", type=int, default=0,
@@ -445,10 +447,236 @@ def run_reference(a):
     print(json.dumps(line), flush=True)
 
 
+# ----------------------------------------------------------------------------------------------- configs[2]
+def _hbm_peak():
+    try:
+        return float(json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def run_quant(a):
+    """the standalone MXFP8 quantizer over rows {4096, 16384, 65536, 142336} x cols {1024,
+    2048, 3584, 6144} of N(0,1) bf16 with 0.5 % of entries x200 and 0.1 % exact zeros; row-wise
+    (mx_quant), column-wise (mx_quant_t) and both from one read (mx_quant_pair).  Each timed call follows
+    a 256 MiB write that evicts L2; the median of `steps` calls per case.  Algorithmic bytes: 3.03125 per
+    element one way (read 2, write 1 + 1/32), 4.0625 both ways.  One GPU (rank 0 under torchrun)."""
+    import torch
+    rank, local = int(os.environ.get("RANK", "0")), int(os.environ.get("LOCAL_RANK", "0"))
+    if rank != 0:
+        return
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    import __graft_entry__
+    __graft_entry__.build()
+    import _mxlib
+    import mxfp8
+    peak, src = _hbm_peak()
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    g = torch.Generator(device=dev).manual_seed(0)
+    modes = (("rows", mxfp8.mx_quant, 3.03125), ("cols", mxfp8.mx_quant_t, 3.03125),
+             ("both", mxfp8.mx_quant_pair, 4.0625))
+    clk = ClockSampler(local)
+    clk.start()
+    launches0 = _mxlib.launch_count()
+    cases = []
+    for rows in (4096, 16384, 65536, 142336):
+        for cols in (1024, 2048, 3584, 6144):
+            x = torch.randn(rows, cols, device=dev, generator=g)
+            u = torch.rand(rows, cols, device=dev, generator=g)
+            x = torch.where(u < 0.005, x * 200.0, x)
+            x = torch.where((u >= 0.005) & (u < 0.006), torch.zeros_like(x), x).to(torch.bfloat16)
+            del u
+            case = {"R": rows, "K": cols}
+            for name, fn, bpe in modes:
+                for _ in range(max(a.warmup, 3)):
+                    fn(x)
+                evs = []
+                for _ in range(a.steps):
+                    flush.fill_(1)
+                    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    e0.record()
+                    out = fn(x)
+                    e1.record()
+                    evs.append((e0, e1))
+                    del out
+                torch.cuda.synchronize()
+                us = statistics.median(e0.elapsed_time(e1) for e0, e1 in evs) * 1e3
+                gbs = bpe * rows * cols / (us * 1e-6) / 1e9
+                case[name] = {"us": round(us, 2), "gbs": round(gbs, 1), "frac": round(gbs / peak, 3)}
+            cases.append(case)
+            del x
+    clocks = clk.stop()
+    launches = _mxlib.launch_count() - launches0
+    med = lambda k: statistics.median(c[k]["gbs"] for c in cases)  # noqa: E731
+    big = [c for c in cases if c["R"] * c["K"] * 2 > (126 << 20)]
+    line = {
+        "metric": "MXFP8 quantizer achieved HBM GB/s (configs[2] sweep, row-wise, median over cases)",
+        "value": med("rows"), "unit": "GB/s", "n_gpus": 1, "steps": a.steps, "warmup": max(a.warmup, 3),
+        "ms_per_step": statistics.median(c["rows"]["us"] for c in cases) / 1e3, "higher_is_better": True,
+        "scaling": "none", "vs_baseline": None, "dtype": "bf16 -> e4m3 + e8m0", "impl": "ours",
+        "data": "synthetic N(0,1), 0.5 % x200 outliers, 0.1 % zeros (seeded)",
+        "config": {"workload": "configs[2]: quantizer sweep rows {4096,16384,65536,142336} x cols "
+                               "{1024,2048,3584,6144}", "l2": "256 MiB write before every timed call"},
+        "median_gbs": {"rows": med("rows"), "cols": med("cols"), "both": med("both")},
+        "median_gbs_inputs_over_l2": {k: statistics.median(c[k]["gbs"] for c in big) for k in ("rows", "cols", "both")},
+        "roofline": {"bound": "hbm", "achieved": med("rows"), "peak": peak, "unit": "GB/s",
+                     "frac": med("rows") / peak, "traffic": None, "kernel": "k_quant",
+                     "peak_source": f"{src} copy bandwidth"},
+        "cases": cases, "gpu_launches": int(launches), "clocks": clocks,
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------------------------------------------- configs[4]
+RAGGED_M = (1, 77, 1000, 2049, 10752)
+
+
+def run_ragged(a):
+    """latency of one fused-MLP fwd+bwd step at the 0.8B shape (hidden 1024, intermediate
+    3584, LoRA r=16, alpha=32) for per-GPU token counts M in RAGGED_M (not multiples of 128), inputs
+    N(0,1) with 1 % of entries x100.  With N > 1 ranks each rank runs its own M tokens and the step ends
+    with the NCCL all-reduce of the LoRA gradients; the latency is the max over ranks of the CUDA-event
+    time per step.  `graph_ms`: the same fwd+bwd captured once in a CUDA graph and replayed (static
+    inputs), the all-reduce after each replay -- what a training loop that graphs its layer step sees."""
+    import torch
+    import torch.distributed as dist
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank, local = int(os.environ.get("RANK", "0")), int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
+    import __graft_entry__
+    __graft_entry__.build()
+    import _mxlib
+    import fused_linear
+    import fused_mlp
+    import mx_dp
+    Hs, Ns = 1024, 3584
+    g = torch.Generator(device="cpu").manual_seed(11)
+    w = lambda *s: (torch.randn(*s, generator=g) * 0.02).to(torch.bfloat16).to(dev)   # noqa: E731
+    layer = fused_mlp.MXMLPWeights.from_bf16(w(Ns, Hs), w(Ns, Hs), w(Hs, Ns))
+    shapes = ((R, Hs), (Ns, R), (R, Hs), (Ns, R), (R, Ns), (Hs, R))
+    params = [(torch.randn(*s, generator=g) * 0.01).to(dev).requires_grad_(True) for s in shapes]
+    bucket = mx_dp.GradBucket(params, device=dev)
+
+    def sync_all():
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return t.item()
+
+    clk = ClockSampler(local)
+    clk.start()
+    launches0 = _mxlib.launch_count()
+    res = []
+    for M in RAGGED_M:
+        gx = torch.Generator(device="cpu").manual_seed(100 + M + rank)
+        def outl(t):
+            u = torch.rand(t.shape, generator=gx)
+            return torch.where(u < 0.01, t * 100.0, t)
+        x = outl(torch.randn(M, Hs, generator=gx)).to(torch.bfloat16).to(dev)
+        dy = outl(torch.randn(M, Hs, generator=gx)).to(torch.bfloat16).to(dev)
+
+        def fwd_bwd():
+            fused_linear.new_step()
+            h = x.detach().requires_grad_(True)
+            y = fused_mlp.mlp_apply(layer, h, *params, scaling=(SCALE, SCALE, SCALE))
+            y.backward(dy)
+
+        def step():
+            fwd_bwd()
+            if world > 1:
+                bucket.allreduce()
+            for p in params:
+                p.grad = None
+
+        def timed(fn):
+            for _ in range(max(a.warmup, 3)):
+                fn()
+            sync_all()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(a.steps):
+                fn()
+            e1.record()
+            torch.cuda.synchronize()
+            return max_over_ranks(e0.elapsed_time(e1) / a.steps)
+
+        eager = timed(step)
+        # CUDA graph of the local fwd+bwd (captured on every rank alike; the all-reduce stays eager)
+        graph_ms, err, graph = None, None, None
+        try:
+            for p in params:
+                p.grad = None
+            side = torch.cuda.Stream()
+            side.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(side):
+                for _ in range(3):
+                    fwd_bwd()
+                    for p in params:
+                        p.grad = None
+            torch.cuda.current_stream().wait_stream(side)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                fwd_bwd()
+        except Exception as e:   # capture is a host-side feature: report, keep the eager number
+            err = f"{type(e).__name__}: {str(e)[:160]}"
+            graph = None
+        ok = graph is not None
+        if world > 1:            # every rank times the graph, or none does (same collectives everywhere)
+            t = torch.tensor([1 if ok else 0], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MIN)
+            ok = bool(t.item())
+        if ok:
+            def replay():
+                graph.replay()
+                if world > 1:
+                    bucket.allreduce()
+            graph_ms = timed(replay)
+        del graph
+        for p in params:
+            p.grad = None
+        res.append({"M": M, "eager_ms": round(eager, 4), "graph_ms": None if graph_ms is None else round(graph_ms, 4),
+                    **({"graph_error": err} if err else {})})
+    clocks = clk.stop()
+    launches = _mxlib.launch_count() - launches0
+    if world > 1:
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    line = {
+        "metric": "fused-MLP fwd+bwd latency per step, 0.8B shape, ragged per-GPU M (mean over M, eager)",
+        "value": statistics.mean(r["eager_ms"] for r in res), "unit": "ms", "n_gpus": world, "steps": a.steps,
+        "warmup": max(a.warmup, 3), "ms_per_step": statistics.mean(r["eager_ms"] for r in res),
+        "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "mxfp8-e4m3/bf16",
+        "impl": "ours", "data": "synthetic N(0,1), 1 % x100 outliers (seeded)",
+        "config": {"workload": "configs[4]: 0.8B MLP shape, per-GPU M in " + str(list(RAGGED_M)),
+                   "hidden": Hs, "intermediate": Ns, "lora_rank": R, "lora_alpha": ALPHA,
+                   "parallelism": f"dp{world} (each rank its own M tokens, NCCL all-reduce of LoRA grads)",
+                   "l2": "small-M latency: working set in L2 by design, no flush"},
+        "per_m": res, "gpu_launches": int(launches), "clocks": clocks,
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     a = _args()
     if a.impl == "reference":
         run_reference(a)
+    elif a.workload == "quant":
+        run_quant(a)
+    elif a.workload == "ragged":
+        run_ragged(a)
     else:
         run_ours(a)
 

@@ -5,11 +5,13 @@
 //   e    = round-up-to-power-of-two(amax / 448) as E8M0        (from amax's bits: mx_e8m0_of_amax)
 //   q    = e4m3_rne(clamp(x * rcp(e), -448, 448)),  rcp(e) = 2^(127-e) (special cases 0/254/255)
 //
-// One CTA owns a 128-row x 128-column tile, which is exactly one 512-byte scale block of the
-// blocked layout, so scales are assembled in shared memory and written as 32 coalesced 16-byte
-// stores.  Loads are 16-byte vectors (8 bf16), fully coalesced; a 32-element block is 4 lanes,
-// reduced with two xor-shuffles.  Memory bound: 3.03 bytes moved per element (rows only),
-// 4.06 for rows + columns from one read.
+// A 128-row x 128-column tile is exactly one 512-byte scale block of the blocked layout, so its scales
+// are assembled in shared memory and leave in one piece.  Two kernels: k_quant_tma (persistent, TMA in
+// and out, used whenever the buffers are 16-byte aligned) and k_quant (one CTA per tile, 16-byte vector
+// loads, the fallback).  Memory bound: 3.03 bytes moved per element one way, 4.06 for rows + columns
+// from one read.
+#include <algorithm>
+
 #include "mx_common.cuh"
 #include "mx_runtime.h"
 
@@ -133,6 +135,210 @@ __global__ void __launch_bounds__(QT) k_quant(const __nv_bfloat16* __restrict__ 
   }
 }
 
+// ------------------------------------------------------------------------------------------------ TMA path
+// Persistent variant for aligned buffers: warp 8 streams 128 x 128 bf16 tiles (two [128 x 64] boxes,
+// 128-byte swizzle) into a 3-stage ring; consumer warps 0-7 quantize each tile from shared memory and
+// assemble its outputs -- row-wise codes [128 rows x 128 B], column-wise (transposed) codes [128 x 128 B],
+// both in the 128-byte swizzled layout, and the two 512-byte scale blocks -- in one of two staging
+// buffers, from which one thread writes them with TMA tensor stores and bulk copies while the next tile
+// is quantized.  Row pass: two lanes per 32-element block (16 values each, one xor-shuffle for the
+// abs-max); column pass: a lane owns two adjacent columns of one 32-row block, read as bf16 pairs, so
+// both columns' abs-maxes come from one packed max.  The arithmetic per element is that of quant8.
+constexpr int QM_ST = 3, QM_CONS = 8;
+constexpr int QM_IN = 128 * 128 * 2;                 // 32 KB input tile
+constexpr int QM_OUT = 128 * 128 * 2 + 1024;         // q tile + qt tile + two scale blocks
+__host__ __device__ constexpr size_t qm_smem() { return 1024 + (size_t)QM_ST * QM_IN + 2 * (size_t)QM_OUT + 256; }
+
+MX_DEV uint32_t qm_abs2(uint32_t a, uint32_t b) {   // packed |a| max |b| with NaN propagation
+  uint32_t r;
+  asm("{\n\t.reg .b32 x, y;\n\tabs.bf16x2 x, %1;\n\tabs.bf16x2 y, %2;\n\tmax.NaN.bf16x2 %0, x, y;\n\t}"
+      : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+MX_DEV uint32_t qm_max2(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("max.NaN.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+MX_DEV float qm_nanmax(float a, float b) {
+  float r;
+  asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+  return r;
+}
+// Two products -> two E4M3 codes (RNE, satfinite: +-inf and |v| > 448 give +-448 as the clamp does);
+// a NaN code comes out as 0x7F / 0xFF and is made canonical by qm_nan_canon4.
+MX_DEV uint32_t qm_e4m3x2(float lo, float hi) {
+  uint16_t r;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+MX_DEV uint32_t qm_nan_canon4(uint32_t w) {   // E4M3 NaN bytes (S.1111.111) -> 0x7F
+  const uint32_t m = ((w & 0x7F7F7F7Fu) + 0x01010101u) & 0x80808080u;
+  return w & ~m;
+}
+MX_DEV void qm_lds128(uint32_t* r, uint32_t a) {
+  asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];" : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(a));
+}
+MX_DEV uint32_t qm_lds32(uint32_t a) {
+  uint32_t r;
+  asm volatile("ld.shared.b32 %0, [%1];" : "=r"(r) : "r"(a));
+  return r;
+}
+MX_DEV void qm_sts128(uint32_t a, uint32_t x, uint32_t y, uint32_t z, uint32_t w) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(x), "r"(y), "r"(z), "r"(w) : "memory");
+}
+MX_DEV void qm_bulk_store(void* dst, uint32_t src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst), "r"(src), "r"(bytes)
+               : "memory");
+}
+// 16-byte chunk c of row r in a 128-byte-row tile with the 128-byte swizzle
+MX_DEV uint32_t qm_sw(uint32_t r, uint32_t c) { return r * 128u + ((c ^ (r & 7u)) << 4); }
+
+template <bool ROWS, bool COLS>
+__global__ void __launch_bounds__(32 * (QM_CONS + 1), 1)
+    k_quant_tma(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_q,
+                const __grid_constant__ CUtensorMap tm_qt, uint8_t* __restrict__ s, uint8_t* __restrict__ st,
+                int64_t R, int nrt, int nct, int64_t s_tiles, int64_t tile_off, int* err) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* ring = smem;
+  uint8_t* outb = ring + QM_ST * QM_IN;   // 2 x [q 16 KB | qt 16 KB | row scales 512 | col scales 512]
+  uint64_t* full = reinterpret_cast<uint64_t*>(outb + 2 * QM_OUT);
+  uint64_t* empty = full + QM_ST;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int num_tiles = nrt * nct;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < QM_ST; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], QM_CONS);
+    }
+    fence_barrier_init();
+  }
+  __syncthreads();
+
+  if (warp == QM_CONS) {   // TMA producer
+    if (lane == 0) {
+      prefetch_tmap(&tm_x);
+      int stage = 0, issued = 0;
+      uint32_t phase = 0;
+      for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
+        if (!mbar_wait(&empty[stage], phase ^ 1, err, MX_DEV_TIMEOUT_PRODUCER)) break;
+        const int tr = t / nct, tc = t % nct;
+        uint8_t* dst = ring + stage * QM_IN;
+        mbar_arrive_expect_tx(&full[stage], QM_IN);
+        tma_load_2d(dst, &tm_x, &full[stage], tc * 128, tr * 128);
+        tma_load_2d(dst + QM_IN / 2, &tm_x, &full[stage], tc * 128 + 64, tr * 128);
+        ++issued;
+        if (++stage == QM_ST) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+      for (int k = 0; k < QM_ST && k < issued; ++k) {   // no copy left in flight
+        const int i = issued - 1 - k;
+        mbar_wait(&full[i % QM_ST], (uint32_t)((i / QM_ST) & 1), err, MX_DEV_TIMEOUT_PRODUCER);
+      }
+    }
+    return;
+  }
+
+  const int tid = threadIdx.x;
+  const uint32_t s_ring = smem_u32(ring), s_out = smem_u32(outb);
+  int stage = 0, it = 0;
+  uint32_t phase = 0;
+  for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++it) {
+    const int tr = t / nct, tc = t % nct;
+    if (!mbar_wait(&full[stage], phase, err, MX_DEV_TIMEOUT_EPILOGUE)) break;
+    const uint32_t in = s_ring + (uint32_t)stage * QM_IN;           // box b at in + b * 16 KB
+    const uint32_t ob = s_out + (uint32_t)(it & 1) * QM_OUT;
+    const uint32_t oq = ob, oqt = ob + 16384, ors = ob + 32768, ocs = ob + 32768 + 512;
+    uint8_t* rs = outb + (it & 1) * QM_OUT + 32768;
+    uint8_t* cs = rs + 512;
+    if (ROWS) {
+      // lane -> (row pair half, box, 16-column quarter of the box); a warp covers 4 rows x 128 columns
+      const int q = lane & 3, rsub = (lane >> 2) & 1, box = (lane >> 3) & 1, rpair = lane >> 4;
+#pragma unroll
+      for (int p = 0; p < 4; ++p) {
+        const uint32_t r = (uint32_t)(32 * p + 4 * warp + 2 * rpair + rsub);
+        uint32_t v[8];
+        qm_lds128(v, in + (uint32_t)box * 16384 + qm_sw(r, (uint32_t)(2 * q)));
+        qm_lds128(v + 4, in + (uint32_t)box * 16384 + qm_sw(r, (uint32_t)(2 * q + 1)));
+        const uint32_t m2 = qm_max2(qm_max2(qm_abs2(v[0], v[1]), qm_abs2(v[2], v[3])),
+                                    qm_max2(qm_abs2(v[4], v[5]), qm_abs2(v[6], v[7])));
+        float m = qm_nanmax(bf16_lo(m2), bf16_hi(m2));
+        m = qm_nanmax(m, __shfl_xor_sync(0xffffffffu, m, 1));   // the other 16 of the 32-column block
+        const uint32_t e = mx_e8m0_of_amax(m);
+        const float rcp = mx_e8m0_rcp(e);
+        uint32_t w[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          w[i] = qm_nan_canon4(qm_e4m3x2(bf16_lo(v[2 * i]) * rcp, bf16_hi(v[2 * i]) * rcp) |
+                               (qm_e4m3x2(bf16_lo(v[2 * i + 1]) * rcp, bf16_hi(v[2 * i + 1]) * rcp) << 16));
+        qm_sts128(oq + qm_sw(r, (uint32_t)(4 * box + q)), w[0], w[1], w[2], w[3]);
+        if ((q & 1) == 0) rs[(r & 31) * 16 + (r >> 5) * 4 + 2 * box + (q >> 1)] = (uint8_t)e;
+      }
+    }
+    if (COLS) {
+      // warp -> (32-row block jb, box); lane -> columns 2 lane, 2 lane + 1 of the box
+      const int jb = warp >> 1, box = warp & 1;
+      const uint32_t base = in + (uint32_t)box * 16384 + (uint32_t)((lane & 3) * 4);
+      uint32_t v[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const uint32_t r = (uint32_t)(32 * jb + i);
+        v[i] = qm_lds32(base + qm_sw(r, (uint32_t)(lane >> 2)));
+      }
+      uint32_t a[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) a[i] = qm_abs2(v[2 * i], v[2 * i + 1]);
+#pragma unroll
+      for (int s2 = 8; s2 >= 1; s2 >>= 1)
+#pragma unroll
+        for (int i = 0; i < s2; ++i) a[i] = qm_max2(a[i], a[i + s2]);
+      const uint32_t e0 = mx_e8m0_of_amax(bf16_lo(a[0])), e1 = mx_e8m0_of_amax(bf16_hi(a[0]));
+      const float r0 = mx_e8m0_rcp(e0), r1 = mx_e8m0_rcp(e1);
+      uint32_t w0[8], w1[8];   // codes of column 2 lane (w0) and 2 lane + 1 (w1), rows 32 jb + 4 i ..
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const uint32_t x0 = v[4 * i], x1 = v[4 * i + 1], x2 = v[4 * i + 2], x3 = v[4 * i + 3];
+        w0[i] = qm_nan_canon4(qm_e4m3x2(bf16_lo(x0) * r0, bf16_lo(x1) * r0) |
+                              (qm_e4m3x2(bf16_lo(x2) * r0, bf16_lo(x3) * r0) << 16));
+        w1[i] = qm_nan_canon4(qm_e4m3x2(bf16_hi(x0) * r1, bf16_hi(x1) * r1) |
+                              (qm_e4m3x2(bf16_hi(x2) * r1, bf16_hi(x3) * r1) << 16));
+      }
+      const uint32_t c0 = (uint32_t)(64 * box + 2 * lane), c1 = c0 + 1;   // output rows of the qt tile
+      qm_sts128(oqt + qm_sw(c0, (uint32_t)(2 * jb)), w0[0], w0[1], w0[2], w0[3]);
+      qm_sts128(oqt + qm_sw(c0, (uint32_t)(2 * jb + 1)), w0[4], w0[5], w0[6], w0[7]);
+      qm_sts128(oqt + qm_sw(c1, (uint32_t)(2 * jb)), w1[0], w1[1], w1[2], w1[3]);
+      qm_sts128(oqt + qm_sw(c1, (uint32_t)(2 * jb + 1)), w1[4], w1[5], w1[6], w1[7]);
+      cs[(c0 & 31) * 16 + (c0 >> 5) * 4 + jb] = (uint8_t)e0;
+      cs[(c1 & 31) * 16 + (c1 >> 5) * 4 + jb] = (uint8_t)e1;
+    }
+    fence_proxy_async();   // the staged outputs are read by the bulk stores below
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[stage]);
+    if (++stage == QM_ST) {
+      stage = 0;
+      phase ^= 1;
+    }
+    if (tid == 0) bulk_wait_read0();   // the previous tile's stores have read the other staging buffer
+    asm volatile("bar.sync 1, %0;" ::"r"(32 * QM_CONS) : "memory");
+    if (tid == 0) {
+      if (ROWS) {
+        tma_store_2d(&tm_q, outb + (it & 1) * QM_OUT, tc * 128, tr * 128);
+        qm_bulk_store(s + ((int64_t)tr * s_tiles + tile_off + tc) * 512, ors, 512);
+      }
+      if (COLS) {
+        tma_store_2d(&tm_qt, outb + (it & 1) * QM_OUT + 16384, tr * 128, tc * 128);
+        qm_bulk_store(st + ((int64_t)tc * nrt + tr) * 512, ocs, 512);
+      }
+      bulk_commit();
+    }
+  }
+  if (tid == 0) bulk_wait0();
+  (void)R;
+}
+
 int check_common(const void* x, int64_t R, int64_t K, int64_t ldx, const char* fn) {
   MX_CHECK_ARG(x != nullptr, "%s: null input", fn);
   MX_CHECK_ARG(R >= 1 && K >= 128 && K % 128 == 0, "%s: need R >= 1 and K %% 128 == 0 (R=%lld K=%lld)", fn,
@@ -149,6 +355,35 @@ template <bool ROWS, bool COLS>
 int launch(const void* x, int64_t R, int64_t K, int64_t ldx, void* q, int64_t ldq, void* s, void* qt, void* st,
            void* stream, int64_t s_tiles = -1, int64_t tile_off = 0) {
   if (s_tiles < 0) s_tiles = K >> 7;
+  // TMA path: 16-byte aligned rows and buffers (tensor maps), the codes' row stride a multiple of 16
+  const bool tma_ok = mx_aligned(x, 16) && (!ROWS || (mx_aligned(q, 16) && ldq % 16 == 0 && mx_aligned(s, 16))) &&
+                      (!COLS || (mx_aligned(qt, 16) && mx_aligned(st, 16) && R % 16 == 0));
+  if (tma_ok) {
+    CUtensorMap tx, tq, tqt;
+    int e = mx_make_tmap_2d(&tx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, x, (uint64_t)K, (uint64_t)R,
+                            (uint64_t)(ldx * 2), 64, 128, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (!e && ROWS)
+      e = mx_make_tmap_2d(&tq, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, q, (uint64_t)K, (uint64_t)R, (uint64_t)ldq, 128, 128,
+                          CU_TENSOR_MAP_SWIZZLE_128B);
+    if (!e && COLS)
+      e = mx_make_tmap_2d(&tqt, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, qt, (uint64_t)R, (uint64_t)K, (uint64_t)R, 128, 128,
+                          CU_TENSOR_MAP_SWIZZLE_128B);
+    if (!e) {
+      if (!ROWS) tq = tqt;
+      if (!COLS) tqt = tq;
+      const int nrt = (int)((R + 127) / 128), nct = (int)(K / 128);
+      const int64_t tiles = (int64_t)nrt * nct;
+      const int grid = (int)std::min<int64_t>(tiles, mxm_num_sms());
+      const size_t smem = qm_smem();
+      cudaError_t ce = cudaFuncSetAttribute(k_quant_tma<ROWS, COLS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            (int)smem);
+      if (ce != cudaSuccess) return mx_cuda_status(ce, "quant tma: set smem");
+      k_quant_tma<ROWS, COLS><<<grid, 32 * (QM_CONS + 1), smem, (cudaStream_t)stream>>>(
+          tx, tq, tqt, (uint8_t*)s, (uint8_t*)st, R, nrt, nct, s_tiles, tile_off, mx_dev_error_ptr());
+      mx_note_launch();
+      return mx_launch_status("quant tma kernel launch");
+    }
+  }
   const size_t smem = COLS ? 128 * 128 * sizeof(uint16_t) : 0;
   if (COLS) {
     cudaError_t e = cudaFuncSetAttribute(k_quant<ROWS, COLS>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
