@@ -107,13 +107,15 @@ MX_DEV void quad_transpose16(uint32_t& r0, uint32_t& r1, int t) {
 // each lane writes 8 consecutive codes, so a quad fills the row's 32-byte sector in one store.
 MX_DEV void quant_block16p(const uint32_t (&pk)[4][2], const QRows& qr, int64_t col0, int t) {
   const int64_t soff = ((col0 >> 7) << 9) + ((col0 >> 5) & 3);  // k-block col0/32 in the blocked layout
+  // both rows' abs-maxes in one bf16x2 (an abs-max of bf16 values is a bf16 value): (row g | row g + 8)
+  const uint32_t m0 = max_bf16x2(absmax_bf16x2(pk[0][0], pk[1][0]), absmax_bf16x2(pk[2][0], pk[3][0]));
+  const uint32_t m1 = max_bf16x2(absmax_bf16x2(pk[0][1], pk[1][1]), absmax_bf16x2(pk[2][1], pk[3][1]));
+  uint32_t mm = max_bf16x2(__byte_perm(m0, m1, 0x5410), __byte_perm(m0, m1, 0x7632));
+  mm = max_bf16x2(mm, __shfl_xor_sync(0xffffffffu, mm, 1));
+  mm = max_bf16x2(mm, __shfl_xor_sync(0xffffffffu, mm, 2));
 #pragma unroll
   for (int h = 0; h < 2; ++h) {
-    const uint32_t m2 = max_bf16x2(absmax_bf16x2(pk[0][h], pk[1][h]), absmax_bf16x2(pk[2][h], pk[3][h]));
-    float m = nanmax(bf16_lo(m2), bf16_hi(m2));
-    m = nanmax(m, __shfl_xor_sync(0xffffffffu, m, 1));
-    m = nanmax(m, __shfl_xor_sync(0xffffffffu, m, 2));
-    const uint32_t e = mx_e8m0_of_amax(m);
+    const uint32_t e = mx_e8m0_of_amax(h ? bf16_hi(mm) : bf16_lo(mm));
     const float rcp = mx_e8m0_rcp(e);
     const float2 r2 = make_float2(rcp, rcp);
     uint32_t c[4];
