@@ -42,8 +42,12 @@ constexpr int EPI_WARP0 = 4, EPI_THREADS = 256;
 
 __host__ __device__ constexpr int gemm_stages(int KR) { return KR == 64 ? 3 : 4; }
 __host__ __device__ constexpr int lora_bytes(int KR) { return (BM + BN) * KR * 2; }
+// Without a LoRA term the epilogue warps stage their output in 2 KB pieces (32 rows x 32 columns each)
+// for TMA stores; with one, shared memory is full and they store from registers.
+__host__ __device__ constexpr int out_bytes(int KR) { return KR == 0 ? 8 * 2048 : 0; }
 __host__ __device__ constexpr size_t gemm_smem(int KR) {
-  return 1024 + (size_t)gemm_stages(KR) * (A_BYTES + B_BYTES + SFA_BYTES + SFB_BYTES) + lora_bytes(KR) + 256;
+  return 1024 + (size_t)gemm_stages(KR) * (A_BYTES + B_BYTES + SFA_BYTES + SFB_BYTES) + lora_bytes(KR) +
+         out_bytes(KR) + 256;
 }
 // UMMA shared-memory layout code for a K-major bf16 tile with kr*2-byte rows (32/64/128-byte swizzle).
 __host__ __device__ constexpr uint32_t lora_layout(int KR) { return KR == 16 ? 6u : (KR == 32 ? 4u : 2u); }
@@ -68,7 +72,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   uint8_t* sSFB = sSFA + STAGES * SFA_BYTES;
   uint8_t* sL = sSFB + STAGES * SFB_BYTES;  // 1024-aligned
   uint8_t* sR = sL + BM * KR * 2;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sL + lora_bytes(KR));
+  uint8_t* sOut = sL + lora_bytes(KR);      // [8 warps][32 rows x 64 B] (KR == 0), 1024-aligned
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sOut + out_bytes(KR));
   uint64_t* full = bars;
   uint64_t* empty = bars + STAGES;
   uint64_t* tmem_full = bars + 2 * STAGES;
@@ -222,6 +227,35 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       tc_fence_before();
       mbar_arrive(tmem_empty);  // the accumulator is free: the next tile's MMAs start now
       acc_phase ^= 1;
+      if constexpr (KR == 0) {
+        // 32-column pieces of this warp's 32 x 128 block: bf16 rows into the warp's 2 KB buffer (64-byte
+        // swizzle), then one TMA store of the [32 x 32] box (rows >= M clipped); the buffer is reused
+        // once the previous store has read it
+        uint8_t* buf = sOut + (warp - EPI_WARP0) * 2048;
+        const uint32_t sb0 = smem_u32(buf) + (uint32_t)lane * 64;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          if (lane == 0) bulk_wait_read0();
+          __syncwarp();
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const uint32_t a = sb0 + ((uint32_t)(j ^ ((lane >> 1) & 3)) << 4);
+            asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a),
+                         "r"(pack_bf16x2(__uint_as_float(r[c][8 * j + 0]), __uint_as_float(r[c][8 * j + 1]))),
+                         "r"(pack_bf16x2(__uint_as_float(r[c][8 * j + 2]), __uint_as_float(r[c][8 * j + 3]))),
+                         "r"(pack_bf16x2(__uint_as_float(r[c][8 * j + 4]), __uint_as_float(r[c][8 * j + 5]))),
+                         "r"(pack_bf16x2(__uint_as_float(r[c][8 * j + 6]), __uint_as_float(r[c][8 * j + 7])))
+                         : "memory");
+          }
+          fence_proxy_async();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&tmL, buf, tn * BN + half * 128 + c * 32, tm * BM + q * 32);
+            bulk_commit();
+          }
+        }
+        continue;
+      }
       const int64_t row = (int64_t)tm * BM + q * 32 + lane;
       if (row < M) {
         uint4* dst = reinterpret_cast<uint4*>(D + row * ldd + (int64_t)tn * BN + half * 128);
@@ -237,6 +271,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             dst[4 * c + j] = o;
           }
       }
+    }
+    if constexpr (KR == 0) {
+      if (lane == 0) bulk_wait0();   // this warp's stores are complete before the CTA exits
     }
   }
 
@@ -628,8 +665,11 @@ int gemm_launch(const void* qa, int64_t lda, const void* sa, const void* qb, int
                                  (uint64_t)kr * 2, kr, BN, lora_swizzle(kr)))
       return st;
   } else {
-    tmL = tmA;  // unused by the kernel
-    tmR = tmA;
+    // no LoRA term: the tmL slot carries the output's map for the epilogue's TMA stores ([32 x 32] boxes)
+    if (int st = mx_make_tmap_2d(&tmL, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, d, (uint64_t)N, (uint64_t)M,
+                                 (uint64_t)ldd * 2, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B))
+      return st;
+    tmR = tmA;  // unused by the kernel
   }
 
   static bool attr_done[4][64] = {};
