@@ -927,7 +927,7 @@ int rowdot_tma(const void* A, int64_t lda, const void* B, int64_t T, int64_t K, 
 // and the matching [64 rows x NJ] rows of E into a 5-stage ring with TMA; warps 0-3 each own 16
 // columns and accumulate D[k x j] = A^T E with m16n8k16 MMAs whose operands come from ldmatrix.trans
 // (A^T and E^T are the transposes of the stored tiles).  Rows past T read as zero.
-constexpr int CD_ST = 5, CD_ROWS = 64, CD_COLS = 64;
+constexpr int CD_ST = 4, CD_ROWS = 64, CD_COLS = 64;   // 4 stages: 4 CTAs per SM at n = 32, 5 at n = 16
 __host__ __device__ constexpr int cd_stage(int NJ) { return CD_ROWS * CD_COLS * 2 + CD_ROWS * NJ * 2; }
 __host__ __device__ constexpr size_t cd_smem(int NJ) { return 1024 + (size_t)CD_ST * cd_stage(NJ) + 2 * CD_ST * 8; }
 
@@ -1575,10 +1575,11 @@ extern "C" int mxm_rowdot_quant(const void* A, int64_t lda, const void* B, int64
 
 extern "C" int mxm_coldot_chunks(int64_t T, int64_t K, int* rows_per_chunk, int* chunks) {
   MX_CHECK_ARG(T >= 1 && K >= 64 && rows_per_chunk && chunks, "mxm_coldot_chunks: bad args");
-  // about four CTAs per SM in all: (K / 64) column blocks x row chunks of a multiple of 64 rows
+  // one wave of four CTAs per SM (the n = 32 occupancy): (K / 64) column blocks x as many row chunks of
+  // a multiple of 64 rows as fit in it, so no partial second wave
   const int64_t ctas_k = (K + CD_COLS - 1) / CD_COLS;
   const int64_t want = 4 * (int64_t)mxm_num_sms();
-  const int64_t nch = (want + ctas_k - 1) / ctas_k;
+  const int64_t nch = std::max<int64_t>(1, want / ctas_k);
   int64_t rpc = (T + nch - 1) / nch;
   rpc = (rpc + CD_ROWS - 1) / CD_ROWS * CD_ROWS;
   if (rpc < 4 * CD_ROWS) rpc = 4 * CD_ROWS;
