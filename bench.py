@@ -52,9 +52,10 @@ def _args():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    ap.add_argument("--workload", choices=("layer", "stack", "quant", "ragged"), default="layer",
-                    help="layer: configs[1] (default); stack: configs[3]; quant: the configs[2] quantizer sweep "
-                         "(HBM GB/s); ragged: configs[4] small-M latency at the 0.8B shape")
+    ap.add_argument("--workload", choices=("layer", "stack", "ckpt", "quant", "ragged"), default="layer",
+                    help="layer: configs[1] (default); stack: configs[3]; ckpt: configs[3] with every layer "
+                         "checkpointed (recompute with need_out=False, as the reference's shared-prefix step); "
+                         "quant: the configs[2] quantizer sweep (HBM GB/s); ragged: configs[4] small-M latency")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end (host buffers) measurement")
     ap.add_argument("--tokens", type=int, default=0,
@@ -194,6 +195,15 @@ def run_ours(a):
         T, L = r1 - r0, STACK_LAYERS
         total_tokens = STACK_TOKENS
     layers = [_make_layer(torch, fused_mlp, dev, seed=1000 + i) for i in range(L)]
+    import torch.utils.checkpoint as tuc
+
+    def ckpt_layer(layer, ps):
+        # the reference's shared-prefix step (scripts/shared_prefix.py:200-203, 246-255): the forward inside
+        # the backward's recompute runs with need_out=False (its output is never read)
+        def fn(h):
+            return fused_mlp.mlp_apply(layer, h, *ps, scaling=(SCALE, SCALE, SCALE),
+                                       need_out=torch._C._current_graph_task_id() == -1)
+        return fn
     params = [p for _, ps in layers for p in ps]
     gx = torch.Generator(device="cpu").manual_seed(7 + rank)
     x_host = torch.randn(T, H, generator=gx).to(torch.bfloat16).pin_memory()
@@ -209,7 +219,10 @@ def run_ours(a):
         h = h.detach().requires_grad_(True)
         y = h
         for layer, ps in layers:
-            y = fused_mlp.mlp_apply(layer, y, *ps, scaling=(SCALE, SCALE, SCALE))
+            if a.workload == "ckpt":
+                y = tuc.checkpoint(ckpt_layer(layer, ps), y, use_reentrant=False)
+            else:
+                y = fused_mlp.mlp_apply(layer, y, *ps, scaling=(SCALE, SCALE, SCALE))
         y.backward(dyin)
         if world > 1:   # bucketed all-reduce of every LoRA gradient (NCCL over NVLink)
             bucket.allreduce()
@@ -297,7 +310,10 @@ def run_ours(a):
         h = xb[b].detach().requires_grad_(True)
         y = h
         for layer, ps in layers:
-            y = fused_mlp.mlp_apply(layer, y, *ps, scaling=(SCALE, SCALE, SCALE))
+            if a.workload == "ckpt":
+                y = tuc.checkpoint(ckpt_layer(layer, ps), y, use_reentrant=False)
+            else:
+                y = fused_mlp.mlp_apply(layer, y, *ps, scaling=(SCALE, SCALE, SCALE))
         y.backward(dyb[b])
         freed[b].record(comp)
         bucket.allreduce()
@@ -359,7 +375,9 @@ def run_ours(a):
         "scaling": "weak" if a.workload == "layer" else "strong", "vs_baseline": None, "dtype": "mxfp8-e4m3/bf16",
         "data": "synthetic (seeded N(0,1) activations, N(0,0.02) frozen weights, N(0,0.01) LoRA A/B)",
         "config": {"workload": ("configs[1]: one Qwen3.5-2B MLP layer, 16384 tokens per rank" if a.workload == "layer"
-                                else "configs[3]: 24-layer Qwen3.5-2B MLP stack, 142336-token step, token-sharded"),
+                                else "configs[3]: 24-layer Qwen3.5-2B MLP stack, 142336-token step, token-sharded"
+                                + (", every layer checkpointed (recompute with need_out=False)"
+                                   if a.workload == "ckpt" else "")),
                    "hidden": H, "intermediate": N, "lora_rank": R, "lora_alpha": ALPHA, "layers": L,
                    "tokens_per_rank": T, "parallelism": f"dp{world} (token shards, NCCL all-reduce of LoRA grads)",
                    "l2": "per-step working set > L2 (gu alone 384 MiB per layer); no flush"},
