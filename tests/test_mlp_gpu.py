@@ -167,3 +167,51 @@ def test_gemm_glu_matches_two_passes(T, H, N):
     d = (xsd.float() - xsd0.float()).abs()
     assert float(d.max()) <= float(xsd0.float().abs().max()) * 2.0 ** -7 + 1e-6
     assert float((xsd != xsd0).float().mean()) < 0.01
+
+
+@pytest.mark.parametrize("T", [77, 2049])
+def test_cuda_graph_replay_matches_eager(T):
+    """One fused fwd+bwd captured in a CUDA graph (static inputs) and replayed gives exactly the eager
+    step's output and gradients: the path makes no host synchronisation and no allocation outside
+    torch's allocator, so small-M callers can graph it (bench.py --workload ragged)."""
+    import fused_linear
+    import fused_mlp
+    H, N, r, s = 1024, 3584, 16, 2.0
+    x, Wg, Wu, Wd, lora, dy = _case(T, H, N, r, seed=T + 5, outlier=100.0)
+    dev = torch.device("cuda")
+    layer = fused_mlp.MXMLPWeights.from_bf16(Wg.to(dev), Wu.to(dev), Wd.to(dev))
+    params = [p.to(dev).clone().requires_grad_(True) for p in lora]
+    xs, dys = x.to(dev), dy.to(dev)
+    out = {}
+
+    def step():
+        fused_linear.new_step()
+        h = xs.detach().requires_grad_(True)
+        y = fused_mlp.mlp_apply(layer, h, *params, scaling=(s, s, s))
+        y.backward(dys)
+        out["y"], out["dx"] = y.detach(), h.grad   # no reference to the autograd graph survives the step
+
+    step()
+    torch.cuda.synchronize()
+    ref = [out["y"].clone(), out["dx"].clone()] + [p.grad.clone() for p in params]
+    for p in params:
+        p.grad = None
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for _ in range(2):
+            step()
+            for p in params:
+                p.grad = None
+    torch.cuda.current_stream().wait_stream(side)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        step()
+    for _ in range(2):
+        g.replay()
+    torch.cuda.synchronize()
+    got = [out["y"], out["dx"]] + [p.grad for p in params]
+    for a, b in zip(got, ref):
+        assert torch.equal(a, b)
+    import _mxlib
+    assert _mxlib.device_error() == 0
