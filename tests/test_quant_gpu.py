@@ -90,3 +90,26 @@ def test_full_size_properties():
     # determinism
     q3, s3 = mxfp8.mx_quant(x)
     assert torch.equal(q.view(torch.uint8), q3.view(torch.uint8)) and torch.equal(s.view(torch.uint8), s3.view(torch.uint8))
+
+
+@pytest.mark.parametrize("R,K", [(77, 256), (300, 1024)])
+def test_fallback_kernel_on_unaligned_code_rows(R, K):
+    """A code row stride that is not a multiple of 16 bytes (and a strided input) takes the per-tile
+    fallback kernel instead of the TMA one; both must give mx_quant's bytes exactly."""
+    import _mxlib
+    import mxfp8
+    x = _rand(R, K, seed=R + K).cuda()
+    wide = torch.zeros(R, K + 8, dtype=torch.bfloat16, device="cuda")
+    wide[:, :K] = x
+    xs = wide[:, :K]                                     # row stride K + 8 elements
+    ldq = K + 8                                          # not a multiple of 16 bytes
+    q = torch.zeros(R, ldq, dtype=torch.uint8, device="cuda")
+    s = torch.zeros(mxfp8.scale_numel(R, K), dtype=torch.uint8, device="cuda")
+    _mxlib.call("mxm_quant_rows", _mxlib.ptr(xs), R, K, K + 8, _mxlib.ptr(q), ldq, _mxlib.ptr(s),
+                _mxlib.stream_of(xs))
+    q0, s0 = mxfp8.mx_quant(x)
+    torch.cuda.synchronize()
+    assert torch.equal(q[:, :K], q0.view(torch.uint8))
+    assert int(q[:, K:].sum()) == 0
+    assert torch.equal(s, s0.view(torch.uint8))
+    assert _mxlib.device_error() == 0
