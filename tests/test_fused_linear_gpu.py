@@ -185,7 +185,12 @@ def test_group_linear_matches_module_calls():
     outs_g, dx_g, gr_g = _step(model, x, dys, dres, True)
     assert fused_linear.STATS.get("lan ngược gộp", 0) == n0 + 2      # both groups took the one-read backward
     assert fused_linear.STATS.get("residual LoRA", 0) == r0 + 1
+    q0, u0 = mxfp8.STATS["quant"], mxfp8.STATS["reuse"]
     outs_m, dx_m, gr_m = _step(model, x, dys, dres, False)
+    # module by module (_MXLinear): q/k/v share one input, quantized once and reused twice
+    # (scripts/mxfp8.py:299-312); o_proj quantizes its own input; the backward quantizes each dy
+    assert mxfp8.STATS["reuse"] - u0 >= 2
+    assert mxfp8.STATS["quant"] - q0 >= 2
     errs = [_rel(a, b) for a, b in zip(outs_g, outs_m)] + [_rel(a, b) for a, b in zip(gr_g, gr_m)]
     assert max(errs) < TOL, errs
     # dx: the grouped path adds the three MX branches in fp32 inside one GEMM and rounds once; calling the
