@@ -1086,8 +1086,17 @@ __global__ void k_sum_parts(const float* __restrict__ src, int nparts, int64_t n
                             float post, float* __restrict__ out_f, bf16* __restrict__ out_h, int64_t tr_a,
                             int64_t tr_b, int round_out) {
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    // partials added in order; eight loads are issued before their adds (latency, not order, changes)
     float v = 0.f;
-    for (int p = 0; p < nparts; ++p) v += src[p * stride + i];
+    int p = 0;
+    for (; p + 8 <= nparts; p += 8) {
+      float x[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) x[u] = __ldg(src + (int64_t)(p + u) * stride + i);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) v += x[u];
+    }
+    for (; p < nparts; ++p) v += __ldg(src + (int64_t)p * stride + i);
     v *= scale;
     int64_t o = i;
     if (tr_a > 0) o = (i % tr_b) * tr_a + i / tr_b;
