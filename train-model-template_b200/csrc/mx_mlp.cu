@@ -261,7 +261,8 @@ __global__ void __launch_bounds__(32 * (bwd_cons(R) + 1), 1)
   uint64_t* rows_full = empty + BWD_ST;
   uint64_t* op_full = rows_full + 1;   // all consumer warps stored the tile's dg | du | h
   uint64_t* op_empty = op_full + 1;    // all column-product blocks of the tile were read
-  uint64_t* rows_empty = op_empty + 1; // all consumer warps are done with the row block in rows_xs / rows_dxd
+  uint64_t* rows_empty = op_empty + 1; // every consumer warp has the block's rows in registers (the producer
+                                       // reloads rows_xs / rows_dxd once its own column products are done too)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nt = N / BWD_BN;                                   // column tiles per row block
   const int items = ((Tpad + SB - 1) / SB) * nt;               // (row block, column tile), column fastest
