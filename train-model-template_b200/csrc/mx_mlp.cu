@@ -1119,39 +1119,56 @@ __global__ void k_sum_parts(const float* __restrict__ src, int nparts, int64_t n
 struct LoraSrc {
   const void* p[6];  // Ag, Au, Bg, Bu, Ad, Bd
 };
+// blockIdx.y = output segment (0 S, 1 bg, 2 bu, 3 ad, 4 bd, 5 bds, 6 bdT, 7 ST).  The six straight
+// segments move four values per thread when r % 4 == 0 (every segment then starts on a 4-element
+// boundary); the two transposes one value per thread, writes coalesced.
 __global__ void k_lora_prep(LoraSrc src, int src_f32, int H, int N, int r, float s_d, bf16* __restrict__ out) {
-  const int64_t nS = 2ll * r * H, nB = (int64_t)N * r, nD = (int64_t)H * r;
-  const int64_t o_bg = nS, o_bu = o_bg + nB, o_ad = o_bu + nB, o_bd = o_ad + nB, o_bds = o_bd + nD,
-                o_bdT = o_bds + nD, o_ST = o_bdT + nD, total = o_ST + nS;
+  const int seg = blockIdx.y;
+  const int64_t rH = (int64_t)r * H, nB = (int64_t)N * r, nD = (int64_t)H * r;
+  const int64_t starts[9] = {0, 2 * rH, 2 * rH + nB, 2 * rH + 2 * nB, 2 * rH + 3 * nB, 2 * rH + 3 * nB + nD,
+                             2 * rH + 3 * nB + 2 * nD, 2 * rH + 3 * nB + 3 * nD, 4 * rH + 3 * nB + 3 * nD};
+  int64_t off = starts[0], len = starts[1];
+#pragma unroll
+  for (int k = 1; k < 8; ++k)
+    if (seg == k) {
+      off = starts[k];
+      len = starts[k + 1] - starts[k];
+    }
   auto ld = [&](int w, int64_t i) -> float {
     return src_f32 ? reinterpret_cast<const float*>(src.p[w])[i]
                    : __bfloat162float(reinterpret_cast<const bf16*>(src.p[w])[i]);
   };
-  auto ldS = [&](int64_t i) -> float {  // S = [Ag; Au] flat [2r, H]
-    return i < (int64_t)r * H ? ld(0, i) : ld(1, i - (int64_t)r * H);
-  };
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-    float v;
-    if (i < o_bg) {
-      v = ldS(i);
-    } else if (i < o_bu) {
-      v = ld(2, i - o_bg);
-    } else if (i < o_ad) {
-      v = ld(3, i - o_bu);
-    } else if (i < o_bd) {
-      v = ld(4, i - o_ad);
-    } else if (i < o_bds) {
-      v = ld(5, i - o_bd);
-    } else if (i < o_bdT) {
-      v = bf16_round_f(bf16_round_f(ld(5, i - o_bds)) * s_d);
-    } else if (i < o_ST) {  // bdT [r, H]: (j, h) <- Bd [H, r] (h, j)
-      const int64_t e = i - o_bdT, j = e / H, h = e % H;
-      v = ld(5, h * r + j);
-    } else {                // ST [H, 2r]: (h, j) <- S [2r, H] (j, h)
-      const int64_t e = i - o_ST, h = e / (2 * r), j = e % (2 * r);
-      v = ldS(j * H + h);
+  auto value = [&](int64_t i) -> float {   // straight segments
+    switch (seg) {
+      case 0: return i < rH ? ld(0, i) : ld(1, i - rH);
+      case 1: return ld(2, i);
+      case 2: return ld(3, i);
+      case 3: return ld(4, i);
+      case 4: return ld(5, i);
+      default: return bf16_round_f(bf16_round_f(ld(5, i)) * s_d);
     }
-    out[i] = __float2bfloat16_rn(v);
+  };
+  const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x, nth = (int64_t)gridDim.x * blockDim.x;
+  bf16* o = out + off;
+  if (seg < 6 && (r & 3) == 0) {
+    for (int64_t i = 4 * tid; i < len; i += 4 * nth) {
+      uint2 w;
+      w.x = pack_bf16x2(value(i), value(i + 1));
+      w.y = pack_bf16x2(value(i + 2), value(i + 3));
+      *reinterpret_cast<uint2*>(o + i) = w;
+    }
+  } else if (seg < 6) {
+    for (int64_t i = tid; i < len; i += nth) o[i] = __float2bfloat16_rn(value(i));
+  } else if (seg == 6) {   // bdT [r, H]: (j, h) <- Bd [H, r] (h, j)
+    for (int64_t e = tid; e < len; e += nth) {
+      const int64_t j = e / H, h = e % H;
+      o[e] = __float2bfloat16_rn(ld(5, h * r + j));
+    }
+  } else {                 // ST [H, 2r]: (h, j) <- S [2r, H] (j, h)
+    for (int64_t e = tid; e < len; e += nth) {
+      const int64_t h = e / (2 * r), j = e % (2 * r);
+      o[e] = __float2bfloat16_rn(j < r ? ld(0, j * H + h) : ld(1, (j - r) * H + h));
+    }
   }
 }
 
@@ -1455,9 +1472,11 @@ extern "C" int mxm_lora_prep(const void* Ag, const void* Au, const void* Bg, con
   MX_CHECK_ARG(H >= 1 && N >= 1 && r >= 1 && r <= 256 && H < (1ll << 31) && N < (1ll << 31),
                "mxm_lora_prep: bad shape");
   LoraSrc src{{Ag, Au, Bg, Bu, Ad, Bd}};
-  const int64_t total = (int64_t)r * (7 * H + 3 * N);
-  k_lora_prep<<<grid_for(total, 256), 256, 0, (cudaStream_t)stream>>>(src, src_fp32, (int)H, (int)N, r, s_d,
-                                                                        (bf16*)out);
+  // grid.y = the eight output segments; grid.x sized for the largest one (four values per thread)
+  const int64_t largest = std::max<int64_t>(2 * (int64_t)r * H, (int64_t)N * r);
+  const int gx = (int)std::min<int64_t>((largest / 4 + 255) / 256 + 1, (int64_t)mxm_num_sms() * 4);
+  k_lora_prep<<<dim3((unsigned)gx, 8u), 256, 0, (cudaStream_t)stream>>>(src, src_fp32, (int)H, (int)N, r, s_d,
+                                                                         (bf16*)out);
   mx_note_launch();
   return mx_launch_status("lora prep");
 }
