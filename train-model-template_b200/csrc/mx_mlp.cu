@@ -1182,8 +1182,7 @@ struct SumJob {
 struct SumJobs {
   SumJob j[3];
 };
-__global__ void __launch_bounds__(256) k_sum_parts4(SumJobs jobs, int nparts, int64_t n4, int64_t stride4) {
-  const SumJob jb = blockIdx.y == 0 ? jobs.j[0] : (blockIdx.y == 1 ? jobs.j[1] : jobs.j[2]);
+MX_DEV void sum_parts4_body(const SumJob& jb, int nparts, int64_t n4, int64_t stride4) {
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (int64_t)gridDim.x * blockDim.x) {
     // partials in order, 16 loads in flight: even parts into v, odd parts into w, then v + w
     float4 v = make_float4(0.f, 0.f, 0.f, 0.f), w = v;
@@ -1216,8 +1215,8 @@ __global__ void __launch_bounds__(256) k_sum_parts4(SumJobs jobs, int nparts, in
 // Row block sbi (rows sb * sbi ..) was worked on by CTAs c_lo .. c_hi of the backward epilogue, whose
 // partials sit in slots 0 .. c_hi - c_lo; they are added in slot order.  Four values per thread.
 template <int R>
-__global__ void k_reduce_dxa(const float* __restrict__ src, int sb, int nt, int per, int T, float s_g, float s_u,
-                             bf16* __restrict__ dxa, bf16* __restrict__ xsd) {
+MX_DEV void reduce_dxa_body(const float* __restrict__ src, int sb, int nt, int per, int T, float s_g, float s_u,
+                            bf16* __restrict__ dxa, bf16* __restrict__ xsd) {
   constexpr int Q = 3 * R / 4;   // float4s per row
   const int64_t n = (int64_t)T * Q;
   const int64_t stride = (int64_t)T * Q;
@@ -1241,6 +1240,19 @@ __global__ void k_reduce_dxa(const float* __restrict__ src, int sb, int nt, int 
     else
       *reinterpret_cast<uint2*>(xsd + row * R + c - 2 * R) = o;
   }
+}
+
+// The backward's fixed-order reductions in one launch: grid rows 0-2 sum the column-product partials
+// (dB_gate, dB_up, dA_down), row 3 the per-row partials into dxa / xS_down.
+template <int R>
+__global__ void __launch_bounds__(256) k_bwd_reduce(SumJobs jobs, int nparts, int64_t n4, const float* __restrict__ dsrc,
+                                                    int sb, int nt, int per, int T, float s_g, float s_u,
+                                                    bf16* __restrict__ dxa, bf16* __restrict__ xsd) {
+  if (blockIdx.y < 3) {
+    const SumJob jb = blockIdx.y == 0 ? jobs.j[0] : (blockIdx.y == 1 ? jobs.j[1] : jobs.j[2]);   // by value
+    sum_parts4_body(jb, nparts, n4, n4);
+  } else
+    reduce_dxa_body<R>(dsrc, sb, nt, per, T, s_g, s_u, dxa, xsd);
 }
 
 int grid_for(int64_t n, int threads) {
@@ -1423,20 +1435,18 @@ extern "C" int mxm_mlp_bwd_reduce(const void* dxa_part, const void* dbg_part, co
   const int nsb = p.nsb;
   cudaStream_t st = (cudaStream_t)stream;
   const int64_t nd = T * 3 * r / 4;
-  if (r == 16)
-    k_reduce_dxa<16><<<grid_for(nd, 256), 256, 0, st>>>((const float*)dxa_part, p.sb, p.nt, p.per, (int)T, s_g, s_u,
-                                                        (bf16*)dxa, (bf16*)xsd);
-  else
-    k_reduce_dxa<32><<<grid_for(nd, 256), 256, 0, st>>>((const float*)dxa_part, p.sb, p.nt, p.per, (int)T, s_g, s_u,
-                                                        (bf16*)dxa, (bf16*)xsd);
-  mx_note_launch();
   const int64_t nb4 = N * r / 4;  // N % 128 == 0
   SumJobs jobs;
   jobs.j[0] = {(const float4*)dbg_part, (float4*)dBg, s_g};
   jobs.j[1] = {(const float4*)dbu_part, (float4*)dBu, s_u};
   jobs.j[2] = {(const float4*)dad_part, (float4*)dAd, 1.f};
-  const int gx = (int)std::min<int64_t>((nb4 + 255) / 256, (int64_t)mxm_num_sms() * 8);
-  k_sum_parts4<<<dim3((unsigned)gx, 3u), 256, 0, st>>>(jobs, nsb, nb4, nb4);
+  const int gx = std::max(grid_for(nd, 256), (int)std::min<int64_t>((nb4 + 255) / 256, (int64_t)mxm_num_sms() * 8));
+  if (r == 16)
+    k_bwd_reduce<16><<<dim3((unsigned)gx, 4u), 256, 0, st>>>(jobs, nsb, nb4, (const float*)dxa_part, p.sb, p.nt, p.per,
+                                                             (int)T, s_g, s_u, (bf16*)dxa, (bf16*)xsd);
+  else
+    k_bwd_reduce<32><<<dim3((unsigned)gx, 4u), 256, 0, st>>>(jobs, nsb, nb4, (const float*)dxa_part, p.sb, p.nt, p.per,
+                                                             (int)T, s_g, s_u, (bf16*)dxa, (bf16*)xsd);
   mx_note_launch();
   return mx_launch_status("mlp bwd reduce");
 }
