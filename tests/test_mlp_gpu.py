@@ -141,7 +141,9 @@ def test_need_out_false_and_determinism():
                                    (4096, 2048, 6144)])
 def test_gemm_glu_matches_two_passes(T, H, N):
     """The gate|up GEMM with the fused forward epilogue gives the same gu and the same MXFP8(h) bytes as the
-    GEMM followed by the separate epilogue kernel; xS_down differs only by the fp32 summation order."""
+    GEMM followed by the separate epilogue kernel; xS_down differs only by the fp32 summation order.
+    T >= 256 runs the CTA-pair kernel (2049: an odd count of 128-row blocks, so the last pair's second CTA
+    holds no rows), smaller T the single-CTA kernel."""
     import fused_mlp
     import mxfp8
     g = torch.Generator().manual_seed(T + N)

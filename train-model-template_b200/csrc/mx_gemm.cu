@@ -24,6 +24,7 @@
 // Every mbarrier wait is bounded (see mbar_wait): on a timeout the kernel records an error code in the
 // device flag and all roles fall through to the TMEM release and exit.
 #include <algorithm>
+#include <mutex>
 
 #include "mx_common.cuh"
 #include "mx_epi.cuh"
@@ -285,46 +286,56 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
 // ------------------------------------------------------------------------------------------------
 // Gate|up GEMM with the SwiGLU-LoRA forward epilogue fused in (the reference's gu GEMM and _fwd_kernel,
-// scripts/fused_mlp.py:279-282 and :81-109).  A 128 x 256 tile pairs gate columns [128 tn, +128) with the
-// up columns N + 128 tn .. of the same 128 outputs: its B stage is two TMA boxes of W_gu rows (gate, up)
-// and its two B scale blocks are the matching ones, so one tcgen05 accumulator holds both halves of 128
-// (g, u) column pairs.  Producer / MMA warps as in k_mx_gemm (3 stages).  The 8 epilogue warps drain the
-// accumulator (warp q|h: lanes 32q.., half h = gate / up), hand it back and stage the bf16 tile in
-// shared memory (128-byte swizzle), from which four TMA stores write gu (the backward reads it) in full
-// 128-byte rows; after one named barrier each warp runs the
-// forward epilogue on 16 rows x 128 pairs of the staged tile -- the LoRA-B terms with mma.sync, SwiGLU,
-// the MXFP8 codes of h, and the per-row xS_down = h A_down^T accumulated in registers -- while the MMAs
-// of the next tile proceed.  A CTA works through a contiguous range of tiles (column tiles fastest), so
-// xS_down accumulates over the columns of a row block and is written as one fp32 partial per (row block,
-// CTA); a fixed-order reduction sums them.  Rank 16 only (the rank-32 slices do not fit shared memory).
-constexpr int GLU_STAGES = 3;
-constexpr int GLU_B_BYTES = 256 * BK;
+// scripts/fused_mlp.py:279-282 and :81-109).  A tile pairs gate columns [128 tn, +128) with the up
+// columns N + 128 tn .. of the same 128 outputs, so one tcgen05 accumulator of 128 rows x 256 columns
+// holds both halves of 128 (g, u) column pairs.  Two launch shapes share one body:
+//   * single CTA (k_mx_gemm_glu): 128-row tiles; a B stage is two TMA boxes of W_gu rows (gate, up) and
+//     its two B scale blocks are the matching ones; 3 stages of 48 KB fit beside the epilogue's buffers.
+//   * CTA pair (k_mx_gemm_glu2, cluster of two, cta_group::2): 256-row tiles; CTA r stages A rows
+//     [256 tm + 128 r, +128) and one half of B (r = 0: the gate rows, r = 1: the up rows), the leader
+//     issues M256 N256 K32 MMAs over both CTAs' shared memory, and each CTA's TMEM receives its own 128
+//     rows x [gate | up] -- the same accumulator the single-CTA epilogue reads.  Per SM a k-block moves
+//     32 KB of operands instead of 48 KB and the 33 KB stages leave room for 4 of them.  The peer's TMA
+//     copies complete on the leader's full barriers; the leader's commits arrive on both CTAs' barriers;
+//     each epilogue warp hands the accumulator back by one remote arrival on the leader's tmem_empty.
+// The 8 epilogue warps drain the accumulator (warp q|h: lanes 32q.., half h = gate / up), hand it back
+// and stage the bf16 tile in shared memory (128-byte swizzle), from which four TMA stores write gu (the
+// backward reads it) in full 128-byte rows; after one named barrier each warp runs the forward epilogue
+// on 16 rows x 128 pairs of the staged tile -- the LoRA-B terms with mma.sync, SwiGLU, the MXFP8 codes
+// of h, and the per-row xS_down = h A_down^T accumulated in registers -- while the MMAs of the next tile
+// proceed.  A CTA (pair) works through a contiguous range of tiles (column tiles fastest), so xS_down
+// accumulates over the columns of a row block and is written as one fp32 partial per (row block, CTA or
+// pair); a fixed-order reduction sums them.  Rank 16 only (the rank-32 slices do not fit shared memory).
 constexpr int GLU_STAGING = 2 * 2 * 128 * 128;   // g | u halves, two [128 x 64] bf16 sub-tiles each
+template <bool PAIR> __host__ __device__ constexpr int glu_stages() { return PAIR ? 4 : 3; }
+template <bool PAIR> __host__ __device__ constexpr int glu_bstage() { return PAIR ? 128 * BK : 256 * BK; }
 __host__ __device__ constexpr int glu_slices(int R) { return 2 * 128 * R * 2 + R * 128 * 2; }
-__host__ __device__ constexpr size_t glu_ring() {
-  return ((size_t)GLU_STAGES * (A_BYTES + GLU_B_BYTES + SFA_BYTES + SFB_BYTES) + 1023) / 1024 * 1024;
+template <bool PAIR> __host__ __device__ constexpr size_t glu_ring() {
+  return ((size_t)glu_stages<PAIR>() * (A_BYTES + glu_bstage<PAIR>() + SFA_BYTES + SFB_BYTES) + 1023) / 1024 * 1024;
 }
-__host__ __device__ constexpr size_t glu_smem(int R) { return 1024 + glu_ring() + GLU_STAGING + glu_slices(R) + 256; }
+template <bool PAIR> __host__ __device__ constexpr size_t glu_smem(int R) {
+  return 1024 + glu_ring<PAIR>() + GLU_STAGING + glu_slices(R) + 256;
+}
 
 MX_DEV void epi_sync() { asm volatile("bar.sync 1, %0;" ::"r"(EPI_THREADS) : "memory"); }
 
-template <int R>
-__global__ void __launch_bounds__(NUM_THREADS, 1)
-    k_mx_gemm_glu(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                  const __grid_constant__ CUtensorMap tmG, const uint8_t* __restrict__ sa,
-                  const uint8_t* __restrict__ sb, int M, int N, int K,
-                  const __nv_bfloat16* __restrict__ xs,
-                  const __nv_bfloat16* __restrict__ bg, const __nv_bfloat16* __restrict__ bu,
-                  const __nv_bfloat16* __restrict__ ad, float s_g, float s_u, uint8_t* __restrict__ qh,
-                  uint8_t* __restrict__ sh, float* __restrict__ xsd_part, int per, int* err) {
-  constexpr int STAGES = GLU_STAGES, KS = R / 16;
+template <int R, bool PAIR>
+MX_DEV void glu_body(const CUtensorMap* tmA, const CUtensorMap* tmB, const CUtensorMap* tmG, const CUtensorMap* tmSA,
+                     const CUtensorMap* tmSB, const uint8_t* __restrict__ sa, const uint8_t* __restrict__ sb, int M,
+                     int N, int K, const __nv_bfloat16* __restrict__ xs, const __nv_bfloat16* __restrict__ bg,
+                     const __nv_bfloat16* __restrict__ bu, const __nv_bfloat16* __restrict__ ad, float s_g, float s_u,
+                     uint8_t* __restrict__ qh, uint8_t* __restrict__ sh, float* __restrict__ xsd_part, int per,
+                     int* err) {
+  constexpr int STAGES = glu_stages<PAIR>(), B_STAGE = glu_bstage<PAIR>(), KS = R / 16;
+  constexpr int TM_ROWS = PAIR ? 256 : BM;                 // rows of one tile (of the pair)
+  constexpr uint32_t STAGE_TX = (PAIR ? 2u : 1u) * (A_BYTES + B_STAGE + SFA_BYTES + SFB_BYTES);
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = sA + STAGES * A_BYTES;
-  uint8_t* sSFA = sB + STAGES * GLU_B_BYTES;
+  uint8_t* sSFA = sB + STAGES * B_STAGE;
   uint8_t* sSFB = sSFA + STAGES * SFA_BYTES;
-  uint8_t* stg = smem + glu_ring();          // [g | u][2 sub-tiles][128 rows x 128 B], 128-byte swizzle
+  uint8_t* stg = smem + glu_ring<PAIR>();     // [g | u][2 sub-tiles][128 rows x 128 B], 128-byte swizzle
   uint8_t* sl = stg + GLU_STAGING;           // Bg, Bu [128 x R] (2R-byte swizzle), Ad [2][R x 128 B]
   uint64_t* bars = reinterpret_cast<uint64_t*>(sl + glu_slices(R));
   uint64_t* full = bars;
@@ -335,11 +346,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int num_m = (M + BM - 1) / BM;
+  const uint32_t rank = PAIR ? cluster_ctarank() : 0u;
+  const bool leader = rank == 0;
+  const int unit = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;   // CTA or pair
+  const int num_m = (M + TM_ROWS - 1) / TM_ROWS;
   const int num_n = N / 128;
   const int num_tiles = num_m * num_n;
   const int KT = K / BK;
-  const int t_lo = blockIdx.x * per, t_hi = min(t_lo + per, num_tiles);
+  const int t_lo = unit * per, t_hi = min(t_lo + per, num_tiles);
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < STAGES; ++i) {
@@ -347,22 +361,35 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       mbar_init(&empty[i], 1);
     }
     mbar_init(tmem_full, 1);
-    mbar_init(tmem_empty, EPI_THREADS);
+    // single CTA: every epilogue thread arrives; pair: one remote arrival per epilogue warp of each CTA
+    mbar_init(tmem_empty, PAIR ? 2 * (EPI_THREADS / 32) : EPI_THREADS);
     fence_barrier_init();
   }
-  if (warp == 2) tmem_alloc(tmem_base, TMEM_COLS);
+  if (warp == 2) {
+    if constexpr (PAIR)
+      tmem_alloc_pair(tmem_base, TMEM_COLS);
+    else
+      tmem_alloc(tmem_base, TMEM_COLS);
+  }
   tc_fence_before();
-  __syncthreads();
+  if constexpr (PAIR)
+    cluster_sync_all();   // barriers and TMEM of both CTAs exist before any cross-CTA operation
+  else
+    __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_base;
   constexpr int SFA_COL = 256, SFB_COL = 260;
 
   if (warp == 0) {
     if (lane == 0) {
-      prefetch_tmap(&tmA);
-      prefetch_tmap(&tmB);
+      prefetch_tmap(tmA);
+      prefetch_tmap(tmB);
+      if constexpr (PAIR) {
+        prefetch_tmap(tmSA);
+        prefetch_tmap(tmSB);
+      }
     }
-    int stage = 0;
+    int stage = 0, issued = 0;
     uint32_t phase = 0;
     bool ok = true;
     for (int tile = t_lo; tile < t_hi && ok; ++tile) {
@@ -373,23 +400,42 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           break;
         }
         if (lane == 0) {
-          uint64_t* fb = &full[stage];
-          mbar_arrive_expect_tx(fb, A_BYTES + GLU_B_BYTES + SFA_BYTES + SFB_BYTES);
-          tma_load_2d(sA + stage * A_BYTES, &tmA, fb, kt * BK, tm * BM);
-          tma_load_2d(sB + stage * GLU_B_BYTES, &tmB, fb, kt * BK, tn * 128);             // gate rows
-          tma_load_2d(sB + stage * GLU_B_BYTES + 128 * BK, &tmB, fb, kt * BK, N + tn * 128); // up rows
-          bulk_load(sSFA + stage * SFA_BYTES, sa + ((int64_t)tm * KT + kt) * 512, 512, fb);
-          bulk_load(sSFB + stage * SFB_BYTES, sb + ((int64_t)tn * KT + kt) * 512, 512, fb);
-          bulk_load(sSFB + stage * SFB_BYTES + 512, sb + ((int64_t)(num_n + tn) * KT + kt) * 512, 512, fb);
+          if constexpr (PAIR) {
+            const uint32_t fb = mapa_shared(smem_u32(&full[stage]), 0);
+            const int mb = tm * 2 + (int)rank;                     // this CTA's 128-row block of A
+            if (leader) mbar_arrive_expect_tx(&full[stage], STAGE_TX);
+            tma_load_2d_pair(sA + stage * A_BYTES, tmA, fb, kt * BK, mb * BM);
+            tma_load_2d_pair(sB + stage * B_STAGE, tmB, fb, kt * BK, (int)rank * N + tn * 128);  // gate / up rows
+            tma_load_2d_pair(sSFA + stage * SFA_BYTES, tmSA, fb, 0, 2 * (mb * KT + kt));
+            tma_load_2d_pair(sSFB + stage * SFB_BYTES, tmSB, fb, 0, 2 * (tn * KT + kt));
+            tma_load_2d_pair(sSFB + stage * SFB_BYTES + 512, tmSB, fb, 0, 2 * ((num_n + tn) * KT + kt));
+          } else {
+            uint64_t* fb = &full[stage];
+            mbar_arrive_expect_tx(fb, STAGE_TX);
+            tma_load_2d(sA + stage * A_BYTES, tmA, fb, kt * BK, tm * BM);
+            tma_load_2d(sB + stage * B_STAGE, tmB, fb, kt * BK, tn * 128);             // gate rows
+            tma_load_2d(sB + stage * B_STAGE + 128 * BK, tmB, fb, kt * BK, N + tn * 128); // up rows
+            bulk_load(sSFA + stage * SFA_BYTES, sa + ((int64_t)tm * KT + kt) * 512, 512, fb);
+            bulk_load(sSFB + stage * SFB_BYTES, sb + ((int64_t)tn * KT + kt) * 512, 512, fb);
+            bulk_load(sSFB + stage * SFB_BYTES + 512, sb + ((int64_t)(num_n + tn) * KT + kt) * 512, 512, fb);
+          }
         }
         __syncwarp();
+        ++issued;
         if (++stage == STAGES) {
           stage = 0;
           phase ^= 1;
         }
       }
     }
-  } else if (warp == 1) {
+    if constexpr (PAIR) {
+      // the leader's last commits to this CTA's empty barriers have landed before the CTA may exit
+      for (int k = 0; k < STAGES && k < issued; ++k) {
+        const int i = issued - 1 - k;
+        mbar_wait(&empty[i % STAGES], (uint32_t)((i / STAGES) & 1), err, MX_DEV_TIMEOUT_PRODUCER);
+      }
+    }
+  } else if (warp == 1 && leader) {
     int stage = 0;
     uint32_t phase = 0, acc_phase = 0;
     bool ok = true;
@@ -405,18 +451,31 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         if (lane == 0) {
           const uint32_t sfa = smem_u32(sSFA + stage * SFA_BYTES);
           const uint32_t sfb = smem_u32(sSFB + stage * SFB_BYTES);
-          tmem_cp_32x128b_x4(tmem + SFA_COL, make_sdesc(sfa, 0, 128, 0));
-          tmem_cp_32x128b_x4(tmem + SFB_COL, make_sdesc(sfb, 0, 128, 0));
-          tmem_cp_32x128b_x4(tmem + SFB_COL + 4, make_sdesc(sfb + 512, 0, 128, 0));
           const uint32_t a0 = smem_u32(sA + stage * A_BYTES);
-          const uint32_t b0 = smem_u32(sB + stage * GLU_B_BYTES);
+          const uint32_t b0 = smem_u32(sB + stage * B_STAGE);
+          if constexpr (PAIR) {
+            tmem_cp_32x128b_x4_pair(tmem + SFA_COL, make_sdesc(sfa, 0, 128, 0));
+            tmem_cp_32x128b_x4_pair(tmem + SFB_COL, make_sdesc(sfb, 0, 128, 0));
+            tmem_cp_32x128b_x4_pair(tmem + SFB_COL + 4, make_sdesc(sfb + 512, 0, 128, 0));
+          } else {
+            tmem_cp_32x128b_x4(tmem + SFA_COL, make_sdesc(sfa, 0, 128, 0));
+            tmem_cp_32x128b_x4(tmem + SFB_COL, make_sdesc(sfb, 0, 128, 0));
+            tmem_cp_32x128b_x4(tmem + SFB_COL + 4, make_sdesc(sfb + 512, 0, 128, 0));
+          }
 #pragma unroll
           for (int k = 0; k < BK / 32; ++k) {
             const uint64_t adsc = make_sdesc(a0 + k * 32, 0, 1024, 2);
             const uint64_t bdsc = make_sdesc(b0 + k * 32, 0, 1024, 2);
-            umma_mxf8(tmem, adsc, bdsc, mx_idesc(BM, 256, k, k), tmem + SFA_COL, tmem + SFB_COL, (kt | k) != 0);
+            if constexpr (PAIR)
+              umma_mxf8_pair(tmem, adsc, bdsc, mx_idesc(256, 256, k, k), tmem + SFA_COL, tmem + SFB_COL,
+                             (kt | k) != 0);
+            else
+              umma_mxf8(tmem, adsc, bdsc, mx_idesc(BM, 256, k, k), tmem + SFA_COL, tmem + SFB_COL, (kt | k) != 0);
           }
-          umma_commit(&empty[stage]);
+          if constexpr (PAIR)
+            umma_commit_both(&empty[stage]);
+          else
+            umma_commit(&empty[stage]);
         }
         __syncwarp();
         if (++stage == STAGES) {
@@ -425,17 +484,25 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
       }
       if (!ok) break;
-      if (lane == 0) umma_commit(tmem_full);
+      if (lane == 0) {
+        if constexpr (PAIR)
+          umma_commit_both(tmem_full);
+        else
+          umma_commit(tmem_full);
+      }
       __syncwarp();
       acc_phase ^= 1;
     }
+    // pair: both CTAs' epilogues have released the last accumulator (their remote arrivals have landed)
+    if constexpr (PAIR) mbar_wait(tmem_empty, acc_phase ^ 1, err, MX_DEV_TIMEOUT_MMA_TMEM);
   } else if (warp >= EPI_WARP0) {
     const int e = warp - EPI_WARP0;            // SwiGLU rows 16e .. 16e+15 of a tile
     const int q = warp & 3, h = e >> 2;        // drain: TMEM lanes 32q .., accumulator half h (0 gate, 1 up)
     const int g = lane >> 2, t = lane & 3, mi = lane >> 3, lr = lane & 7;
     const int et = e * 32 + lane;              // 0 .. 255
-    const int64_t Tpad = (int64_t)num_m * BM;
+    const int64_t Tpad = (int64_t)((M + BM - 1) / BM) * BM;
     const int lrow = e * 16 + (mi & 1) * 8 + lr;
+    const uint32_t tmem_empty_l = PAIR ? mapa_shared(smem_u32(tmem_empty), 0) : 0u;
     uint32_t o_gu[4], o_b[4][KS], o_ad[4][KS];
 #pragma unroll
     for (int p = 0; p < 4; ++p) {
@@ -453,8 +520,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     QRows qr{};
     int cur_tm = -1;
     int64_t ra = 0, rb = 0;
-    auto flush = [&](int tm_done) {   // this CTA's partial of xS_down for its rows of row block tm_done
-      const int slot = (int)blockIdx.x - (tm_done * num_n) / per;
+    auto flush = [&](int tm_done) {   // this unit's partial of xS_down for its rows of row block tm_done
+      const int slot = unit - (tm_done * num_n) / per;
       float* P = xsd_part + (int64_t)slot * M * R;
 #pragma unroll
       for (int jt = 0; jt < R / 8; ++jt) {
@@ -466,10 +533,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     uint32_t acc_phase = 0;
     for (int tile = t_lo; tile < t_hi; ++tile) {
       const int tm = tile / num_n, tn = tile % num_n;
+      const int64_t rowb = (int64_t)tm * TM_ROWS + rank * BM;   // this CTA's first row of the tile
       if (tm != cur_tm) {
         if (cur_tm >= 0) flush(cur_tm);
         cur_tm = tm;
-        ra = (int64_t)tm * BM + e * 16 + g;
+        ra = rowb + e * 16 + g;
         rb = ra + 8;
         const bool va = ra < M, vb = rb < M;
 #pragma unroll
@@ -502,9 +570,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           tmem_ld32(taddr + c2 * 64, r[0]);
           tmem_ld32(taddr + c2 * 64 + 32, r[1]);
           tmem_ld_wait();
-          if (c2 == 1) {
+          if (c2 == 1) {   // the MMAs of the next tile start now
             tc_fence_before();
-            mbar_arrive(tmem_empty);   // the MMAs of the next tile start now
+            if constexpr (PAIR) {
+              __syncwarp();
+              if (lane == 0) mbar_arrive_cluster(tmem_empty_l);
+            } else {
+              mbar_arrive(tmem_empty);
+            }
           }
 #pragma unroll
           for (int c = 0; c < 2; ++c)
@@ -549,7 +622,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         for (int hh = 0; hh < 2; ++hh)
 #pragma unroll
           for (int c2 = 0; c2 < 2; ++c2)
-            tma_store_2d(&tmG, stg + (hh * 2 + c2) * (128 * 128), hh * N + tn * 128 + c2 * 64, tm * BM);
+            tma_store_2d(tmG, stg + (hh * 2 + c2) * (128 * 128), hh * N + tn * 128 + c2 * 64, (int)rowb);
         bulk_commit();
       }
       // 3. the forward epilogue on rows 16e .. 16e+15, two 64-column sub-tiles
@@ -612,17 +685,49 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   }
 
   tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  if (warp == 2) tmem_dealloc(tmem, TMEM_COLS);
+  if constexpr (PAIR) {
+    cluster_sync_all();
+    tc_fence_after();
+    if (warp == 2) tmem_dealloc_pair(tmem, TMEM_COLS);
+  } else {
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 2) tmem_dealloc(tmem, TMEM_COLS);
+  }
 }
 
-// xsd [M, R] bf16 = the fixed-order sum of the CTAs' partials of each row block (k_mx_gemm_glu).
-__global__ void k_glu_xsd_reduce(const float* __restrict__ part, int M, int R, int num_n, int per,
+template <int R>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    k_mx_gemm_glu(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                  const __grid_constant__ CUtensorMap tmG, const uint8_t* __restrict__ sa,
+                  const uint8_t* __restrict__ sb, int M, int N, int K, const __nv_bfloat16* __restrict__ xs,
+                  const __nv_bfloat16* __restrict__ bg, const __nv_bfloat16* __restrict__ bu,
+                  const __nv_bfloat16* __restrict__ ad, float s_g, float s_u, uint8_t* __restrict__ qh,
+                  uint8_t* __restrict__ sh, float* __restrict__ xsd_part, int per, int* err) {
+  glu_body<R, false>(&tmA, &tmB, &tmG, nullptr, nullptr, sa, sb, M, N, K, xs, bg, bu, ad, s_g, s_u, qh, sh, xsd_part,
+                     per, err);
+}
+
+// CTA-pair launch shape: scale blocks come in by TMA as [blocks * KT * 2, 256] byte tensors (tmSA, tmSB)
+template <int R>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
+    k_mx_gemm_glu2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const __grid_constant__ CUtensorMap tmG, const __grid_constant__ CUtensorMap tmSA,
+                   const __grid_constant__ CUtensorMap tmSB, int M, int N, int K, const __nv_bfloat16* __restrict__ xs,
+                   const __nv_bfloat16* __restrict__ bg, const __nv_bfloat16* __restrict__ bu,
+                   const __nv_bfloat16* __restrict__ ad, float s_g, float s_u, uint8_t* __restrict__ qh,
+                   uint8_t* __restrict__ sh, float* __restrict__ xsd_part, int per, int* err) {
+  glu_body<R, true>(&tmA, &tmB, &tmG, &tmSA, &tmSB, nullptr, nullptr, M, N, K, xs, bg, bu, ad, s_g, s_u, qh, sh,
+                    xsd_part, per, err);
+}
+
+// xsd [M, R] bf16 = the fixed-order sum of the units' partials of each row block of `rows_blk` rows
+// (k_mx_gemm_glu: 128-row blocks, one partial per CTA; k_mx_gemm_glu2: 256-row blocks, one per pair).
+__global__ void k_glu_xsd_reduce(const float* __restrict__ part, int M, int R, int num_n, int per, int rows_blk,
                                  __nv_bfloat16* __restrict__ xsd) {
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < (int64_t)M * R; i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t row = i / R;
-    const int tm = (int)(row / BM);
+    const int tm = (int)(row / rows_blk);
     const int c_lo = (tm * num_n) / per, c_hi = ((tm + 1) * num_n - 1) / per;
     float v = 0.f;
     for (int c = 0; c <= c_hi - c_lo; ++c) v += part[(int64_t)c * M * R + i];
@@ -717,15 +822,52 @@ extern "C" int mxm_gemm_lora(const void* qa, int64_t lda, const void* sa, const 
 }
 
 // ------------------------------------------------------------------------------------------------ fused gate|up
+namespace {
+// CTA pairs of k_mx_gemm_glu2 that can be resident at once on the current device; 0 selects the
+// single-CTA kernel (no room for a cluster of two).  Queried once per device.
+int glu_pairs() {
+  static int pairs[64] = {};
+  static bool done[64] = {};
+  static std::mutex mu;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return 0;
+  std::lock_guard<std::mutex> lock(mu);
+  if (!done[dev]) {
+    done[dev] = true;
+    const size_t smem = glu_smem<true>(16);
+    int n = 0;
+    cudaError_t e = cudaFuncSetAttribute(k_mx_gemm_glu2<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e == cudaSuccess) {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(2 * (unsigned)(mxm_num_sms() / 2), 1, 1);
+      cfg.blockDim = dim3(NUM_THREADS, 1, 1);
+      cfg.dynamicSmemBytes = smem;
+      e = cudaOccupancyMaxActiveClusters(&n, k_mx_gemm_glu2<16>, &cfg);
+    }
+    if (e != cudaSuccess) {   // refused: clear the error and run the single-CTA kernel instead
+      cudaGetLastError();
+      n = 0;
+    }
+    pairs[dev] = n;
+  }
+  return pairs[dev];
+}
+bool glu_use_pairs(int64_t M) { return M >= 256 && glu_pairs() > 0; }
+}  // namespace
+
 extern "C" int mxm_gemm_glu_partition(int64_t M, int64_t N, int* per, int* grid, int* slots) {
   MX_CHECK_ARG(M >= 1 && N >= 128 && N % 128 == 0 && per && grid && slots, "mxm_gemm_glu_partition: bad args");
-  const int64_t num_n = N / 128, tiles = ((M + BM - 1) / BM) * num_n;
-  int64_t g = tiles < mxm_num_sms() ? tiles : mxm_num_sms();
+  // units: CTA pairs over 256-row tiles when they fit, otherwise single CTAs over 128-row tiles
+  const bool pair = glu_use_pairs(M);
+  const int64_t rows = pair ? 256 : BM, units = pair ? glu_pairs() : mxm_num_sms();
+  const int64_t num_n = N / 128, tiles = ((M + rows - 1) / rows) * num_n;
+  int64_t g = tiles < units ? tiles : units;
   const int64_t p = (tiles + g - 1) / g;
   g = (tiles + p - 1) / p;
   *per = (int)p;
-  *grid = (int)g;
-  *slots = (int)((num_n + p - 1) / p + 1);   // CTAs that can touch one row block
+  *grid = (int)(pair ? 2 * g : g);
+  *slots = (int)((num_n + p - 1) / p + 1);   // units that can touch one row block
   return MXM_OK;
 }
 
@@ -744,6 +886,7 @@ extern "C" int mxm_gemm_glu(const void* qa, int64_t lda, const void* sa, const v
                "mxm_gemm_glu: alignment");
   int per = 0, grid = 0, slots = 0;
   if (int e = mxm_gemm_glu_partition(M, N, &per, &grid, &slots)) return e;
+  const bool pair = glu_use_pairs(M);
   CUtensorMap tmA, tmB, tmG;
   if (int st = mx_make_tmap_2d(&tmA, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, qa, (uint64_t)K, (uint64_t)M, (uint64_t)lda, BK,
                                BM, CU_TENSOR_MAP_SWIZZLE_128B))
@@ -754,26 +897,43 @@ extern "C" int mxm_gemm_glu(const void* qa, int64_t lda, const void* sa, const v
   if (int st = mx_make_tmap_2d(&tmG, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, gu, (uint64_t)(2 * N), (uint64_t)M,
                                (uint64_t)(4 * N), 64, BM, CU_TENSOR_MAP_SWIZZLE_128B))
     return st;
-  static bool attr_done[64] = {};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  const size_t smem = glu_smem(16);
-  if (dev >= 0 && dev < 64 && !attr_done[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(k_mx_gemm_glu<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return mx_cuda_status(e, "gemm glu: set smem");
-    attr_done[dev] = true;
-  }
   cudaStream_t st = (cudaStream_t)stream;
-  k_mx_gemm_glu<16><<<grid, NUM_THREADS, smem, st>>>(tmA, tmB, tmG, (const uint8_t*)sa, (const uint8_t*)sb, (int)M, (int)N,
-                                                     (int)K, (const __nv_bfloat16*)xs,
-                                                     (const __nv_bfloat16*)bg, (const __nv_bfloat16*)bu,
-                                                     (const __nv_bfloat16*)ad, s_g, s_u, (uint8_t*)qh, (uint8_t*)sh,
-                                                     (float*)xsd_part, per, mx_dev_error_ptr());
+  if (pair) {
+    // scale blocks as [blocks * KT * 2, 256] byte tensors: one 512-byte block = two 256-byte rows
+    const int64_t KT = K / BK;
+    CUtensorMap tmSA, tmSB;
+    if (int e = mx_make_tmap_2d(&tmSA, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, sa, 256, (uint64_t)((M + 127) / 128 * KT * 2),
+                                256, 256, 2, CU_TENSOR_MAP_SWIZZLE_NONE))
+      return e;
+    if (int e = mx_make_tmap_2d(&tmSB, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, sb, 256, (uint64_t)(2 * N / 128 * KT * 2), 256,
+                                256, 2, CU_TENSOR_MAP_SWIZZLE_NONE))
+      return e;
+    k_mx_gemm_glu2<16><<<grid, NUM_THREADS, glu_smem<true>(16), st>>>(
+        tmA, tmB, tmG, tmSA, tmSB, (int)M, (int)N, (int)K, (const __nv_bfloat16*)xs, (const __nv_bfloat16*)bg,
+        (const __nv_bfloat16*)bu, (const __nv_bfloat16*)ad, s_g, s_u, (uint8_t*)qh, (uint8_t*)sh, (float*)xsd_part, per,
+        mx_dev_error_ptr());
+  } else {
+    static bool attr_done[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const size_t smem = glu_smem<false>(16);
+    if (dev >= 0 && dev < 64 && !attr_done[dev]) {
+      cudaError_t e = cudaFuncSetAttribute(k_mx_gemm_glu<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      if (e != cudaSuccess) return mx_cuda_status(e, "gemm glu: set smem");
+      attr_done[dev] = true;
+    }
+    k_mx_gemm_glu<16><<<grid, NUM_THREADS, smem, st>>>(tmA, tmB, tmG, (const uint8_t*)sa, (const uint8_t*)sb, (int)M,
+                                                       (int)N, (int)K, (const __nv_bfloat16*)xs,
+                                                       (const __nv_bfloat16*)bg, (const __nv_bfloat16*)bu,
+                                                       (const __nv_bfloat16*)ad, s_g, s_u, (uint8_t*)qh, (uint8_t*)sh,
+                                                       (float*)xsd_part, per, mx_dev_error_ptr());
+  }
   mx_note_launch();
   if (int e = mx_launch_status("gemm glu")) return e;
   const int64_t n = M * r;
   const int rg = (int)std::min<int64_t>((n + 255) / 256, (int64_t)mxm_num_sms() * 8);
-  k_glu_xsd_reduce<<<rg, 256, 0, st>>>((const float*)xsd_part, (int)M, r, (int)(N / 128), per, (__nv_bfloat16*)xsd);
+  k_glu_xsd_reduce<<<rg, 256, 0, st>>>((const float*)xsd_part, (int)M, r, (int)(N / 128), per, pair ? 256 : BM,
+                                       (__nv_bfloat16*)xsd);
   mx_note_launch();
   return mx_launch_status("gemm glu xsd reduce");
 }
