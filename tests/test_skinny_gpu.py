@@ -77,3 +77,36 @@ def test_coldot_vs_torch(T, K, n):
     torch.cuda.synchronize()
     assert _rel(out, ref) < TOL
     assert torch.equal(outT, out.t().contiguous())
+
+
+def test_tma_path_from_a_fresh_thread():
+    """A thread whose first CUDA call is one of ours (autograd's device thread runs the backward's
+    rowdot_quant first) still gets the TMA kernels: the tensor-map encoder runs with the device context
+    bound, leaves no error, and the result equals the main thread's."""
+    import threading
+
+    import _mxlib
+    import fused_mlp
+    A = _rand((1024, 2048), 31).cuda()
+    B = _rand((16, 2048), 32, 0.05).cuda()
+    # the outputs go back to torch's cache, so the thread's allocations need no CUDA call of their own
+    ref = [t.clone() for t in fused_mlp.rowdot_quant(A, B, post=2.0)]
+    torch.cuda.synchronize()
+    got, err = {}, {}
+
+    def run():
+        try:
+            got["r"] = fused_mlp.rowdot_quant(A, B, post=2.0)
+            torch.cuda.synchronize()
+            err["msg"] = _mxlib.last_error()   # per-thread message: set by any failed call in this thread
+        except Exception as e:   # pragma: no cover - reported below
+            err["exc"] = repr(e)
+
+    t = threading.Thread(target=run)
+    t.start()
+    t.join()
+    assert "exc" not in err, err
+    assert err["msg"] == "", err["msg"]
+    for a, b in zip(ref, got["r"]):
+        assert torch.equal(a.view(torch.uint8) if a.dtype != torch.bfloat16 else a,
+                           b.view(torch.uint8) if b.dtype != torch.bfloat16 else b)

@@ -894,19 +894,24 @@ __global__ void __launch_bounds__(32 * (RD_CONS + 1), 1)
 
 // Launches the TMA row-product kernel when B fits in shared memory and the code rows allow 16-byte
 // stores; returns -1 (nothing launched) otherwise, so the caller can fall back to k_rowdot.
+// rowdot_tma's answer when the request does not fit the TMA kernel (B too large, K or a stride or a pointer
+// not aligned for TMA): the caller runs k_rowdot.  Never an MXM status; a real failure returns its status.
+constexpr int RD_NOT_APPLICABLE = 1;
+
 int rowdot_tma(const void* A, int64_t lda, const void* B, int64_t T, int64_t K, int n, float post, int round_once,
                void* out, int64_t ldo, uint8_t* q, int64_t ldq, uint8_t* s, int64_t scols, int kb_off,
                cudaStream_t st) {
   const int64_t b_bytes = (int64_t)n * K * 2;
-  if (b_bytes > (int64_t)RD_B_MAX || K % RD_KB != 0 || T >= (1ll << 31)) return -1;
-  if (q && (ldq % 16 != 0 || !mx_aligned(q, 16) || !mx_aligned(s, 2) || kb_off % 2 != 0)) return -1;
+  if (b_bytes > (int64_t)RD_B_MAX || K % RD_KB != 0 || T >= (1ll << 31)) return RD_NOT_APPLICABLE;
+  if (!mx_aligned(A, 16) || lda % 8 != 0 || !mx_aligned(B, 16)) return RD_NOT_APPLICABLE;
+  if (q && (ldq % 16 != 0 || !mx_aligned(q, 16) || !mx_aligned(s, 2) || kb_off % 2 != 0)) return RD_NOT_APPLICABLE;
   CUtensorMap ta, tb;
-  if (mx_make_tmap_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, A, (uint64_t)K, (uint64_t)T, (uint64_t)(lda * 2), RD_KB,
-                      RD_ROWS, CU_TENSOR_MAP_SWIZZLE_128B))
-    return -1;
-  if (mx_make_tmap_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, B, (uint64_t)K, (uint64_t)n, (uint64_t)(K * 2), RD_KB,
-                      (uint32_t)n, CU_TENSOR_MAP_SWIZZLE_128B))
-    return -1;
+  if (int e = mx_make_tmap_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, A, (uint64_t)K, (uint64_t)T, (uint64_t)(lda * 2),
+                              RD_KB, RD_ROWS, CU_TENSOR_MAP_SWIZZLE_128B))
+    return e;
+  if (int e = mx_make_tmap_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, B, (uint64_t)K, (uint64_t)n, (uint64_t)(K * 2),
+                              RD_KB, (uint32_t)n, CU_TENSOR_MAP_SWIZZLE_128B))
+    return e;
   const int stages = rd_stages(b_bytes);
   const size_t smem = rd_smem(b_bytes, stages);
   const int nrb = (int)((T + RD_ROWS - 1) / RD_ROWS);
@@ -1459,7 +1464,7 @@ extern "C" int mxm_rowdot(const void* A, int64_t lda, const void* B, int64_t T, 
   MX_CHECK_ARG(mx_aligned(A, 16) && mx_aligned(B, 16) && mx_aligned(out, 4), "mxm_rowdot: alignment");
   cudaStream_t st = (cudaStream_t)stream;
   const int e = rowdot_tma(A, lda, B, T, K, n, post, 0, out, ldo, nullptr, 0, nullptr, K, 0, st);
-  if (e >= 0) return e;
+  if (e != RD_NOT_APPLICABLE) return e;
   const unsigned grid = (unsigned)((T + 15) / 16);
   auto go = [&](auto kern) {
     kern<<<grid, 128, 0, st>>>((const bf16*)A, lda, (const bf16*)B, (int)T, (int)K, post, 0, (bf16*)out, ldo, nullptr,
@@ -1517,8 +1522,8 @@ extern "C" int mxm_lora_bwd(const void* dy, int64_t ldy, int64_t T, int64_t N, c
   uint8_t* qc = q ? (uint8_t*)q + col_tile_off * 128 : nullptr;
   const int et = rowdot_tma(dy, ldy, Bt, T, N, r, scale, 1, dxa_out, ld_dxa, qc, ldq, (uint8_t*)s, s_cols,
                             (int)(col_tile_off * 4), st);
-  if (et > 0) return et;
-  if (et < 0) {
+  if (et != RD_NOT_APPLICABLE && et != MXM_OK) return et;
+  if (et == RD_NOT_APPLICABLE) {
     auto go = [&](auto kern) {
       kern<<<grid, 128, 0, st>>>((const bf16*)dy, ldy, (const bf16*)Bt, (int)T, (int)N, scale, 1, (bf16*)dxa_out,
                                  ld_dxa, qc, ldq, (uint8_t*)s, s_cols, (int)(col_tile_off * 4));
@@ -1596,7 +1601,7 @@ extern "C" int mxm_rowdot_quant(const void* A, int64_t lda, const void* B, int64
                "mxm_rowdot_quant: alignment");
   cudaStream_t st = (cudaStream_t)stream;
   const int e = rowdot_tma(A, lda, B, T, K, n, post, 0, out, ldo, (uint8_t*)q, ldq, (uint8_t*)s, K, 0, st);
-  if (e >= 0) return e;
+  if (e != RD_NOT_APPLICABLE) return e;
   const unsigned grid = (unsigned)((T + 127) / 128 * 8);  // 16-row CTAs over the padded rows
   auto go = [&](auto kern) {
     kern<<<grid, 128, 0, st>>>((const bf16*)A, lda, (const bf16*)B, (int)T, (int)K, post, 0, (bf16*)out, ldo,

@@ -356,9 +356,10 @@ int launch(const void* x, int64_t R, int64_t K, int64_t ldx, void* q, int64_t ld
            void* stream, int64_t s_tiles = -1, int64_t tile_off = 0) {
   if (s_tiles < 0) s_tiles = K >> 7;
   // TMA path: 16-byte aligned rows and buffers (tensor maps), the codes' row stride a multiple of 16
-  const bool tma_ok = mx_aligned(x, 16) && (!ROWS || (mx_aligned(q, 16) && ldq % 16 == 0 && mx_aligned(s, 16))) &&
+  const bool tma_ok = mx_aligned(x, 16) && ldx % 8 == 0 &&
+                      (!ROWS || (mx_aligned(q, 16) && ldq % 16 == 0 && mx_aligned(s, 16))) &&
                       (!COLS || (mx_aligned(qt, 16) && mx_aligned(st, 16) && R % 16 == 0));
-  if (tma_ok) {
+  if (tma_ok) {   // from here on a failure is an error, not a reason to fall back
     CUtensorMap tx, tq, tqt;
     int e = mx_make_tmap_2d(&tx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, x, (uint64_t)K, (uint64_t)R,
                             (uint64_t)(ldx * 2), 64, 128, CU_TENSOR_MAP_SWIZZLE_128B);
@@ -368,7 +369,8 @@ int launch(const void* x, int64_t R, int64_t K, int64_t ldx, void* q, int64_t ld
     if (!e && COLS)
       e = mx_make_tmap_2d(&tqt, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, qt, (uint64_t)R, (uint64_t)K, (uint64_t)R, 128, 128,
                           CU_TENSOR_MAP_SWIZZLE_128B);
-    if (!e) {
+    if (e) return e;
+    {
       if (!ROWS) tq = tqt;
       if (!COLS) tqt = tq;
       const int nrt = (int)((R + 127) / 128), nct = (int)(K / 128);

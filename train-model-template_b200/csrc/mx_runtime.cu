@@ -107,6 +107,17 @@ int mx_make_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, uint32_t elem_b
                       (unsigned long long)row_stride_bytes);
     return MXM_ERR_ARG;
   }
+  // The encoder is a driver call and needs a current context; the runtime binds the primary context to
+  // a thread only at that thread's first runtime call that needs it, and a fresh thread (autograd's
+  // device thread runs the backward) may reach this first.  cudaSetDevice binds it (no synchronization).
+  static thread_local bool bound = false;
+  if (!bound) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e == cudaSuccess) e = cudaSetDevice(dev);
+    if (e != cudaSuccess) return mx_cuda_status(e, "bind the device context for cuTensorMapEncodeTiled");
+    bound = true;
+  }
   cuuint64_t dims[2] = {inner, outer};
   cuuint64_t strides[1] = {row_stride_bytes};
   cuuint32_t box[2] = {box_inner, box_outer};
