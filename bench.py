@@ -374,13 +374,15 @@ def run_ours(a):
         "warmup": max(a.warmup, 3), "ms_per_step": ms, "higher_is_better": True,
         "scaling": "weak" if a.workload == "layer" else "strong", "vs_baseline": None, "dtype": "mxfp8-e4m3/bf16",
         "data": "synthetic (seeded N(0,1) activations, N(0,0.02) frozen weights, N(0,0.01) LoRA A/B)",
-        "config": {"workload": ("configs[1]: one Qwen3.5-2B MLP layer, 16384 tokens per rank" if a.workload == "layer"
+        "config": {"workload": ((f"configs[1]: one Qwen3.5-2B MLP layer, {T} tokens per rank" if T == LAYER_TOKENS
+                                 else f"one Qwen3.5-2B MLP layer, {T} tokens per rank (configs[1] holds {LAYER_TOKENS})")
+                                if a.workload == "layer"
                                 else "configs[3]: 24-layer Qwen3.5-2B MLP stack, 142336-token step, token-sharded"
                                 + (", every layer checkpointed (recompute with need_out=False)"
                                    if a.workload == "ckpt" else "")),
                    "hidden": H, "intermediate": N, "lora_rank": R, "lora_alpha": ALPHA, "layers": L,
                    "tokens_per_rank": T, "parallelism": f"dp{world} (token shards, NCCL all-reduce of LoRA grads)",
-                   "l2": "per-step working set > L2 (gu alone 384 MiB per layer); no flush"},
+                   "l2": f"per-step working set > L2 (gu alone {T * 4 * N // 2**20} MiB per layer); no flush"},
         "e2e": None if a.no_e2e else {"value": tok / (e2e_ms * 1e-3), "unit": UNIT,
                 "h2d_bytes_per_step": x_host.numel() * 2 + dy_host.numel() * 2,
                 "d2h_bytes_per_step": flat_host.numel() * 4},
