@@ -106,7 +106,11 @@ int mxm_mlp_fwd_epilogue(const void* gu, const void* xs, const void* bg, const v
  * (rows: gate then up) with their blocked scales; and from the same tiles qh / sh = MXFP8(h) [M, N],
  * h = bf16(silu(g) u), g = bf16(gu_gate + s_g xs_g bg^T), u likewise, and xsd [M, r] bf16 = bf16(h ad^T).
  * xs [M, 2r] bf16 contiguous, bg / bu [N, r], ad [r, N] bf16 contiguous; r = 16; N % 128 == 0.
- * xsd_part: fp32 scratch of slots * M * r elements (mxm_gemm_glu_partition). */
+ * xsd_part: fp32 scratch of slots * M * r elements (mxm_gemm_glu_partition: per = tiles per work unit,
+ * grid = CTAs launched, slots = units that can touch one row block).  For M >= 256 the work units are CTA
+ * pairs (clusters of two on the tensor cores' cta_group::2 path, 256-row tiles, grid = 2 x pairs), below
+ * that single CTAs over 128-row tiles; the choice depends only on M and the device, so the partition and
+ * the launch agree. */
 int mxm_gemm_glu_partition(int64_t M, int64_t N, int* per, int* grid, int* slots);
 int mxm_gemm_glu(const void* qa, int64_t lda, const void* sa, const void* qb, int64_t ldb, const void* sb, int64_t M,
                  int64_t N, int64_t K, void* gu, const void* xs, const void* bg, const void* bu, const void* ad, int r,
