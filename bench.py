@@ -399,8 +399,8 @@ def run_ours(a):
 
 
 # ----------------------------------------------------------------------------------------------- CPU leg
-def _cpu_sample(workload, tokens):
-    """Time the oracle port (numpy, the reference algorithm) on `tokens` tokens of one 2B layer."""
+def _cpu_setup(tokens):
+    """Seeded 2B-layer operands for the oracle port: frozen MX weights (quantized once), LoRA, x, dy."""
     import numpy as np
     from oracle import mx_oracle as O
     rng = np.random.default_rng(0)
@@ -412,11 +412,25 @@ def _cpu_sample(workload, tokens):
             for s in ((R, H), (N, R), (R, H), (N, R), (R, N), (H, R))]
     x = bf(rng.standard_normal((tokens, H)))
     dy = bf(rng.standard_normal((tokens, H)))
+    return W, lora, x, dy
+
+
+def _cpu_step(W, lora, x, dy):
+    """One fwd+bwd of the oracle port (the reference algorithm in numpy); returns its wall time in s."""
+    from oracle import mx_oracle as O
+    t0 = time.perf_counter()
+    y, ctx = O.mlp_forward(x, W, *lora, SCALE, SCALE, SCALE)
+    O.mlp_backward(dy, ctx)
+    return time.perf_counter() - t0
+
+
+def _cpu_sample(workload, tokens):
+    """Time the oracle port on `tokens` tokens of one 2B layer (up to 3 repetitions or ~10 s)."""
+    W, lora, x, dy = _cpu_setup(tokens)
     t0 = time.perf_counter()
     reps = 0
     while True:
-        y, ctx = O.mlp_forward(x, W, *lora, SCALE, SCALE, SCALE)
-        O.mlp_backward(dy, ctx)
+        _cpu_step(W, lora, x, dy)
         reps += 1
         if time.perf_counter() - t0 > 10.0 or reps >= 3:
             break
@@ -446,15 +460,17 @@ def run_reference(a):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if rank != 0:
         return
-    tokens = 1024
-    _cpu_sample(a.workload, 256)   # warm-up (numpy / BLAS thread start)
-    vals = []
-    for _ in range(max(1, min(a.steps, 3))):
-        v, dt = _cpu_sample(a.workload, tokens)
-        vals.append(v)
+    # each step is a bounded token sample (about 3.7 s per 1,024 tokens on 8 host threads); the sample
+    # shrinks for long runs so that --steps K --warmup W stays within about two minutes
+    steps, warm = max(1, a.steps), max(a.warmup, 3)
+    tokens = int(min(1024, max(128, 120.0 / (3.7 * steps) * 1024)) // 128 * 128)
+    W, lora, x, dy = _cpu_setup(tokens)
+    for _ in range(warm):   # warm-up steps on a 128-token slice (numpy / BLAS threads, page-in)
+        _cpu_step(W, lora, x[:128], dy[:128])
+    vals = [tokens / _cpu_step(W, lora, x, dy) for _ in range(steps)]
     v = statistics.median(vals)
     line = {
-        "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": world, "steps": len(vals), "warmup": 1,
+        "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": world, "steps": steps, "warmup": warm,
         "ms_per_step": tokens / v * 1e3, "higher_is_better": True, "scaling": "weak" if a.workload == "layer" else "strong",
         "vs_baseline": None, "dtype": "mxfp8-e4m3/fp32 (CPU)", "data": "synthetic",
         "config": {"workload": "one Qwen3.5-2B MLP layer (hidden 2048, intermediate 6144, r 16), bounded token sample",
