@@ -616,15 +616,9 @@ MX_DEV void glu_body(const CUtensorMap* tmA, const CUtensorMap* tmB, const CUten
                      : "memory");
       }
       epi_sync();
-      // gu leaves from the staged tile: four [128 x 64] boxes (gate, up) x (sub-tile), rows >= M clipped
-      if (et == 0) {
-#pragma unroll
-        for (int hh = 0; hh < 2; ++hh)
-#pragma unroll
-          for (int c2 = 0; c2 < 2; ++c2)
-            tma_store_2d(tmG, stg + (hh * 2 + c2) * (128 * 128), hh * N + tn * 128 + c2 * 64, (int)rowb);
-        bulk_commit();
-      }
+      // gu leaves from the staged tile as four [128 x 64] TMA stores (gate, up) x (sub-tile), rows >= M
+      // clipped, one per SwiGLU sub-step below: spread out, they hold the TMA unit back from the next
+      // tile's operand loads less than one 64 KB burst does
       // 3. the forward epilogue on rows 16e .. 16e+15, two 64-column sub-tiles
 #pragma unroll 1
       for (int sbk = 0; sbk < 2; ++sbk) {
@@ -632,6 +626,11 @@ MX_DEV void glu_body(const CUtensorMap* tmA, const CUtensorMap* tmB, const CUten
         const uint32_t tbg = s_bg + sbk * (64 * R * 2), tbu = s_bu + sbk * (64 * R * 2), tad = s_ad + sbk * (R * 128);
 #pragma unroll
         for (int b = 0; b < 2; ++b) {
+          if (et == 0) {   // box (gate / up) x (sub-tile) number 2 sbk + b
+            const int bx = 2 * sbk + b, hh = bx >> 1, c2 = bx & 1;
+            tma_store_2d(tmG, stg + (hh * 2 + c2) * (128 * 128), hh * N + tn * 128 + c2 * 64, (int)rowb);
+            bulk_commit();
+          }
           uint32_t hp[4][2];
 #pragma unroll
           for (int pp = 0; pp < 2; ++pp) {
