@@ -299,11 +299,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 //     copies complete on the leader's full barriers; the leader's commits arrive on both CTAs' barriers;
 //     each epilogue warp hands the accumulator back by one remote arrival on the leader's tmem_empty.
 // The 8 epilogue warps drain the accumulator (warp q|h: lanes 32q.., half h = gate / up), hand it back
-// and stage the bf16 tile in shared memory (128-byte swizzle), from which four TMA stores write gu (the
-// backward reads it) in full 128-byte rows; after one named barrier each warp runs the forward epilogue
-// on 16 rows x 128 pairs of the staged tile -- the LoRA-B terms with mma.sync, SwiGLU, the MXFP8 codes
-// of h, and the per-row xS_down = h A_down^T accumulated in registers -- while the MMAs of the next tile
-// proceed.  A CTA (pair) works through a contiguous range of tiles (column tiles fastest), so xS_down
+// and stage the bf16 tile in shared memory (128-byte swizzle); after one named barrier each warp runs
+// the forward epilogue on 16 rows x 128 pairs of the staged tile -- the LoRA-B terms with mma.sync,
+// SwiGLU, the MXFP8 codes of h, and the per-row xS_down = h A_down^T accumulated in registers -- while
+// the MMAs of the next tile proceed, and four TMA stores, one per SwiGLU sub-step, write gu (the
+// backward reads it) from the staged tile in full 128-byte rows.  A CTA (pair) works through a contiguous range of tiles (column tiles fastest), so xS_down
 // accumulates over the columns of a row block and is written as one fp32 partial per (row block, CTA or
 // pair); a fixed-order reduction sums them.  Rank 16 only (the rank-32 slices do not fit shared memory).
 constexpr int GLU_STAGING = 2 * 2 * 128 * 128;   // g | u halves, two [128 x 64] bf16 sub-tiles each
