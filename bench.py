@@ -39,6 +39,7 @@ for _p in (ROOT, PKG):
 H, N, R, ALPHA = 2048, 6144, 16, 32
 SCALE = ALPHA / R
 LAYER_TOKENS = 16384
+GEMM_TRAFFIC_BYTES = 1352104960   # ncu dram__bytes_read + write, 4 GEMM launches, 16,384-token layer step
 STACK_TOKENS, STACK_LAYERS = 142336, 24
 METRIC = "MXFP8 fused-MLP fwd+bwd tokens/s (2B shape)"
 UNIT = "tokens/s"
@@ -388,7 +389,11 @@ def run_ours(a):
                 "d2h_bytes_per_step": flat_host.numel() * 4},
         "gpu_launches": int(launches),
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                     "frac": (achieved / peak) if achieved else None, "traffic": None,
+                     "frac": (achieved / peak) if achieved else None,
+                     # DRAM bytes (read + write) of the step's four GEMM launches from one ncu capture of
+                     # this workload (profiles/gemm_traffic_2B_T16384.md); other token counts: not captured
+                     "traffic": GEMM_TRAFFIC_BYTES if (a.workload == "layer" and T == LAYER_TOKENS) else None,
+                     "traffic_unit": "bytes per step (4 GEMM launches)",
                      "kernel": "k_mx_gemm (tcgen05 MXFP8 GEMMs, 4 launches per layer per step)",
                      "flops_per_step": g_fl / a.steps, "peak_source": peak_note},
         "mlp_tflops": FLOP_PER_TOKEN * tok / (ms * 1e-3) / 1e12,
