@@ -1,22 +1,28 @@
 """Benchmark of the MXFP8 fused SwiGLU-LoRA MLP (forward + backward) on B200.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload layer|stack]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload stack|layer|ckpt|quant|ragged]
 
-One step = the fused MLP forward + autograd backward (dX, dA, dB of the three LoRA adapters) over one
-batch of tokens, plus, with N > 1 ranks, the NCCL all-reduce of the LoRA gradients (the only data
-exchange of token-sharded data parallelism).
+One step = the fused MLP forward + autograd backward (dX, dA, dB of the three LoRA adapters) of every
+layer over one batch of tokens, plus, with N > 1 ranks, the NCCL all-reduce of the LoRA gradients (the
+only data exchange of token-sharded data parallelism), issued per layer as soon as that layer's
+gradients exist and overlapped with the next layer's backward.
 
 Workloads:
-  layer  (default) one Qwen3.5-2B MLP layer (hidden 2048, intermediate 6144, LoRA r=16, alpha=32) over
-         16,384 tokens per rank -- configs[1] at N=1; every rank adds its own 16,384-token shard
-         ("scaling": "weak").
-  stack  the 24-layer 2B MLP stack over one 142,336-token step (16 packed conversations of 8,896
-         tokens), token-sharded over the ranks -- configs[3] ("scaling": "strong").
+  stack  (default) the 24-layer Qwen3.5-2B MLP stack (hidden 2048, intermediate 6144, LoRA r=16,
+         alpha=32) over one 142,336-token step (16 packed conversations of 8,896 tokens), token-sharded
+         over the ranks -- configs[3] ("scaling": "strong").
+  layer  one 2B MLP layer over 16,384 tokens per rank -- configs[1] at N=1 ("scaling": "weak").
+  ckpt   the stack with every layer under non-reentrant activation checkpointing, the recompute
+         calling the MLP with need_out=False (the reference's shared-prefix step).
+  quant  the configs[2] quantizer sweep (HBM GB/s); ragged: configs[4] small-M latency.
 
 The metric is MLP layer-tokens per second over the whole job (tokens x layers / step time, max over
-ranks), i.e. tokens/s for the single-layer workload.  Inputs are synthetic (seeded N(0,1)
-activations, N(0,0.02) frozen weights, N(0,0.01) LoRA A/B).  The per-step working set (gu alone is
-T x 2N bf16 = 384 MiB per layer) is larger than the 126 MB L2, so no explicit L2 flush is needed.
+ranks).  Inputs are synthetic (seeded N(0,1) activations, N(0,0.02) frozen weights, N(0,0.01) LoRA A/B).
+The per-step working set (gu alone is T x 2N bf16 = 384 MiB per 16K tokens per layer) is larger than
+the 126 MB L2, so no explicit L2 flush is needed.  At N=1 the default line also carries the configs[2]
+quantizer sweep, the configs[4] ragged latencies and the checkpointed step (f4); at N>1 the ragged
+latencies and the checkpointed step.
 
 `--impl reference` times the reference algorithm on the host CPU (the oracle port, all host threads)
 on a bounded token sample of the same workload, and prints the same JSON line with "impl": "reference".
@@ -39,12 +45,14 @@ for _p in (ROOT, PKG):
 H, N, R, ALPHA = 2048, 6144, 16, 32
 SCALE = ALPHA / R
 LAYER_TOKENS = 16384
-GEMM_TRAFFIC_BYTES = 1352104960   # ncu dram__bytes_read + write, 4 GEMM launches, 16,384-token layer step
 STACK_TOKENS, STACK_LAYERS = 142336, 24
 METRIC = "MXFP8 fused-MLP fwd+bwd tokens/s (2B shape)"
 UNIT = "tokens/s"
 FLOP_PER_TOKEN = 12 * H * N             # MXFP8 GEMM flops per token per layer, fwd + bwd
 LORA_FLOP_PER_TOKEN = 2 * R * (9 * H + 12 * N)
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of the four GEMM launches of one layer step,
+# by tokens per layer: one-pass ncu captures of this build's kernels (kept in the repository's profiles).
+GEMM_TRAFFIC_BYTES = {16384: 1352104960}
 
 
 def _args():
@@ -53,15 +61,24 @@ def _args():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    ap.add_argument("--workload", choices=("layer", "stack", "ckpt", "quant", "ragged"), default="layer",
-                    help="layer: configs[1] (default); stack: configs[3]; ckpt: configs[3] with every layer "
+    ap.add_argument("--workload", choices=("stack", "layer", "ckpt", "quant", "ragged"), default="stack",
+                    help="stack: configs[3] (default); layer: configs[1]; ckpt: configs[3] with every layer "
                          "checkpointed (recompute with need_out=False, as the reference's shared-prefix step); "
                          "quant: the configs[2] quantizer sweep (HBM GB/s); ragged: configs[4] small-M latency")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end (host buffers) measurement")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="skip the configs[2] / configs[4] / checkpointed-step measurements of the default line")
     ap.add_argument("--tokens", type=int, default=0,
                     help="tokens per rank for the layer workload (default 16384; smaller cases for profiling)")
     return ap.parse_args()
+
+
+def _host_cores():
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
 
 
 # ----------------------------------------------------------------------------------------------- clocks
@@ -157,6 +174,29 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(rows), "source": "nvidia-smi"}
 
 
+def _peaks():
+    try:
+        return json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+    except Exception:
+        return {}
+
+
+def tensor_peak(clocks):
+    """Dense MXFP8 peak (TFLOP/s) for the roofline: twice the measured bf16 cuBLAS rate (dense MXFP8 runs at
+    twice bf16 on B200).  The burst figure when the timed region held the SM clock at its maximum (no power
+    cap engaged), the sustained figure (measured under the 1000 W cap) when the clock sagged."""
+    pk = _peaks()
+    burst, sus = pk.get("bf16_tflops"), pk.get("bf16_tflops_sustained")
+    src = "measured (MEASURED_PEAKS.json)"
+    if not burst:
+        burst, sus, src = 1590.0, 1400.0, "fallback"
+    sus = sus or burst
+    held = bool(clocks and clocks.get("sm_mhz") and clocks.get("sm_max_mhz")
+                and clocks["sm_mhz"] >= 0.97 * clocks["sm_max_mhz"])
+    kind = "burst" if held else "sustained"
+    return 2.0 * (burst if held else sus), 2.0 * burst, 2.0 * sus, f"2 x {kind} bf16 cuBLAS, {src}"
+
+
 # ----------------------------------------------------------------------------------------------- our arm
 def _make_layer(torch, fused_mlp, dev, seed):
     g = torch.Generator(device="cpu").manual_seed(seed)
@@ -165,6 +205,30 @@ def _make_layer(torch, fused_mlp, dev, seed):
     shapes = ((R, H), (N, R), (R, H), (N, R), (R, N), (H, R))
     params = [(torch.randn(*s, generator=g) * 0.01).to(dev).requires_grad_(True) for s in shapes]
     return layer, params
+
+
+def _config(workload, world, T, L):
+    if workload == "layer":
+        wl = (f"configs[1]: one Qwen3.5-2B MLP layer, {T} tokens per rank" if T == LAYER_TOKENS
+              else f"one Qwen3.5-2B MLP layer, {T} tokens per rank (configs[1] holds {LAYER_TOKENS})")
+    else:
+        wl = ("configs[3]: 24-layer Qwen3.5-2B MLP stack, 142336-token step (16 x 8896-token conversations), "
+              "token-sharded" + (", every layer checkpointed (recompute with need_out=False)"
+                                 if workload == "ckpt" else ""))
+    return {"workload": wl, "hidden": H, "intermediate": N, "lora_rank": R, "lora_alpha": ALPHA, "layers": L,
+            "tokens_per_rank": T, "global_tokens": T * world if workload == "layer" else STACK_TOKENS,
+            "value_counts": "layer-tokens (tokens x layers) per second",
+            "parallelism": f"dp{world} (token shards; per-layer NCCL all-reduce of LoRA grads overlapped with "
+                           f"the backward)",
+            "l2": f"per-step working set > L2 (gu alone {T * 4 * N // 2**20} MiB per layer); no flush"}
+
+
+def _workload_shape(a, world, rank):
+    import mx_dp
+    if a.workload == "layer":
+        return (a.tokens or LAYER_TOKENS), 1, (a.tokens or LAYER_TOKENS) * world
+    r0, r1 = mx_dp.shard_rows(STACK_TOKENS, world, rank)
+    return r1 - r0, STACK_LAYERS, STACK_TOKENS
 
 
 def run_ours(a):
@@ -187,16 +251,17 @@ def run_ours(a):
     import fused_mlp
     import mx_dp
     import mxfp8
-
-    if a.workload == "layer":
-        T, L = (a.tokens or LAYER_TOKENS), 1
-        total_tokens = T * world
-    else:
-        r0, r1 = mx_dp.shard_rows(STACK_TOKENS, world, rank)
-        T, L = r1 - r0, STACK_LAYERS
-        total_tokens = STACK_TOKENS
-    layers = [_make_layer(torch, fused_mlp, dev, seed=1000 + i) for i in range(L)]
     import torch.utils.checkpoint as tuc
+
+    T, L, total_tokens = _workload_shape(a, world, rank)
+    layers = [_make_layer(torch, fused_mlp, dev, seed=1000 + i) for i in range(L)]
+    # gradient storage: A_gate next to A_up in every layer (the backward writes [dA_gate; dA_up] as one block)
+    grads = mx_dp.LayerGrads([[ps[0], ps[2], ps[1], ps[3], ps[4], ps[5]] for _, ps in layers], device=dev)
+    gx = torch.Generator(device="cpu").manual_seed(7 + rank)
+    x_host = torch.randn(T, H, generator=gx).to(torch.bfloat16).pin_memory()
+    dy_host = torch.randn(T, H, generator=gx).to(torch.bfloat16).pin_memory()
+    x = x_host.to(dev)
+    dy = dy_host.to(dev)
 
     def ckpt_layer(layer, ps):
         # the reference's shared-prefix step (scripts/shared_prefix.py:200-203, 246-255): the forward inside
@@ -205,64 +270,75 @@ def run_ours(a):
             return fused_mlp.mlp_apply(layer, h, *ps, scaling=(SCALE, SCALE, SCALE),
                                        need_out=torch._C._current_graph_task_id() == -1)
         return fn
-    params = [p for _, ps in layers for p in ps]
-    gx = torch.Generator(device="cpu").manual_seed(7 + rank)
-    x_host = torch.randn(T, H, generator=gx).to(torch.bfloat16).pin_memory()
-    dy_host = torch.randn(T, H, generator=gx).to(torch.bfloat16).pin_memory()
-    x = x_host.to(dev)
-    dy = dy_host.to(dev)
-    bucket = mx_dp.GradBucket(params, device=dev)    # the LoRA gradients: the only cross-rank exchange
-    flat_host = torch.empty(bucket.flat.shape, dtype=torch.float32).pin_memory()
 
-    def step(xin, dyin):
+    def forward_backward(xin, dyin, ckpt, before_backward=None):
         fused_linear.new_step()
-        h = xin.requires_grad_(False)
-        h = h.detach().requires_grad_(True)
+        h = xin.detach().requires_grad_(True)
         y = h
         for layer, ps in layers:
-            if a.workload == "ckpt":
+            if ckpt:
                 y = tuc.checkpoint(ckpt_layer(layer, ps), y, use_reentrant=False)
             else:
                 y = fused_mlp.mlp_apply(layer, y, *ps, scaling=(SCALE, SCALE, SCALE))
+        if before_backward is not None:
+            before_backward()
+        grads.begin()
         y.backward(dyin)
-        if world > 1:   # bucketed all-reduce of every LoRA gradient (NCCL over NVLink)
-            bucket.allreduce()
-        for p in params:
-            p.grad = None
-        return h
+        grads.finish()      # the compute stream now waits for every layer's all-reduce
 
-    # GEMM launches timed with CUDA events on the launching stream (the roofline's dominant kernel)
-    gemm_ms, gemm_flops, recording = [], [], [False]
-    orig_mm, orig_lora = mxfp8.mx_mm, fused_mlp.mx_mm_lora
+    ckpt_main = a.workload == "ckpt"
 
-    def timed(fn):
-        def wrap(a_, b_, *rest, **kw):
+    def step(xin, dyin):
+        forward_backward(xin, dyin, ckpt_main)
+        grads.zero()
+
+    # the four MXFP8 GEMM launches of each layer step, timed with CUDA events on the launching stream
+    gemm_ev, recording = [], [False]
+    orig = {"mm": mxfp8.mx_mm, "lora": fused_mlp.mx_mm_lora, "glu": fused_mlp.gemm_glu}
+
+    def timed(kind, fn):
+        def wrap(*args, **kw):
             if not recording[0]:
-                return fn(a_, b_, *rest, **kw)
+                return fn(*args, **kw)
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record()
-            out = fn(a_, b_, *rest, **kw)
+            out = fn(*args, **kw)
             e1.record()
-            gemm_ms.append((e0, e1))
-            gemm_flops.append(2 * a_.shape[0] * a_.shape[1] * b_.shape[1])
+            M, K = args[0].shape
+            if kind == "glu":           # gemm_glu(q [T, H], scales, W_gu [2N, H], ...)
+                name, n_out = "gate_up", args[2].shape[0]
+            elif kind == "mm":          # mx_mm(a [M, K], b [K, N'] view, ...): dh = dy W_down
+                name, n_out = "dh", args[1].shape[1]
+            else:                       # mx_mm_lora(a [M, K], b [K, N'], ...): down (K = N) or dx (K = 2N)
+                name, n_out = ("down" if K == N else "dx"), args[1].shape[1]
+            gemm_ev.append((name, e0, e1, 2.0 * M * K * n_out))
             return out
         return wrap
 
-    mxfp8.mx_mm = timed(orig_mm)
-    fused_mlp.mx_mm_lora = timed(orig_lora)
+    mxfp8.mx_mm = timed("mm", orig["mm"])
+    fused_mlp.mx_mm_lora = timed("lora", orig["lora"])
+    fused_mlp.gemm_glu = timed("glu", orig["glu"])
+
+    def barrier():
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return t.item()
 
     for _ in range(max(a.warmup, 3)):
         step(x, dy)
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
+    barrier()
     clk = ClockSampler(local)
     clk.start()
     launches0 = _mxlib.launch_count()
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
+    barrier()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     recording[0] = True
     ev0.record()
@@ -271,30 +347,31 @@ def run_ours(a):
     ev1.record()
     torch.cuda.synchronize()
     recording[0] = False
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
+    barrier()
     clocks = clk.stop()
     launches = _mxlib.launch_count() - launches0
-    ms = ev0.elapsed_time(ev1) / a.steps
-    g_ms = sum(e0.elapsed_time(e1) for e0, e1 in gemm_ms)
-    g_fl = float(sum(gemm_flops))
-    gemm_ms.clear()
-    if world > 1:
-        t = torch.tensor([ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = t.item()
+    ms = max_over_ranks(ev0.elapsed_time(ev1) / a.steps)
+    per_kind = {}
+    for name, e0, e1, fl in gemm_ev:
+        d = per_kind.setdefault(name, [0.0, 0.0, 0])
+        d[0] += e0.elapsed_time(e1)
+        d[1] += fl
+        d[2] += 1
+    gemm_ev.clear()
+    assert _mxlib.device_error() == 0, "a kernel recorded a device-side error"
 
     # end to end through the public API: pinned host inputs -> device, step, LoRA grads -> host.  Every
     # step's x and dy are copied from pinned host memory inside the timed region; the copies of step i+1
     # run on a side stream into the second of two device buffer sets while step i computes (the usual
-    # input pipelining of a training loop), so the step time is max(copy, compute), not their sum.
-    recording[0] = False
+    # input pipelining of a training loop), and the gradients' copy to the host runs on the same side
+    # stream, overlapped with the next step's forward.
     comp = torch.cuda.current_stream()
     copy_s = torch.cuda.Stream()
     xb, dyb = [x, torch.empty_like(x)], [dy, torch.empty_like(dy)]
     loaded = [torch.cuda.Event(), torch.cuda.Event()]
     freed = [torch.cuda.Event(), torch.cuda.Event()]
+    grads_host = torch.empty(grads.flat.shape, dtype=torch.float32).pin_memory()
+    grads_ready, grads_read = torch.cuda.Event(), torch.cuda.Event()
 
     def e2e_load(i):
         b = i % 2
@@ -307,24 +384,20 @@ def run_ours(a):
     def e2e_step(i):
         b = i % 2
         comp.wait_event(loaded[b])
-        fused_linear.new_step()
-        h = xb[b].detach().requires_grad_(True)
-        y = h
-        for layer, ps in layers:
-            if a.workload == "ckpt":
-                y = tuc.checkpoint(ckpt_layer(layer, ps), y, use_reentrant=False)
-            else:
-                y = fused_mlp.mlp_apply(layer, y, *ps, scaling=(SCALE, SCALE, SCALE))
-        y.backward(dyb[b])
+        # the previous step's gradients must have reached the host before this backward overwrites them
+        forward_backward(xb[b], dyb[b], ckpt_main, before_backward=lambda: comp.wait_event(grads_read))
         freed[b].record(comp)
-        bucket.allreduce()
-        flat_host.copy_(bucket.flat, non_blocking=True)
-        for p in params:
-            p.grad = None
+        grads_ready.record(comp)
+        with torch.cuda.stream(copy_s):
+            copy_s.wait_event(grads_ready)
+            grads_host.copy_(grads.flat, non_blocking=True)
+            grads_read.record(copy_s)
+        grads.zero()
 
     def e2e_run(n):
         for b in range(2):
             freed[b].record(comp)
+        grads_read.record(comp)
         e2e_load(0)
         for i in range(n):
             if i + 1 < n:
@@ -334,71 +407,92 @@ def run_ours(a):
     e2e_ms = float("nan")
     if not a.no_e2e:
         e2e_run(2)
-        torch.cuda.synchronize()
-        if world > 1:
-            dist.barrier()
+        barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
         e2e_run(a.steps)
+        copy_s.synchronize()          # the last step's gradients are on the host
         e1.record()
         torch.cuda.synchronize()
-        e2e_ms = e0.elapsed_time(e1) / a.steps
-    if world > 1 and not a.no_e2e:
-        t = torch.tensor([e2e_ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = t.item()
+        e2e_ms = max_over_ranks(e0.elapsed_time(e1) / a.steps)
+    del xb, dyb
+
+    extras = {}
+    if not a.no_extras and a.workload == "stack":
+        barrier()
+        # f4: the same stack with every layer checkpointed (recompute with need_out=False)
+        for _ in range(2):
+            forward_backward(x, dy, True)
+            grads.zero()
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ck_steps = max(2, min(a.steps, 5))
+        e0.record()
+        for _ in range(ck_steps):
+            forward_backward(x, dy, True)
+            grads.zero()
+        e1.record()
+        torch.cuda.synchronize()
+        ck_ms = max_over_ranks(e0.elapsed_time(e1) / ck_steps)
+        extras["ckpt_step"] = {"workload": "configs[3] with every layer checkpointed (recompute need_out=False)",
+                               "ms_per_step": ck_ms, "value": total_tokens * L / (ck_ms * 1e-3), "steps": ck_steps}
+    mxfp8.mx_mm, fused_mlp.mx_mm_lora, fused_mlp.gemm_glu = orig["mm"], orig["lora"], orig["glu"]
+    grads.close()
+    del layers, grads, x, dy
+    torch.cuda.empty_cache()
+    if not a.no_extras and a.workload == "stack":
+        barrier()
+        extras["configs4_ragged"] = ragged_latency(torch, dev, world, min(a.steps, 10), a.warmup, max_over_ranks)
+        if world == 1:
+            extras["configs2_quant"] = quant_sweep(torch, dev, min(a.steps, 5), a.warmup, summary=True)
 
     cpu = None
     if rank == 0 and world == 1 and not a.no_cpu_baseline:
-        cpu = cpu_baseline(a.workload)
+        cpu = cpu_baseline()
 
     if world > 1:
         dist.destroy_process_group()
     if rank != 0:
         return
-    import json as _j
-    peaks = {}
-    try:
-        peaks = _j.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
-    except Exception:
-        pass
-    if peaks.get("bf16_tflops_sustained"):
-        peak = 2.0 * float(peaks["bf16_tflops_sustained"])
-        peak_note = "2 x measured sustained bf16 cuBLAS (MEASURED_PEAKS.json): dense MXFP8 rate is twice bf16"
-    else:
-        peak = 2.0 * 1400.0
-        peak_note = "2 x fallback sustained bf16 1.4 PFLOP/s"
+    peak, peak_burst, peak_sus, peak_note = tensor_peak(clocks)
+    g_ms = sum(v[0] for v in per_kind.values())
+    g_fl = sum(v[1] for v in per_kind.values())
     achieved = g_fl / (g_ms * 1e-3) / 1e12 if g_ms > 0 else None
+    launches_gemm = {k: {"launches": v[2], "us_per_launch": 1e3 * v[0] / v[2],
+                         "tflops": v[1] / (v[0] * 1e-3) / 1e12, "frac": v[1] / (v[0] * 1e-3) / 1e12 / peak}
+                     for k, v in sorted(per_kind.items())}
     tok = total_tokens * L
+    step_tflops = FLOP_PER_TOKEN * tok / (ms * 1e-3) / 1e12
+    traffic = GEMM_TRAFFIC_BYTES.get(T)
     line = {
         "metric": METRIC, "value": tok / (ms * 1e-3), "unit": UNIT, "n_gpus": world, "steps": a.steps,
         "warmup": max(a.warmup, 3), "ms_per_step": ms, "higher_is_better": True,
         "scaling": "weak" if a.workload == "layer" else "strong", "vs_baseline": None, "dtype": "mxfp8-e4m3/bf16",
         "data": "synthetic (seeded N(0,1) activations, N(0,0.02) frozen weights, N(0,0.01) LoRA A/B)",
-        "config": {"workload": ((f"configs[1]: one Qwen3.5-2B MLP layer, {T} tokens per rank" if T == LAYER_TOKENS
-                                 else f"one Qwen3.5-2B MLP layer, {T} tokens per rank (configs[1] holds {LAYER_TOKENS})")
-                                if a.workload == "layer"
-                                else "configs[3]: 24-layer Qwen3.5-2B MLP stack, 142336-token step, token-sharded"
-                                + (", every layer checkpointed (recompute with need_out=False)"
-                                   if a.workload == "ckpt" else "")),
-                   "hidden": H, "intermediate": N, "lora_rank": R, "lora_alpha": ALPHA, "layers": L,
-                   "tokens_per_rank": T, "parallelism": f"dp{world} (token shards, NCCL all-reduce of LoRA grads)",
-                   "l2": f"per-step working set > L2 (gu alone {T * 4 * N // 2**20} MiB per layer); no flush"},
+        "config": _config(a.workload, world, T, L),
         "e2e": None if a.no_e2e else {"value": tok / (e2e_ms * 1e-3), "unit": UNIT,
-                "h2d_bytes_per_step": x_host.numel() * 2 + dy_host.numel() * 2,
-                "d2h_bytes_per_step": flat_host.numel() * 4},
+                                      "h2d_bytes_per_step": x_host.numel() * 2 + dy_host.numel() * 2,
+                                      "d2h_bytes_per_step": grads_host.numel() * 4},
         "gpu_launches": int(launches),
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                      "frac": (achieved / peak) if achieved else None,
-                     # DRAM bytes (read + write) of the step's four GEMM launches from one ncu capture of
-                     # this workload (profiles/gemm_traffic_2B_T16384.md); other token counts: not captured
-                     "traffic": GEMM_TRAFFIC_BYTES if (a.workload == "layer" and T == LAYER_TOKENS) else None,
-                     "traffic_unit": "bytes per step (4 GEMM launches)",
-                     "kernel": "k_mx_gemm (tcgen05 MXFP8 GEMMs, 4 launches per layer per step)",
-                     "flops_per_step": g_fl / a.steps, "peak_source": peak_note},
-        "mlp_tflops": FLOP_PER_TOKEN * tok / (ms * 1e-3) / 1e12,
+                     "kernel": "the four tcgen05 MXFP8 GEMM launches of each layer step (k_mx_gemm_glu2 gate|up "
+                               "with the fused forward epilogue, k_mx_gemm down / dh / dx)",
+                     "flops_per_step": g_fl / a.steps,
+                     "per_launch": launches_gemm,
+                     "step_frac": step_tflops / peak,
+                     "frac_vs_burst": (achieved / peak_burst) if achieved else None,
+                     "frac_vs_sustained": (achieved / peak_sus) if achieved else None,
+                     "step_frac_vs_burst": step_tflops / peak_burst,
+                     "traffic": traffic,
+                     "traffic_unit": "DRAM bytes per layer step (4 GEMM launches), one-pass ncu capture at "
+                                     f"{T} tokens per layer" if traffic else "not captured for this token count",
+                     "peak_source": peak_note},
+        "mlp_tflops": step_tflops,
+        "step_tokens_per_s": total_tokens / (ms * 1e-3),
         "clocks": clocks,
         "cpu_baseline": cpu,
+        **extras,
     }
     print(json.dumps(line), flush=True)
 
@@ -429,9 +523,26 @@ def _cpu_step(W, lora, x, dy):
     return time.perf_counter() - t0
 
 
-def _cpu_sample(workload, tokens):
-    """Time the oracle port on `tokens` tokens of one 2B layer (up to 3 repetitions or ~10 s)."""
+def _all_threads():
+    """Raise every BLAS / OpenMP pool to all host cores (torchrun exports OMP_NUM_THREADS=1); returns the
+    thread count the BLAS pool reports afterwards."""
+    n = _host_cores()
+    try:
+        from threadpoolctl import threadpool_info, threadpool_limits
+        threadpool_limits(limits=n)
+        got = [i.get("num_threads", 1) for i in threadpool_info() if i.get("user_api") == "blas"]
+        return max(got) if got else n
+    except Exception:
+        return n
+
+
+def cpu_baseline():
+    """The oracle port on a 1,024-token sample of one 2B layer (up to 3 repetitions or ~10 s), all host
+    threads; layer-tokens/s, extrapolated per token to the workload (the layer is token-wise)."""
+    cores = _all_threads()
+    tokens = 1024
     W, lora, x, dy = _cpu_setup(tokens)
+    _cpu_step(W, lora, x[:128], dy[:128])
     t0 = time.perf_counter()
     reps = 0
     while True:
@@ -440,24 +551,9 @@ def _cpu_sample(workload, tokens):
         if time.perf_counter() - t0 > 10.0 or reps >= 3:
             break
     dt = (time.perf_counter() - t0) / reps
-    return tokens / dt, dt
-
-
-def _threads():
-    try:
-        from threadpoolctl import threadpool_info
-        n = [i.get("num_threads", 1) for i in threadpool_info() if i.get("user_api") == "blas"]
-        return max(n) if n else os.cpu_count()
-    except Exception:
-        return os.cpu_count()
-
-
-def cpu_baseline(workload):
-    tokens = 1024
-    v, dt = _cpu_sample(workload, tokens)
-    return {"value": v, "unit": UNIT, "cores": _threads(), "kind": "port",
+    return {"value": tokens / dt, "unit": UNIT, "cores": cores, "kind": "port",
             "sample": f"{tokens} tokens of one 2B MLP layer, fwd+bwd, numpy oracle port of the reference algorithm "
-                      f"({dt:.2f} s per sample step; layer-tokens/s)"}
+                      f"({dt:.2f} s per sample step); layer-tokens/s extrapolated per token to the workload"}
 
 
 def run_reference(a):
@@ -465,7 +561,13 @@ def run_reference(a):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if rank != 0:
         return
-    # each step is a bounded token sample (about 3.7 s per 1,024 tokens on 8 host threads); the sample
+    # all host threads, whatever the launcher exported (torchrun sets OMP_NUM_THREADS=1): set before numpy
+    # loads its BLAS, and raised again through threadpoolctl afterwards
+    n = str(_host_cores())
+    for k in ("OMP_NUM_THREADS", "OPENBLAS_NUM_THREADS", "MKL_NUM_THREADS"):
+        os.environ[k] = n
+    cores = _all_threads()
+    # each step is a bounded token sample (about 2.6 s per 1,024 tokens on 16 host threads); the sample
     # shrinks for long runs so that --steps K --warmup W stays within about two minutes
     steps, warm = max(1, a.steps), max(a.warmup, 3)
     tokens = int(min(1024, max(128, 120.0 / (3.7 * steps) * 1024)) // 128 * 128)
@@ -474,15 +576,19 @@ def run_reference(a):
         _cpu_step(W, lora, x[:128], dy[:128])
     vals = [tokens / _cpu_step(W, lora, x, dy) for _ in range(steps)]
     v = statistics.median(vals)
+    T, L, _ = _workload_shape(a, world, 0) if a.workload in ("stack", "layer", "ckpt") else (LAYER_TOKENS, 1, 0)
     line = {
         "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": world, "steps": steps, "warmup": warm,
-        "ms_per_step": tokens / v * 1e3, "higher_is_better": True, "scaling": "weak" if a.workload == "layer" else "strong",
+        "ms_per_step": tokens / v * 1e3, "higher_is_better": True,
+        "scaling": "weak" if a.workload == "layer" else "strong",
         "vs_baseline": None, "dtype": "mxfp8-e4m3/fp32 (CPU)", "data": "synthetic",
-        "config": {"workload": "one Qwen3.5-2B MLP layer (hidden 2048, intermediate 6144, r 16), bounded token sample",
-                   "tokens_per_sample": tokens},
+        "config": _config(a.workload if a.workload in ("stack", "layer", "ckpt") else "layer", world, T, L),
         "impl": "reference",
-        "cpu_baseline": {"value": v, "unit": UNIT, "cores": _threads(), "kind": "port",
-                         "sample": f"{tokens} tokens of one 2B MLP layer, fwd+bwd (numpy port of the reference algorithm)"},
+        "cpu_baseline": {"value": v, "unit": UNIT, "cores": cores, "kind": "port",
+                         "sample": f"{tokens} tokens of one 2B MLP layer per step, fwd+bwd (numpy port of the "
+                                   f"reference algorithm; the reference's own path is GPU-only); layer-tokens/s "
+                                   f"extrapolated per token to the workload, rank 0 only"},
+        "extrapolated": True,
         "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -490,39 +596,29 @@ def run_reference(a):
 
 # ----------------------------------------------------------------------------------------------- configs[2]
 def _hbm_peak():
-    try:
-        return float(json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))["hbm_gbs"]), "measured"
-    except Exception:
-        return 6650.0, "fallback"
+    pk = _peaks()
+    if pk.get("hbm_gbs"):
+        return float(pk["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
 
 
-def run_quant(a):
-    """the standalone MXFP8 quantizer over rows {4096, 16384, 65536, 142336} x cols {1024,
-    2048, 3584, 6144} of N(0,1) bf16 with 0.5 % of entries x200 and 0.1 % exact zeros; row-wise
-    (mx_quant), column-wise (mx_quant_t) and both from one read (mx_quant_pair).  Each timed call follows
-    a 256 MiB write that evicts L2; the median of `steps` calls per case.  Algorithmic bytes: 3.03125 per
-    element one way (read 2, write 1 + 1/32), 4.0625 both ways.  One GPU (rank 0 under torchrun)."""
-    import torch
-    rank, local = int(os.environ.get("RANK", "0")), int(os.environ.get("LOCAL_RANK", "0"))
-    if rank != 0:
-        return
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    import __graft_entry__
-    __graft_entry__.build()
-    import _mxlib
+QUANT_ROWS, QUANT_COLS = (4096, 16384, 65536, 142336), (1024, 2048, 3584, 6144)
+
+
+def quant_sweep(torch, dev, steps, warmup, summary=False):
+    """the standalone MXFP8 quantizer over rows x cols of N(0,1) bf16 with 0.5 % of entries x200
+    and 0.1 % exact zeros; row-wise (mx_quant), column-wise (mx_quant_t) and both from one read
+    (mx_quant_pair).  Each timed call follows a 256 MiB write that evicts L2; the median of `steps` calls
+    per case.  Algorithmic bytes: 3.03125 per element one way (read 2, write 1 + 1/32), 4.0625 both."""
     import mxfp8
     peak, src = _hbm_peak()
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     g = torch.Generator(device=dev).manual_seed(0)
     modes = (("rows", mxfp8.mx_quant, 3.03125), ("cols", mxfp8.mx_quant_t, 3.03125),
              ("both", mxfp8.mx_quant_pair, 4.0625))
-    clk = ClockSampler(local)
-    clk.start()
-    launches0 = _mxlib.launch_count()
     cases = []
-    for rows in (4096, 16384, 65536, 142336):
-        for cols in (1024, 2048, 3584, 6144):
+    for rows in QUANT_ROWS:
+        for cols in QUANT_COLS:
             x = torch.randn(rows, cols, device=dev, generator=g)
             u = torch.rand(rows, cols, device=dev, generator=g)
             x = torch.where(u < 0.005, x * 200.0, x)
@@ -530,10 +626,10 @@ def run_quant(a):
             del u
             case = {"R": rows, "K": cols}
             for name, fn, bpe in modes:
-                for _ in range(max(a.warmup, 3)):
+                for _ in range(max(warmup, 3)):
                     fn(x)
                 evs = []
-                for _ in range(a.steps):
+                for _ in range(steps):
                     flush.fill_(1)
                     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                     e0.record()
@@ -547,23 +643,50 @@ def run_quant(a):
                 case[name] = {"us": round(us, 2), "gbs": round(gbs, 1), "frac": round(gbs / peak, 3)}
             cases.append(case)
             del x
+    del flush
+    med = lambda k, cs: statistics.median(c[k]["gbs"] for c in cs)  # noqa: E731
+    big = [c for c in cases if c["R"] * c["K"] * 2 > (126 << 20)]
+    res = {"median_gbs": {k: med(k, cases) for k in ("rows", "cols", "both")},
+           "median_gbs_inputs_over_l2": {k: med(k, big) for k in ("rows", "cols", "both")},
+           "peak_gbs": peak, "peak_source": f"{src} copy bandwidth",
+           "frac_inputs_over_l2": {k: med(k, big) / peak for k in ("rows", "cols", "both")},
+           "steps": steps, "l2": "256 MiB write before every timed call"}
+    if not summary:
+        res["cases"] = cases
+    else:
+        res["largest"] = cases[-1]
+    return res
+
+
+def run_quant(a):
+    import torch
+    rank, local = int(os.environ.get("RANK", "0")), int(os.environ.get("LOCAL_RANK", "0"))
+    if rank != 0:
+        return
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    import __graft_entry__
+    __graft_entry__.build()
+    import _mxlib
+    clk = ClockSampler(local)
+    clk.start()
+    launches0 = _mxlib.launch_count()
+    res = quant_sweep(torch, dev, a.steps, a.warmup)
     clocks = clk.stop()
     launches = _mxlib.launch_count() - launches0
-    med = lambda k: statistics.median(c[k]["gbs"] for c in cases)  # noqa: E731
-    big = [c for c in cases if c["R"] * c["K"] * 2 > (126 << 20)]
+    cases = res["cases"]
     line = {
         "metric": "MXFP8 quantizer achieved HBM GB/s (configs[2] sweep, row-wise, median over cases)",
-        "value": med("rows"), "unit": "GB/s", "n_gpus": 1, "steps": a.steps, "warmup": max(a.warmup, 3),
-        "ms_per_step": statistics.median(c["rows"]["us"] for c in cases) / 1e3, "higher_is_better": True,
-        "scaling": "none", "vs_baseline": None, "dtype": "bf16 -> e4m3 + e8m0", "impl": "ours",
-        "data": "synthetic N(0,1), 0.5 % x200 outliers, 0.1 % zeros (seeded)",
+        "value": res["median_gbs"]["rows"], "unit": "GB/s", "n_gpus": 1, "steps": a.steps,
+        "warmup": max(a.warmup, 3), "ms_per_step": statistics.median(c["rows"]["us"] for c in cases) / 1e3,
+        "higher_is_better": True, "scaling": "none", "vs_baseline": None, "dtype": "bf16 -> e4m3 + e8m0",
+        "impl": "ours", "data": "synthetic N(0,1), 0.5 % x200 outliers, 0.1 % zeros (seeded)",
         "config": {"workload": "configs[2]: quantizer sweep rows {4096,16384,65536,142336} x cols "
                                "{1024,2048,3584,6144}", "l2": "256 MiB write before every timed call"},
-        "median_gbs": {"rows": med("rows"), "cols": med("cols"), "both": med("both")},
-        "median_gbs_inputs_over_l2": {k: statistics.median(c[k]["gbs"] for c in big) for k in ("rows", "cols", "both")},
-        "roofline": {"bound": "hbm", "achieved": med("rows"), "peak": peak, "unit": "GB/s",
-                     "frac": med("rows") / peak, "traffic": None, "kernel": "k_quant",
-                     "peak_source": f"{src} copy bandwidth"},
+        "median_gbs": res["median_gbs"], "median_gbs_inputs_over_l2": res["median_gbs_inputs_over_l2"],
+        "roofline": {"bound": "hbm", "achieved": res["median_gbs"]["rows"], "peak": res["peak_gbs"], "unit": "GB/s",
+                     "frac": res["median_gbs"]["rows"] / res["peak_gbs"], "traffic": None, "kernel": "k_quant_tma",
+                     "peak_source": res["peak_source"]},
         "cases": cases, "gpu_launches": int(launches), "clocks": clocks,
     }
     print(json.dumps(line), flush=True)
@@ -573,28 +696,18 @@ def run_quant(a):
 RAGGED_M = (1, 77, 1000, 2049, 10752)
 
 
-def run_ragged(a):
+def ragged_latency(torch, dev, world, steps, warmup, max_over_ranks):
     """latency of one fused-MLP fwd+bwd step at the 0.8B shape (hidden 1024, intermediate
     3584, LoRA r=16, alpha=32) for per-GPU token counts M in RAGGED_M (not multiples of 128), inputs
     N(0,1) with 1 % of entries x100.  With N > 1 ranks each rank runs its own M tokens and the step ends
     with the NCCL all-reduce of the LoRA gradients; the latency is the max over ranks of the CUDA-event
     time per step.  `graph_ms`: the same fwd+bwd captured once in a CUDA graph and replayed (static
     inputs), the all-reduce after each replay -- what a training loop that graphs its layer step sees."""
-    import torch
     import torch.distributed as dist
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank, local = int(os.environ.get("RANK", "0")), int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world > 1:
-        from datetime import timedelta
-        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
-    import __graft_entry__
-    __graft_entry__.build()
-    import _mxlib
     import fused_linear
     import fused_mlp
     import mx_dp
+    rank = int(os.environ.get("RANK", "0"))
     Hs, Ns = 1024, 3584
     g = torch.Generator(device="cpu").manual_seed(11)
     w = lambda *s: (torch.randn(*s, generator=g) * 0.02).to(torch.bfloat16).to(dev)   # noqa: E731
@@ -609,19 +722,10 @@ def run_ragged(a):
             dist.barrier()
         torch.cuda.synchronize()
 
-    def max_over_ranks(v):
-        if world == 1:
-            return v
-        t = torch.tensor([v], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return t.item()
-
-    clk = ClockSampler(local)
-    clk.start()
-    launches0 = _mxlib.launch_count()
     res = []
     for M in RAGGED_M:
         gx = torch.Generator(device="cpu").manual_seed(100 + M + rank)
+
         def outl(t):
             u = torch.rand(t.shape, generator=gx)
             return torch.where(u < 0.01, t * 100.0, t)
@@ -642,16 +746,16 @@ def run_ragged(a):
                 p.grad = None
 
         def timed(fn):
-            for _ in range(max(a.warmup, 3)):
+            for _ in range(max(warmup, 3)):
                 fn()
             sync_all()
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record()
-            for _ in range(a.steps):
+            for _ in range(steps):
                 fn()
             e1.record()
             torch.cuda.synchronize()
-            return max_over_ranks(e0.elapsed_time(e1) / a.steps)
+            return max_over_ranks(e0.elapsed_time(e1) / steps)
 
         eager = timed(step)
         # CUDA graph of the local fwd+bwd (captured on every rank alike; the all-reduce stays eager)
@@ -689,6 +793,35 @@ def run_ragged(a):
             p.grad = None
         res.append({"M": M, "eager_ms": round(eager, 4), "graph_ms": None if graph_ms is None else round(graph_ms, 4),
                     **({"graph_error": err} if err else {})})
+    return {"workload": "configs[4]: 0.8B MLP shape, per-GPU M in " + str(list(RAGGED_M)), "n_gpus": world,
+            "steps": steps, "per_m": res, "mean_eager_ms": statistics.mean(r["eager_ms"] for r in res)}
+
+
+def run_ragged(a):
+    import torch
+    import torch.distributed as dist
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank, local = int(os.environ.get("RANK", "0")), int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
+    import __graft_entry__
+    __graft_entry__.build()
+    import _mxlib
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return t.item()
+
+    clk = ClockSampler(local)
+    clk.start()
+    launches0 = _mxlib.launch_count()
+    res = ragged_latency(torch, dev, world, a.steps, a.warmup, max_over_ranks)
     clocks = clk.stop()
     launches = _mxlib.launch_count() - launches0
     if world > 1:
@@ -697,15 +830,15 @@ def run_ragged(a):
         return
     line = {
         "metric": "fused-MLP fwd+bwd latency per step, 0.8B shape, ragged per-GPU M (mean over M, eager)",
-        "value": statistics.mean(r["eager_ms"] for r in res), "unit": "ms", "n_gpus": world, "steps": a.steps,
-        "warmup": max(a.warmup, 3), "ms_per_step": statistics.mean(r["eager_ms"] for r in res),
+        "value": res["mean_eager_ms"], "unit": "ms", "n_gpus": world, "steps": a.steps,
+        "warmup": max(a.warmup, 3), "ms_per_step": res["mean_eager_ms"],
         "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "mxfp8-e4m3/bf16",
         "impl": "ours", "data": "synthetic N(0,1), 1 % x100 outliers (seeded)",
-        "config": {"workload": "configs[4]: 0.8B MLP shape, per-GPU M in " + str(list(RAGGED_M)),
-                   "hidden": Hs, "intermediate": Ns, "lora_rank": R, "lora_alpha": ALPHA,
+        "config": {"workload": res["workload"], "hidden": 1024, "intermediate": 3584, "lora_rank": R,
+                   "lora_alpha": ALPHA,
                    "parallelism": f"dp{world} (each rank its own M tokens, NCCL all-reduce of LoRA grads)",
                    "l2": "small-M latency: working set in L2 by design, no flush"},
-        "per_m": res, "gpu_launches": int(launches), "clocks": clocks,
+        "per_m": res["per_m"], "gpu_launches": int(launches), "clocks": clocks,
     }
     print(json.dumps(line), flush=True)
 

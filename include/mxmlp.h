@@ -44,8 +44,17 @@ int mxm_version(void);
 const char* mxm_last_error(void);
 
 /* Reads the device-side error flag of the current device into *code (0 = none); clears it when
- * `clear` is nonzero.  Synchronizes the device (host-side diagnostics only). */
+ * `clear` is nonzero.  Returns MXM_ERR_DEVICE (with a message naming the code) when a kernel recorded
+ * an error, i.e. one of its bounded waits ran out and it returned early.  Synchronizes the device
+ * (host-side diagnostics only).  No counterpart in the reference, whose watchdog is host-side
+ * (SlowGuard, scripts/train.py:249-278). */
 int mxm_device_error(int* code, int clear);
+
+/* Test entry for the bounded waits: launches one CTA that waits on an mbarrier nothing arrives on, with
+ * a wait limit of limit_ns nanoseconds (0 < limit_ns <= 1e8) instead of the kernels' 2 s.  The wait runs
+ * out, the kernel records code 9 in the device error flag and returns; mxm_device_error then reports
+ * MXM_ERR_DEVICE.  No counterpart in the reference (see mxm_device_error). */
+int mxm_selftest_wait(int64_t limit_ns, void* stream);
 
 /* Number of kernels this library has launched in this process (all devices, host-side count). */
 unsigned long long mxm_launch_count(void);
@@ -192,17 +201,23 @@ int mxm_coldot(const void* A, int64_t lda, const void* E, int64_t lde, int64_t T
 /* Allocation-free variant of mxm_coldot, for callers that cannot allocate device memory: code running
  * inside a custom device allocator (a nested allocation would re-enter it) and services that reserve
  * their whole memory budget up front.  No counterpart in the reference.
- * Same arguments and result as mxm_coldot without the `part` / chunking arguments: the partial sums use
- * one fixed 16 MiB array in device memory that the library holds on every GPU that loads it until the
- * process exits.  Requires K * n <= 4,194,304 (one row chunk of fp32 partials must fit); larger
- * requests fail with MXM_ERR_ARG and a message.  It calls no cudaMalloc / cudaFree and no allocating
- * library routine.  The first call on each device looks up the array's device address (with that device
- * current) and caches it: make that first call before any stream capture.  All calls share the array
- * and it keeps the last call's partials (every value read is written first in the same call, so
- * nothing needs clearing); calls whose executions overlap on the GPU race on it, so serialize them
- * (one stream, or events). */
+ * Same arguments and result as mxm_coldot without the `part` / chunking / `out_fp32` arguments: the
+ * output is bf16 only, and the partial sums use one fixed 16 MiB array in device memory that the
+ * library holds on every GPU that loads it until the process exits.  Requires K * n <= 4,194,304 (one
+ * row chunk of fp32 partials must fit); larger requests fail with MXM_ERR_ARG and a message.  It calls
+ * no cudaMalloc / cudaFree and no allocating library routine.  The first call on each device looks up
+ * the array's device address (with that device current) and caches it: make that first call before any
+ * stream capture.  All calls share the array and it keeps the last call's partials (every value read is
+ * written first in the same call, so nothing needs clearing); calls whose executions overlap on the GPU
+ * race on it, so serialize them (one stream, or events). */
 int mxm_coldot_noalloc(const void* A, int64_t lda, const void* E, int64_t lde, int64_t T, int64_t K, int n,
                        float post, int transpose_out, void* out, void* stream);
+
+/* The row chunking mxm_coldot_noalloc uses for [T, K] x [T, n] on a device with num_sms SMs (0 = the
+ * current device): mxm_coldot_chunks' chunking, with fewer and taller chunks where its partials would
+ * not fit the fixed scratch (devices with more than about 256 SMs).  A query; no counterpart in the
+ * reference. */
+int mxm_coldot_noalloc_chunks(int64_t T, int64_t K, int n, int num_sms, int* rows_per_chunk, int* chunks);
 
 #ifdef __cplusplus
 }

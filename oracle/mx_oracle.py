@@ -259,6 +259,41 @@ def _gu(gu, xs, bg, bu, s_g, s_u, N, r):
     return g, u
 
 
+def fwd_epilogue(gu, xs, bg, bu, ad, s_g, s_u):
+    """``mlp_fwd`` / ``_fwd_kernel`` (scripts/fused_mlp.py:65-109,198-215) on gu [T, 2N]: returns
+    (h, q_h, s_h, xS_down) with h = bf16(silu(g) u), MXFP8(h) along N and xS_down = bf16(h Ad^T)."""
+    N, r = gu.shape[1] // 2, ad.shape[0]
+    g, u = _gu(gu, xs, bg, bu, s_g, s_u, N, r)                               # :69-70
+    h = bf16_round(_silu_parts(g) * u)                                       # :104
+    qh, sh = mx_quant(h)                                                     # :106 (_mx_store)
+    xsd = bf16_round(np.matmul(h, ad.T, dtype=np.float32))                   # :108,214
+    return h, qh, sh, xsd
+
+
+def bwd_epilogue(gu, xs, dhm, dxd, bg, bu, ad, s_g, s_u):
+    """``mlp_bwd`` / ``_bwd_kernel`` (scripts/fused_mlp.py:112-175,235-259) on gu [T, 2N] and dh_mx [T, N]:
+    MXFP8([dg | du]) and the unscaled fp32 products dBg = dg^T xa_g, dBu = du^T xa_u, dAd = (h^T dxd)^T,
+    dxa_g = dg Bg, dxa_u = du Bu, xS_down = h Ad^T."""
+    N, r = gu.shape[1] // 2, ad.shape[0]
+    g, u = _gu(gu, xs, bg, bu, s_g, s_u, N, r)                               # :151
+    silu = _silu_parts(g)                                                    # :152
+    h = bf16_round(silu * u)                                                 # :153
+    dh = bf16_round(dhm + np.matmul(dxd, ad, dtype=np.float32))              # :155
+    du = bf16_round(dh * silu)                                               # :157
+    sig = _sigmoid(g)                                                        # :158
+    dg = bf16_round(((dh * u) * sig) * (g * (np.float32(1.0) - sig) + np.float32(1.0)))   # :159
+    dgu = np.concatenate([dg, du], 1)
+    q_dgu, s_dgu = mx_quant(dgu)                                             # :160-162 (per-block == whole row)
+    return dict(
+        dg=dg, du=du, h=h, q_dgu=q_dgu, s_dgu=s_dgu,
+        dBg=np.matmul(dg.T, xs[:, :r], dtype=np.float32),                    # :163
+        dBu=np.matmul(du.T, xs[:, r:2 * r], dtype=np.float32),               # :164
+        dAd=np.matmul(h.T, dxd, dtype=np.float32).T.copy(),                  # :165,175
+        dxa_g=np.matmul(dg, bg, dtype=np.float32),                           # :166
+        dxa_u=np.matmul(du, bu, dtype=np.float32),                           # :167
+        xsd=np.matmul(h, ad.T, dtype=np.float32))                            # :168
+
+
 def lora_params_bf16(Ag, Bg, Au, Bu, Ad, Bd):
     """The bf16 casts ``_MLP.forward`` makes of the LoRA parameters (scripts/fused_mlp.py:272-276)."""
     S = bf16_round(np.concatenate([Ag, Au], 0))
@@ -280,10 +315,7 @@ def mlp_forward(x, W: MXWeights, Ag, Bg, Au, Bu, Ad, Bd, s_g, s_u, s_d, need_out
     ctx = dict(x=x, xs=xs, gu=gu, S=S, bg=bg, bu=bu, ad=ad, bd=bd, s=(s_g, s_u, s_d), W=W, r=r)
     if not need_out:
         return None, ctx
-    g, u = _gu(gu, xs, bg, bu, s_g, s_u, N, r)                               # :69-70
-    h = bf16_round(_silu_parts(g) * u)                                       # :104
-    qh, sh = mx_quant(h)                                                     # :106 (_mx_store)
-    xsd = bf16_round(np.matmul(h, ad.T, dtype=np.float32))                   # :108,214
+    h, qh, sh, xsd = fwd_epilogue(gu, xs, bg, bu, ad, s_g, s_u)
     y = mx_gemm(qh, sh, W.w_d, W.ws_d, T, H, N)                              # :283
     y = bf16_round(y + np.float32(s_d) * np.matmul(xsd, bd.T, dtype=np.float32))   # :284 addmm_
     ctx.update(h=h, qh=qh, sh=sh, xsd=xsd)
@@ -309,22 +341,9 @@ def mlp_backward(dy, ctx, need_x=True):
     dxd = bf16_round(np.matmul(dy, bd, dtype=np.float32))                    # :311
     if s_d != 1:
         dxd = bf16_round(dxd * np.float32(s_d))                              # :312-313
-    # mlp_bwd / _bwd_kernel
-    g, u = _gu(gu, xs, bg, bu, s_g, s_u, N, r)                               # :151
-    silu = _silu_parts(g)                                                    # :152
-    h = bf16_round(silu * u)                                                 # :153
-    dh = bf16_round(dhm + np.matmul(dxd, ad, dtype=np.float32))              # :155
-    du = bf16_round(dh * silu)                                               # :157
-    sig = _sigmoid(g)                                                        # :158
-    dg = bf16_round(((dh * u) * sig) * (g * (np.float32(1.0) - sig) + np.float32(1.0)))   # :159
-    dgu = np.concatenate([dg, du], 1)
-    q_dgu, s_dgu = mx_quant(dgu)                                             # :160-162 (per-block == whole row)
-    dBg = np.matmul(dg.T, xs[:, :r], dtype=np.float32)                       # :163
-    dBu = np.matmul(du.T, xs[:, r:2 * r], dtype=np.float32)                  # :164
-    dAd = np.matmul(h.T, dxd, dtype=np.float32).T.copy()                     # :165,175
-    dxa_g = np.matmul(dg, bg, dtype=np.float32)                              # :166
-    dxa_u = np.matmul(du, bu, dtype=np.float32)                              # :167
-    xsd = np.matmul(h, ad.T, dtype=np.float32)                               # :168
+    e = bwd_epilogue(gu, xs, dhm, dxd, bg, bu, ad, s_g, s_u)                 # mlp_bwd / _bwd_kernel
+    q_dgu, s_dgu, dBg, dBu, dAd = e["q_dgu"], e["s_dgu"], e["dBg"], e["dBu"], e["dAd"]
+    dxa_g, dxa_u, xsd = e["dxa_g"], e["dxa_u"], e["xsd"]
     dBd = bf16_round(np.matmul(dy.T, bf16_round(xsd), dtype=np.float32))     # :316
     if s_d != 1:
         dBd = bf16_round(dBd * np.float32(s_d))                              # :317-318

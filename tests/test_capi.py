@@ -42,3 +42,24 @@ def test_version_and_errors_without_gpu():
     assert "K % 128" in str(ei.value)
     with pytest.raises(_mxlib.MXError):
         _mxlib.call("mxm_gemm", None, 128, None, None, 128, None, 128, 256, 128, None, 256, None)
+
+
+def test_noalloc_chunking_fits_the_fixed_scratch():
+    """mxm_coldot_noalloc's row chunking (host arithmetic, no GPU): mxm_coldot's chunking on a B200-sized
+    device, fewer and taller chunks where the partials would not fit the 16 MiB scratch."""
+    import _mxlib
+    def chunks(T, K, n, sms):
+        rpc, nch = ctypes.c_int(0), ctypes.c_int(0)
+        _mxlib.call("mxm_coldot_noalloc_chunks", T, K, n, sms, ctypes.byref(rpc), ctypes.byref(nch))
+        return rpc.value, nch.value
+    for T, K, n in ((16384, 2048, 16), (142336, 6144, 64), (77, 64, 16), (20000, 2048, 64)):
+        for sms in (148, 1024, 4096):
+            rpc, nch = chunks(T, K, n, sms)
+            assert rpc % 64 == 0 and rpc * nch >= T and (nch - 1) * rpc < T
+            assert nch * K * n * 4 <= 16 << 20
+        a, b = ctypes.c_int(0), ctypes.c_int(0)
+        _mxlib.call("mxm_coldot_chunks", T, K, ctypes.byref(a), ctypes.byref(b))
+        assert chunks(T, K, n, 148) == (a.value, b.value)   # below the cap: the regular chunking
+    assert chunks(20000, 2048, 64, 1024)[1] == 32             # the cap: 16 MiB / (2048 * 64 * 4 B)
+    with pytest.raises(_mxlib.MXError):
+        chunks(128, 131072, 64, 148)

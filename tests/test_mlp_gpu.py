@@ -217,3 +217,99 @@ def test_cuda_graph_replay_matches_eager(T):
         assert torch.equal(a, b)
     import _mxlib
     assert _mxlib.device_error() == 0
+
+
+def _codes_differ(a, b):
+    """Share of E4M3 codes that differ (two NaN codes count as equal)."""
+    a, b = np.asarray(a, np.uint8), np.asarray(b, np.uint8)
+    nan = ((a & 0x7F) == 0x7F) & ((b & 0x7F) == 0x7F)
+    return float(((a != b) & ~nan).mean())
+
+
+@pytest.mark.parametrize("T", [1024, 2049])
+def test_mlp_2b_shape_vs_oracle(T):
+    """The benchmarked shape (Qwen3.5-2B MLP: hidden 2048, intermediate 6144, r 16, alpha 32): y, dx and
+    all six LoRA gradients within 5e-3 of the oracle.  T = 2049 is an odd count of 128-row blocks, so the
+    CTA-pair gate|up kernel's last pair has a second CTA without rows."""
+    H, N, r, s = 2048, 6144, 16, 2.0
+    case = _case(T, H, N, r, seed=20000 + T, outlier=100.0)
+    y, dx, grads = _run(*case, s)
+    yo, go, _ = _oracle(*case, s)
+    assert O.rel_fro(y.numpy(), yo) < TOL
+    assert O.rel_fro(dx.numpy(), go["dx"]) < TOL
+    for gr, k in zip(grads, NAMES):
+        assert O.rel_fro(gr.numpy(), go[k]) < TOL, (k, O.rel_fro(gr.numpy(), go[k]))
+
+
+@pytest.mark.parametrize("T", [1024, 2049])
+def test_epilogue_bytes_2b_vs_oracle(T):
+    """At the 2B shape, the kernels the step runs -- the gate|up GEMM with the fused forward epilogue and
+    the backward epilogue -- against the oracle's epilogues fed the same gu / dh_mx: MXFP8(h) and
+    MXFP8([dg | du]) codes and scales equal except where exp / reciprocal differ by an ulp (< 1e-3 of the
+    codes), the partial products within 2e-3."""
+    import fused_linear
+    import fused_mlp
+    import mxfp8
+    fused_linear.new_step()
+    H, N, r, s = 2048, 6144, 16, 2.0
+    x, Wg, Wu, Wd, lora, dy = _case(T, H, N, r, seed=30000 + T, outlier=100.0)
+    dev = torch.device("cuda")
+    layer = fused_mlp.MXMLPWeights.from_bf16(Wg.to(dev), Wu.to(dev), Wd.to(dev))
+    P = fused_mlp.lora_prep(*(p.to(dev) for p in (lora[0], lora[2], lora[1], lora[3], lora[4], lora[5])), s)
+    S, bg, bu, ad, bd, bds, bdT, ST = P
+    xd, dyd = x.to(dev), dy.to(dev)
+    xs, q, sc = fused_mlp.rowdot_quant(xd, S)
+    gu, qh, sh, xsd = fused_mlp.gemm_glu(q, sc, layer.hold.w, layer.hold.ws, xs, bg, bu, ad, s, s)
+    dxd, qd, sd = fused_mlp.rowdot_quant(dyd, bdT, post=s)
+    wt, wts = mxfp8.mx_wt(layer.down)
+    dhm = mxfp8.mx_mm(qd, wt.t(), sd, wts)
+    qg, sg, dxa, dbg, dbu, dad = fused_mlp.mlp_bwd(gu, xs, dhm, dxd, bg, bu, ad, s, s, True)
+    torch.cuda.synchronize()
+    import _mxlib
+    assert _mxlib.device_error() == 0
+    f = lambda t: t.float().cpu().numpy()  # noqa: E731
+    h_o, qh_o, sh_o, xsd_o = O.fwd_epilogue(f(gu), f(xs), f(bg), f(bu), f(ad), s, s)
+    assert _codes_differ(qh.view(torch.uint8).cpu().numpy(), qh_o) < 1e-3
+    assert float((sh.view(torch.uint8).cpu().numpy() != sh_o).mean()) < 1e-3
+    assert O.rel_fro(f(xsd), xsd_o) < 2e-3
+    e = O.bwd_epilogue(f(gu), f(xs), f(dhm), f(dxd), f(bg), f(bu), f(ad), s, s)
+    assert _codes_differ(qg.view(torch.uint8).cpu().numpy(), e["q_dgu"]) < 1e-3
+    assert float((sg.view(torch.uint8).cpu().numpy() != e["s_dgu"]).mean()) < 1e-3
+    assert O.rel_fro(f(dbg), e["dBg"]) < 2e-3 and O.rel_fro(f(dbu), e["dBu"]) < 2e-3
+    assert O.rel_fro(f(dad), e["dAd"]) < 2e-3
+    assert O.rel_fro(f(dxa)[:, :r], e["dxa_g"]) < 2e-3 and O.rel_fro(f(dxa)[:, r:2 * r], e["dxa_u"]) < 2e-3
+    assert O.rel_fro(f(dxa)[:, 2 * r:], e["xsd"]) < 2e-3
+
+
+def test_configs0_exact():
+    """configs[0] as BASELINE states it: 0.8B MLP shape, X bf16 [512, 1024] ~ N(0,1); W_gate, W_up
+    [3584, 1024] and W_down [1024, 3584] ~ N(0, 0.02); LoRA r 16, alpha 32 on all three with A, B ~
+    N(0, 0.01); dY ~ N(0,1) bf16; seed 0 (one torch generator, drawn in that order)."""
+    T, H, N, r, s = 512, 1024, 3584, 16, 2.0
+    g = torch.Generator().manual_seed(0)
+    x = torch.randn(T, H, generator=g).to(torch.bfloat16)
+    Wg = (torch.randn(N, H, generator=g) * 0.02).to(torch.bfloat16)
+    Wu = (torch.randn(N, H, generator=g) * 0.02).to(torch.bfloat16)
+    Wd = (torch.randn(H, N, generator=g) * 0.02).to(torch.bfloat16)
+    lora = [torch.randn(*sh, generator=g) * 0.01 for sh in ((r, H), (N, r), (r, H), (N, r), (r, N), (H, r))]
+    dy = torch.randn(T, H, generator=g).to(torch.bfloat16)
+    case = (x, Wg, Wu, Wd, lora, dy)
+    y, dx, grads = _run(*case, s)
+    yo, go, _ = _oracle(*case, s)
+    assert O.rel_fro(y.numpy(), yo) < TOL
+    assert O.rel_fro(dx.numpy(), go["dx"]) < TOL
+    for gr, k in zip(grads, NAMES):
+        assert O.rel_fro(gr.numpy(), go[k]) < TOL, (k, O.rel_fro(gr.numpy(), go[k]))
+
+
+def test_ragged_10752_vs_oracle():
+    """configs[4]'s largest ragged M (10752 = 84 blocks of 128, not a multiple of 256) at the 0.8B shape
+    with 1 % x100 outliers."""
+    T, H, N, r, s = 10752, 1024, 3584, 16, 2.0
+    case = _case(T, H, N, r, seed=10752, outlier=100.0)
+    y, dx, grads = _run(*case, s)
+    yo, go, _ = _oracle(*case, s)
+    assert O.rel_fro(y.numpy(), yo) < TOL
+    assert O.rel_fro(dx.numpy(), go["dx"]) < TOL
+    for gr, k in zip(grads, NAMES):
+        assert O.rel_fro(gr.numpy(), go[k]) < TOL, (k, O.rel_fro(gr.numpy(), go[k]))

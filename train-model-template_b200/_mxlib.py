@@ -26,6 +26,7 @@ _SIGS = {
     "mxm_version": [],
     "mxm_last_error": [],
     "mxm_device_error": [ctypes.POINTER(ctypes.c_int), _int],
+    "mxm_selftest_wait": [_i64, _vp],
     "mxm_num_sms": [],
     "mxm_launch_count": [],
     "mxm_quant_rows": [_vp, _i64, _i64, _i64, _vp, _i64, _vp, _vp],
@@ -55,6 +56,7 @@ _SIGS = {
     "mxm_res_lora": [_vp, _vp, _vp, _i64, _vp, _i64, _i64, _int, ctypes.c_float, _vp, _vp],
     "mxm_lora_prep": [_vp, _vp, _vp, _vp, _vp, _vp, _int, _i64, _i64, _int, ctypes.c_float, _vp, _vp],
     "mxm_coldot_noalloc": [_vp, _i64, _vp, _i64, _i64, _i64, _int, ctypes.c_float, _int, _vp, _vp],
+    "mxm_coldot_noalloc_chunks": [_i64, _i64, _int, _int, ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_int)],
 }
 _RESTYPE = {"mxm_last_error": ctypes.c_char_p, "mxm_launch_count": ctypes.c_ulonglong}
 
@@ -90,9 +92,16 @@ def version():
     return _lib.mxm_version()
 
 
+MXM_ERR_DEVICE = -4
+
+
 def device_error(clear=True):
+    """The device-side error code of the current device (0 = none; a kernel gave up a bounded wait
+    otherwise), cleared when `clear`.  Synchronizes the device."""
     c = ctypes.c_int(0)
-    call("mxm_device_error", ctypes.byref(c), 1 if clear else 0)
+    st = _lib.mxm_device_error(ctypes.byref(c), 1 if clear else 0)
+    if st not in (0, MXM_ERR_DEVICE):
+        raise MXError("mxm_device_error", st, last_error())
     return c.value
 
 

@@ -23,6 +23,7 @@ enum MxDevError : int {
   MX_DEV_TIMEOUT_MMA = 2,
   MX_DEV_TIMEOUT_EPILOGUE = 3,
   MX_DEV_TIMEOUT_MMA_TMEM = 4,
+  MX_DEV_TIMEOUT_SELFTEST = 9,   // the wait of mxm_selftest_wait (nobody arrives by design)
 };
 
 MX_DEV void mx_set_error(int* flag, int code) {
@@ -148,17 +149,32 @@ MX_DEV bool mbar_test(uint64_t* bar, uint32_t parity) {
 #ifndef MX_WAIT_LIMIT_NS
 #define MX_WAIT_LIMIT_NS 2000000000ull  // 2 s
 #endif
-MX_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, int* flag, int err) {
+MX_DEV bool mbar_wait_ns(uint64_t* bar, uint32_t parity, int* flag, int err, uint64_t limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = mx_globaltimer();
   while (true) {
     for (int i = 0; i < 64; ++i)
       if (mbar_try_wait(bar, parity)) return true;
-    if (mx_globaltimer() - t0 > MX_WAIT_LIMIT_NS) {
+    if (mx_globaltimer() - t0 > limit_ns) {
       mx_set_error(flag, err);
       return false;
     }
   }
+}
+MX_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, int* flag, int err) {
+  return mbar_wait_ns(bar, parity, flag, err, MX_WAIT_LIMIT_NS);
+}
+
+// Named barrier `id` over `nthreads` threads that also ORs a predicate across them: warps that wait on
+// the same mbarrier with their own clocks decide to give up together (a warp that gave up alone would
+// leave the others waiting at the next named barrier).
+MX_DEV bool bar_any(uint32_t id, uint32_t nthreads, bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 q, %1, 0;\n\tbar.red.or.pred p, %2, %3, q;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(r) : "r"((uint32_t)v), "r"(id), "r"(nthreads) : "memory");
+  return r != 0;
 }
 
 // ------------------------------------------------------------------------------------------------

@@ -557,10 +557,11 @@ MX_DEV void glu_body(const CUtensorMap* tmA, const CUtensorMap* tmB, const CUten
         for (int j = 0; j < R / 8; ++j) accx[j][0] = accx[j][1] = accx[j][2] = accx[j][3] = 0.f;
         qr = qrows_init(ra, M, Tpad, qh, N, sh, N, t);
       }
-      // 1. drain the accumulator, hand it back, store gu and stage the bf16 tile
-      if (!mbar_wait(tmem_full, acc_phase, err, MX_DEV_TIMEOUT_EPILOGUE)) break;
-      tc_fence_after();
-      {
+      // 1. drain the accumulator, hand it back, store gu and stage the bf16 tile (a warp whose wait ran
+      // out skips this and the epilogue warps give up together at the named barrier below)
+      const bool acc_ok = mbar_wait(tmem_full, acc_phase, err, MX_DEV_TIMEOUT_EPILOGUE);
+      if (acc_ok) {
+        tc_fence_after();
         const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + h * 128;
         const int rl = q * 32 + lane;
         const uint32_t sbase = s_stg + (uint32_t)h * (2 * 128 * 128);
@@ -615,7 +616,7 @@ MX_DEV void glu_body(const CUtensorMap* tmA, const CUtensorMap* tmB, const CUten
         asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
                      : "memory");
       }
-      epi_sync();
+      if (bar_any(1, EPI_THREADS, !acc_ok)) break;   // the epi_sync of this tile, and the give-up decision
       // gu leaves from the staged tile as four [128 x 64] TMA stores (gate, up) x (sub-tile), rows >= M
       // clipped, one per SwiGLU sub-step below: spread out, they hold the TMA unit back from the next
       // tile's operand loads less than one 64 KB burst does

@@ -1700,26 +1700,42 @@ static int noalloc_scratch(float** out) {
   return MXM_OK;
 }
 
-extern "C" int mxm_coldot_noalloc(const void* A, int64_t lda, const void* E, int64_t lde, int64_t T, int64_t K, int n,
-                                  float post, int transpose_out, void* out, void* stream) {
-  MX_CHECK_ARG(A && E && out, "mxm_coldot_noalloc: null pointer");
-  MX_CHECK_ARG(T >= 1 && K >= 64 && K % 64 == 0 && (n == 16 || n == 32 || n == 64),
-               "mxm_coldot_noalloc: need T >= 1, K %% 64 == 0, n in {16, 32, 64}");
+extern "C" int mxm_coldot_noalloc_chunks(int64_t T, int64_t K, int n, int num_sms, int* rows_per_chunk, int* chunks) {
+  MX_CHECK_ARG(T >= 1 && K >= 64 && K % 64 == 0 && (n == 16 || n == 32 || n == 64) && num_sms >= 0 && rows_per_chunk &&
+                   chunks, "mxm_coldot_noalloc_chunks: bad args");
   const int64_t per_chunk = K * n * (int64_t)sizeof(float);
   MX_CHECK_ARG(per_chunk <= (int64_t)MXM_NOALLOC_SCRATCH_BYTES,
                "mxm_coldot_noalloc: K * n = %lld needs %lld bytes of scratch per row chunk, more than the fixed "
                "%u-byte scratch (K * n must be <= %u)",
                (long long)(K * n), (long long)per_chunk, MXM_NOALLOC_SCRATCH_BYTES,
                MXM_NOALLOC_SCRATCH_BYTES / (unsigned)sizeof(float));
-  int rpc = 0, chunks = 0;
-  if (int e = mxm_coldot_chunks(T, K, &rpc, &chunks)) return e;
+  // mxm_coldot's chunking (one wave of four CTAs per SM); on a B200 (148 SMs) its partials need at most
+  // 4 * 148 * 64 * n * 4 bytes (9.7 MB at n = 64), inside the scratch; a device with more SMs gets fewer,
+  // taller row chunks so the partials still fit
+  const int64_t ctas_k = K / CD_COLS;
+  const int64_t want = 4 * (int64_t)(num_sms > 0 ? num_sms : mxm_num_sms());
+  const int64_t nch = std::max<int64_t>(1, want / ctas_k);
+  int64_t rpc = (T + nch - 1) / nch;
+  rpc = std::max<int64_t>((rpc + CD_ROWS - 1) / CD_ROWS * CD_ROWS, 4 * CD_ROWS);
+  int64_t nc = (T + rpc - 1) / rpc;
   const int64_t max_chunks = (int64_t)MXM_NOALLOC_SCRATCH_BYTES / per_chunk;
-  if (chunks > max_chunks) {  // fewer, taller row chunks so the partials fit the fixed scratch
-    int64_t r = (T + max_chunks - 1) / max_chunks;
-    r = (r + CD_ROWS - 1) / CD_ROWS * CD_ROWS;
-    rpc = (int)r;
-    chunks = (int)((T + r - 1) / r);
+  if (nc > max_chunks) {
+    rpc = (T + max_chunks - 1) / max_chunks;
+    rpc = (rpc + CD_ROWS - 1) / CD_ROWS * CD_ROWS;
+    nc = (T + rpc - 1) / rpc;
   }
+  *rows_per_chunk = (int)rpc;
+  *chunks = (int)nc;
+  return MXM_OK;
+}
+
+extern "C" int mxm_coldot_noalloc(const void* A, int64_t lda, const void* E, int64_t lde, int64_t T, int64_t K, int n,
+                                  float post, int transpose_out, void* out, void* stream) {
+  MX_CHECK_ARG(A && E && out, "mxm_coldot_noalloc: null pointer");
+  MX_CHECK_ARG(T >= 1 && K >= 64 && K % 64 == 0 && (n == 16 || n == 32 || n == 64),
+               "mxm_coldot_noalloc: need T >= 1, K %% 64 == 0, n in {16, 32, 64}");
+  int rpc = 0, chunks = 0;
+  if (int e = mxm_coldot_noalloc_chunks(T, K, n, 0, &rpc, &chunks)) return e;
   float* scratch = nullptr;
   if (int e = noalloc_scratch(&scratch)) return e;
   // every partial the reduction reads is written by k_coldot first: nothing needs clearing

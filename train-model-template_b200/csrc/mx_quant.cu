@@ -248,13 +248,14 @@ __global__ void __launch_bounds__(32 * (QM_CONS + 1), 1)
   uint32_t phase = 0;
   for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++it) {
     const int tr = t / nct, tc = t % nct;
-    if (!mbar_wait(&full[stage], phase, err, MX_DEV_TIMEOUT_EPILOGUE)) break;
+    // a warp whose wait ran out skips the tile; the consumer warps give up together at the named barrier
+    const bool ok = mbar_wait(&full[stage], phase, err, MX_DEV_TIMEOUT_EPILOGUE);
     const uint32_t in = s_ring + (uint32_t)stage * QM_IN;           // box b at in + b * 16 KB
     const uint32_t ob = s_out + (uint32_t)(it & 1) * QM_OUT;
     const uint32_t oq = ob, oqt = ob + 16384, ors = ob + 32768, ocs = ob + 32768 + 512;
     uint8_t* rs = outb + (it & 1) * QM_OUT + 32768;
     uint8_t* cs = rs + 512;
-    if (ROWS) {
+    if (ROWS && ok) {
       // lane -> (row pair half, box, 16-column quarter of the box); a warp covers 4 rows x 128 columns
       const int q = lane & 3, rsub = (lane >> 2) & 1, box = (lane >> 3) & 1, rpair = lane >> 4;
 #pragma unroll
@@ -278,7 +279,7 @@ __global__ void __launch_bounds__(32 * (QM_CONS + 1), 1)
         if ((q & 1) == 0) rs[(r & 31) * 16 + (r >> 5) * 4 + 2 * box + (q >> 1)] = (uint8_t)e;
       }
     }
-    if (COLS) {
+    if (COLS && ok) {
       // warp -> (32-row block jb, box); lane -> columns 2 lane, 2 lane + 1 of the box
       const int jb = warp >> 1, box = warp & 1;
       const uint32_t base = in + (uint32_t)box * 16384 + (uint32_t)((lane & 3) * 4);
@@ -316,13 +317,13 @@ __global__ void __launch_bounds__(32 * (QM_CONS + 1), 1)
     }
     fence_proxy_async();   // the staged outputs are read by the bulk stores below
     __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[stage]);
+    if (lane == 0 && ok) mbar_arrive(&empty[stage]);
     if (++stage == QM_ST) {
       stage = 0;
       phase ^= 1;
     }
     if (tid == 0) bulk_wait_read0();   // the previous tile's stores have read the other staging buffer
-    asm volatile("bar.sync 1, %0;" ::"r"(32 * QM_CONS) : "memory");
+    if (bar_any(1, 32 * QM_CONS, !ok)) break;
     if (tid == 0) {
       if (ROWS) {
         tma_store_2d(&tm_q, outb + (it & 1) * QM_OUT, tc * 128, tr * 128);

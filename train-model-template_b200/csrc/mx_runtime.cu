@@ -7,6 +7,7 @@
 #include <atomic>
 #include <mutex>
 
+#include "mx_common.cuh"
 #include "mx_runtime.h"
 
 __device__ int g_mx_dev_error = 0;
@@ -61,8 +62,40 @@ extern "C" int mxm_device_error(int* code, int clear) {
   if (clear && v) {
     const int zero = 0;
     st = mx_cuda_status(cudaMemcpyToSymbol(g_mx_dev_error, &zero, sizeof(int)), "clear device error flag");
+    if (st) return st;
   }
-  return st;
+  if (v) {
+    static const char* what[] = {"", "producer", "MMA issue", "epilogue", "MMA accumulator hand-back"};
+    mx_set_last_error("a kernel gave up a bounded wait (device error code %d: %s)", v,
+                      v == MX_DEV_TIMEOUT_SELFTEST ? "self-test wait" : (v > 0 && v < 5 ? what[v] : "unknown"));
+    return MXM_ERR_DEVICE;
+  }
+  return MXM_OK;
+}
+
+// One CTA waits on an mbarrier that nothing arrives on, with a bounded wait of limit_ns: the wait runs
+// out, records MX_DEV_TIMEOUT_SELFTEST in the device error flag and the kernel returns.
+__global__ void k_selftest_wait(uint64_t limit_ns, int* err) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_barrier_init();
+  }
+  __syncthreads();
+  mbar_wait_ns(&bar, 0, err, MX_DEV_TIMEOUT_SELFTEST, limit_ns);
+}
+
+extern "C" int mxm_selftest_wait(int64_t limit_ns, void* stream) {
+  MX_CHECK_ARG(limit_ns > 0 && limit_ns <= 100000000, "mxm_selftest_wait: limit_ns must be in (0, 1e8] (got %lld)",
+               (long long)limit_ns);
+  int* err = mx_dev_error_ptr();
+  if (!err) {
+    mx_set_last_error("mxm_selftest_wait: no device error flag on the current device");
+    return MXM_ERR_CUDA;
+  }
+  k_selftest_wait<<<1, 32, 0, (cudaStream_t)stream>>>((uint64_t)limit_ns, err);
+  mx_note_launch();
+  return mx_launch_status("mxm_selftest_wait");
 }
 
 extern "C" int mxm_num_sms(void) {

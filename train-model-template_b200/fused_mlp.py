@@ -23,6 +23,7 @@ import types
 import torch
 
 import _mxlib as _nx
+import mx_dp
 import mxfp8
 from fused_linear import STATS, _cast, _part
 
@@ -67,16 +68,20 @@ def rowdot_quant(A, B, post=1.0):
     return out, q, s.view(_E8)
 
 
-def coldot(A, E, post=1.0, transpose_out=False, out_dtype=torch.bfloat16):
+def coldot(A, E, post=1.0, transpose_out=False, out_dtype=torch.bfloat16, out=None):
     """bf16(bf16(A^T @ E) * post): A [T, K] bf16, E [T, n] bf16 (n in {16, 32, 64}) -> [K, n] (or [n, K]);
-    out_dtype float32 stores the same bf16-valued numbers in fp32 (a gradient for an fp32 parameter)."""
+    out_dtype float32 stores the same bf16-valued numbers in fp32 (a gradient for an fp32 parameter).
+    `out`: a contiguous destination of that shape and dtype (else one is allocated)."""
     T, K = A.shape
     n = E.shape[1]
     assert out_dtype in (torch.bfloat16, torch.float32)
     rpc, nch = _i(0), _i(0)
     _nx.call("mxm_coldot_chunks", T, K, _nx.ctypes_ref(rpc), _nx.ctypes_ref(nch))
     part = torch.empty((nch.value, K, n), dtype=torch.float32, device=A.device)
-    out = torch.empty((n, K) if transpose_out else (K, n), dtype=out_dtype, device=A.device)
+    shape = (n, K) if transpose_out else (K, n)
+    if out is None:
+        out = torch.empty(shape, dtype=out_dtype, device=A.device)
+    assert out.shape == shape and out.dtype == out_dtype and out.is_contiguous(), (out.shape, out.dtype)
     _nx.call("mxm_coldot", _nx.ptr(A), A.stride(0), _nx.ptr(E), E.stride(0), T, K, n, float(post),
              1 if transpose_out else 0, _nx.ptr(part), rpc.value, nch.value, _nx.ptr(out),
              1 if out_dtype == torch.float32 else 0, _nx.stream_of(A))
@@ -237,6 +242,7 @@ class _MLP(torch.autograd.Function):
         ctx.meta = (hold, down, (s_g, s_u, s_d), dt, lead, K, x.dtype)
         ctx.tr = (bdT, ST)   # parameter-derived transposes (not activations)
         ctx.gdt = tuple(w.dtype for w in (Ag, Au, Bd))
+        ctx.params = (Ag, Bg, Au, Bu, Ad, Bd)   # to place bucketed gradients (mx_dp.LayerGrads)
         return y.view(*lead, y.shape[-1])
 
     @staticmethod
@@ -259,27 +265,37 @@ class _MLP(torch.autograd.Function):
         qg, sg, (dxa_p, dbg_p, dbu_p, dad_p, sb, ncg) = _bwd_launch(gu, xs, dhm, dxd, bg, bu, ad, s_g, s_u, need_x)
         del dhm
         dev = gu.device
+        Ag, Bg, Au, Bu, Ad, Bd = ctx.params
+        ws_in = ctx.needs_input_grad[3:]
+        dst = lambda p, k: mx_dp.grad_out(p) if ws_in[k] else None  # noqa: E731  (storage of a bucketed grad)
         dxa = torch.empty((T, 2 * R), dtype=dt, device=dev)
         xsd = torch.empty((T, R), dtype=dt, device=dev)
-        dB_g = torch.empty((N, R), dtype=torch.float32, device=dev)
-        dB_u = torch.empty((N, R), dtype=torch.float32, device=dev)
-        dA_d = torch.empty((R, N), dtype=torch.float32, device=dev)
+        dB_g = _or_empty(dst(Bg, 1), (N, R), dev)
+        dB_u = _or_empty(dst(Bu, 3), (N, R), dev)
+        dA_d = _or_empty(dst(Ad, 4), (R, N), dev)
         _nx.call("mxm_mlp_bwd_reduce", _nx.ptr(dxa_p), _nx.ptr(dbg_p), _nx.ptr(dbu_p), _nx.ptr(dad_p), T, N, R,
                  float(s_g), float(s_u), sb, ncg, _nx.ptr(dxa), _nx.ptr(xsd), _nx.ptr(dB_g), _nx.ptr(dB_u),
                  _nx.ptr(dA_d), _nx.stream_of(gu))
         del dxa_p, dbg_p, dbu_p, dad_p
         f32 = lambda k: torch.float32 if ctx.gdt[k] == torch.float32 else torch.bfloat16  # noqa: E731
-        dB_d = coldot(dy2, xsd, post=s_d, out_dtype=f32(2))              # bf16(bf16(dy^T xS_down) * s_d) [H, R]
+        dB_d = coldot(dy2, xsd, post=s_d, out_dtype=f32(2),              # bf16(bf16(dy^T xS_down) * s_d) [H, R]
+                      out=dst(Bd, 5) if f32(2) == torch.float32 else None)
         dx = None
         if need_x:
             dx = mx_mm_lora(qg, hold.wt.t(), sg.view(_E8), hold.wts, dxa, ST)   # K = 2N: gate + up
             del qg, sg
             dx = dx.view(*lead, K).to(xdt)
-        dA = coldot(x2, dxa, transpose_out=True,
-                    out_dtype=f32(0) if ctx.gdt[0] == ctx.gdt[1] else torch.bfloat16)   # [2R, H]
+        dA_dt = f32(0) if ctx.gdt[0] == ctx.gdt[1] else torch.bfloat16
+        lg = mx_dp._ACTIVE[0]
+        dA_out = (lg.slot_pair(Ag, Au, (2 * R, x2.shape[1]))
+                  if lg is not None and dA_dt == torch.float32 and ws_in[0] and ws_in[2] else None)
+        dA = coldot(x2, dxa, transpose_out=True, out_dtype=dA_dt, out=dA_out)   # [2R, H] = [dA_gate; dA_up]
         grads = [dA[:R], dB_g, dA[R:], dB_u, dA_d, dB_d]
-        ws_in = ctx.needs_input_grad[3:]
         return (dx, None, None, *[g if ws_in[k] else None for k, g in enumerate(grads)])
+
+
+def _or_empty(t, shape, dev):
+    return t if t is not None else torch.empty(shape, dtype=torch.float32, device=dev)
 
 
 def _r_ok(r):
