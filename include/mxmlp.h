@@ -168,6 +168,32 @@ int mxm_lora_bwd(const void* dy, int64_t ldy, int64_t T, int64_t N, const void* 
                  void* dxa_out, int64_t ld_dxa, void* dB_out, void* part, int rows_per_chunk, int chunks,
                  void* stream);
 
+/* One branch of a linear group's backward (see mxm_group_lora_bwd). */
+typedef struct {
+  const void* dy;    /* [T, N] bf16, row stride ldy elements (multiple of 8, 16-byte aligned) */
+  int64_t ldy;
+  int64_t N;         /* output width of the linear, N % 128 == 0 */
+  const void* xa;    /* [T, r] bf16 = this branch's columns of x S^T (row stride ldxa); NULL: no LoRA branch */
+  int64_t ldxa;
+  const void* Bt;    /* B^T [r, N] bf16 contiguous */
+  int r;             /* LoRA rank: 16, 32 or 64 */
+  float scale;       /* LoRA scaling */
+  void* dxa_out;     /* [T, r] bf16 = bf16(scale * dy B), row stride ld_dxa */
+  int64_t ld_dxa;
+  void* dB_out;      /* [N, r] fp32 = scale * dy^T xa */
+} mxm_group_branch;
+
+/* The backward of a group of MX linears sharing one input, in one call (the reference's one-read grouped
+ * backward, scripts/fused_linear.py:219-278, with mxfp8.lora_bwd per branch, scripts/mxfp8.py:219-263):
+ * branch i's dy is read once for its row-wise MXFP8 codes -- written into columns [sum_{j<i} N_j, +N_i) of
+ * the group's K-concatenated operand q [ceil128(T), s_cols] (row stride ldq) with scales in that operand's
+ * blocked layout s -- and, for a LoRA branch, d(xa) and dB.  q / s may be NULL (no dx needed; every branch
+ * must then carry a LoRA term).  part: fp32 scratch of part_bytes, at least max over LoRA branches of
+ * chunks * N * r * 4 with mxm_coldot_chunks(T, N) chunking.  Returns MXM_ERR_UNSUPPORTED (before any
+ * launch) for a LoRA rank the kernels do not take; the caller then runs its general path. */
+int mxm_group_lora_bwd(int64_t T, int nb, const mxm_group_branch* br, void* q, int64_t ldq, void* s, int64_t s_cols,
+                       void* part, int64_t part_bytes, void* stream);
+
 /* out = bf16(x + bf16(y + scale * xa B^T)) for x, y, out [T, N] bf16 contiguous, xa [T, r] (row stride ldxa),
  * B [N, r] contiguous (reference res_lora, scripts/mxfp8.py:265-296).  N % 64 == 0, r in {16, 32, 64}. */
 int mxm_res_lora(const void* x, const void* y, const void* xa, int64_t ldxa, const void* B, int64_t T, int64_t N,

@@ -21,6 +21,13 @@ except OSError as e:  # pragma: no cover - depends on the machine
 
 _vp, _i64, _int = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int
 
+
+class GroupBranch(ctypes.Structure):
+    """mxm_group_branch (include/mxmlp.h): one branch of a linear group's backward."""
+    _fields_ = [("dy", _vp), ("ldy", _i64), ("N", _i64), ("xa", _vp), ("ldxa", _i64), ("Bt", _vp), ("r", _int),
+                ("scale", ctypes.c_float), ("dxa_out", _vp), ("ld_dxa", _i64), ("dB_out", _vp)]
+
+
 # name -> argument types (all return int status unless listed in _RESTYPE)
 _SIGS = {
     "mxm_version": [],
@@ -55,6 +62,7 @@ _SIGS = {
                      _vp, _vp, _int, _int, _vp],
     "mxm_res_lora": [_vp, _vp, _vp, _i64, _vp, _i64, _i64, _int, ctypes.c_float, _vp, _vp],
     "mxm_lora_prep": [_vp, _vp, _vp, _vp, _vp, _vp, _int, _i64, _i64, _int, ctypes.c_float, _vp, _vp],
+    "mxm_group_lora_bwd": [_i64, _int, ctypes.POINTER(GroupBranch), _vp, _i64, _vp, _i64, _vp, _i64, _vp],
     "mxm_coldot_noalloc": [_vp, _i64, _vp, _i64, _i64, _i64, _int, ctypes.c_float, _int, _vp, _vp],
     "mxm_coldot_noalloc_chunks": [_i64, _i64, _int, _int, ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_int)],
 }

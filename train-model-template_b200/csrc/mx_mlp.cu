@@ -1569,6 +1569,55 @@ extern "C" int mxm_lora_bwd(const void* dy, int64_t ldy, int64_t T, int64_t N, c
   return mx_launch_status("lora bwd sum");
 }
 
+// The backward of a group of MX linears that share one input (q|k|v, qkv|z, o_proj alone), one branch after
+// another on the caller's stream: each branch's dy is read once by the fused rowdot (its MXFP8 codes into
+// columns of the group's K-concatenated operand, and for a LoRA branch d(xa) = bf16(scale dy B)), then a
+// LoRA branch's dB = scale dy^T xa by the coldot.  The branches reuse one partial-sum buffer: stream order
+// finishes a branch's reduction before the next branch's coldot writes it.
+extern "C" int mxm_group_lora_bwd(int64_t T, int nb, const mxm_group_branch* br, void* q, int64_t ldq, void* s,
+                                  int64_t s_cols, void* part, int64_t part_bytes, void* stream) {
+  MX_CHECK_ARG(br && nb >= 1 && T >= 1 && T < (1ll << 31), "mxm_group_lora_bwd: need T >= 1 and branches");
+  MX_CHECK_ARG((q == nullptr) == (s == nullptr), "mxm_group_lora_bwd: q and s go together");
+  int64_t cols = 0;
+  for (int i = 0; i < nb; ++i) {   // validate every branch before the first launch
+    const mxm_group_branch& b = br[i];
+    MX_CHECK_ARG(b.dy && b.N >= 128 && b.N % 128 == 0, "mxm_group_lora_bwd: branch %d needs dy with N %% 128 == 0", i);
+    if (b.xa) {
+      if (!(b.r == 16 || b.r == 32 || b.r == 64)) {
+        mx_set_last_error("mxm_group_lora_bwd: branch %d has LoRA rank %d (the kernels take 16, 32, 64)", i, b.r);
+        return MXM_ERR_UNSUPPORTED;
+      }
+      MX_CHECK_ARG(b.Bt && b.dxa_out && b.dB_out, "mxm_group_lora_bwd: branch %d: null LoRA pointer", i);
+      int rpc = 0, nch = 0;
+      if (int e = mxm_coldot_chunks(T, b.N, &rpc, &nch)) return e;
+      MX_CHECK_ARG((int64_t)nch * b.N * b.r * 4 <= part_bytes,
+                   "mxm_group_lora_bwd: branch %d needs %lld bytes of partials, %lld given", i,
+                   (long long)nch * b.N * b.r * 4, (long long)part_bytes);
+    } else {
+      MX_CHECK_ARG(q != nullptr, "mxm_group_lora_bwd: branch %d has neither a LoRA branch nor a quantization", i);
+    }
+    cols += b.N;
+  }
+  MX_CHECK_ARG(q == nullptr || cols <= s_cols, "mxm_group_lora_bwd: branches span %lld columns, operand has %lld",
+               (long long)cols, (long long)s_cols);
+  int64_t tile = 0;
+  for (int i = 0; i < nb; ++i) {
+    const mxm_group_branch& b = br[i];
+    int e;
+    if (b.xa) {
+      int rpc = 0, nch = 0;
+      mxm_coldot_chunks(T, b.N, &rpc, &nch);
+      e = mxm_lora_bwd(b.dy, b.ldy, T, b.N, b.xa, b.ldxa, b.Bt, b.r, b.scale, q, ldq, s, s_cols, tile, b.dxa_out,
+                       b.ld_dxa, b.dB_out, part, rpc, nch, stream);
+    } else {
+      e = mxm_quant_rows_into(b.dy, T, b.N, b.ldy, q, ldq, s, s_cols, tile, stream);
+    }
+    if (e) return e;
+    tile += b.N / 128;
+  }
+  return MXM_OK;
+}
+
 // out = bf16(x + bf16(y + scale * xa B^T)), x / y / out [T, N] bf16 contiguous, xa [T, r] (row stride ldxa),
 // B [N, r] contiguous (reference res_lora, scripts/mxfp8.py:285-296).
 extern "C" int mxm_res_lora(const void* x, const void* y, const void* xa, int64_t ldxa, const void* B, int64_t T,

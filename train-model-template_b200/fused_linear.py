@@ -1,15 +1,21 @@
-"""Linears that share one input computed in ONE autograd node, on the B200 kernels: drop-in for the
-reference module of the same name (scripts/fused_linear.py).
+"""Linears that share one input, computed in ONE autograd node on the B200 kernels: drop-in for the
+reference module of the same name (scripts/fused_linear.py).  Public surface kept: ``group_linear``,
+``residual_add``, ``Deferred``, ``_part``, ``_cast`` / ``new_step`` and ``STATS`` (``fused_mlp`` imports
+the last three, scripts/fused_mlp.py:27; ``shared_prefix`` calls the first ones).
 
-* ``group_linear(x, mods, need_out, defer)`` -- q/k/v, qkv/z/b/a, o_proj ... as one node: x read once for all
-  LoRA A's, one MXFP8 quantization of x for the group, LoRA gradients into dx through one addmm; on the
-  MX path the backward reads each dy once (``mxfp8.lora_bwd``) and computes the group's dx as one MXFP8
-  GEMM against the concatenated W^T.
-* ``residual_add(x, y)`` -- the residual add, with the deferred LoRA term of o_proj / out_proj added in the
-  same kernel (``mxfp8.res_lora``).
-* ``_part``, ``_cast`` / ``new_step``, ``STATS`` -- the LoRA-layer decomposition, the per-step bf16 cast cache
-  and the path counters that ``fused_mlp`` imports (scripts/fused_mlp.py:27) and ``shared_prefix`` uses.
+A call ``group_linear(x, mods)`` is described by a ``_Layout``: the columns of the skinny matrix S
+(every LoRA A of the group, then the weights of thin frozen linears of <= 64 outputs) and, per output,
+whether its frozen weight is MXFP8 (``mxfp8.enable_mxfp8``).  Forward: x S^T once for the whole group
+(tensor-core rowdot), x quantized once for every MX output, each MX output one tcgen05 GEMM with its LoRA
+term accumulated in the same accumulator (or left to ``residual_add`` when deferred).  Backward, when the
+whole group is MX and bf16 (``_one_read_plan``): ONE native call (``mxm_group_lora_bwd``) reads each dy
+once for its MXFP8 codes (into the group's K-concatenated operand), its d(xa) and its dB; the group's
+dx is ONE MXFP8 GEMM against the concatenated W^T with dS S accumulated inside it, and dA = dS^T x one
+coldot.  Any other group (fp32, bf16 weights, a missing output gradient, a rank the kernels do not
+take) runs the general path, with the reference's arithmetic.
 """
+import collections
+
 import torch
 from torch import nn
 
@@ -17,34 +23,38 @@ _THIN = 64
 STATS = {"gộp": 0, "gọi thẳng": 0}
 
 
+def _bump(key):
+    STATS[key] = STATS.get(key, 0) + 1
+
+
 def _part(m):
     """(base Linear, A, B, scaling) of a PEFT LoRA Linear, (m, None, None, 1.0) for a plain frozen Linear,
-    None when the layer cannot take the fused path (scripts/fused_linear.py:30-48)."""
+    None when the layer cannot take the grouped path: trainable or biased base, merged / disabled adapters,
+    several active adapters, DoRA or another variant, a LoRA bias, dropout (scripts/fused_linear.py:30-48)."""
     base = getattr(m, "base_layer", None)
     if base is None:
-        if type(m) is nn.Linear and m.bias is None and not m.weight.requires_grad:
-            return m, None, None, 1.0
-        return None
+        plain = type(m) is nn.Linear and m.bias is None and not m.weight.requires_grad
+        return (m, None, None, 1.0) if plain else None
     if base.bias is not None or base.weight.requires_grad or m.merged or m.disable_adapters:
         return None
-    ads = [a for a in m.active_adapters if a in m.lora_A]
-    if len(ads) != 1:
+    active = [a for a in m.active_adapters if a in m.lora_A]
+    if len(active) != 1:
         return None
-    a = ads[0]
+    a = active[0]
     drop = m.lora_dropout[a]
-    if (a in getattr(m, "lora_variant", {}) or m.use_dora.get(a, False) or m.lora_B[a].bias is not None
-            or not (isinstance(drop, nn.Identity) or getattr(drop, "p", 1) == 0)):
+    no_drop = isinstance(drop, nn.Identity) or getattr(drop, "p", 1) == 0
+    if a in getattr(m, "lora_variant", {}) or m.use_dora.get(a, False) or m.lora_B[a].bias is not None or not no_drop:
         return None
     return base, m.lora_A[a].weight, m.lora_B[a].weight, m.scaling[a]
 
 
-def _mx(base):
+def _is_mx(base):
     return getattr(base, "_mx_w", None) is not None
 
 
-# bf16 copies of the LoRA parameters, made once per step (scripts/fused_linear.py:55-69).  The
-# optimizer updates parameters in place without bumping _version, so the cache is keyed by id and
-# cleared by new_step() at the start of each step.
+# Per-step cache of derived LoRA tensors (bf16 casts, concatenations, transposes).  Optimizers update the
+# parameters in place without bumping their version counter, so entries are keyed by parameter identity
+# and the whole cache is dropped by new_step() at the start of every step (scripts/fused_linear.py:55-69).
 _CAST = {}
 
 
@@ -53,229 +63,270 @@ def new_step():
 
 
 def _cast(key, make):
-    t = _CAST.get(key)
-    if t is None:
-        t = _CAST[key] = make()
-    return t
-
-
-# ------------------------------------------------------------------------------------------------ grouped linears
-def _base_mm(base, x2, dt, q):
-    """x2 @ W^T of a frozen base linear: the MXFP8 GEMM when enable_mxfp8 quantized it (q = MXFP8(x2)),
-    a plain matmul otherwise (scripts/fused_linear.py:72-76)."""
-    if _mx(base):
-        import mxfp8
-        return mxfp8.mx_mm(q[0], base._mx_w.t(), q[1], base._mx_ws)
-    return x2 @ base.weight.to(dt).t()
+    hit = _CAST.get(key)
+    if hit is None:
+        hit = _CAST[key] = make()
+    return hit
 
 
 def _compute_dtype(x):
     return torch.get_autocast_dtype("cuda") if torch.is_autocast_enabled("cuda") else x.dtype
 
 
-class _Group(torch.autograd.Function):
-    """Linears that share one input (q/k/v, qkv/z/b/a, gate/up, o_proj alone ...) as one autograd node
-    (scripts/fused_linear.py:79-196).  x is read once for every LoRA A of the group and for the weights of
-    thin frozen linears (<= _THIN outputs), stacked as the rows of one matrix S; the gradients of all
-    LoRA branches and thin linears reach dx through one addmm with S; dA for every branch is one GEMM.
-    Inputs after `defer`: (A, B) of each LoRA branch in group order."""
+Branch = collections.namedtuple("Branch", "out col rank scale")   # a LoRA branch: output, S column, r, s
+Thin = collections.namedtuple("Thin", "out col width")            # a thin frozen linear inside S
+
+
+class _Layout:
+    """Column layout of one group call.  S rows: the LoRA A's in output order, then thin frozen weights."""
+
+    def __init__(self, parts):
+        self.parts = parts
+        self.branches, self.thin, col = [], [], 0
+        for i, (base, A, B, s) in enumerate(parts):
+            if A is not None:
+                self.branches.append(Branch(i, col, A.shape[0], s))
+                col += A.shape[0]
+        self.lora_width = col
+        for i, (base, A, B, s) in enumerate(parts):
+            if A is None and not _is_mx(base) and base.weight.shape[0] <= _THIN:
+                self.thin.append(Thin(i, col, base.weight.shape[0]))
+                col += base.weight.shape[0]
+        self.width = col
+        self.thin_outs = {t.out for t in self.thin}
+        self.by_out = {b.out: b for b in self.branches}
+        self.mx = [i for i, p in enumerate(parts) if _is_mx(p[0])]
+
+    def s_rows(self):
+        return [self.parts[b.out][1] for b in self.branches] + [self.parts[t.out][0].weight for t in self.thin]
+
+
+def _rowdot_ok(x2, S):
+    return (x2.dtype == S.dtype == torch.bfloat16 and S.shape[0] in (16, 32, 64) and x2.shape[1] % 128 == 0
+            and x2.is_contiguous())
+
+
+def _skinny(x2, S):
+    """x2 @ S^T: the tensor-core rowdot for 16 / 32 / 64 bf16 columns, a plain matmul otherwise."""
+    if _rowdot_ok(x2, S):
+        import fused_mlp
+        return fused_mlp.rowdot(x2, S)
+    return x2 @ S.t()
+
+
+class _GroupFn(torch.autograd.Function):
+    """The group as one autograd node (scripts/fused_linear.py:79-196).  Inputs after `defer`: (A, B) of
+    every LoRA branch in output order."""
 
     @staticmethod
-    def forward(ctx, x, parts, need_out, defer, *ws):
-        ctx.set_materialize_grads(False)   # an unused output gives a None gradient, not zeros
+    def forward(ctx, x, lay, need_out, defer, *ws):
+        ctx.set_materialize_grads(False)   # an output nobody uses gets a None gradient, not zeros
         dt = _compute_dtype(x)
         lead, K = x.shape[:-1], x.shape[-1]
         x2 = x.reshape(-1, K)
         if x2.dtype != dt or not x2.is_contiguous():
             x2 = x2.to(dt).contiguous()
-        srows, Bs, lora, thin = [], [], [], []   # rows of S; bf16 B's; (part, row offset, rank, s); (part, offset, n)
-        for i, (base, A, B, s) in enumerate(parts):
-            if A is not None:
-                lora.append((i, sum(r.shape[0] for r in srows), A.shape[0], s))
-                srows.append(A)
-                Bs.append(_cast((id(B), dt), lambda B=B: B.detach().to(dt)))
-        for i, (base, A, B, s) in enumerate(parts):
-            if A is None and not _mx(base) and base.weight.shape[0] <= _THIN:
-                thin.append((i, sum(r.shape[0] for r in srows), base.weight.shape[0]))
-                srows.append(base.weight)
-        S = None
-        if srows:
-            S = _cast((tuple(id(r) for r in srows), dt), lambda: torch.cat([r.detach().to(dt) for r in srows]))
-        xS = x2 @ S.t() if S is not None else None
-        thin_idx = {i for i, _, _ in thin}
-        outs = [None] * len(parts)
+        rows = lay.s_rows()
+        S = _cast(("S", tuple(id(r) for r in rows), dt), lambda: torch.cat([r.detach().to(dt) for r in rows])) \
+            if rows else None
+        Bs = [_cast((id(lay.parts[b.out][2]), dt), lambda b=b: lay.parts[b.out][2].detach().to(dt).contiguous())
+              for b in lay.branches]
+        xS = _skinny(x2, S) if S is not None else None
+        outs = [None] * len(lay.parts)
         if need_out:
-            q = None
-            if any(_mx(p[0]) for p in parts):
-                import mxfp8
-                q = mxfp8.mx_quant(x2)           # one quantization for the whole group
-            for i, (base, A, B, s) in enumerate(parts):
-                if i not in thin_idx:
-                    outs[i] = _base_mm(base, x2, dt, q)
-            for j, (i, o, r, s) in enumerate(lora):
-                if defer is not None and _mx(parts[i][0]) and dt == torch.bfloat16:
-                    defer[i] = (xS[:, o:o + r], Bs[j], s)   # added by residual_add inside the residual kernel
-                else:
-                    outs[i].addmm_(xS[:, o:o + r], Bs[j].t(), alpha=s)
-        else:   # graph only (checkpoint recompute): x2 and xS are saved, nobody reads the outputs
-            STATS["bỏ đầu ra"] = STATS.get("bỏ đầu ra", 0) + 1
-            for i, (base, A, B, s) in enumerate(parts):
-                if i not in thin_idx:
+            _forward_outputs(lay, x2, xS, Bs, dt, defer, outs)
+        else:   # graph only (checkpoint recompute): nothing reads the outputs, the backward needs x2 and xS
+            _bump("bỏ đầu ra")
+            for i, (base, A, B, s) in enumerate(lay.parts):
+                if i not in lay.thin_outs:
                     outs[i] = x2.new_empty(x2.shape[0], base.out_features)
-        for i, o, n in thin:
-            outs[i] = xS[:, o:o + n].contiguous()
+        for t in lay.thin:
+            outs[t.out] = xS[:, t.col:t.col + t.width].contiguous()
         ctx.save_for_backward(x2, xS, S, *Bs)
-        ctx.meta = (parts, lora, thin, lead, K, dt, x.dtype)
+        ctx.lay, ctx.shape, ctx.dt = lay, (lead, K, x.dtype), dt
         return tuple(y.view(*lead, y.shape[-1]) for y in outs)
 
     @staticmethod
     def backward(ctx, *dys):
         x2, xS, S, *Bs = ctx.saved_tensors
-        parts, lora, thin, lead, K, dt, xdt = ctx.meta
+        lay, dt = ctx.lay, ctx.dt
         need_x = ctx.needs_input_grad[0]
         flat = [None if dy is None else dy.reshape(-1, dy.shape[-1]).to(dt) for dy in dys]
-        plan = _fused_bwd_plan(parts, flat, dt, need_x)
+        plan = _one_read_plan(lay, flat, dt, need_x, xS, Bs)
         if plan is not None:
-            return _fused_backward(ctx, x2, xS, S, Bs, flat, plan, need_x)
-        # the general path (scripts/fused_linear.py:132-196)
-        thin_idx = {i for i, _, _ in thin}
-        dx = None
-        if need_x:
-            for i, (base, A, B, s) in enumerate(parts):
-                dy = flat[i]
-                if dy is None or i in thin_idx:
-                    continue
-                if _mx(base):
-                    import mxfp8
-                    d = dy if dy.is_contiguous() else dy.contiguous()
-                    qd, sd = mxfp8.mx_quant(d)
-                    wt, wts = mxfp8.wt_of(base)
-                    g = mxfp8.mx_mm(qd, wt, sd, wts)
-                    dx = g if dx is None else dx.add_(g)
-                else:
-                    w = base.weight.to(dt)
-                    dx = dy @ w if dx is None else dx.addmm_(dy, w)
-        grads = [None] * (2 * len(lora))
-        cols, col_rows, live = [], [], []        # columns of dS, the S rows they multiply, active branches
-        for j, (i, o, r, s) in enumerate(lora):
-            dy = flat[i]
-            if dy is None:
-                continue
-            xa = xS[:, o:o + r]
-            dB, dxa = dy.t() @ xa, dy @ Bs[j]
-            if s != 1:
-                dB.mul_(s)
-                dxa.mul_(s)
-            grads[2 * j + 1] = dB
-            cols.append(dxa)
-            col_rows.append((o, r))
-            live.append(j)
-        n_live = sum(r for _, r in col_rows)
-        if need_x:
-            for i, o, n in thin:
-                if flat[i] is not None:
-                    cols.append(flat[i])
-                    col_rows.append((o, n))
-        if cols:
-            dS = torch.cat(cols, 1) if len(cols) > 1 else cols[0]
-            if need_x:
-                Sa = S if len(col_rows) == len(lora) + len(thin) else torch.cat([S[o:o + n] for o, n in col_rows])
-                dx = dS @ Sa if dx is None else dx.addmm_(dS, Sa)
-            if live:
-                dA = dS[:, :n_live].t() @ x2
-                c = 0
-                for j in live:
-                    r = lora[j][2]
-                    grads[2 * j] = dA[c:c + r]
-                    c += r
-        return _grads_out(ctx, dx, grads, lead, K, xdt)
+            dx, grads = _backward_one_read(lay, x2, xS, S, Bs, flat, plan, need_x)
+            _bump("lan ngược gộp")
+        else:
+            dx, grads = _backward_general(lay, x2, xS, S, Bs, flat, dt, need_x)
+        lead, K, xdt = ctx.shape
+        keep = ctx.needs_input_grad[4:]
+        grads = [g if (g is not None and keep[k]) else None for k, g in enumerate(grads)]
+        return (None if dx is None else dx.view(*lead, K).to(xdt), None, None, None, *grads)
 
 
-def _grads_out(ctx, dx, grads, lead, K, xdt):
-    ws_in = ctx.needs_input_grad[4:]
-    out = [None if (g is None or not ws_in[k]) else g for k, g in enumerate(grads)]
-    dx = None if dx is None else dx.view(*lead, K).to(xdt)
-    return (dx, None, None, None, *out)
-
-
-def _cdiv(a, b):
-    return -(-a // b)
-
-
-def _fused_bwd_plan(parts, flat, dt, need_x):
-    """The one-read backward applies when the compute dtype is bf16, every output has a gradient, every MX
-    branch is one enable_mxfp8 marked for it (mxfp8.FUSED_BWD) and, when dx is needed, the group's MX
-    weights form one concatenated W^T in group order: returns (MX branch indices, (mat2, scales) or None),
-    else None (scripts/fused_linear.py:203-216)."""
-    if dt != torch.bfloat16 or any(dy is None for dy in flat):
-        return None
-    mx_idx = [i for i, p in enumerate(parts) if _mx(p[0])]
-    if not mx_idx or not all(getattr(parts[i][0], "_mx_fbwd", False) for i in mx_idx):
-        return None
+def _forward_outputs(lay, x2, xS, Bs, dt, defer, outs):
+    """Frozen-weight products of the non-thin outputs with their LoRA terms: MX outputs on the tcgen05 GEMM
+    (x quantized once for the group), bf16 ones with a matmul."""
     import mxfp8
-    wt = mxfp8.group_wt([parts[i][0] for i in mx_idx]) if need_x else None
-    if need_x and wt is None:
-        return None
-    return mx_idx, wt
-
-
-def _fused_backward(ctx, x2, xS, S, Bs, flat, plan, need_x):
-    """_Group.backward on the one-read path (scripts/fused_linear.py:219-278): each MX branch's dy is read once
-    by mxfp8.lora_bwd (its MXFP8 into one K-concatenated buffer, its d(xa) into dS, its dB), and the
-    group's dx is ONE MXFP8 GEMM against the concatenated W^T (the branches add in fp32 inside it), plus
-    the bf16 branches and dS @ S."""
-    import mxfp8
-    parts, lora, thin, lead, K, dt, xdt = ctx.meta
-    mx_idx, wt = plan
-    T, dev = x2.shape[0], x2.device
-    branch = {i: (j, o, r, s) for j, (i, o, r, s) in enumerate(lora)}
-    n_lora = sum(r for _, _, r, _ in lora)
-    width = n_lora + (sum(n for _, _, n in thin) if need_x else 0)
-    dS = torch.empty((T, width), dtype=dt, device=dev) if width else None
-    grads = [None] * (2 * len(lora))
-    q = sbuf = None
-    if need_x:
-        n_mx = sum(flat[i].shape[1] for i in mx_idx)
-        q = torch.empty((T, n_mx), dtype=mxfp8.F8, device=dev)
-        sbuf = torch.empty(_cdiv(T, 128) * (n_mx // 128) * 512, dtype=torch.uint8, device=dev)
-    tile = 0
-    for i in mx_idx:
-        dy = flat[i] if flat[i].stride(1) == 1 else flat[i].contiguous()
-        if i in branch:
-            j, o, r, s = branch[i]
-            grads[2 * j + 1] = mxfp8.lora_bwd(dy, xS[:, o:o + r], Bs[j], s, q=q, s=sbuf, col_tile_off=tile,
-                                              dxa_out=dS[:, o:o + r])
-        elif need_x:
-            mxfp8.lora_bwd(dy, q=q, s=sbuf, col_tile_off=tile)
-        tile += dy.shape[1] // 128
-    for j, (i, o, r, s) in enumerate(lora):   # LoRA over a bf16 (non-MX) base: as on the general path
-        if i in mx_idx:
+    qx = mxfp8.mx_quant(x2) if lay.mx else None
+    for i, (base, A, B, s) in enumerate(lay.parts):
+        if i in lay.thin_outs:
             continue
-        dy = flat[i]
-        dB = dy.t() @ xS[:, o:o + r]
-        dS[:, o:o + r] = dy @ Bs[j]
-        if s != 1:
-            dB.mul_(s)
-            dS[:, o:o + r].mul_(s)
-        grads[2 * j + 1] = dB
+        br = lay.by_out.get(i)
+        xa = None if br is None else xS[:, br.col:br.col + br.rank]
+        j = None if br is None else lay.branches.index(br)
+        if _is_mx(base):
+            if br is not None and defer is not None and dt == torch.bfloat16:
+                outs[i] = mxfp8.mx_mm(qx[0], base._mx_w.t(), qx[1], base._mx_ws)
+                defer[i] = (xa, Bs[j], s)          # residual_add adds the LoRA term in its kernel
+                continue
+            if br is not None:
+                Bsc = _cast(("scaled", id(B), s, dt), lambda: (Bs[j].float() * s).to(dt).contiguous())
+                if mxfp8.mx_mm_lora_ok(xa, Bsc):
+                    outs[i] = mxfp8.mx_mm_lora(qx[0], base._mx_w.t(), qx[1], base._mx_ws, xa, Bsc)
+                    continue
+            outs[i] = mxfp8.mx_mm(qx[0], base._mx_w.t(), qx[1], base._mx_ws)
+        else:
+            outs[i] = x2 @ base.weight.to(dt).t()
+        if br is not None:
+            outs[i].addmm_(xa, Bs[j].t(), alpha=s)
+
+
+# ------------------------------------------------------------------------------------------------ backward
+def _one_read_plan(lay, flat, dt, need_x, xS, Bs):
+    """The one-read backward applies when the compute dtype is bf16, every output has a gradient, every MX
+    output was marked for it by enable_mxfp8 (mxfp8.FUSED_BWD), the group's MX weights form one
+    concatenated W^T in output order (when dx is needed), every bf16-base LoRA branch is absent and the
+    kernels take every branch (scripts/fused_linear.py:203-216).  Returns the W^T operand (or True when dx
+    is not needed), else None."""
+    import mxfp8
+    if dt != torch.bfloat16 or any(d is None for d in flat) or not lay.mx:
+        return None
+    if not all(getattr(lay.parts[i][0], "_mx_fbwd", False) for i in lay.mx):
+        return None
+    if any(not _is_mx(lay.parts[b.out][0]) for b in lay.branches):
+        return None
+    for i in lay.mx:
+        br = lay.by_out.get(i)
+        if not mxfp8.lora_bwd_ok(flat[i], None if br is None else xS[:, br.col:br.col + br.rank], None
+                                 if br is None else Bs[lay.branches.index(br)]):
+            return None
+    if not need_x:
+        return True
+    return mxfp8.group_wt([lay.parts[i][0] for i in lay.mx])
+
+
+def _backward_one_read(lay, x2, xS, S, Bs, flat, wt, need_x):
+    """(scripts/fused_linear.py:219-278): per MX output one read of dy in ONE native call, then dx as ONE
+    MX GEMM with dS S accumulated inside it and dA = dS^T x2."""
+    import fused_mlp
+    import mxfp8
+    T, dev, dt = x2.shape[0], x2.device, x2.dtype
+    dS = torch.empty((T, lay.width), dtype=dt, device=dev) if lay.width else None
+    grads = [None] * (2 * len(lay.branches))
+    q = s = None
+    if need_x:
+        n_mx = sum(flat[i].shape[1] for i in lay.mx)
+        q = torch.empty((T, n_mx), dtype=mxfp8.F8, device=dev)
+        s = torch.empty(mxfp8.scale_numel(T, n_mx), dtype=torch.uint8, device=dev)
+    work = []
+    for i in lay.mx:
+        dy = flat[i] if flat[i].stride(1) == 1 else flat[i].contiguous()
+        flat[i] = dy
+        br = lay.by_out.get(i)
+        if br is None:
+            work.append((dy, None, None, 0.0, None, None))
+            continue
+        j = lay.branches.index(br)
+        Bt = _cast(("T", id(lay.parts[i][2]), dt), lambda j=j: Bs[j].t().contiguous())
+        grads[2 * j + 1] = torch.empty((dy.shape[1], br.rank), dtype=torch.float32, device=dev)
+        work.append((dy, xS[:, br.col:br.col + br.rank], Bt, br.scale, dS[:, br.col:br.col + br.rank],
+                     grads[2 * j + 1]))
+    if q is None:   # no dx: only the LoRA branches have work
+        work = [w for w in work if w[1] is not None]
+    if work:
+        mxfp8.group_lora_bwd(T, work, q, s, device=dev)
     dx = None
     if need_x:
-        dx = mxfp8.mx_mm(q, wt[0], sbuf.view(mxfp8.E8), wt[1])
-        del q, sbuf
-        thin_idx = {i for i, _, _ in thin}
-        for i, (base, A, B, s) in enumerate(parts):   # plain bf16 linears (neither MX nor thin)
-            if i not in thin_idx and not _mx(base):
+        for t in lay.thin:
+            dS[:, t.col:t.col + t.width].copy_(flat[t.out])
+        sv = s.view(mxfp8.E8)
+        ST = _cast(("ST", id(S)), lambda: S.t().contiguous()) if S is not None else None
+        if dS is not None and mxfp8.mx_mm_lora_ok(dS, ST):
+            dx = mxfp8.mx_mm_lora(q, wt[0], sv, wt[1], dS, ST)            # dy W (all MX outputs) + dS S
+        else:
+            dx = mxfp8.mx_mm(q, wt[0], sv, wt[1])
+            if dS is not None:
+                dx.addmm_(dS, S)
+        del q, s
+        for i, (base, A, B, sc) in enumerate(lay.parts):                  # plain bf16 linears, if any
+            if i not in lay.thin_outs and not _is_mx(base):
                 dx.addmm_(flat[i], base.weight.to(dt))
-        for i, o, n in thin:
-            dS[:, o:o + n].copy_(flat[i])
-        if dS is not None:
-            dx.addmm_(dS, S)
-    if lora:
-        dA = dS[:, :n_lora].t() @ x2
-        for j, (i, o, r, s) in enumerate(lora):
-            grads[2 * j] = dA[o:o + r]
-    STATS["lan ngược gộp"] = STATS.get("lan ngược gộp", 0) + 1
-    return _grads_out(ctx, dx, grads, lead, K, xdt)
+    if lay.branches:
+        n = lay.lora_width
+        if n in (16, 32, 64) and x2.shape[1] % 64 == 0:
+            dA = fused_mlp.coldot(x2, dS[:, :n], transpose_out=True)     # [n, K] = dS^T x2
+        else:
+            dA = dS[:, :n].t() @ x2
+        for j, br in enumerate(lay.branches):
+            grads[2 * j] = dA[br.col:br.col + br.rank]
+    return dx, grads
+
+
+def _backward_general(lay, x2, xS, S, Bs, flat, dt, need_x):
+    """The general path (scripts/fused_linear.py:132-196): frozen-weight dx per output (MX outputs through
+    MXFP8(dy) and their own W^T), LoRA dB / d(xa) per branch, thin linears' dy as columns of dS, then
+    dx += dS S and dA = dS^T x2 for the branches that got a gradient."""
+    import mxfp8
+    dx = None
+    if need_x:
+        for i, (base, A, B, s) in enumerate(lay.parts):
+            dy = flat[i]
+            if dy is None or i in lay.thin_outs:
+                continue
+            if _is_mx(base):
+                d = dy if dy.is_contiguous() else dy.contiguous()
+                qd, sd = mxfp8.mx_quant(d)
+                mat2, ws = mxfp8.wt_of(base)
+                g = mxfp8.mx_mm(qd, mat2, sd, ws)
+                dx = g if dx is None else dx.add_(g)
+            else:
+                w = base.weight.to(dt)
+                dx = dy @ w if dx is None else dx.addmm_(dy, w)
+    grads = [None] * (2 * len(lay.branches))
+    cols, srows, live = [], [], []
+    for j, br in enumerate(lay.branches):
+        dy = flat[br.out]
+        if dy is None:
+            continue
+        xa = xS[:, br.col:br.col + br.rank]
+        dB, dxa = dy.t() @ xa, dy @ Bs[j]
+        if br.scale != 1:
+            dB.mul_(br.scale)
+            dxa.mul_(br.scale)
+        grads[2 * j + 1] = dB
+        cols.append(dxa)
+        srows.append((br.col, br.rank))
+        live.append(j)
+    n_live = sum(w for _, w in srows)
+    if need_x:
+        for t in lay.thin:
+            if flat[t.out] is not None:
+                cols.append(flat[t.out])
+                srows.append((t.col, t.width))
+    if cols:
+        dS = torch.cat(cols, 1) if len(cols) > 1 else cols[0]
+        if need_x:
+            Sa = S if sum(w for _, w in srows) == lay.width else torch.cat([S[c:c + w] for c, w in srows])
+            dx = dS @ Sa if dx is None else dx.addmm_(dS, Sa)
+        if live:
+            dA = dS[:, :n_live].t() @ x2
+            c = 0
+            for j in live:
+                r = lay.branches[j].rank
+                grads[2 * j] = dA[c:c + r]
+                c += r
+    return dx, grads
 
 
 # ------------------------------------------------------------------------------------------------ residual + LoRA
@@ -284,10 +335,9 @@ class Deferred(tuple):
     residual_add adds inside the residual kernel (scripts/fused_linear.py:282-283)."""
 
 
-class _ResidualLoRA(torch.autograd.Function):
-    """x + (y + s * xa @ B^T) in one kernel (scripts/fused_linear.py:286-299).  xa and B come detached: the
-    LoRA branch's gradients (dB, d(xa) -> dA, dx) are produced by _Group.backward from the same dy, so
-    this node only passes dy through to x and y."""
+class _ResidualAdd(torch.autograd.Function):
+    """x + (y + s * xa @ B^T) in one kernel (scripts/fused_linear.py:286-299).  xa and B arrive detached: the
+    LoRA branch's gradients come from the group's backward (same dy), so this node passes dy to x and y."""
 
     @staticmethod
     def forward(ctx, x, y, xa, B, s):
@@ -302,31 +352,32 @@ class _ResidualLoRA(torch.autograd.Function):
 
 def residual_add(x, y):
     """x + y; when y is a Deferred (group_linear(..., defer=True)) its LoRA term is added inside the
-    residual kernel (scripts/fused_linear.py:302-312)."""
+    residual kernel (scripts/fused_linear.py:302-312), or by an addmm where the kernel does not apply."""
     if not isinstance(y, Deferred):
         return x + y
+    import mxfp8
     y, xa, B, s = y
     N = x.shape[-1]
-    if (x.dtype == y.dtype == torch.bfloat16 and x.shape == y.shape and x.is_contiguous() and y.is_contiguous()
-            and N % 128 == 0 and xa.stride(1) == 1 and B.is_contiguous()):
-        STATS["residual LoRA"] = STATS.get("residual LoRA", 0) + 1
-        return _ResidualLoRA.apply(x, y, xa, B, s)
+    if x.shape == y.shape and mxfp8.res_lora_ok(x.reshape(-1, N), y.reshape(-1, N), xa, B):
+        _bump("residual LoRA")
+        return _ResidualAdd.apply(x, y, xa, B, s)
     return x + torch.addmm(y.reshape(-1, N), xa, B.t(), alpha=s).view(y.shape)
 
 
 def group_linear(x, mods, need_out=True, defer=False):
-    """(m(x) for m in mods) with the grouping above (scripts/fused_linear.py:315-335).  need_out=False builds
-    only the graph for backward (the outputs are uninitialized; gradients are unchanged) -- the last
-    layer of a checkpointed segment being recomputed.  defer=True returns the MX bf16 outputs that carry
-    a LoRA branch as Deferred, for a residual_add that follows right away."""
+    """(m(x) for m in mods) through one node (scripts/fused_linear.py:315-335).  need_out=False builds only
+    the graph for backward (outputs uninitialized, gradients unchanged) -- the last layer of a checkpointed
+    segment being recomputed.  defer=True returns the MX bf16 outputs that carry a LoRA branch as Deferred,
+    for a residual_add that follows right away."""
     parts = tuple(_part(m) for m in mods)
     if any(p is None for p in parts):
         STATS["gọi thẳng"] += 1
         return tuple(m(x) for m in mods)
     STATS["gộp"] += 1
-    ws = [w for p in parts if p[1] is not None for w in (p[1], p[2])]
+    lay = _Layout(parts)
+    ws = [w for b in lay.branches for w in (parts[b.out][1], parts[b.out][2])]
     box = {} if defer and need_out else None
-    outs = _Group.apply(x, parts, need_out, box, *ws)
+    outs = _GroupFn.apply(x, lay, need_out, box, *ws)
     if not box:
         return outs
     return tuple(Deferred((y,) + box[i]) if i in box else y for i, y in enumerate(outs))

@@ -109,18 +109,9 @@ def lora_prep(Ag, Au, Bg, Bu, Ad, Bd, s_d):
     return tuple(p.view(sh) for p, sh in zip(torch.split(buf, sizes), shapes))
 
 
-def mx_mm_lora(a, b, scale_a, scale_b, L, Rm):
-    """bf16(mx_mm(a, b, ...) + L @ Rm^T): the MX GEMM with the rank-r LoRA term accumulated on the tensor
-    core (Rm [N, r] bf16 contiguous already carries the LoRA scaling)."""
-    M, K = a.shape
-    N = b.shape[1]
-    bt = b.t()
-    kr = L.shape[1]
-    assert Rm.is_contiguous() and Rm.shape == (N, kr) and L.stride(1) == 1
-    out = torch.empty((M, N), dtype=torch.bfloat16, device=a.device)
-    _nx.call("mxm_gemm_lora", _nx.ptr(a), a.stride(0), _nx.ptr(scale_a), _nx.ptr(bt), bt.stride(0), _nx.ptr(scale_b),
-             M, N, K, _nx.ptr(L), L.stride(0), _nx.ptr(Rm), kr, _nx.ptr(out), out.stride(0), _nx.stream_of(a))
-    return out
+# the MX GEMM with the LoRA term in its accumulator (mxfp8.mx_mm_lora); a module-level name so that callers
+# and benchmarks can reach it as fused_mlp.mx_mm_lora
+mx_mm_lora = mxfp8.mx_mm_lora
 
 
 # ------------------------------------------------------------------------------------------------ epilogues
