@@ -194,6 +194,18 @@ MX_DEV void tma_store_2d(const CUtensorMap* map, const void* src, int32_t x, int
   asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];"
                ::"l"(map), "r"(x), "r"(y), "r"(smem_u32(src)) : "memory");
 }
+// L2 policy for data written once and not read again soon (streamed outputs): evict first, so the lines
+// of a GEMM's operands, reused across tiles, are the ones that stay in L2.
+MX_DEV uint64_t l2_evict_first() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+// tma_store_2d with an L2 cache policy (l2_evict_first for streamed outputs).
+MX_DEV void tma_store_2d_hint(const CUtensorMap* map, const void* src, int32_t x, int32_t y, uint64_t pol) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group.L2::cache_hint [%0, {%1, %2}], [%3], %4;"
+               ::"l"(map), "r"(x), "r"(y), "r"(smem_u32(src)), "l"(pol) : "memory");
+}
 MX_DEV void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 // The shared-memory sources of this thread's committed bulk stores have been read.
 MX_DEV void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }

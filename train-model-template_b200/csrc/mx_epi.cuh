@@ -34,6 +34,15 @@ MX_DEV void stg8_if(void* p, uint32_t v, bool pred) {
   asm volatile("{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %2, 0;\n\t@q st.global.b8 [%0], %1;\n\t}" ::"l"(p),
                "h"((uint16_t)v), "r"((int)pred));
 }
+// the same with an L2 cache policy (evict-first for streamed outputs)
+MX_DEV void stg64_if_hint(void* p, uint32_t lo, uint32_t hi, bool pred, uint64_t pol) {
+  asm volatile("{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %3, 0;\n\t@q st.global.L2::cache_hint.v2.b32 [%0], {%1, %2}, %4;\n\t}"
+               ::"l"(p), "r"(lo), "r"(hi), "r"((int)pred), "l"(pol));
+}
+MX_DEV void stg8_if_hint(void* p, uint32_t v, bool pred, uint64_t pol) {
+  asm volatile("{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %2, 0;\n\t@q st.global.L2::cache_hint.b8 [%0], %1, %3;\n\t}"
+               ::"l"(p), "h"((uint16_t)v), "r"((int)pred), "l"(pol));
+}
 
 // ---- packed helpers: two values per instruction (Blackwell f32x2 ALU ops, bf16x2 conversions)
 MX_DEV float2 up2(uint32_t p) { return make_float2(bf16_lo(p), bf16_hi(p)); }
@@ -72,6 +81,7 @@ struct QRows {
   uint8_t* code[2];
   uint8_t* scale[2];
   bool live[2], slive[2];
+  uint64_t pol;   // L2 policy of the code / scale stores (evict first: the outputs are streamed)
 };
 MX_DEV QRows qrows_init(int64_t row_g, int64_t T, int64_t Tpad, uint8_t* q, int64_t ldq, uint8_t* s, int64_t scols,
                         int t) {
@@ -84,6 +94,7 @@ MX_DEV QRows qrows_init(int64_t row_g, int64_t T, int64_t Tpad, uint8_t* q, int6
     r.code[h] = q ? q + (r.live[h] ? row : 0) * ldq + 2 * t : nullptr;
     r.scale[h] = s ? s + mx_scale_offset(row < Tpad ? row : 0, 0, scols) : nullptr;
   }
+  r.pol = l2_evict_first();
   return r;
 }
 
@@ -126,8 +137,8 @@ MX_DEV void quant_block16p(const uint32_t (&pk)[4][2], const QRows& qr, int64_t 
     }
     uint32_t r0 = __byte_perm(c[0], c[1], 0x5410), r1 = __byte_perm(c[2], c[3], 0x5410);
     quad_transpose16(r0, r1, t);
-    stg64_if(qr.code[h] + col0 + 6 * t, r0, r1, qr.live[h]);   // code[h] already points at column 2t
-    stg8_if(qr.scale[h] + soff, e, qr.slive[h]);
+    stg64_if_hint(qr.code[h] + col0 + 6 * t, r0, r1, qr.live[h], qr.pol);   // code[h] points at column 2t
+    stg8_if_hint(qr.scale[h] + soff, e, qr.slive[h], qr.pol);
   }
 }
 

@@ -234,6 +234,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         // once the previous store has read it
         uint8_t* buf = sOut + (warp - EPI_WARP0) * 2048;
         const uint32_t sb0 = smem_u32(buf) + (uint32_t)lane * 64;
+        const uint64_t pol = l2_evict_first();   // dh is streamed to the backward epilogue
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           if (lane == 0) bulk_wait_read0();
@@ -251,7 +252,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           fence_proxy_async();
           __syncwarp();
           if (lane == 0) {
-            tma_store_2d(&tmL, buf, tn * BN + half * 128 + c * 32, tm * BM + q * 32);
+            tma_store_2d_hint(&tmL, buf, tn * BN + half * 128 + c * 32, tm * BM + q * 32, pol);
             bulk_commit();
           }
         }
@@ -324,7 +325,7 @@ MX_DEV void glu_body(const CUtensorMap* tmA, const CUtensorMap* tmB, const CUten
                      const CUtensorMap* tmSB, const uint8_t* __restrict__ sa, const uint8_t* __restrict__ sb, int M,
                      int N, int K, const __nv_bfloat16* __restrict__ xs, const __nv_bfloat16* __restrict__ bg,
                      const __nv_bfloat16* __restrict__ bu, const __nv_bfloat16* __restrict__ ad, float s_g, float s_u,
-                     uint8_t* __restrict__ qh, uint8_t* __restrict__ sh, float* __restrict__ xsd_part, int per,
+                     uint8_t* __restrict__ qh, uint8_t* __restrict__ sh, float* __restrict__ xsd_part, int chunk,
                      int* err) {
   constexpr int STAGES = glu_stages<PAIR>(), B_STAGE = glu_bstage<PAIR>(), KS = R / 16;
   constexpr int TM_ROWS = PAIR ? 256 : BM;                 // rows of one tile (of the pair)
@@ -351,9 +352,20 @@ MX_DEV void glu_body(const CUtensorMap* tmA, const CUtensorMap* tmB, const CUten
   const int unit = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;   // CTA or pair
   const int num_m = (M + TM_ROWS - 1) / TM_ROWS;
   const int num_n = N / 128;
-  const int num_tiles = num_m * num_n;
   const int KT = K / BK;
-  const int t_lo = unit * per, t_hi = min(t_lo + per, num_tiles);
+  // Schedule: a row block's column tiles are cut into chunks of `chunk` consecutive tiles (chunk divides
+  // num_n); unit u takes chunks u, u + units, u + 2 units, ... in order, so at any time the units work on
+  // neighbouring chunks -- a few row blocks of A and all of W_gu stay in L2 -- and each chunk's xS_down
+  // partial goes to slot (chunk index within its row block).
+  const int units = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
+  const int ncpr = num_n / chunk;
+  const int num_chunks = num_m * ncpr;
+  const int my_tiles = unit < num_chunks ? ((num_chunks - 1 - unit) / units + 1) * chunk : 0;
+  auto tile_of = [&](int i, int& tm, int& tn) {
+    const int c = unit + (i / chunk) * units;
+    tm = c / ncpr;
+    tn = (c % ncpr) * chunk + i % chunk;
+  };
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < STAGES; ++i) {
@@ -392,8 +404,9 @@ MX_DEV void glu_body(const CUtensorMap* tmA, const CUtensorMap* tmB, const CUten
     int stage = 0, issued = 0;
     uint32_t phase = 0;
     bool ok = true;
-    for (int tile = t_lo; tile < t_hi && ok; ++tile) {
-      const int tm = tile / num_n, tn = tile % num_n;
+    for (int i = 0; i < my_tiles && ok; ++i) {
+      int tm, tn;
+      tile_of(i, tm, tn);
       for (int kt = 0; kt < KT; ++kt) {
         if (!mbar_wait(&empty[stage], phase ^ 1, err, MX_DEV_TIMEOUT_PRODUCER)) {
           ok = false;
@@ -439,7 +452,7 @@ MX_DEV void glu_body(const CUtensorMap* tmA, const CUtensorMap* tmB, const CUten
     int stage = 0;
     uint32_t phase = 0, acc_phase = 0;
     bool ok = true;
-    for (int tile = t_lo; tile < t_hi && ok; ++tile) {
+    for (int i = 0; i < my_tiles && ok; ++i) {
       if (!mbar_wait(tmem_empty, acc_phase ^ 1, err, MX_DEV_TIMEOUT_MMA_TMEM)) break;
       tc_fence_after();
       for (int kt = 0; kt < KT; ++kt) {
@@ -518,10 +531,8 @@ MX_DEV void glu_body(const CUtensorMap* tmA, const CUtensorMap* tmB, const CUten
     float accx[R / 8][4];
     uint32_t axg[KS][4], axu[KS][4];
     QRows qr{};
-    int cur_tm = -1;
     int64_t ra = 0, rb = 0;
-    auto flush = [&](int tm_done) {   // this unit's partial of xS_down for its rows of row block tm_done
-      const int slot = unit - (tm_done * num_n) / per;
+    auto flush = [&](int slot) {   // this chunk's partial of xS_down for this warp's rows
       float* P = xsd_part + (int64_t)slot * M * R;
 #pragma unroll
       for (int jt = 0; jt < R / 8; ++jt) {
@@ -531,12 +542,11 @@ MX_DEV void glu_body(const CUtensorMap* tmA, const CUtensorMap* tmB, const CUten
       }
     };
     uint32_t acc_phase = 0;
-    for (int tile = t_lo; tile < t_hi; ++tile) {
-      const int tm = tile / num_n, tn = tile % num_n;
+    for (int i = 0; i < my_tiles; ++i) {
+      int tm, tn;
+      tile_of(i, tm, tn);
       const int64_t rowb = (int64_t)tm * TM_ROWS + rank * BM;   // this CTA's first row of the tile
-      if (tm != cur_tm) {
-        if (cur_tm >= 0) flush(cur_tm);
-        cur_tm = tm;
+      if (i % chunk == 0) {              // a new chunk: this warp's rows of xs, zeroed xS_down sums
         ra = rowb + e * 16 + g;
         rb = ra + 8;
         const bool va = ra < M, vb = rb < M;
@@ -627,9 +637,10 @@ MX_DEV void glu_body(const CUtensorMap* tmA, const CUtensorMap* tmB, const CUten
         const uint32_t tbg = s_bg + sbk * (64 * R * 2), tbu = s_bu + sbk * (64 * R * 2), tad = s_ad + sbk * (R * 128);
 #pragma unroll
         for (int b = 0; b < 2; ++b) {
-          if (et == 0) {   // box (gate / up) x (sub-tile) number 2 sbk + b
+          if (et == 0) {   // box (gate / up) x (sub-tile) number 2 sbk + b; gu is next read by the backward
             const int bx = 2 * sbk + b, hh = bx >> 1, c2 = bx & 1;
-            tma_store_2d(tmG, stg + (hh * 2 + c2) * (128 * 128), hh * N + tn * 128 + c2 * 64, (int)rowb);
+            tma_store_2d_hint(tmG, stg + (hh * 2 + c2) * (128 * 128), hh * N + tn * 128 + c2 * 64, (int)rowb,
+                              qr.pol);
             bulk_commit();
           }
           uint32_t hp[4][2];
@@ -679,9 +690,9 @@ MX_DEV void glu_body(const CUtensorMap* tmA, const CUtensorMap* tmB, const CUten
       }
       if (et == 0) bulk_wait_read0();   // the gu stores have read the staged tile
       epi_sync();   // staged tile and slices are free for the next tile
+      if (i % chunk == chunk - 1) flush((unit + (i / chunk) * units) % ncpr);
     }
     if (et == 0) bulk_wait0();
-    if (cur_tm >= 0) flush(cur_tm);
   }
 
   tc_fence_before();
@@ -703,9 +714,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                   const uint8_t* __restrict__ sb, int M, int N, int K, const __nv_bfloat16* __restrict__ xs,
                   const __nv_bfloat16* __restrict__ bg, const __nv_bfloat16* __restrict__ bu,
                   const __nv_bfloat16* __restrict__ ad, float s_g, float s_u, uint8_t* __restrict__ qh,
-                  uint8_t* __restrict__ sh, float* __restrict__ xsd_part, int per, int* err) {
+                  uint8_t* __restrict__ sh, float* __restrict__ xsd_part, int chunk, int* err) {
   glu_body<R, false>(&tmA, &tmB, &tmG, nullptr, nullptr, sa, sb, M, N, K, xs, bg, bu, ad, s_g, s_u, qh, sh, xsd_part,
-                     per, err);
+                     chunk, err);
 }
 
 // CTA-pair launch shape: scale blocks come in by TMA as [blocks * KT * 2, 256] byte tensors (tmSA, tmSB)
@@ -716,21 +727,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
                    const __grid_constant__ CUtensorMap tmSB, int M, int N, int K, const __nv_bfloat16* __restrict__ xs,
                    const __nv_bfloat16* __restrict__ bg, const __nv_bfloat16* __restrict__ bu,
                    const __nv_bfloat16* __restrict__ ad, float s_g, float s_u, uint8_t* __restrict__ qh,
-                   uint8_t* __restrict__ sh, float* __restrict__ xsd_part, int per, int* err) {
+                   uint8_t* __restrict__ sh, float* __restrict__ xsd_part, int chunk, int* err) {
   glu_body<R, true>(&tmA, &tmB, &tmG, &tmSA, &tmSB, nullptr, nullptr, M, N, K, xs, bg, bu, ad, s_g, s_u, qh, sh,
-                    xsd_part, per, err);
+                    xsd_part, chunk, err);
 }
 
-// xsd [M, R] bf16 = the fixed-order sum of the units' partials of each row block of `rows_blk` rows
-// (k_mx_gemm_glu: 128-row blocks, one partial per CTA; k_mx_gemm_glu2: 256-row blocks, one per pair).
-__global__ void k_glu_xsd_reduce(const float* __restrict__ part, int M, int R, int num_n, int per, int rows_blk,
+// xsd [M, R] bf16 = the fixed-order sum over the `slots` chunk partials (chunk 0, 1, .. of each row block).
+__global__ void k_glu_xsd_reduce(const float* __restrict__ part, int M, int R, int slots,
                                  __nv_bfloat16* __restrict__ xsd) {
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < (int64_t)M * R; i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t row = i / R;
-    const int tm = (int)(row / rows_blk);
-    const int c_lo = (tm * num_n) / per, c_hi = ((tm + 1) * num_n - 1) / per;
     float v = 0.f;
-    for (int c = 0; c <= c_hi - c_lo; ++c) v += part[(int64_t)c * M * R + i];
+    for (int c = 0; c < slots; ++c) v += part[(int64_t)c * M * R + i];
     xsd[i] = __float2bfloat16_rn(v);
   }
 }
@@ -860,14 +867,29 @@ extern "C" int mxm_gemm_glu_partition(int64_t M, int64_t N, int* per, int* grid,
   MX_CHECK_ARG(M >= 1 && N >= 128 && N % 128 == 0 && per && grid && slots, "mxm_gemm_glu_partition: bad args");
   // units: CTA pairs over 256-row tiles when they fit, otherwise single CTAs over 128-row tiles
   const bool pair = glu_use_pairs(M);
-  const int64_t rows = pair ? 256 : BM, units = pair ? glu_pairs() : mxm_num_sms();
-  const int64_t num_n = N / 128, tiles = ((M + rows - 1) / rows) * num_n;
-  int64_t g = tiles < units ? tiles : units;
-  const int64_t p = (tiles + g - 1) / g;
-  g = (tiles + p - 1) / p;
-  *per = (int)p;
-  *grid = (int)(pair ? 2 * g : g);
-  *slots = (int)((num_n + p - 1) / p + 1);   // units that can touch one row block
+  const int64_t rows = pair ? 256 : BM, units_max = pair ? glu_pairs() : mxm_num_sms();
+  const int64_t num_m = (M + rows - 1) / rows, num_n = N / 128;
+  // chunk = column tiles per chunk, a divisor of num_n: the one with the least estimated time, counting the
+  // busiest unit's tiles (a tile ~ rows x 256 x 2048 x 2 FLOP at ~2.4 PFLOP/s over the units) and the
+  // xS_down partials (slots x M x 16 fp32, written and read back, at ~6 TB/s)
+  const double t_tile = 2.0 * rows * 256 * 2048 / (2.4e15 / (double)units_max);
+  int64_t best_c = 1;
+  double best_t = 1e30;
+  for (int64_t c = 1; c <= num_n; ++c) {
+    if (num_n % c) continue;
+    const int64_t chunks = num_m * (num_n / c);
+    const int64_t busiest = (chunks + units_max - 1) / units_max * c;
+    const double t = busiest * t_tile + (double)(num_n / c) * (double)M * 16 * 4 * 2 / 6e12;
+    if (t < best_t * (1.0 - 1e-9)) {
+      best_t = t;
+      best_c = c;
+    }
+  }
+  const int64_t chunks = num_m * (num_n / best_c);
+  const int64_t u = chunks < units_max ? chunks : units_max;
+  *per = (int)best_c;
+  *grid = (int)(pair ? 2 * u : u);
+  *slots = (int)(num_n / best_c);   // chunks per row block: one xS_down partial each
   return MXM_OK;
 }
 
@@ -911,7 +933,7 @@ extern "C" int mxm_gemm_glu(const void* qa, int64_t lda, const void* sa, const v
     k_mx_gemm_glu2<16><<<grid, NUM_THREADS, glu_smem<true>(16), st>>>(
         tmA, tmB, tmG, tmSA, tmSB, (int)M, (int)N, (int)K, (const __nv_bfloat16*)xs, (const __nv_bfloat16*)bg,
         (const __nv_bfloat16*)bu, (const __nv_bfloat16*)ad, s_g, s_u, (uint8_t*)qh, (uint8_t*)sh, (float*)xsd_part, per,
-        mx_dev_error_ptr());
+        mx_dev_error_ptr());   // per: column tiles per chunk
   } else {
     static bool attr_done[64] = {};
     int dev = 0;
@@ -932,8 +954,7 @@ extern "C" int mxm_gemm_glu(const void* qa, int64_t lda, const void* sa, const v
   if (int e = mx_launch_status("gemm glu")) return e;
   const int64_t n = M * r;
   const int rg = (int)std::min<int64_t>((n + 255) / 256, (int64_t)mxm_num_sms() * 8);
-  k_glu_xsd_reduce<<<rg, 256, 0, st>>>((const float*)xsd_part, (int)M, r, (int)(N / 128), per, pair ? 256 : BM,
-                                       (__nv_bfloat16*)xsd);
+  k_glu_xsd_reduce<<<rg, 256, 0, st>>>((const float*)xsd_part, (int)M, r, slots, (__nv_bfloat16*)xsd);
   mx_note_launch();
   return mx_launch_status("gemm glu xsd reduce");
 }
