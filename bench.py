@@ -462,7 +462,8 @@ def run_ours(a):
                          "tflops": v[1] / (v[0] * 1e-3) / 1e12, "frac": v[1] / (v[0] * 1e-3) / 1e12 / peak}
                      for k, v in sorted(per_kind.items())}
     tok = total_tokens * L
-    step_tflops = FLOP_PER_TOKEN * tok / (ms * 1e-3) / 1e12
+    step_tflops = FLOP_PER_TOKEN * tok / (ms * 1e-3) / 1e12     # whole job
+    gpu_tflops = step_tflops / world                            # per GPU: what the roofline compares
     traffic = GEMM_TRAFFIC_BYTES.get(T)
     line = {
         "metric": METRIC, "value": tok / (ms * 1e-3), "unit": UNIT, "n_gpus": world, "steps": a.steps,
@@ -480,10 +481,10 @@ def run_ours(a):
                                "with the fused forward epilogue, k_mx_gemm down / dh / dx)",
                      "flops_per_step": g_fl / a.steps,
                      "per_launch": launches_gemm,
-                     "step_frac": step_tflops / peak,
+                     "step_frac": gpu_tflops / peak,
                      "frac_vs_burst": (achieved / peak_burst) if achieved else None,
                      "frac_vs_sustained": (achieved / peak_sus) if achieved else None,
-                     "step_frac_vs_burst": step_tflops / peak_burst,
+                     "step_frac_vs_burst": gpu_tflops / peak_burst,
                      "traffic": traffic,
                      "traffic_unit": "DRAM bytes per layer step (4 GEMM launches), one-pass ncu capture at "
                                      f"{T} tokens per layer" if traffic else "not captured for this token count",
