@@ -110,3 +110,24 @@ def test_scale_from_amax_bits_equals_division():
     e = np.maximum(((bits.astype(np.int64) + 0x1F) >> 7) - 8, 0)
     e = np.where(bits == 0x7F80, 254, np.where(bits > 0x7F80, 255, e))
     assert np.array_equal(e, ref)
+
+
+def test_scale_rule_matches_the_reference_arithmetic_on_b200():
+    """tests/golden/scale_rule_b200.npz (made by make_scale_rule_b200.py on a B200) holds, for every
+    non-negative bf16 block abs-max, the scale code of the reference's GPU arithmetic: Triton's fp32
+    division amax / 448 followed by cvt.rp.satfinite.ue8m0 (scripts/mxfp8.py:61-63).  That division is not
+    IEEE-exact (one ulp high in about half the quotients) but it is exact where amax = 7 * 2^k, so every
+    code equals the kernels' rule from the abs-max's bits and the oracle's IEEE division."""
+    z = np.load(os.path.join(G, "scale_rule_b200.npz"))
+    bits = z["amax_bits"].astype(np.int64)
+    e = z["e"].astype(np.int64)
+    assert len(bits) == 0x8000 and str(z["device"]).startswith("NVIDIA B200")
+    rule = np.maximum(((bits + 0x1F) >> 7) - 8, 0)
+    rule = np.where(bits == 0x7F80, 254, np.where(bits > 0x7F80, 255, rule))
+    assert np.array_equal(rule, e)
+    amax = (bits.astype(np.uint32) << np.uint32(16)).view(np.float32)
+    with np.errstate(invalid="ignore"):
+        assert np.array_equal(O.e8m0_rceil(amax / np.float32(448.0)).astype(np.int64), e)
+    exact = (bits & 0x7F) == 0x60      # amax = 7 * 2^k: the quotient is a power of two
+    assert np.array_equal(z["descale_bits"][exact & (bits < 0x7F80)],
+                          (amax / np.float32(448.0)).view(np.uint32)[exact & (bits < 0x7F80)])

@@ -113,3 +113,29 @@ def test_fallback_kernel_on_unaligned_code_rows(R, K):
     assert int(q[:, K:].sum()) == 0
     assert torch.equal(s, s0.view(torch.uint8))
     assert _mxlib.device_error() == 0
+
+
+def test_scales_match_the_reference_arithmetic_on_b200():
+    """Every non-negative bf16 value as the abs-max of a 32-element block (the other 31 elements a smaller
+    value of the same sign pattern), quantized by the kernel row-wise and column-wise: the scale codes equal
+    those of the reference's GPU arithmetic recorded in scale_rule_b200.npz (Triton's fp32 amax / 448, then
+    cvt.rp.satfinite.ue8m0; see make_scale_rule_b200.py)."""
+    import os
+    import mxfp8
+    z = np.load(os.path.join(os.path.dirname(__file__), "golden", "scale_rule_b200.npz"))
+    bits = z["amax_bits"].astype(np.int64)
+    want = z["e"]
+    n = len(bits)                                   # 32,768 blocks = 256 rows x 128 blocks of 32
+    rows, cols = 256, 128 * 32
+    blk = np.zeros((n, 32), dtype=np.uint16)
+    blk[:, 0] = bits                                # the block's abs-max (NaN / inf included)
+    blk[:, 1::2] = bits >> 1                        # smaller magnitudes elsewhere, half of them negative
+    blk[:, 2::2] = (bits >> 2) | 0x8000
+    x = torch.from_numpy(blk.reshape(rows, cols).view(np.int16)).view(torch.bfloat16).cuda()
+    q, s = mxfp8.mx_quant(x)
+    from oracle import mx_oracle as O
+    got = O.unblock_scales(s.view(torch.uint8).cpu().numpy(), rows, cols).reshape(-1)
+    assert np.array_equal(got, want)
+    qt, st = mxfp8.mx_quant_t(x.t().contiguous())   # the column-wise kernel on the transpose: same blocks
+    got_t = O.unblock_scales(st.view(torch.uint8).cpu().numpy(), rows, cols).reshape(-1)
+    assert np.array_equal(got_t, want)
