@@ -129,8 +129,8 @@ def test_scales_match_the_reference_arithmetic_on_b200():
     rows, cols = 256, 128 * 32
     blk = np.zeros((n, 32), dtype=np.uint16)
     blk[:, 0] = bits                                # the block's abs-max (NaN / inf included)
-    blk[:, 1::2] = bits >> 1                        # smaller magnitudes elsewhere, half of them negative
-    blk[:, 2::2] = (bits >> 2) | 0x8000
+    blk[:, 1::2] = (bits >> 1)[:, None]             # smaller magnitudes elsewhere, half of them negative
+    blk[:, 2::2] = ((bits >> 2) | 0x8000)[:, None]
     x = torch.from_numpy(blk.reshape(rows, cols).view(np.int16)).view(torch.bfloat16).cuda()
     q, s = mxfp8.mx_quant(x)
     from oracle import mx_oracle as O

@@ -68,6 +68,29 @@ MX_DEV uint32_t absmax_bf16x2(uint32_t a, uint32_t b) {
       : "=r"(r) : "r"(a), "r"(b));
   return r;
 }
+// max(|a|, |b|) per half with the xor of the signs as the sign (NaN if either is NaN): chains of these
+// give a block's abs-max up to its sign bit, which the caller clears once.
+MX_DEV uint32_t amax_xs_bf16x2(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("max.NaN.xorsign.abs.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+// {f32(lo(p)) + c.x, f32(hi(p)) + c.y}, each rounded once: the bf16 halves feed the adds directly.
+MX_DEV float2 add_bf16x2_f32(uint32_t p, float2 c) {
+  float2 r;
+  asm("{\n\t.reg .b16 lo, hi;\n\tmov.b32 {lo, hi}, %2;\n\tadd.rn.f32.bf16 %0, lo, %3;\n\t"
+      "add.rn.f32.bf16 %1, hi, %4;\n\t}"
+      : "=f"(r.x), "=f"(r.y) : "r"(p), "f"(c.x), "f"(c.y));
+  return r;
+}
+// {f32(lo(p)) * s, f32(hi(p)) * s} for a bf16 power of two s (exact scaling; -0 addend keeps -0 products).
+MX_DEV float2 scale_bf16x2(uint32_t p, uint16_t s) {
+  float2 r;
+  asm("{\n\t.reg .b16 lo, hi;\n\t.reg .f32 z;\n\tmov.b32 {lo, hi}, %2;\n\tmov.b32 z, 0x80000000;\n\t"
+      "fma.rn.f32.bf16 %0, lo, %3, z;\n\tfma.rn.f32.bf16 %1, hi, %3, z;\n\t}"
+      : "=f"(r.x), "=f"(r.y) : "r"(p), "h"(s));
+  return r;
+}
 MX_DEV uint32_t max_bf16x2(uint32_t a, uint32_t b) {
   uint32_t r;
   asm("max.NaN.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
@@ -118,21 +141,22 @@ MX_DEV void quad_transpose16(uint32_t& r0, uint32_t& r1, int t) {
 // each lane writes 8 consecutive codes, so a quad fills the row's 32-byte sector in one store.
 MX_DEV void quant_block16p(const uint32_t (&pk)[4][2], const QRows& qr, int64_t col0, int t) {
   const int64_t soff = ((col0 >> 7) << 9) + ((col0 >> 5) & 3);  // k-block col0/32 in the blocked layout
-  // both rows' abs-maxes in one bf16x2 (an abs-max of bf16 values is a bf16 value): (row g | row g + 8)
-  const uint32_t m0 = max_bf16x2(absmax_bf16x2(pk[0][0], pk[1][0]), absmax_bf16x2(pk[2][0], pk[3][0]));
-  const uint32_t m1 = max_bf16x2(absmax_bf16x2(pk[0][1], pk[1][1]), absmax_bf16x2(pk[2][1], pk[3][1]));
-  uint32_t mm = max_bf16x2(__byte_perm(m0, m1, 0x5410), __byte_perm(m0, m1, 0x7632));
-  mm = max_bf16x2(mm, __shfl_xor_sync(0xffffffffu, mm, 1));
-  mm = max_bf16x2(mm, __shfl_xor_sync(0xffffffffu, mm, 2));
+  // both rows' abs-maxes in one bf16x2 (an abs-max of bf16 values is a bf16 value): (row g | row g + 8);
+  // the xorsign maxima carry a meaningless sign, cleared at the end
+  const uint32_t m0 = amax_xs_bf16x2(amax_xs_bf16x2(pk[0][0], pk[1][0]), amax_xs_bf16x2(pk[2][0], pk[3][0]));
+  const uint32_t m1 = amax_xs_bf16x2(amax_xs_bf16x2(pk[0][1], pk[1][1]), amax_xs_bf16x2(pk[2][1], pk[3][1]));
+  uint32_t mm = amax_xs_bf16x2(__byte_perm(m0, m1, 0x5410), __byte_perm(m0, m1, 0x7632));
+  mm = amax_xs_bf16x2(mm, __shfl_xor_sync(0xffffffffu, mm, 1));
+  mm = amax_xs_bf16x2(mm, __shfl_xor_sync(0xffffffffu, mm, 2)) & 0x7FFF7FFFu;
 #pragma unroll
   for (int h = 0; h < 2; ++h) {
     const uint32_t e = mx_e8m0_of_amax(h ? bf16_hi(mm) : bf16_lo(mm));
-    const float rcp = mx_e8m0_rcp(e);
-    const float2 r2 = make_float2(rcp, rcp);
+    // 2^(127 - e) (1.0, 2^-127, NaN for e = 0, 254, 255) is a bf16 value: its high half
+    const uint16_t rcp = (uint16_t)(__float_as_uint(mx_e8m0_rcp(e)) >> 16);
     uint32_t c[4];
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      const float2 v = __fmul2_rn(up2(pk[i][h]), r2);
+      const float2 v = scale_bf16x2(pk[i][h], rcp);
       c[i] = e4m3x2_sat(v.x, v.y);
     }
     uint32_t r0 = __byte_perm(c[0], c[1], 0x5410), r1 = __byte_perm(c[2], c[3], 0x5410);

@@ -545,7 +545,7 @@ __global__ void __launch_bounds__(32 * (bwd_cons(R) + 1), 1)
             const float2 sig = sigmoid2(gg);
             const float2 sl = __fmul2_rn(gg, sig);                                 // silu(g)
             hp[i][h] = rn2(__fmul2_rn(sl, uu));                                     // h = bf16(silu * u)
-            const float2 dh = up2(rn2(__fadd2_rn(up2(D[2 * qq + h]), make_float2(dd[qq][2 * h], dd[qq][2 * h + 1]))));
+            const float2 dh = up2(rn2(add_bf16x2_f32(D[2 * qq + h], make_float2(dd[qq][2 * h], dd[qq][2 * h + 1]))));
             dup[i][h] = rn2(__fmul2_rn(dh, sl));                                    // du = bf16(dh * silu)
             const float2 om = __ffma2_rn(sig, make_float2(-1.f, -1.f), make_float2(1.f, 1.f));  // 1 - sig
             const float2 f = __ffma2_rn(gg, om, make_float2(1.f, 1.f));             // g (1 - sig) + 1
