@@ -69,6 +69,9 @@ def _args():
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end (host buffers) measurement")
     ap.add_argument("--no-extras", action="store_true",
                     help="skip the configs[2] / configs[4] / checkpointed-step measurements of the default line")
+    ap.add_argument("--grad-sync", choices=("layer", "end"), default="layer",
+                    help="layer: each layer's LoRA gradients all-reduced as soon as they exist (overlapped with the "
+                         "backward below); end: one all-reduce of all of them after the backward")
     ap.add_argument("--tokens", type=int, default=0,
                     help="tokens per rank for the layer workload (default 16384; smaller cases for profiling)")
     return ap.parse_args()
@@ -207,7 +210,7 @@ def _make_layer(torch, fused_mlp, dev, seed):
     return layer, params
 
 
-def _config(workload, world, T, L):
+def _config(workload, world, T, L, sync="layer"):
     if workload == "layer":
         wl = (f"configs[1]: one Qwen3.5-2B MLP layer, {T} tokens per rank" if T == LAYER_TOKENS
               else f"one Qwen3.5-2B MLP layer, {T} tokens per rank (configs[1] holds {LAYER_TOKENS})")
@@ -218,8 +221,9 @@ def _config(workload, world, T, L):
     return {"workload": wl, "hidden": H, "intermediate": N, "lora_rank": R, "lora_alpha": ALPHA, "layers": L,
             "tokens_per_rank": T, "global_tokens": T * world if workload == "layer" else STACK_TOKENS,
             "value_counts": "layer-tokens (tokens x layers) per second",
-            "parallelism": f"dp{world} (token shards; per-layer NCCL all-reduce of LoRA grads overlapped with "
-                           f"the backward)",
+            "parallelism": f"dp{world} (token shards; " + ("per-layer NCCL all-reduce of LoRA grads overlapped with "
+                                                            "the backward)" if sync == "layer" else
+                                                            "one NCCL all-reduce of all LoRA grads after the backward)"),
             "l2": f"per-step working set > L2 (gu alone {T * 4 * N // 2**20} MiB per layer); no flush"}
 
 
@@ -256,7 +260,8 @@ def run_ours(a):
     T, L, total_tokens = _workload_shape(a, world, rank)
     layers = [_make_layer(torch, fused_mlp, dev, seed=1000 + i) for i in range(L)]
     # gradient storage: A_gate next to A_up in every layer (the backward writes [dA_gate; dA_up] as one block)
-    grads = mx_dp.LayerGrads([[ps[0], ps[2], ps[1], ps[3], ps[4], ps[5]] for _, ps in layers], device=dev)
+    grads = mx_dp.LayerGrads([[ps[0], ps[2], ps[1], ps[3], ps[4], ps[5]] for _, ps in layers], device=dev,
+                             overlap=a.grad_sync == "layer")
     gx = torch.Generator(device="cpu").manual_seed(7 + rank)
     x_host = torch.randn(T, H, generator=gx).to(torch.bfloat16).pin_memory()
     dy_host = torch.randn(T, H, generator=gx).to(torch.bfloat16).pin_memory()
@@ -470,7 +475,7 @@ def run_ours(a):
         "warmup": max(a.warmup, 3), "ms_per_step": ms, "higher_is_better": True,
         "scaling": "weak" if a.workload == "layer" else "strong", "vs_baseline": None, "dtype": "mxfp8-e4m3/bf16",
         "data": "synthetic (seeded N(0,1) activations, N(0,0.02) frozen weights, N(0,0.01) LoRA A/B)",
-        "config": _config(a.workload, world, T, L),
+        "config": _config(a.workload, world, T, L, a.grad_sync),
         "e2e": None if a.no_e2e else {"value": tok / (e2e_ms * 1e-3), "unit": UNIT,
                                       "h2d_bytes_per_step": x_host.numel() * 2 + dy_host.numel() * 2,
                                       "d2h_bytes_per_step": grads_host.numel() * 4},

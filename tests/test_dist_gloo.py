@@ -192,7 +192,7 @@ def test_layer_grads_copies_in_gradients_made_elsewhere():
     lg.close()
 
 
-def _layer_grads_worker(rank, world, port, out):
+def _layer_grads_worker(rank, world, port, out, overlap=True):
     import sys
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
     sys.path[:0] = [root, os.path.join(root, "train-model-template_b200")]
@@ -201,7 +201,7 @@ def _layer_grads_worker(rank, world, port, out):
     dist.init_process_group("gloo", rank=rank, world_size=world)
     F = _fake_fn()
     ps = _layer_params(4)
-    lg = mx_dp.LayerGrads(ps)
+    lg = mx_dp.LayerGrads(ps, overlap=overlap)
     order = []
     orig = lg._accumulated
 
@@ -247,5 +247,25 @@ def test_layer_grads_allreduce_per_layer_in_backward_order():
     assert order == [3, 2, 1, 0, 3, 2, 1, 0]          # last layer first: its backward finishes first
     for step, grads in enumerate(res):
         dsum = sum(2.0 * (r + 1 + step) for r in range(world))   # dy.sum() of each rank, summed
+        for (li, k), g in grads.items():
+            assert torch.allclose(g, torch.full(g.shape, dsum * (k + 1) * (li + 1)))
+
+
+def test_layer_grads_one_allreduce_after_the_backward():
+    """overlap=False: the same sums from one all-reduce of the whole buffer in finish()."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    world = 2
+    procs = [ctx.Process(target=_layer_grads_worker, args=(r, world, port, q, False)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res, order, exchanges, copied = q.get(timeout=240)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    assert exchanges == 2 and copied == 0 and order == []     # one per step, none from the hooks
+    for step, grads in enumerate(res):
+        dsum = sum(2.0 * (r + 1 + step) for r in range(world))
         for (li, k), g in grads.items():
             assert torch.allclose(g, torch.full(g.shape, dsum * (k + 1) * (li + 1)))

@@ -55,8 +55,11 @@ class LayerGrads:
     (for the fused MLP: A_gate then A_up) sit next to each other.
     """
 
-    def __init__(self, layer_params, device=None, group=None):
+    def __init__(self, layer_params, device=None, group=None, overlap=True):
+        """overlap=True: each layer's slice is all-reduced as soon as its gradients exist, overlapped with the
+        backward of the layers below; False: one all-reduce of the whole buffer in finish()."""
         self.group = group
+        self.overlap = overlap
         self.layers = [list(ps) for ps in layer_params]
         dev = device if device is not None else self.layers[0][0].device
         self.where = {}                 # id(p) -> (layer index, offset, numel)
@@ -114,7 +117,7 @@ class LayerGrads:
             p.grad = self.flat[off:off + n].view(p.shape)
             self.copied += 1
         self.left[li] -= 1
-        if self.left[li] == 0 and _distributed(self.group):
+        if self.left[li] == 0 and self.overlap and _distributed(self.group):
             o, k = self.spans[li]
             self.works.append(dist.all_reduce(self.flat[o:o + k], op=dist.ReduceOp.SUM, group=self.group,
                                               async_op=True))
@@ -134,6 +137,9 @@ class LayerGrads:
                     p.grad = v
                     self._accumulated(p)
         _ACTIVE[0] = None
+        if not self.overlap and _distributed(self.group):
+            dist.all_reduce(self.flat, op=dist.ReduceOp.SUM, group=self.group)
+            self.exchanges += 1
         for w in self.works:
             w.wait()
         self.works = []
