@@ -5,8 +5,8 @@
 
 One step = the fused MLP forward + autograd backward (dX, dA, dB of the three LoRA adapters) of every
 layer over one batch of tokens, plus, with N > 1 ranks, the NCCL all-reduce of the LoRA gradients (the
-only data exchange of token-sharded data parallelism), issued per layer as soon as that layer's
-gradients exist and overlapped with the next layer's backward.
+only data exchange of token-sharded data parallelism): one collective over the flat gradient buffer
+after the backward (--grad-sync end), or one per layer overlapped with the backward (--grad-sync layer).
 
 Workloads:
   stack  (default) the 24-layer Qwen3.5-2B MLP stack (hidden 2048, intermediate 6144, LoRA r=16,
@@ -69,9 +69,10 @@ def _args():
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end (host buffers) measurement")
     ap.add_argument("--no-extras", action="store_true",
                     help="skip the configs[2] / configs[4] / checkpointed-step measurements of the default line")
-    ap.add_argument("--grad-sync", choices=("layer", "end"), default="layer",
-                    help="layer: each layer's LoRA gradients all-reduced as soon as they exist (overlapped with the "
-                         "backward below); end: one all-reduce of all of them after the backward")
+    ap.add_argument("--grad-sync", choices=("layer", "end"), default="end",
+                    help="end (default): one all-reduce of all LoRA gradients after the backward; layer: each layer's "
+                         "all-reduced as soon as they exist, overlapped with the backward below (slower on B200: the "
+                         "collective's CTAs hold SMs that the next persistent GEMM waits for)")
     ap.add_argument("--tokens", type=int, default=0,
                     help="tokens per rank for the layer workload (default 16384; smaller cases for profiling)")
     return ap.parse_args()
@@ -210,7 +211,7 @@ def _make_layer(torch, fused_mlp, dev, seed):
     return layer, params
 
 
-def _config(workload, world, T, L, sync="layer"):
+def _config(workload, world, T, L, sync="end"):
     if workload == "layer":
         wl = (f"configs[1]: one Qwen3.5-2B MLP layer, {T} tokens per rank" if T == LAYER_TOKENS
               else f"one Qwen3.5-2B MLP layer, {T} tokens per rank (configs[1] holds {LAYER_TOKENS})")
