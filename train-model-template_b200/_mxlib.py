@@ -128,11 +128,50 @@ def ctypes_ref(x):
 
 
 def ptr(t):
-    """Device pointer of a tensor (None -> NULL)."""
-    return None if t is None else ctypes.c_void_p(t.data_ptr())
+    """Device pointer of a tensor as an integer for a void* argument (None -> NULL)."""
+    return None if t is None else t.data_ptr()
+
+
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
 
 
 def stream_of(t=None):
-    """The current torch CUDA stream handle for t's device, as a void*."""
+    """The current torch CUDA stream handle of t's device (the current device for None), for a void*."""
+    if _raw_stream is not None:
+        return _raw_stream(t.device.index if t is not None and t.device.index is not None
+                           else torch.cuda.current_device())
     dev = t.device if t is not None else None
-    return ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+    return torch.cuda.current_stream(dev).cuda_stream
+
+
+# ---- partition queries: pure functions of the shape and the device, asked once per shape
+_QUERY = {}
+
+
+def _query(name, *args, n_out):
+    key = (name, torch.cuda.current_device() if torch.cuda.is_available() else -1) + args
+    hit = _QUERY.get(key)
+    if hit is None:
+        outs = [ctypes.c_int(0) for _ in range(n_out)]
+        call(name, *args, *[ctypes.byref(o) for o in outs])
+        hit = _QUERY[key] = tuple(o.value for o in outs)
+    return hit
+
+
+def coldot_chunks(T, K):
+    """(rows per chunk, chunks) of mxm_coldot's partial buffer for a [T, K] operand."""
+    return _query("mxm_coldot_chunks", T, K, n_out=2)
+
+
+def glu_partition(T, N):
+    """(column tiles per chunk, grid, xS_down partial slots) of mxm_gemm_glu."""
+    return _query("mxm_gemm_glu_partition", T, N, n_out=3)
+
+
+def mlp_fwd_partitions(T, N, R):
+    return _query("mxm_mlp_fwd_partitions", T, N, R, n_out=1)[0]
+
+
+def mlp_bwd_partitions(T, N, R):
+    """(super block rows, dxa partial slots) of the backward epilogue."""
+    return _query("mxm_mlp_bwd_partitions", T, N, R, n_out=2)

@@ -917,7 +917,7 @@ int rowdot_tma(const void* A, int64_t lda, const void* B, int64_t T, int64_t K, 
   const int nrb = (int)((T + RD_ROWS - 1) / RD_ROWS);
   const int grid = std::min(nrb, mxm_num_sms());
   auto go = [&](auto kern) -> int {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaError_t e = mx_smem_attr((const void*)kern, smem);
     if (e != cudaSuccess) return mx_cuda_status(e, "rowdot tma: set smem");
     kern<<<grid, 32 * (RD_CONS + 1), smem, st>>>(ta, tb, (int)T, (int)K, nrb, stages, post, round_once, (bf16*)out,
                                                   ldo, q, ldq, s, scols, kb_off, mx_dev_error_ptr());
@@ -1316,7 +1316,7 @@ extern "C" int mxm_mlp_fwd_epilogue(const void* gu, const void* xs, const void* 
   bf16* direct = col_groups == 1 ? (bf16*)xsd : nullptr;
   const size_t smem = fwd_smem(r);
   auto go = [&](auto kern) -> int {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaError_t e = mx_smem_attr((const void*)kern, smem);
     if (e != cudaSuccess) return mx_cuda_status(e, "mlp fwd epilogue: set smem");
     kern<<<grid, FWD_THREADS, smem, st>>>(tm, tbg, tbu, tad, (const bf16*)xs, (uint8_t*)qh, (uint8_t*)sh,
                                           (float*)xsd_part, direct, (int)T, Tpad, (int)N, s_g, s_u, tpg,
@@ -1414,7 +1414,7 @@ extern "C" int mxm_mlp_bwd_epilogue(const void* gu, const void* xs, const void* 
   const size_t smem = bwd_smem(r);
   cudaStream_t st = (cudaStream_t)stream;
   auto go = [&](auto kern) -> int {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaError_t e = mx_smem_attr((const void*)kern, smem);
     if (e != cudaSuccess) return mx_cuda_status(e, "mlp bwd epilogue: set smem");
     kern<<<p.grid, 32 * (bwd_cons(r) + 1), smem, st>>>(tgu, tdh, tbg, tbu, tad, txs, tdxd, (uint8_t*)q, (uint8_t*)s,
                                                        (float*)dxa_part, (float*)dbg_part, (float*)dbu_part,
@@ -1555,7 +1555,7 @@ extern "C" int mxm_lora_bwd(const void* dy, int64_t ldy, int64_t T, int64_t N, c
   dim3 cgrid((unsigned)(N / CD_COLS), (unsigned)chunks);
   auto goc = [&](auto kern, int nj) -> int {
     const size_t smem = cd_smem(nj);
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaError_t e = mx_smem_attr((const void*)kern, smem);
     if (e != cudaSuccess) return mx_cuda_status(e, "lora bwd: set smem");
     kern<<<cgrid, 160, smem, st>>>(ta, te, (int)N, rows_per_chunk, (int)T, (float*)part, mx_dev_error_ptr());
     mx_note_launch();
@@ -1705,7 +1705,7 @@ extern "C" int mxm_coldot(const void* A, int64_t lda, const void* E, int64_t lde
   cudaStream_t st = (cudaStream_t)stream;
   auto go = [&](auto kern, int nj) -> int {
     const size_t smem = cd_smem(nj);
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaError_t e = mx_smem_attr((const void*)kern, smem);
     if (e != cudaSuccess) return mx_cuda_status(e, "coldot: set smem");
     kern<<<grid, 160, smem, st>>>(ta, te, (int)K, rows_per_chunk, (int)T, (float*)part, mx_dev_error_ptr());
     mx_note_launch();

@@ -378,8 +378,7 @@ int launch(const void* x, int64_t R, int64_t K, int64_t ldx, void* q, int64_t ld
       const int64_t tiles = (int64_t)nrt * nct;
       const int grid = (int)std::min<int64_t>(tiles, mxm_num_sms());
       const size_t smem = qm_smem();
-      cudaError_t ce = cudaFuncSetAttribute(k_quant_tma<ROWS, COLS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                            (int)smem);
+      cudaError_t ce = mx_smem_attr((const void*)k_quant_tma<ROWS, COLS>, smem);
       if (ce != cudaSuccess) return mx_cuda_status(ce, "quant tma: set smem");
       k_quant_tma<ROWS, COLS><<<grid, 32 * (QM_CONS + 1), smem, (cudaStream_t)stream>>>(
           tx, tq, tqt, (uint8_t*)s, (uint8_t*)st, R, nrt, nct, s_tiles, tile_off, mx_dev_error_ptr());
@@ -389,7 +388,7 @@ int launch(const void* x, int64_t R, int64_t K, int64_t ldx, void* q, int64_t ld
   }
   const size_t smem = COLS ? 128 * 128 * sizeof(uint16_t) : 0;
   if (COLS) {
-    cudaError_t e = cudaFuncSetAttribute(k_quant<ROWS, COLS>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaError_t e = mx_smem_attr((const void*)k_quant<ROWS, COLS>, smem);
     if (e != cudaSuccess) return mx_cuda_status(e, "quant: set smem");
   }
   dim3 grid((unsigned)((R + 127) / 128), (unsigned)(K / 128));

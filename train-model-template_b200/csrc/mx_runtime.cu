@@ -98,6 +98,31 @@ extern "C" int mxm_selftest_wait(int64_t limit_ns, void* stream) {
   return mx_launch_status("mxm_selftest_wait");
 }
 
+cudaError_t mx_smem_attr(const void* fn, size_t bytes) {
+  struct Entry {
+    const void* fn;
+    int dev;
+    size_t bytes;
+  };
+  static std::mutex mu;
+  static Entry tab[256];
+  static int n = 0;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    for (int i = 0; i < n; ++i)
+      if (tab[i].fn == fn && tab[i].dev == dev && tab[i].bytes >= bytes) return cudaSuccess;
+  }
+  e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+  if (e == cudaSuccess) {
+    std::lock_guard<std::mutex> lock(mu);
+    if (n < 256) tab[n++] = Entry{fn, dev, bytes};
+  }
+  return e;
+}
+
 extern "C" int mxm_num_sms(void) {
   static int cache[64] = {0};
   int dev = 0;

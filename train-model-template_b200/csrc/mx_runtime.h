@@ -14,6 +14,10 @@ int mx_launch_status(const char* what);
 // Counts kernel launches made by this library (host side), read with mxm_launch_count().
 void mx_note_launch(int n = 1);
 
+// cudaFuncSetAttribute(fn, MaxDynamicSharedMemorySize, bytes) once per (kernel, device): later calls with
+// no larger size return at once (the attribute is a per-context property of the kernel).
+cudaError_t mx_smem_attr(const void* fn, size_t bytes);
+
 // Device address of the device-side error flag on the current device (nullptr if unavailable).
 int* mx_dev_error_ptr();
 

@@ -37,11 +37,6 @@ def _cdiv(a, b):
     return -(-a // b)
 
 
-def _i(v):
-    import ctypes
-    return ctypes.c_int(v)
-
-
 # ------------------------------------------------------------------------------------------------ skinny ops
 def rowdot(A, B, post=1.0, out=None):
     """bf16(bf16(A @ B^T) * post): A [T, K] bf16 (K % 32 == 0), B [n, K] bf16 contiguous, n in {16, 32}."""
@@ -75,15 +70,14 @@ def coldot(A, E, post=1.0, transpose_out=False, out_dtype=torch.bfloat16, out=No
     T, K = A.shape
     n = E.shape[1]
     assert out_dtype in (torch.bfloat16, torch.float32)
-    rpc, nch = _i(0), _i(0)
-    _nx.call("mxm_coldot_chunks", T, K, _nx.ctypes_ref(rpc), _nx.ctypes_ref(nch))
-    part = torch.empty((nch.value, K, n), dtype=torch.float32, device=A.device)
+    rpc, nch = _nx.coldot_chunks(T, K)
+    part = torch.empty((nch, K, n), dtype=torch.float32, device=A.device)
     shape = (n, K) if transpose_out else (K, n)
     if out is None:
         out = torch.empty(shape, dtype=out_dtype, device=A.device)
     assert out.shape == shape and out.dtype == out_dtype and out.is_contiguous(), (out.shape, out.dtype)
     _nx.call("mxm_coldot", _nx.ptr(A), A.stride(0), _nx.ptr(E), E.stride(0), T, K, n, float(post),
-             1 if transpose_out else 0, _nx.ptr(part), rpc.value, nch.value, _nx.ptr(out),
+             1 if transpose_out else 0, _nx.ptr(part), rpc, nch, _nx.ptr(out),
              1 if out_dtype == torch.float32 else 0, _nx.stream_of(A))
     return out
 
@@ -121,9 +115,7 @@ def mlp_fwd(gu, xs, bg, bu, ad, s_g, s_u, write_q):
     T, N2 = gu.shape
     N, R = N2 // 2, ad.shape[0]
     dev = gu.device
-    cs = _i(0)
-    _nx.call("mxm_mlp_fwd_partitions", T, N, R, _nx.ctypes_ref(cs))
-    cs = cs.value
+    cs = _nx.mlp_fwd_partitions(T, N, R)
     q = s = None
     if write_q:
         q = torch.empty((T, N), dtype=_F8, device=dev)
@@ -143,12 +135,11 @@ def gemm_glu(q, sc, w, ws, xs, bg, bu, ad, s_g, s_u):
     N2 = w.shape[0]
     N, R = N2 // 2, ad.shape[0]
     dev = q.device
-    per, grid, slots = _i(0), _i(0), _i(0)
-    _nx.call("mxm_gemm_glu_partition", T, N, _nx.ctypes_ref(per), _nx.ctypes_ref(grid), _nx.ctypes_ref(slots))
+    per, grid, slots = _nx.glu_partition(T, N)
     gu = torch.empty((T, N2), dtype=torch.bfloat16, device=dev)
     qh = torch.empty((T, N), dtype=_F8, device=dev)
     sh = torch.empty(_cdiv(T, 128) * (N // 128) * 512, dtype=torch.uint8, device=dev)
-    part = torch.empty((slots.value, T, R), dtype=torch.float32, device=dev)
+    part = torch.empty((slots, T, R), dtype=torch.float32, device=dev)
     xsd = torch.empty((T, R), dtype=torch.bfloat16, device=dev)
     _nx.call("mxm_gemm_glu", _nx.ptr(q), q.stride(0), _nx.ptr(sc), _nx.ptr(w), w.stride(0), _nx.ptr(ws), T, N, H,
              _nx.ptr(gu), _nx.ptr(xs), _nx.ptr(bg), _nx.ptr(bu), _nx.ptr(ad), R, float(s_g), float(s_u),
@@ -163,9 +154,7 @@ def _bwd_launch(gu, xs, dhm, dxd, bg, bu, ad, s_g, s_u, need_q, zero_slots=False
     T, N2 = gu.shape
     N, R = N2 // 2, ad.shape[0]
     dev = gu.device
-    sb, ncg = _i(0), _i(0)
-    _nx.call("mxm_mlp_bwd_partitions", T, N, R, _nx.ctypes_ref(sb), _nx.ctypes_ref(ncg))
-    sb, ncg = sb.value, ncg.value
+    sb, ncg = _nx.mlp_bwd_partitions(T, N, R)
     nsb = _cdiv(_cdiv(T, 128) * 128, sb)
     q = s = None
     if need_q:

@@ -20,7 +20,6 @@ on B200 (sm_100a) kernels.  Drop-in for the reference module of the same name
   (scripts/mxfp8.py:88-296).  Requests the kernels do not take raise ``MXError`` with status
   ``MXM_ERR_UNSUPPORTED``; callers check ``lora_bwd_ok`` / ``res_lora_ok`` first.
 """
-import ctypes
 import os
 import types
 import weakref
@@ -163,9 +162,7 @@ def group_lora_bwd(T, branches, q=None, s=None, device=None):
     need = 0
     for dy, xa, _, _, _, _ in branches:
         if xa is not None:
-            rpc, nch = ctypes.c_int(0), ctypes.c_int(0)
-            _nx.call("mxm_coldot_chunks", T, dy.shape[1], _nx.ctypes_ref(rpc), _nx.ctypes_ref(nch))
-            need = max(need, nch.value * dy.shape[1] * xa.shape[1])
+            need = max(need, _nx.coldot_chunks(T, dy.shape[1])[1] * dy.shape[1] * xa.shape[1])
     part = torch.empty(max(need, 1), dtype=torch.float32, device=device or branches[0][0].device)
     _nx.call("mxm_group_lora_bwd", T, len(branches), recs, _nx.ptr(q), q.stride(0) if q is not None else 0,
              _nx.ptr(s), q.shape[1] if q is not None else 0, _nx.ptr(part), part.numel() * 4,
@@ -198,14 +195,13 @@ def lora_bwd(dy, xa=None, B=None, scale=1.0, q=None, s=None, col_tile_off=0, dxa
     assert B.is_contiguous() and B.shape == (N, R) and B.dtype == torch.bfloat16
     assert dxa_out.shape == (T, R) and dxa_out.stride(1) == 1
     Bt = B.t().contiguous()                                            # [r, N]: rows of the rowdot operand
-    rpc, nch = ctypes.c_int(0), ctypes.c_int(0)
-    _nx.call("mxm_coldot_chunks", T, N, _nx.ctypes_ref(rpc), _nx.ctypes_ref(nch))
-    part = torch.empty((nch.value, N, R), dtype=torch.float32, device=dy.device)
+    rpc, nch = _nx.coldot_chunks(T, N)
+    part = torch.empty((nch, N, R), dtype=torch.float32, device=dy.device)
     dB = torch.empty((N, R), dtype=torch.float32, device=dy.device)
     _nx.call("mxm_lora_bwd", _nx.ptr(dy), dy.stride(0), T, N, _nx.ptr(xa), xa.stride(0), _nx.ptr(Bt), R,
              float(scale), _nx.ptr(q) if do_q else None, q.stride(0) if do_q else 0, _nx.ptr(s) if do_q else None,
              q.shape[1] if do_q else 0, col_tile_off, _nx.ptr(dxa_out), dxa_out.stride(0), _nx.ptr(dB),
-             _nx.ptr(part), rpc.value, nch.value, _nx.stream_of(dy))
+             _nx.ptr(part), rpc, nch, _nx.stream_of(dy))
     return dB
 
 
