@@ -43,9 +43,13 @@ constexpr int EPI_WARP0 = 4, EPI_THREADS = 256;
 
 __host__ __device__ constexpr int gemm_stages(int KR) { return KR == 64 ? 3 : 4; }
 __host__ __device__ constexpr int lora_bytes(int KR) { return (BM + BN) * KR * 2; }
-// Without a LoRA term the epilogue warps stage their output in 2 KB pieces (32 rows x 32 columns each)
-// for TMA stores; with one, shared memory is full and they store from registers.
-__host__ __device__ constexpr int out_bytes(int KR) { return KR == 0 ? 8 * 2048 : 0; }
+// Without a LoRA term or with a rank-16 one the epilogue warps stage their output in 2 KB pieces (32 rows x
+// 32 columns each) for TMA stores; with a larger one shared memory is full and they store from registers.
+__host__ __device__ constexpr bool tma_out(int KR) { return KR <= 16; }
+// columns of one staged piece: 32 (2 KB, 64-byte swizzle) without a LoRA term, 16 (1 KB, 32-byte swizzle)
+// with the rank-16 one, whose LoRA tiles leave room for only half the staging
+__host__ __device__ constexpr int out_cols(int KR) { return KR == 0 ? 32 : 16; }
+__host__ __device__ constexpr int out_bytes(int KR) { return tma_out(KR) ? 8 * 32 * out_cols(KR) * 2 : 0; }
 __host__ __device__ constexpr size_t gemm_smem(int KR) {
   return 1024 + (size_t)gemm_stages(KR) * (A_BYTES + B_BYTES + SFA_BYTES + SFB_BYTES) + lora_bytes(KR) +
          out_bytes(KR) + 256;
@@ -62,8 +66,9 @@ template <int KR>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     k_mx_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
               const __grid_constant__ CUtensorMap tmL, const __grid_constant__ CUtensorMap tmR,
-              const uint8_t* __restrict__ sa, const uint8_t* __restrict__ sb, int M, int N, int K,
-              __nv_bfloat16* __restrict__ D, int64_t ldd, int* err) {
+              const __grid_constant__ CUtensorMap tmD, const uint8_t* __restrict__ sa,
+              const uint8_t* __restrict__ sb, int M, int N, int K, __nv_bfloat16* __restrict__ D, int64_t ldd,
+              int* err) {
   constexpr int STAGES = gemm_stages(KR);
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -73,7 +78,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   uint8_t* sSFB = sSFA + STAGES * SFA_BYTES;
   uint8_t* sL = sSFB + STAGES * SFB_BYTES;  // 1024-aligned
   uint8_t* sR = sL + BM * KR * 2;
-  uint8_t* sOut = sL + lora_bytes(KR);      // [8 warps][32 rows x 64 B] (KR == 0), 1024-aligned
+  uint8_t* sOut = sL + lora_bytes(KR);      // [8 warps][32 rows x 64 B] (tma_out), 1024-aligned
   uint64_t* bars = reinterpret_cast<uint64_t*>(sOut + out_bytes(KR));
   uint64_t* full = bars;
   uint64_t* empty = bars + STAGES;
@@ -228,31 +233,34 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       tc_fence_before();
       mbar_arrive(tmem_empty);  // the accumulator is free: the next tile's MMAs start now
       acc_phase ^= 1;
-      if constexpr (KR == 0) {
-        // 32-column pieces of this warp's 32 x 128 block: bf16 rows into the warp's 2 KB buffer (64-byte
-        // swizzle), then one TMA store of the [32 x 32] box (rows >= M clipped); the buffer is reused
-        // once the previous store has read it
-        uint8_t* buf = sOut + (warp - EPI_WARP0) * 2048;
-        const uint32_t sb0 = smem_u32(buf) + (uint32_t)lane * 64;
-        const uint64_t pol = l2_evict_first();   // dh is streamed to the backward epilogue
+      if constexpr (tma_out(KR)) {
+        // pieces of OC columns of this warp's 32 x 128 block: bf16 rows into the warp's buffer (2*OC-byte
+        // rows, matching swizzle), then one TMA store of the [32 x OC] box (rows >= M clipped); the buffer is
+        // reused once the previous store has read it
+        constexpr int OC = out_cols(KR), RB = 2 * OC;
+        uint8_t* buf = sOut + (warp - EPI_WARP0) * (32 * RB);
+        const uint32_t sb0 = smem_u32(buf) + (uint32_t)lane * RB;
+        const uint64_t pol = l2_evict_first();   // dh / y are streamed to the next kernel
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
+        for (int pc = 0; pc < 128 / OC; ++pc) {
           if (lane == 0) bulk_wait_read0();
           __syncwarp();
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const uint32_t a = sb0 + ((uint32_t)(j ^ ((lane >> 1) & 3)) << 4);
+          for (int j = 0; j < OC / 8; ++j) {
+            const int col = pc * OC + 8 * j;   // of the warp's 128 columns: r[col / 32][col % 32 ..]
+            const uint32_t* v = &r[col >> 5][col & 31];
+            const uint32_t a = sb0 + ((uint32_t)(j ^ ((lane >> (RB == 64 ? 1 : 2)) & (RB / 16 - 1))) << 4);
             asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a),
-                         "r"(pack_bf16x2(__uint_as_float(r[c][8 * j + 0]), __uint_as_float(r[c][8 * j + 1]))),
-                         "r"(pack_bf16x2(__uint_as_float(r[c][8 * j + 2]), __uint_as_float(r[c][8 * j + 3]))),
-                         "r"(pack_bf16x2(__uint_as_float(r[c][8 * j + 4]), __uint_as_float(r[c][8 * j + 5]))),
-                         "r"(pack_bf16x2(__uint_as_float(r[c][8 * j + 6]), __uint_as_float(r[c][8 * j + 7])))
+                         "r"(pack_bf16x2(__uint_as_float(v[0]), __uint_as_float(v[1]))),
+                         "r"(pack_bf16x2(__uint_as_float(v[2]), __uint_as_float(v[3]))),
+                         "r"(pack_bf16x2(__uint_as_float(v[4]), __uint_as_float(v[5]))),
+                         "r"(pack_bf16x2(__uint_as_float(v[6]), __uint_as_float(v[7])))
                          : "memory");
           }
           fence_proxy_async();
           __syncwarp();
           if (lane == 0) {
-            tma_store_2d_hint(&tmL, buf, tn * BN + half * 128 + c * 32, tm * BM + q * 32, pol);
+            tma_store_2d_hint(&tmD, buf, tn * BN + half * 128 + pc * OC, tm * BM + q * 32, pol);
             bulk_commit();
           }
         }
@@ -274,7 +282,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           }
       }
     }
-    if constexpr (KR == 0) {
+    if constexpr (tma_out(KR)) {
       if (lane == 0) bulk_wait0();   // this warp's stores are complete before the CTA exits
     }
   }
@@ -762,7 +770,7 @@ int gemm_launch(const void* qa, int64_t lda, const void* sa, const void* qb, int
                  "%s: LoRA operands must be 16-byte aligned with row stride %% 8 == 0", fn);
   }
 
-  CUtensorMap tmA, tmB, tmL, tmR;
+  CUtensorMap tmA, tmB, tmL, tmR, tmD;
   if (int st = mx_make_tmap_2d(&tmA, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, qa, (uint64_t)K, (uint64_t)M, (uint64_t)lda, BK,
                                BM, CU_TENSOR_MAP_SWIZZLE_128B))
     return st;
@@ -777,11 +785,16 @@ int gemm_launch(const void* qa, int64_t lda, const void* sa, const void* qb, int
                                  (uint64_t)kr * 2, kr, BN, lora_swizzle(kr)))
       return st;
   } else {
-    // no LoRA term: the tmL slot carries the output's map for the epilogue's TMA stores ([32 x 32] boxes)
-    if (int st = mx_make_tmap_2d(&tmL, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, d, (uint64_t)N, (uint64_t)M,
-                                 (uint64_t)ldd * 2, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B))
+    tmL = tmR = tmA;  // unused by the kernel
+  }
+  if (kr <= 16) {
+    // the output's map for the epilogue's TMA stores ([32 x 32] boxes)
+    if (int st = mx_make_tmap_2d(&tmD, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, d, (uint64_t)N, (uint64_t)M,
+                                 (uint64_t)ldd * 2, (uint32_t)out_cols(kr), 32,
+                                 kr == 0 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B))
       return st;
-    tmR = tmA;  // unused by the kernel
+  } else {
+    tmD = tmA;        // unused: the epilogue stores from registers
   }
 
   static bool attr_done[4][64] = {};
@@ -799,7 +812,7 @@ int gemm_launch(const void* qa, int64_t lda, const void* sa, const void* qb, int
   const int num_tiles = (int)(((M + BM - 1) / BM) * (N / BN));
   const int grid = num_tiles < mxm_num_sms() ? num_tiles : mxm_num_sms();
   auto go = [&](auto kern) {
-    kern<<<grid, NUM_THREADS, smem_by[vi], (cudaStream_t)stream>>>(tmA, tmB, tmL, tmR, (const uint8_t*)sa,
+    kern<<<grid, NUM_THREADS, smem_by[vi], (cudaStream_t)stream>>>(tmA, tmB, tmL, tmR, tmD, (const uint8_t*)sa,
                                                                   (const uint8_t*)sb, (int)M, (int)N, (int)K,
                                                                   (__nv_bfloat16*)d, ldd, mx_dev_error_ptr());
   };
