@@ -52,7 +52,7 @@ FLOP_PER_TOKEN = 12 * H * N             # MXFP8 GEMM flops per token per layer, 
 LORA_FLOP_PER_TOKEN = 2 * R * (9 * H + 12 * N)
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of the four GEMM launches of one layer step,
 # by tokens per layer: one-pass ncu captures of this build's kernels (kept in the repository's profiles).
-GEMM_TRAFFIC_BYTES = {16384: 1352104960}
+GEMM_TRAFFIC_BYTES = {16384: 1274611712, 17792: 1322004992, 142336: 11404338944}
 
 
 def _args():
