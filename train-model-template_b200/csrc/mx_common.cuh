@@ -177,6 +177,11 @@ MX_DEV bool bar_any(uint32_t id, uint32_t nthreads, bool v) {
   return r != 0;
 }
 
+// Named barrier `id` over `nthreads` threads (a multiple of 32).
+MX_DEV void bar_sync(uint32_t id, uint32_t nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
 // ------------------------------------------------------------------------------------------------
 // TMA (no multicast anywhere in this project).
 MX_DEV void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int32_t x, int32_t y) {
@@ -205,6 +210,11 @@ MX_DEV uint64_t l2_evict_first() {
 MX_DEV void tma_store_2d_hint(const CUtensorMap* map, const void* src, int32_t x, int32_t y, uint64_t pol) {
   asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group.L2::cache_hint [%0, {%1, %2}], [%3], %4;"
                ::"l"(map), "r"(x), "r"(y), "r"(smem_u32(src)), "l"(pol) : "memory");
+}
+// The same for a 3-D box (x innermost).
+MX_DEV void tma_store_3d_hint(const CUtensorMap* map, const void* src, int32_t x, int32_t y, int32_t z, uint64_t pol) {
+  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group.L2::cache_hint [%0, {%1, %2, %3}], [%4], %5;"
+               ::"l"(map), "r"(x), "r"(y), "r"(z), "r"(smem_u32(src)), "l"(pol) : "memory");
 }
 MX_DEV void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 // The shared-memory sources of this thread's committed bulk stores have been read.
@@ -280,7 +290,28 @@ MX_DEV void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
         "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
       : "r"(taddr));
 }
+// 32 lanes x 8 consecutive 32-bit columns -> 8 registers per thread.
+MX_DEV void tmem_ld8(uint32_t taddr, uint32_t (&r)[8]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr));
+}
+// 32 lanes x 16 consecutive 32-bit columns -> 16 registers per thread.
+MX_DEV void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
 MX_DEV void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// Instruction descriptor of kind::f16 with bf16 A / B and fp32 D; a_mn / b_mn select the MN-major
+// (transposed) layout of A / B in shared memory instead of K-major.
+__host__ __device__ constexpr uint32_t f16_idesc(int M, int N, bool a_mn, bool b_mn) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((a_mn ? 1u : 0u) << 15) | ((b_mn ? 1u : 0u) << 16) |
+         ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
 
 // ---- CTA pairs (cluster of two, cta_group::2): the leader (rank 0) issues MMAs that read both CTAs'
 // shared memory and write both CTAs' TMEM.  No load here is multicast.

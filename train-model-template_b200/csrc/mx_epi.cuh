@@ -39,6 +39,10 @@ MX_DEV void stg64_if_hint(void* p, uint32_t lo, uint32_t hi, bool pred, uint64_t
   asm volatile("{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %3, 0;\n\t@q st.global.L2::cache_hint.v2.b32 [%0], {%1, %2}, %4;\n\t}"
                ::"l"(p), "r"(lo), "r"(hi), "r"((int)pred), "l"(pol));
 }
+MX_DEV void stg128_if_hint(void* p, uint32_t a, uint32_t b, uint32_t c, uint32_t d, bool pred, uint64_t pol) {
+  asm volatile("{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %5, 0;\n\t@q st.global.L2::cache_hint.v4.b32 [%0], {%1, %2, %3, %4}, %6;\n\t}"
+               ::"l"(p), "r"(a), "r"(b), "r"(c), "r"(d), "r"((int)pred), "l"(pol));
+}
 MX_DEV void stg8_if_hint(void* p, uint32_t v, bool pred, uint64_t pol) {
   asm volatile("{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %2, 0;\n\t@q st.global.L2::cache_hint.b8 [%0], %1, %3;\n\t}"
                ::"l"(p), "h"((uint16_t)v), "r"((int)pred), "l"(pol));
@@ -164,6 +168,40 @@ MX_DEV void quant_block16p(const uint32_t (&pk)[4][2], const QRows& qr, int64_t 
     stg64_if_hint(qr.code[h] + col0 + 6 * t, r0, r1, qr.live[h], qr.pol);   // code[h] points at column 2t
     stg8_if_hint(qr.scale[h] + soff, e, qr.slive[h], qr.pol);
   }
+}
+
+// The same quantization for a 32-column block held whole by one thread (pk[i] = columns 2i, 2i+1): the
+// 32 codes go to code[0 .. 31] in two 16-byte stores, the E8M0 scale to *scale; the same arithmetic as
+// quant_block16p, without the shuffles.
+MX_DEV void quant_row32(const uint32_t (&pk)[16], uint8_t* code, uint8_t* scale, bool live, bool slive, uint64_t pol) {
+  uint32_t m[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) m[i] = amax_xs_bf16x2(pk[2 * i], pk[2 * i + 1]);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) m[i] = amax_xs_bf16x2(m[2 * i], m[2 * i + 1]);
+  m[0] = amax_xs_bf16x2(amax_xs_bf16x2(m[0], m[1]), amax_xs_bf16x2(m[2], m[3]));
+  const uint32_t am = amax_xs_bf16x2(m[0], __byte_perm(m[0], 0u, 0x1032)) & 0x7FFFu;  // low half, sign cleared
+  const uint32_t e = mx_e8m0_of_amax(__uint_as_float(am << 16));
+  const uint16_t rcp = (uint16_t)(__float_as_uint(mx_e8m0_rcp(e)) >> 16);
+  uint32_t w[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const float2 v0 = scale_bf16x2(pk[2 * k], rcp), v1 = scale_bf16x2(pk[2 * k + 1], rcp);
+    w[k] = e4m3x2_sat(v0.x, v0.y) | (e4m3x2_sat(v1.x, v1.y) << 16);
+  }
+  stg128_if_hint(code, w[0], w[1], w[2], w[3], live, pol);
+  stg128_if_hint(code + 16, w[4], w[5], w[6], w[7], live, pol);
+  stg8_if_hint(scale, e, slive, pol);
+}
+
+// 16-byte shared-memory load / store (ordered with the surrounding barrier waits and arrivals).
+MX_DEV void lds128(uint32_t a, uint32_t* r) {
+  asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];" : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(a)
+               : "memory");
+}
+MX_DEV void sts128(uint32_t a, const uint32_t* v) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3])
+               : "memory");
 }
 
 // Byte offset of 16-byte chunk `chunk` of row `row` in a tile with RB-byte rows stored by TMA with the

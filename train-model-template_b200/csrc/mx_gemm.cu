@@ -617,8 +617,8 @@ MX_DEV void glu_body(const CUtensorMap* tmA, const CUtensorMap* tmB, const CUten
         fence_proxy_async();   // the staged tile is read by the TMA stores below
       }
       // 2. this tile's B_gate / B_up rows and A_down columns into shared memory
-      for (int i = et; i < 128 * (R / 8); i += EPI_THREADS) {
-        const int n = i / (R / 8), c = i % (R / 8);
+      for (int k = et; k < 128 * (R / 8); k += EPI_THREADS) {
+        const int n = k / (R / 8), c = k % (R / 8);
         const uint4 vg = __ldg(reinterpret_cast<const uint4*>(bg + ((int64_t)tn * 128 + n) * R + 8 * c));
         const uint4 vu = __ldg(reinterpret_cast<const uint4*>(bu + ((int64_t)tn * 128 + n) * R + 8 * c));
         const uint32_t o = swz<2 * R>((uint32_t)n, (uint32_t)c);
@@ -627,8 +627,8 @@ MX_DEV void glu_body(const CUtensorMap* tmA, const CUtensorMap* tmB, const CUten
         asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(s_bu + o), "r"(vu.x), "r"(vu.y), "r"(vu.z),
                      "r"(vu.w) : "memory");
       }
-      for (int i = et; i < R * 16; i += EPI_THREADS) {
-        const int j = i / 16, c8 = i % 16;
+      for (int k = et; k < R * 16; k += EPI_THREADS) {
+        const int j = k / 16, c8 = k % 16;
         const uint4 v = __ldg(reinterpret_cast<const uint4*>(ad + (int64_t)j * N + (int64_t)tn * 128 + 8 * c8));
         const uint32_t a = s_ad + (uint32_t)(c8 >> 3) * (R * 128) + swz<128>((uint32_t)j, (uint32_t)(c8 & 7));
         asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)

@@ -603,6 +603,443 @@ __global__ void __launch_bounds__(32 * (bwd_cons(R) + 1), 1)
   }
 }
 
+// ------------------------------------------------------------------------------------------------ backward, r = 16
+// The backward epilogue with every rank-16 product on the 5th-generation tensor cores (tcgen05.mma
+// kind::f16, fp32 accumulators in TMEM) and the element-wise work on rows held by threads.  Work item =
+// (row block of 256 rows, 32-column tile), column tile fastest; each CTA walks a contiguous run of `per`
+// items.  Warp 17 streams per item the [256 x 32] bf16 tiles of g, u and dh (64-byte rows, 64-byte
+// swizzle) and the tile's slices of B_gate, B_up ([32 n x 16], 32-byte swizzle) and A_down ([16 x 32 n],
+// 64-byte swizzle) into a 3-stage ring, and per row block its xa_gate, xa_up and dxd rows (three
+// [256 x 16] buffers, 32-byte swizzle).  Warp 16 (one elected lane) issues per item
+//   * the LoRA terms xa_gate B_gate^T, xa_up B_up^T and dxd A_down of the tile (2 halves of 128 rows x
+//     3 x 32 TMEM columns), one item ahead of the element-wise warps;
+//   * once those warps stored the tile's dg | du | h (bf16, [256 x 32] each, the g tile's layout) in
+//     shared memory: the per-row products [dg B_gate | du B_up | h A_down^T], accumulated in TMEM over the
+//     run's tiles of the row block (2 halves x 48 columns; B_gate / B_up slices read as MN-major B), and
+//     the column products [dg | du | h]^T [xa_gate | xa_up | dxd] over the block's 256 rows: one M = 128,
+//     N = 48 MMA per 16 rows with the three 32-column tiles as MN-major A (M atoms 16 KB apart; the
+//     fourth atom reads the row buffers and lands in result rows 96-127, which nobody reads) and the three
+//     row buffers as MN-major B (N atoms 8 KB apart).  The diagonal 32 x 16 blocks of the 128 x 48 result
+//     are dB_gate^T, dB_up^T and dA_down^T of the tile; two result buffers alternate.
+// Warps 0-15: warp w holds block rows 128 h + 32 q + lane (h = (w / 4) % 2, q = w % 4: its TMEM lane
+// quarter) and columns 16 c .. 16 c + 15 (c = w / 8) of the tile; warps w and w + 8 form a pair that
+// shares rows.  Each thread reads its LoRA terms from TMEM and g, u, dh from shared memory, computes
+// dg, du and h with the reference's rounding points, and quantizes dg and du: the two threads of a row
+// exchange their half-block abs-maxima through shared memory, and the codes leave through shared memory
+// as one TMA store per warp.  The warps then store the operand tiles and drain the finished products into
+// the fp32 partial buffers (warps 0-2: the previous tile's column products; all: the per-row products
+// when the run leaves a row block).  Every wait is bounded, and the two warps of a pair leave together;
+// no atomics, so the result is deterministic.
+constexpr int BT_ROWS = 256, BT_BN = 32, BT_ST = 3, BT_CONS = 16, BT_THREADS = 32 * (BT_CONS + 2);
+constexpr int BT_TILE = BT_ROWS * BT_BN * 2;           // 16 KB: [256 x 32] bf16
+constexpr int BT_SLICE = 32 * 16 * 2;                  // 1 KB: [32 x 16] or [16 x 32] bf16
+constexpr int BT_STAGE = 3 * BT_TILE + 3 * BT_SLICE;   // g | u | dh | bg | bu | ad
+constexpr int BT_RB = BT_ROWS * 16 * 2;                // 8 KB: one [256 x 16] row buffer
+constexpr int BT_NBARS = 2 * BT_ST + 12;
+constexpr size_t BT_SMEM = 1024 + (size_t)BT_ST * BT_STAGE + 3 * BT_TILE + 3 * BT_RB + BT_NBARS * 8 + 16;
+static_assert(BT_SMEM <= 232448, "backward epilogue: shared memory");
+static_assert(BT_STAGE % 1024 == 0 && BT_RB % 1024 == 0, "backward epilogue: swizzle alignment");
+// TMEM columns: LoRA terms (2 halves x [g | u | dh] x 32), per-row products (2 halves x 48), column
+// products (2 buffers x 48)
+constexpr uint32_t BT_REC = 0, BT_ROWC = 192, BT_COLC = 288, BT_TMEM_COLS = 512;
+
+__global__ void __launch_bounds__(BT_THREADS, 1)
+    k_mlp_bwd_tc(const __grid_constant__ CUtensorMap tm_gu, const __grid_constant__ CUtensorMap tm_dh,
+                 const __grid_constant__ CUtensorMap tm_bg, const __grid_constant__ CUtensorMap tm_bu,
+                 const __grid_constant__ CUtensorMap tm_ad, const __grid_constant__ CUtensorMap tm_xs,
+                 const __grid_constant__ CUtensorMap tm_dxd, const __grid_constant__ CUtensorMap tm_q,
+                 uint8_t* __restrict__ s, float* __restrict__ dxa_part, float* __restrict__ dbg_part,
+                 float* __restrict__ dbu_part, float* __restrict__ dad_part, int T, int Tpad, int N, float s_g,
+                 float s_u, int per, int write_q, int* err) {
+  constexpr int R = 16, R3 = 3 * R;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align1024(smem_raw);
+  uint8_t* opbuf = smem + BT_ST * BT_STAGE;   // dg | du | h tiles
+  uint8_t* rowbuf = opbuf + 3 * BT_TILE;      // xa_gate | xa_up | dxd rows of the block
+  uint64_t* full = reinterpret_cast<uint64_t*>(rowbuf + 3 * BT_RB);   // [BT_ST] TMA bytes of a stage
+  uint64_t* empty = full + BT_ST;             // [BT_ST] 16 element-wise warps + the commit of the tile's products
+  uint64_t* rows_full = empty + BT_ST;        // TMA bytes of a block's row buffers
+  uint64_t* rows_empty = rows_full + 1;       // commit after the block's last products
+  uint64_t* lora_full = rows_full + 2;        // commit after a tile's LoRA-term MMAs
+  uint64_t* lora_empty = rows_full + 3;       // 16 element-wise warps read the LoRA terms
+  uint64_t* op_full = rows_full + 4;          // 16 element-wise warps stored dg | du | h
+  uint64_t* op_empty = rows_full + 5;         // commit after the tile's products
+  uint64_t* colp_full = rows_full + 6;        // [2] commit after a tile's column products
+  uint64_t* colp_empty = rows_full + 8;       // [2] warps 0-2 drained them
+  uint64_t* row_full = rows_full + 10;        // commit after a block's last per-row products
+  uint64_t* row_empty = rows_full + 11;       // 16 element-wise warps drained them
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(rows_full + 12);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nt = N / BT_BN;
+  const int items = ((Tpad + BT_ROWS - 1) / BT_ROWS) * nt;
+  const int it_lo = blockIdx.x * per, it_hi = min(it_lo + per, items), cnt = max(it_hi - it_lo, 0);
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < BT_ST; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], BT_CONS + 1);
+    }
+    mbar_init(rows_full, 1);
+    mbar_init(rows_empty, 1);
+    mbar_init(lora_full, 1);
+    mbar_init(lora_empty, BT_CONS);
+    mbar_init(op_full, BT_CONS);
+    mbar_init(op_empty, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&colp_full[i], 1);
+      mbar_init(&colp_empty[i], 3);
+    }
+    mbar_init(row_full, 1);
+    mbar_init(row_empty, BT_CONS);
+    fence_barrier_init();
+  }
+  if (warp == BT_CONS) tmem_alloc(tmem_slot, BT_TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t s_ring = smem_u32(smem), s_op = smem_u32(opbuf), s_rows = smem_u32(rowbuf);
+
+  if (warp == BT_CONS + 1) {   // TMA producer: the ring, and the row buffers when a row block starts
+    if (lane == 0) {
+      prefetch_tmap(&tm_gu);
+      prefetch_tmap(&tm_dh);
+      prefetch_tmap(&tm_bg);
+      prefetch_tmap(&tm_bu);
+      prefetch_tmap(&tm_ad);
+      prefetch_tmap(&tm_xs);
+      prefetch_tmap(&tm_dxd);
+    }
+    // two queues polled in turn (lane 0 tests, the warp follows): the next row block's rows (once the
+    // previous block's products are done: rows_empty) and the next tile (once its stage is free)
+    int stage = 0;
+    uint32_t phase = 0;
+    int issued = 0, row_loads = 0, rows_at = 0;   // rows_at: local index of the next row block's first tile
+    uint64_t t0 = mx_globaltimer();
+    while (issued < cnt || rows_at < cnt) {
+      bool prog = false;
+      if (rows_at < cnt &&
+          (row_loads == 0 ||
+           __shfl_sync(0xffffffffu, lane == 0 ? (int)mbar_test(rows_empty, (uint32_t)((row_loads - 1) & 1)) : 0, 0))) {
+        const int sbr = (it_lo + rows_at) / nt;
+        if (lane == 0) {
+          mbar_arrive_expect_tx(rows_full, 3 * BT_RB);
+          tma_load_2d(rowbuf, &tm_xs, rows_full, 0, sbr * BT_ROWS);
+          tma_load_2d(rowbuf + BT_RB, &tm_xs, rows_full, R, sbr * BT_ROWS);
+          tma_load_2d(rowbuf + 2 * BT_RB, &tm_dxd, rows_full, 0, sbr * BT_ROWS);
+        }
+        __syncwarp();
+        ++row_loads;
+        rows_at = (sbr + 1) * nt - it_lo;
+        prog = true;
+      }
+      if (issued < cnt && __shfl_sync(0xffffffffu, lane == 0 ? (int)mbar_test(&empty[stage], phase ^ 1) : 0, 0)) {
+        const int it = it_lo + issued;
+        const int n0 = (it % nt) * BT_BN, r0 = (it / nt) * BT_ROWS;
+        if (lane == 0) {
+          uint8_t* dst = smem + stage * BT_STAGE;
+          uint64_t* fb = &full[stage];
+          mbar_arrive_expect_tx(fb, BT_STAGE);
+          tma_load_2d(dst, &tm_gu, fb, n0, r0);
+          tma_load_2d(dst + BT_TILE, &tm_gu, fb, N + n0, r0);
+          tma_load_2d(dst + 2 * BT_TILE, &tm_dh, fb, n0, r0);
+          tma_load_2d(dst + 3 * BT_TILE, &tm_bg, fb, 0, n0);
+          tma_load_2d(dst + 3 * BT_TILE + BT_SLICE, &tm_bu, fb, 0, n0);
+          tma_load_2d(dst + 3 * BT_TILE + 2 * BT_SLICE, &tm_ad, fb, n0, 0);
+        }
+        __syncwarp();
+        ++issued;
+        if (++stage == BT_ST) {
+          stage = 0;
+          phase ^= 1;
+        }
+        prog = true;
+      }
+      if (prog) {
+        t0 = mx_globaltimer();
+      } else {
+        if (mx_globaltimer() - t0 > MX_WAIT_LIMIT_NS) {
+          if (lane == 0) mx_set_error(err, MX_DEV_TIMEOUT_PRODUCER);
+          break;
+        }
+        __nanosleep(64);
+      }
+    }
+    // leave no copy in flight: wait (bounded) for the last load of every stage that was used
+    for (int k = 0; k < BT_ST && k < issued; ++k) {
+      const int i = issued - 1 - k, st = i % BT_ST;
+      mbar_wait(&full[st], (uint32_t)((i / BT_ST) & 1), err, MX_DEV_TIMEOUT_PRODUCER);
+    }
+    if (row_loads > 0) mbar_wait(rows_full, (uint32_t)((row_loads - 1) & 1), err, MX_DEV_TIMEOUT_PRODUCER);
+  } else if (warp == BT_CONS) {   // MMA issue: the whole warp waits, lane 0 issues and commits
+    constexpr uint32_t ID_REC = f16_idesc(128, 32, false, false);      // B = B_gate / B_up slice [32 n][16 k]
+    constexpr uint32_t ID_REC_AD = f16_idesc(128, 32, false, true);    // B = A_down slice [16 k][32 n]
+    constexpr uint32_t ID_ROW = f16_idesc(128, 16, false, false);      // B = A_down slice [16 n][32 k]
+    constexpr uint32_t ID_ROW_MN = f16_idesc(128, 16, false, true);    // B = B_gate / B_up slice [32 k][16 n]
+    constexpr uint32_t ID_COL = f16_idesc(128, 48, true, true);        // A = [dg | du | h] tiles, B = rows
+    int n_rec = 0, n_prod = 0;
+    // the LoRA terms of local tile t (the whole block's rows: two M = 128 halves)
+    auto rec = [&](int t, bool first, int b) -> bool {
+      const int st = t % BT_ST;
+      if (first && !mbar_wait(rows_full, (uint32_t)(b & 1), err, MX_DEV_TIMEOUT_MMA)) return false;
+      if (!mbar_wait(&full[st], (uint32_t)((t / BT_ST) & 1), err, MX_DEV_TIMEOUT_MMA)) return false;
+      if (t > 0 && !mbar_wait(lora_empty, (uint32_t)((t - 1) & 1), err, MX_DEV_TIMEOUT_MMA_TMEM)) return false;
+      tc_fence_after();
+      if (lane == 0) {
+        const uint32_t sl = s_ring + st * BT_STAGE + 3 * BT_TILE;   // bg | bu | ad slices
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const uint32_t d = tmem + BT_REC + 96 * h, ro = s_rows + 4096 * h;   // rows 128 h .. 128 h + 127
+          umma_bf16(d, make_sdesc(ro, 0, 256, 6), make_sdesc(sl, 0, 256, 6), ID_REC, 0u);
+          umma_bf16(d + 32, make_sdesc(ro + BT_RB, 0, 256, 6), make_sdesc(sl + BT_SLICE, 0, 256, 6), ID_REC, 0u);
+          umma_bf16(d + 64, make_sdesc(ro + 2 * BT_RB, 0, 256, 6), make_sdesc(sl + 2 * BT_SLICE, BT_SLICE, 512, 4),
+                    ID_REC_AD, 0u);
+        }
+        umma_commit(lora_full);
+      }
+      __syncwarp();
+      ++n_rec;
+      return true;
+    };
+    int blk = -1;
+    bool rec_ahead = false;
+    for (int t = 0; t < cnt; ++t) {
+      const int it = it_lo + t;
+      const bool first = t == 0 || it % nt == 0;
+      const bool last = t + 1 == cnt || (it + 1) % nt == 0;
+      if (first) ++blk;
+      if (!rec_ahead && !rec(t, first, blk)) break;
+      rec_ahead = false;
+      if (!last) {   // the next tile's LoRA terms, while the element-wise warps work on this one
+        if (!rec(t + 1, false, blk)) break;
+        rec_ahead = true;
+      }
+      if (!mbar_wait(op_full, (uint32_t)(t & 1), err, MX_DEV_TIMEOUT_MMA)) break;
+      if (t >= 2 && !mbar_wait(&colp_empty[t & 1], (uint32_t)(((t - 2) >> 1) & 1), err, MX_DEV_TIMEOUT_MMA_TMEM))
+        break;
+      if (first && blk > 0 && !mbar_wait(row_empty, (uint32_t)((blk - 1) & 1), err, MX_DEV_TIMEOUT_MMA_TMEM)) break;
+      tc_fence_after();
+      if (lane == 0) {
+        const int st = t % BT_ST;
+        const uint32_t sl = s_ring + st * BT_STAGE + 3 * BT_TILE;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const uint32_t d = tmem + BT_ROWC + 48 * h, ao = s_op + 8192 * h;   // rows 128 h .. of the tiles
+#pragma unroll
+          for (int k = 0; k < 2; ++k) {   // K = the tile's 32 columns, 16 per MMA
+            const uint32_t acc = (first && k == 0) ? 0u : 1u;
+            umma_bf16(d, make_sdesc(ao + 32 * k, 0, 512, 4), make_sdesc(sl + 512 * k, BT_SLICE, 256, 6), ID_ROW_MN,
+                      acc);
+            umma_bf16(d + 16, make_sdesc(ao + BT_TILE + 32 * k, 0, 512, 4),
+                      make_sdesc(sl + BT_SLICE + 512 * k, BT_SLICE, 256, 6), ID_ROW_MN, acc);
+            umma_bf16(d + 32, make_sdesc(ao + 2 * BT_TILE + 32 * k, 0, 512, 4),
+                      make_sdesc(sl + 2 * BT_SLICE + 32 * k, 0, 512, 4), ID_ROW, acc);
+          }
+        }
+        const uint32_t dc = tmem + BT_COLC + 48 * (uint32_t)(t & 1);
+#pragma unroll 4
+        for (int k = 0; k < BT_ROWS / 16; ++k)   // K = the block's 256 rows, 16 per MMA
+          umma_bf16(dc, make_sdesc(s_op + 1024 * k, BT_TILE, 512, 4), make_sdesc(s_rows + 512 * k, BT_RB, 256, 6),
+                    ID_COL, k > 0 ? 1u : 0u);
+        umma_commit(op_empty);
+        umma_commit(&empty[st]);
+        umma_commit(&colp_full[t & 1]);
+        if (last) {
+          umma_commit(row_full);
+          umma_commit(rows_empty);
+        }
+      }
+      __syncwarp();
+      ++n_prod;
+    }
+    // no MMA in flight at exit (bounded): the last commits cover every MMA issued before them
+    if (n_prod > 0) mbar_wait(op_empty, (uint32_t)((n_prod - 1) & 1), err, MX_DEV_TIMEOUT_MMA);
+    if (n_rec > 0) mbar_wait(lora_full, (uint32_t)((n_rec - 1) & 1), err, MX_DEV_TIMEOUT_MMA);
+  } else {   // element-wise warps 0-15
+    const int c = warp >> 3, hq = warp & 7, half = hq >> 2, qw = hq & 3;
+    const int r0w = half * 128 + qw * 32;                 // first block row of the pair (warps hq, hq + 8)
+    const int rl = r0w + lane;                            // this thread's block row
+    const uint32_t pid = 1u + (uint32_t)hq;               // the pair's named barrier
+    const uint32_t lb = (uint32_t)(qw * 32) << 16;        // TMEM lane quarter
+    const uint32_t trec = tmem + lb + BT_REC + 96 * half + 16 * c, trow = tmem + lb + BT_ROWC + 48 * half;
+    const uint32_t o_row = (uint32_t)rl * 64, sw = (uint32_t)((rl >> 1) & 3);   // 64-byte rows, 64-byte swizzle
+    const float2 sg2 = make_float2(s_g, s_g), su2 = make_float2(s_u, s_u);
+    const int64_t N2 = 2 * (int64_t)N;
+    const uint64_t pol = l2_evict_first();
+    // column products of local tile tt (warps 0-2, TMEM lane quarters 0-2: dg, du, h columns)
+    auto drain_col = [&](int tt) -> bool {
+      const int b = tt & 1;
+      if (!mbar_wait(&colp_full[b], (uint32_t)((tt >> 1) & 1), err, MX_DEV_TIMEOUT_EPILOGUE)) return false;
+      tc_fence_after();
+      uint32_t v[16];
+      tmem_ld16(tmem + lb + BT_COLC + 48 * b + 16 * warp, v);
+      tmem_ld_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&colp_empty[b]);
+      const int itt = it_lo + tt;
+      const int64_t sbt = itt / nt, n = (int64_t)(itt % nt) * BT_BN + lane;
+      if (warp < 2) {   // [n_blocks, N, r]: element (n, j)
+        uint4* P = reinterpret_cast<uint4*>((warp == 0 ? dbg_part : dbu_part) + (sbt * N + n) * R);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) P[k] = make_uint4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
+      } else {          // [n_blocks, r, N]: element (j, n)
+        float* P = dad_part + sbt * R * N + n;
+#pragma unroll
+        for (int j = 0; j < R; ++j) P[(int64_t)j * N] = __uint_as_float(v[j]);
+      }
+      return true;
+    };
+    int stage = 0;
+    uint32_t phase = 0;
+    int blk = -1;
+    bool ok = true;
+    for (int t = 0; t < cnt; ++t) {
+      const int it = it_lo + t, sbi = it / nt, n0 = (it % nt) * BT_BN;
+      const bool last = t + 1 == cnt || (it + 1) % nt == 0;
+      if (t == 0 || n0 == 0) ++blk;
+      const int64_t row = (int64_t)sbi * BT_ROWS + rl;
+      const bool good = ok && mbar_wait(&full[stage], phase, err, MX_DEV_TIMEOUT_EPILOGUE) &&
+                        mbar_wait(lora_full, (uint32_t)(t & 1), err, MX_DEV_TIMEOUT_EPILOGUE);
+      if (bar_any(pid, 64, !good)) {   // both warps of the pair leave together
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t sb = s_ring + (uint32_t)stage * BT_STAGE;
+      uint32_t pg[8], pu[8], ph[8];   // dg, du, h of the thread's 16 columns, bf16 pairs
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {   // 8 columns at a time: 16 c + 8 k ..
+        uint32_t lg[8], lu[8], ld[8], G[4], U[4], D[4];
+        tmem_ld8(trec + 8 * k, lg);
+        tmem_ld8(trec + 32 + 8 * k, lu);
+        tmem_ld8(trec + 64 + 8 * k, ld);
+        const uint32_t a = sb + o_row + (((uint32_t)(2 * c + k) ^ sw) << 4);
+        lds128(a, G);
+        lds128(a + BT_TILE, U);
+        lds128(a + 2 * BT_TILE, D);
+        tmem_ld_wait();
+        if (k == 1) {   // the LoRA terms are in registers: the next tile's may overwrite them
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(lora_empty);
+        }
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 gg = up2(rn2(__ffma2_rn(sg2, make_float2(__uint_as_float(lg[2 * e]), __uint_as_float(lg[2 * e + 1])), up2(G[e]))));
+          const float2 uu = up2(rn2(__ffma2_rn(su2, make_float2(__uint_as_float(lu[2 * e]), __uint_as_float(lu[2 * e + 1])), up2(U[e]))));
+          const float2 sig = sigmoid2(gg);
+          const float2 sl = __fmul2_rn(gg, sig);                                 // silu(g)
+          ph[4 * k + e] = rn2(__fmul2_rn(sl, uu));                                // h = bf16(silu * u)
+          const float2 dh = up2(rn2(add_bf16x2_f32(D[e], make_float2(__uint_as_float(ld[2 * e]), __uint_as_float(ld[2 * e + 1])))));
+          pu[4 * k + e] = rn2(__fmul2_rn(dh, sl));                                // du = bf16(dh * silu)
+          const float2 om = __ffma2_rn(sig, make_float2(-1.f, -1.f), make_float2(1.f, 1.f));   // 1 - sig
+          const float2 f = __ffma2_rn(gg, om, make_float2(1.f, 1.f));             // g (1 - sig) + 1
+          pg[4 * k + e] = rn2(__fmul2_rn(__fmul2_rn(__fmul2_rn(dh, uu), sig), f));   // dg
+        }
+      }
+      // (1) both warps of the pair have read the stage's rows r0w .. r0w + 31: from here on the pair's u rows
+      // carry the abs-max exchange and its g rows the staged codes
+      bar_sync(pid, 64);
+      const uint32_t xch = sb + BT_TILE + (uint32_t)r0w * 64 + (uint32_t)lane * 8;   // 8 bytes per row
+      uint32_t amx = 0;   // abs-max of this thread's 16 columns: dg (low half) | du (high half), signs cleared
+      if (write_q) {
+        uint32_t mg = amax_xs_bf16x2(amax_xs_bf16x2(pg[0], pg[1]), amax_xs_bf16x2(pg[2], pg[3]));
+        mg = amax_xs_bf16x2(mg, amax_xs_bf16x2(amax_xs_bf16x2(pg[4], pg[5]), amax_xs_bf16x2(pg[6], pg[7])));
+        uint32_t mu = amax_xs_bf16x2(amax_xs_bf16x2(pu[0], pu[1]), amax_xs_bf16x2(pu[2], pu[3]));
+        mu = amax_xs_bf16x2(mu, amax_xs_bf16x2(amax_xs_bf16x2(pu[4], pu[5]), amax_xs_bf16x2(pu[6], pu[7])));
+        // each half of mg / mu is a column-parity maximum: fold them, (dg | du) in one bf16x2
+        amx = amax_xs_bf16x2(__byte_perm(mg, mu, 0x5410), __byte_perm(mg, mu, 0x7632)) & 0x7FFF7FFFu;
+        asm volatile("st.shared.b32 [%0], %1;" ::"r"(xch + 4 * c), "r"(amx) : "memory");
+      }
+      bar_sync(pid, 64);   // (2)
+      if (write_q) {
+        uint32_t oth;
+        asm volatile("ld.shared.b32 %0, [%1];" : "=r"(oth) : "r"(xch + 4 * (1 - c)) : "memory");
+        const uint32_t mm = max_bf16x2(amx, oth);   // the rows' 32-column abs-maxima (NaN propagates)
+        const uint32_t eg = mx_e8m0_of_amax(bf16_lo(mm)), eu = mx_e8m0_of_amax(bf16_hi(mm));
+        const uint16_t rg = (uint16_t)(__float_as_uint(mx_e8m0_rcp(eg)) >> 16);
+        const uint16_t ru = (uint16_t)(__float_as_uint(mx_e8m0_rcp(eu)) >> 16);
+        uint32_t wg[4], wu[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float2 g0 = scale_bf16x2(pg[2 * k], rg), g1 = scale_bf16x2(pg[2 * k + 1], rg);
+          const float2 u0 = scale_bf16x2(pu[2 * k], ru), u1 = scale_bf16x2(pu[2 * k + 1], ru);
+          wg[k] = e4m3x2_sat(g0.x, g0.y) | (e4m3x2_sat(g1.x, g1.y) << 16);
+          wu[k] = e4m3x2_sat(u0.x, u0.y) | (e4m3x2_sat(u1.x, u1.y) << 16);
+        }
+        // the warp's [32 rows][dg | du][16] code box, in the pair's g rows (1 KB per warp)
+        const uint32_t box = sb + (uint32_t)r0w * 64 + (uint32_t)c * 1024;
+        sts128(box + (uint32_t)lane * 32, wg);
+        sts128(box + (uint32_t)lane * 32 + 16, wu);
+        fence_proxy_async();
+        __syncwarp();
+        const int64_t z = (int64_t)sbi * BT_ROWS + r0w;
+        if (lane == 0 && z < T) {   // rows >= T of the box are clipped by the store
+          tma_store_3d_hint(&tm_q, smem + (box - s_ring), n0 + 16 * c, 0, (int)z, pol);
+          bulk_commit();
+        }
+        // the scale bytes: dg's by the thread of column half 0, du's by the other
+        if (row < Tpad)
+          stg8_if_hint(s + mx_scale_offset(row, (c == 0 ? n0 : N + n0) / 32, N2), c == 0 ? eg : eu, true, pol);
+      }
+      // dg | du | h into the operand tiles, once the previous tile's products have read them
+      if (t > 0 && !mbar_wait(op_empty, (uint32_t)((t - 1) & 1), err, MX_DEV_TIMEOUT_EPILOGUE)) ok = false;
+      if (ok) {
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+          const uint32_t a = s_op + o_row + (((uint32_t)(2 * c + k) ^ sw) << 4);
+          sts128(a, pg + 4 * k);
+          sts128(a + BT_TILE, pu + 4 * k);
+          sts128(a + 2 * BT_TILE, ph + 4 * k);
+        }
+        fence_proxy_async();   // read next by the tensor cores
+        __syncwarp();
+        if (lane == 0) mbar_arrive(op_full);
+      }
+      if (ok && warp < 3 && t > 0 && !drain_col(t - 1)) ok = false;
+      if (ok && last) {   // leaving the row block: its per-row products into this CTA's slot
+        if (!mbar_wait(row_full, (uint32_t)(blk & 1), err, MX_DEV_TIMEOUT_EPILOGUE)) {
+          ok = false;
+        } else {
+          tc_fence_after();
+          uint32_t v0[16], v1[16];   // column half 0: dg B_gate and h A_down^T; half 1: du B_up
+          tmem_ld16(trow + (c == 0 ? 0 : 16), v0);
+          if (c == 0) tmem_ld16(trow + 32, v1);
+          tmem_ld_wait();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(row_empty);
+          if (row < T) {
+            const int slot = (int)blockIdx.x - (sbi * nt) / per;
+            uint4* P = reinterpret_cast<uint4*>(dxa_part + ((int64_t)slot * T + row) * R3) + (c == 0 ? 0 : 4);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) P[k] = make_uint4(v0[4 * k], v0[4 * k + 1], v0[4 * k + 2], v0[4 * k + 3]);
+            if (c == 0) {
+#pragma unroll
+              for (int k = 0; k < 4; ++k) P[8 + k] = make_uint4(v1[4 * k], v1[4 * k + 1], v1[4 * k + 2], v1[4 * k + 3]);
+            }
+          }
+        }
+      }
+      // the stage is free once the code store has read its g rows
+      if (write_q && lane == 0) bulk_wait_read0();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[stage]);
+      if (++stage == BT_ST) {
+        stage = 0;
+        phase ^= 1;
+      }
+    }
+    if (ok && warp < 3 && cnt > 0) drain_col(cnt - 1);
+    if (write_q && lane == 0) bulk_wait0();   // the code stores are complete
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == BT_CONS) tmem_dealloc(tmem, BT_TMEM_COLS);
+}
+
 // ------------------------------------------------------------------------------------------------ skinny
 // E4M3 bytes that are NaN (S.1111.111) -> the canonical 0x7F, four codes per word.
 MX_DEV uint32_t nan_canon4(uint32_t w) {
@@ -1347,7 +1784,7 @@ struct BwdPlan {
 };
 BwdPlan bwd_plan(int64_t T, int64_t N, int r) {
   BwdPlan p;
-  p.sb = r == 16 ? bwd_rows(16) : bwd_rows(32);
+  p.sb = r == 16 ? BT_ROWS : bwd_rows(32);
   const int64_t tpad = (T + 127) / 128 * 128;
   p.nsb = (int)((tpad + p.sb - 1) / p.sb);
   p.nt = (int)(N / BWD_BN);
@@ -1404,26 +1841,45 @@ extern "C" int mxm_mlp_bwd_epilogue(const void* gu, const void* xs, const void* 
                               (uint64_t)(2 * N), BWD_BN, r, CU_TENSOR_MAP_SWIZZLE_64B))
     return e;
   CUtensorMap txs, tdxd;
+  // xs: r = 16 reads xa_gate and xa_up as two [rows x 16] boxes (32-byte rows), r = 32 as one [rows x 64] box
   if (int e = mx_make_tmap_2d(&txs, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, xs, (uint64_t)(2 * r), (uint64_t)T,
-                              (uint64_t)(4 * r), 2 * r, super_block, r == 16 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B))
+                              (uint64_t)(4 * r), r == 16 ? r : 2 * r, super_block,
+                              r == 16 ? CU_TENSOR_MAP_SWIZZLE_32B : CU_TENSOR_MAP_SWIZZLE_128B))
     return e;
   if (int e = mx_make_tmap_2d(&tdxd, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, dxd, (uint64_t)r, (uint64_t)T,
                               (uint64_t)(2 * r), r, super_block, r == 16 ? CU_TENSOR_MAP_SWIZZLE_32B : CU_TENSOR_MAP_SWIZZLE_64B))
     return e;
   const int64_t tpad = (T + 127) / 128 * 128;
-  const size_t smem = bwd_smem(r);
   cudaStream_t st = (cudaStream_t)stream;
-  auto go = [&](auto kern) -> int {
-    cudaError_t e = mx_smem_attr((const void*)kern, smem);
+  if (r == 16) {
+    // codes of [dg | du] as a [T][2][N] byte array: one [32 rows][2][16] box per warp and tile
+    CUtensorMap tq = tgu;   // unused when q is null
+    if (q) {
+      MX_CHECK_ARG(mx_aligned(q, 16), "mxm_mlp_bwd_epilogue: q must be 16-byte aligned");
+      const uint64_t dims[3] = {(uint64_t)N, 2, (uint64_t)T}, strides[2] = {(uint64_t)N, (uint64_t)(2 * N)};
+      const uint32_t box[3] = {16, 2, 32};
+      if (int e = mx_make_tmap_3d(&tq, CU_TENSOR_MAP_DATA_TYPE_UINT8, q, dims, strides, box,
+                                  CU_TENSOR_MAP_SWIZZLE_NONE))
+        return e;
+    }
+    cudaError_t e = mx_smem_attr((const void*)k_mlp_bwd_tc, BT_SMEM);
     if (e != cudaSuccess) return mx_cuda_status(e, "mlp bwd epilogue: set smem");
-    kern<<<p.grid, 32 * (bwd_cons(r) + 1), smem, st>>>(tgu, tdh, tbg, tbu, tad, txs, tdxd, (uint8_t*)q, (uint8_t*)s,
-                                                       (float*)dxa_part, (float*)dbg_part, (float*)dbu_part,
-                                                       (float*)dad_part, (int)T, (int)tpad, (int)N, s_g, s_u, p.per,
-                                                       q != nullptr, mx_dev_error_ptr());
+    k_mlp_bwd_tc<<<p.grid, BT_THREADS, BT_SMEM, st>>>(tgu, tdh, tbg, tbu, tad, txs, tdxd, tq, (uint8_t*)s,
+                                                      (float*)dxa_part, (float*)dbg_part, (float*)dbu_part,
+                                                      (float*)dad_part, (int)T, (int)tpad, (int)N, s_g, s_u, p.per,
+                                                      q != nullptr, mx_dev_error_ptr());
     mx_note_launch();
     return mx_launch_status("mlp bwd epilogue");
-  };
-  return r == 16 ? go(k_mlp_bwd<16>) : go(k_mlp_bwd<32>);
+  }
+  const size_t smem = bwd_smem(r);
+  cudaError_t e = mx_smem_attr((const void*)k_mlp_bwd<32>, smem);
+  if (e != cudaSuccess) return mx_cuda_status(e, "mlp bwd epilogue: set smem");
+  k_mlp_bwd<32><<<p.grid, 32 * (bwd_cons(32) + 1), smem, st>>>(
+      tgu, tdh, tbg, tbu, tad, txs, tdxd, (uint8_t*)q, (uint8_t*)s, (float*)dxa_part, (float*)dbg_part,
+      (float*)dbu_part, (float*)dad_part, (int)T, (int)tpad, (int)N, s_g, s_u, p.per, q != nullptr,
+      mx_dev_error_ptr());
+  mx_note_launch();
+  return mx_launch_status("mlp bwd epilogue");
 }
 
 extern "C" int mxm_mlp_bwd_reduce(const void* dxa_part, const void* dbg_part, const void* dbu_part,

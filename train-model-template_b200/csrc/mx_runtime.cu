@@ -152,17 +152,19 @@ static EncodeTiledFn get_encoder() {
   return fn;
 }
 
-int mx_make_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, uint32_t elem_bytes, const void* base,
-                    uint64_t inner, uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner,
-                    uint32_t box_outer, CUtensorMapSwizzle swizzle) {
+// Tiled tensor map of rank 2 or 3: dims / box innermost first, strides (bytes) of dims 1 .. rank-1.
+static int make_tmap(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, int rank, const uint64_t* dims,
+                     const uint64_t* strides, const uint32_t* box, CUtensorMapSwizzle swizzle) {
   EncodeTiledFn enc = get_encoder();
   if (!enc) {
     mx_set_last_error("cuTensorMapEncodeTiled unavailable from the driver");
     return MXM_ERR_CUDA;
   }
-  if (((uintptr_t)base & 15) || (row_stride_bytes & 15)) {
-    mx_set_last_error("TMA operand not 16-byte aligned (base %p, row stride %llu bytes)", base,
-                      (unsigned long long)row_stride_bytes);
+  bool aligned = ((uintptr_t)base & 15) == 0;
+  for (int i = 0; i + 1 < rank; ++i) aligned = aligned && (strides[i] & 15) == 0;
+  if (!aligned) {
+    mx_set_last_error("TMA operand not 16-byte aligned (base %p, stride %llu bytes)", base,
+                      (unsigned long long)strides[0]);
     return MXM_ERR_ARG;
   }
   // The encoder is a driver call and needs a current context; the runtime binds the primary context to
@@ -176,17 +178,34 @@ int mx_make_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, uint32_t elem_b
     if (e != cudaSuccess) return mx_cuda_status(e, "bind the device context for cuTensorMapEncodeTiled");
     bound = true;
   }
-  cuuint64_t dims[2] = {inner, outer};
-  cuuint64_t strides[1] = {row_stride_bytes};
-  cuuint32_t box[2] = {box_inner, box_outer};
-  cuuint32_t estr[2] = {1, 1};
-  (void)elem_bytes;
-  CUresult r = enc(map, dtype, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+  cuuint64_t d[3], st[2];
+  cuuint32_t b[3], estr[3] = {1, 1, 1};
+  for (int i = 0; i < rank; ++i) {
+    d[i] = dims[i];
+    b[i] = box[i];
+    if (i + 1 < rank) st[i] = strides[i];
+  }
+  CUresult r = enc(map, dtype, (cuuint32_t)rank, const_cast<void*>(base), d, st, b, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                    swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
-    mx_set_last_error("cuTensorMapEncodeTiled failed (%d) for [%llu x %llu] box [%u x %u]", (int)r,
-                      (unsigned long long)outer, (unsigned long long)inner, box_outer, box_inner);
+    mx_set_last_error("cuTensorMapEncodeTiled failed (%d) for a rank-%d map, dims [%llu x %llu], box [%u x %u]",
+                      (int)r, rank, (unsigned long long)dims[rank - 1], (unsigned long long)dims[0], box[rank - 1],
+                      box[0]);
     return MXM_ERR_CUDA;
   }
   return MXM_OK;
+}
+
+int mx_make_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, uint32_t elem_bytes, const void* base,
+                    uint64_t inner, uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner,
+                    uint32_t box_outer, CUtensorMapSwizzle swizzle) {
+  (void)elem_bytes;
+  const uint64_t dims[2] = {inner, outer}, strides[1] = {row_stride_bytes};
+  const uint32_t box[2] = {box_inner, box_outer};
+  return make_tmap(map, dtype, base, 2, dims, strides, box, swizzle);
+}
+
+int mx_make_tmap_3d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, const uint64_t (&dims)[3],
+                    const uint64_t (&strides_bytes)[2], const uint32_t (&box)[3], CUtensorMapSwizzle swizzle) {
+  return make_tmap(map, dtype, base, 3, dims, strides_bytes, box, swizzle);
 }

@@ -26,6 +26,10 @@ int mx_make_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, uint32_t elem_b
                     uint64_t inner, uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner,
                     uint32_t box_outer, CUtensorMapSwizzle swizzle);
 
+// 3-D tiled tensor map: dims and box innermost first, strides (bytes) of dims 1 and 2.
+int mx_make_tmap_3d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, const uint64_t (&dims)[3],
+                    const uint64_t (&strides_bytes)[2], const uint32_t (&box)[3], CUtensorMapSwizzle swizzle);
+
 #define MX_CHECK_ARG(cond, ...)        \
   do {                                 \
     if (!(cond)) {                     \
