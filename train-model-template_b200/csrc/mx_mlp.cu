@@ -610,10 +610,11 @@ __global__ void __launch_bounds__(32 * (bwd_cons(R) + 1), 1)
 // items.  Warp 17 streams per item the [256 x 32] bf16 tiles of g, u and dh (64-byte rows, 64-byte
 // swizzle) and the tile's slices of B_gate, B_up ([32 n x 16], 32-byte swizzle) and A_down ([16 x 32 n],
 // 64-byte swizzle) into a 3-stage ring, and per row block its xa_gate, xa_up and dxd rows (three
-// [256 x 16] buffers, 32-byte swizzle).  Warp 16 (one elected lane) issues per item
-//   * the LoRA terms xa_gate B_gate^T, xa_up B_up^T and dxd A_down of the tile (2 halves of 128 rows x
-//     3 x 32 TMEM columns), one item ahead of the element-wise warps;
-//   * once those warps stored the tile's dg | du | h (bf16, [256 x 32] each, the g tile's layout) in
+// [256 x 16] buffers, 32-byte swizzle).  Two warps issue the MMAs (one elected lane each, descriptors
+// computed once; a small MMA costs ~50 cycles of issue, so the two streams go out side by side):
+//   * warp 18: the LoRA terms xa_gate B_gate^T, xa_up B_up^T and dxd A_down of the tile (2 halves of 128
+//     rows x 3 x 32 TMEM columns), one item ahead of the element-wise warps;
+//   * warp 16, once those warps stored the tile's dg | du | h (bf16, [256 x 32] each, the g tile's layout) in
 //     shared memory: the per-row products [dg B_gate | du B_up | h A_down^T], accumulated in TMEM over the
 //     run's tiles of the row block (2 halves x 48 columns; B_gate / B_up slices read as MN-major B), and
 //     the column products [dg | du | h]^T [xa_gate | xa_up | dxd] over the block's 256 rows: one M = 128,
@@ -630,7 +631,8 @@ __global__ void __launch_bounds__(32 * (bwd_cons(R) + 1), 1)
 // the fp32 partial buffers (warps 0-2: the previous tile's column products; all: the per-row products
 // when the run leaves a row block).  Every wait is bounded, and the two warps of a pair leave together;
 // no atomics, so the result is deterministic.
-constexpr int BT_ROWS = 256, BT_BN = 32, BT_ST = 3, BT_CONS = 16, BT_THREADS = 32 * (BT_CONS + 2);
+constexpr int BT_ROWS = 256, BT_BN = 32, BT_ST = 3, BT_CONS = 16, BT_THREADS = 32 * (BT_CONS + 3);
+constexpr int BT_W_PROD = BT_CONS, BT_W_TMA = BT_CONS + 1, BT_W_REC = BT_CONS + 2;   // warp roles
 constexpr int BT_TILE = BT_ROWS * BT_BN * 2;           // 16 KB: [256 x 32] bf16
 constexpr int BT_SLICE = 32 * 16 * 2;                  // 1 KB: [32 x 16] or [16 x 32] bf16
 constexpr int BT_STAGE = 3 * BT_TILE + 3 * BT_SLICE;   // g | u | dh | bg | bu | ad
@@ -693,14 +695,14 @@ __global__ void __launch_bounds__(BT_THREADS, 1)
     mbar_init(row_empty, BT_CONS);
     fence_barrier_init();
   }
-  if (warp == BT_CONS) tmem_alloc(tmem_slot, BT_TMEM_COLS);
+  if (warp == BT_W_PROD) tmem_alloc(tmem_slot, BT_TMEM_COLS);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const uint32_t s_ring = smem_u32(smem), s_op = smem_u32(opbuf), s_rows = smem_u32(rowbuf);
 
-  if (warp == BT_CONS + 1) {   // TMA producer: the ring, and the row buffers when a row block starts
+  if (warp == BT_W_TMA) {   // TMA producer: the ring, and the row buffers when a row block starts
     if (lane == 0) {
       prefetch_tmap(&tm_gu);
       prefetch_tmap(&tm_dh);
@@ -771,49 +773,57 @@ __global__ void __launch_bounds__(BT_THREADS, 1)
       mbar_wait(&full[st], (uint32_t)((i / BT_ST) & 1), err, MX_DEV_TIMEOUT_PRODUCER);
     }
     if (row_loads > 0) mbar_wait(rows_full, (uint32_t)((row_loads - 1) & 1), err, MX_DEV_TIMEOUT_PRODUCER);
-  } else if (warp == BT_CONS) {   // MMA issue: the whole warp waits, lane 0 issues and commits
+  } else if (warp == BT_W_REC) {   // LoRA-term MMAs: the whole warp waits, lane 0 issues and commits
+    // descriptors of stage 0 / row half 0; the start-address field (address / 16) takes plain offsets
     constexpr uint32_t ID_REC = f16_idesc(128, 32, false, false);      // B = B_gate / B_up slice [32 n][16 k]
     constexpr uint32_t ID_REC_AD = f16_idesc(128, 32, false, true);    // B = A_down slice [16 k][32 n]
-    constexpr uint32_t ID_ROW = f16_idesc(128, 16, false, false);      // B = A_down slice [16 n][32 k]
-    constexpr uint32_t ID_ROW_MN = f16_idesc(128, 16, false, true);    // B = B_gate / B_up slice [32 k][16 n]
-    constexpr uint32_t ID_COL = f16_idesc(128, 48, true, true);        // A = [dg | du | h] tiles, B = rows
-    int n_rec = 0, n_prod = 0;
-    // the LoRA terms of local tile t (the whole block's rows: two M = 128 halves)
-    auto rec = [&](int t, bool first, int b) -> bool {
-      const int st = t % BT_ST;
-      if (first && !mbar_wait(rows_full, (uint32_t)(b & 1), err, MX_DEV_TIMEOUT_MMA)) return false;
-      if (!mbar_wait(&full[st], (uint32_t)((t / BT_ST) & 1), err, MX_DEV_TIMEOUT_MMA)) return false;
-      if (t > 0 && !mbar_wait(lora_empty, (uint32_t)((t - 1) & 1), err, MX_DEV_TIMEOUT_MMA_TMEM)) return false;
+    const uint32_t sl0 = s_ring + 3 * BT_TILE;                         // bg | bu | ad slices of stage 0
+    const uint64_t a_xg = make_sdesc(s_rows, 0, 256, 6), a_xu = make_sdesc(s_rows + BT_RB, 0, 256, 6);
+    const uint64_t a_xd = make_sdesc(s_rows + 2 * BT_RB, 0, 256, 6);
+    const uint64_t b_g = make_sdesc(sl0, 0, 256, 6), b_u = make_sdesc(sl0 + BT_SLICE, 0, 256, 6);
+    const uint64_t b_d = make_sdesc(sl0 + 2 * BT_SLICE, BT_SLICE, 512, 4);
+    int n_rec = 0, blk = -1;
+    for (int t = 0; t < cnt; ++t) {
+      const int it = it_lo + t, st = t % BT_ST;
+      const bool first = t == 0 || it % nt == 0;
+      if (first) ++blk;
+      if (first && !mbar_wait(rows_full, (uint32_t)(blk & 1), err, MX_DEV_TIMEOUT_MMA)) break;
+      if (!mbar_wait(&full[st], (uint32_t)((t / BT_ST) & 1), err, MX_DEV_TIMEOUT_MMA)) break;
+      if (t > 0 && !mbar_wait(lora_empty, (uint32_t)((t - 1) & 1), err, MX_DEV_TIMEOUT_MMA_TMEM)) break;
       tc_fence_after();
       if (lane == 0) {
-        const uint32_t sl = s_ring + st * BT_STAGE + 3 * BT_TILE;   // bg | bu | ad slices
+        const uint64_t so = (uint64_t)((st * BT_STAGE) >> 4);
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const uint32_t d = tmem + BT_REC + 96 * h, ro = s_rows + 4096 * h;   // rows 128 h .. 128 h + 127
-          umma_bf16(d, make_sdesc(ro, 0, 256, 6), make_sdesc(sl, 0, 256, 6), ID_REC, 0u);
-          umma_bf16(d + 32, make_sdesc(ro + BT_RB, 0, 256, 6), make_sdesc(sl + BT_SLICE, 0, 256, 6), ID_REC, 0u);
-          umma_bf16(d + 64, make_sdesc(ro + 2 * BT_RB, 0, 256, 6), make_sdesc(sl + 2 * BT_SLICE, BT_SLICE, 512, 4),
-                    ID_REC_AD, 0u);
+        for (int h = 0; h < 2; ++h) {   // rows 128 h .. 128 h + 127 (4 KB into each row buffer)
+          const uint32_t d = tmem + BT_REC + 96 * h;
+          const uint64_t ho = (uint64_t)(256 * h);
+          umma_bf16(d, a_xg + ho, b_g + so, ID_REC, 0u);
+          umma_bf16(d + 32, a_xu + ho, b_u + so, ID_REC, 0u);
+          umma_bf16(d + 64, a_xd + ho, b_d + so, ID_REC_AD, 0u);
         }
         umma_commit(lora_full);
       }
       __syncwarp();
       ++n_rec;
-      return true;
-    };
-    int blk = -1;
-    bool rec_ahead = false;
+    }
+    if (n_rec > 0) mbar_wait(lora_full, (uint32_t)((n_rec - 1) & 1), err, MX_DEV_TIMEOUT_MMA);   // none in flight
+  } else if (warp == BT_W_PROD) {   // product MMAs: the whole warp waits, lane 0 issues and commits
+    constexpr uint32_t ID_ROW = f16_idesc(128, 16, false, false);      // B = A_down slice [16 n][32 k]
+    constexpr uint32_t ID_ROW_MN = f16_idesc(128, 16, false, true);    // B = B_gate / B_up slice [32 k][16 n]
+    constexpr uint32_t ID_COL = f16_idesc(128, 48, true, true);        // A = [dg | du | h] tiles, B = rows
+    const uint32_t sl0 = s_ring + 3 * BT_TILE;
+    // per-row products: A = dg / du / h tile (K-major, rows 128 h .., K step 32 bytes); B = the stage's slices
+    const uint64_t a_r = make_sdesc(s_op, 0, 512, 4);
+    const uint64_t b_rg = make_sdesc(sl0, BT_SLICE, 256, 6), b_ru = make_sdesc(sl0 + BT_SLICE, BT_SLICE, 256, 6);
+    const uint64_t b_rd = make_sdesc(sl0 + 2 * BT_SLICE, 0, 512, 4);
+    // column products: A = the three tiles as MN-major atoms 16 KB apart, B = the row buffers 8 KB apart
+    const uint64_t a_c = make_sdesc(s_op, BT_TILE, 512, 4), b_c = make_sdesc(s_rows, BT_RB, 256, 6);
+    int n_prod = 0, blk = -1;
     for (int t = 0; t < cnt; ++t) {
       const int it = it_lo + t;
       const bool first = t == 0 || it % nt == 0;
       const bool last = t + 1 == cnt || (it + 1) % nt == 0;
       if (first) ++blk;
-      if (!rec_ahead && !rec(t, first, blk)) break;
-      rec_ahead = false;
-      if (!last) {   // the next tile's LoRA terms, while the element-wise warps work on this one
-        if (!rec(t + 1, false, blk)) break;
-        rec_ahead = true;
-      }
       if (!mbar_wait(op_full, (uint32_t)(t & 1), err, MX_DEV_TIMEOUT_MMA)) break;
       if (t >= 2 && !mbar_wait(&colp_empty[t & 1], (uint32_t)(((t - 2) >> 1) & 1), err, MX_DEV_TIMEOUT_MMA_TMEM))
         break;
@@ -821,26 +831,23 @@ __global__ void __launch_bounds__(BT_THREADS, 1)
       tc_fence_after();
       if (lane == 0) {
         const int st = t % BT_ST;
-        const uint32_t sl = s_ring + st * BT_STAGE + 3 * BT_TILE;
+        const uint64_t so = (uint64_t)((st * BT_STAGE) >> 4);
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
-          const uint32_t d = tmem + BT_ROWC + 48 * h, ao = s_op + 8192 * h;   // rows 128 h .. of the tiles
+          const uint32_t d = tmem + BT_ROWC + 48 * h;
 #pragma unroll
           for (int k = 0; k < 2; ++k) {   // K = the tile's 32 columns, 16 per MMA
             const uint32_t acc = (first && k == 0) ? 0u : 1u;
-            umma_bf16(d, make_sdesc(ao + 32 * k, 0, 512, 4), make_sdesc(sl + 512 * k, BT_SLICE, 256, 6), ID_ROW_MN,
-                      acc);
-            umma_bf16(d + 16, make_sdesc(ao + BT_TILE + 32 * k, 0, 512, 4),
-                      make_sdesc(sl + BT_SLICE + 512 * k, BT_SLICE, 256, 6), ID_ROW_MN, acc);
-            umma_bf16(d + 32, make_sdesc(ao + 2 * BT_TILE + 32 * k, 0, 512, 4),
-                      make_sdesc(sl + 2 * BT_SLICE + 32 * k, 0, 512, 4), ID_ROW, acc);
+            const uint64_t ao = (uint64_t)(512 * h + 2 * k);   // 8 KB per row half, 32 bytes per K step
+            umma_bf16(d, a_r + ao, b_rg + so + 32 * k, ID_ROW_MN, acc);
+            umma_bf16(d + 16, a_r + ao + BT_TILE / 16, b_ru + so + 32 * k, ID_ROW_MN, acc);
+            umma_bf16(d + 32, a_r + ao + 2 * BT_TILE / 16, b_rd + so + 2 * k, ID_ROW, acc);
           }
         }
         const uint32_t dc = tmem + BT_COLC + 48 * (uint32_t)(t & 1);
-#pragma unroll 4
-        for (int k = 0; k < BT_ROWS / 16; ++k)   // K = the block's 256 rows, 16 per MMA
-          umma_bf16(dc, make_sdesc(s_op + 1024 * k, BT_TILE, 512, 4), make_sdesc(s_rows + 512 * k, BT_RB, 256, 6),
-                    ID_COL, k > 0 ? 1u : 0u);
+#pragma unroll
+        for (int k = 0; k < BT_ROWS / 16; ++k)   // K = the block's 256 rows, 16 per MMA (1 KB of A, 512 B of B)
+          umma_bf16(dc, a_c + 64 * k, b_c + 32 * k, ID_COL, k > 0 ? 1u : 0u);
         umma_commit(op_empty);
         umma_commit(&empty[st]);
         umma_commit(&colp_full[t & 1]);
@@ -852,9 +859,7 @@ __global__ void __launch_bounds__(BT_THREADS, 1)
       __syncwarp();
       ++n_prod;
     }
-    // no MMA in flight at exit (bounded): the last commits cover every MMA issued before them
-    if (n_prod > 0) mbar_wait(op_empty, (uint32_t)((n_prod - 1) & 1), err, MX_DEV_TIMEOUT_MMA);
-    if (n_rec > 0) mbar_wait(lora_full, (uint32_t)((n_rec - 1) & 1), err, MX_DEV_TIMEOUT_MMA);
+    if (n_prod > 0) mbar_wait(op_empty, (uint32_t)((n_prod - 1) & 1), err, MX_DEV_TIMEOUT_MMA);   // none in flight
   } else {   // element-wise warps 0-15
     const int c = warp >> 3, hq = warp & 7, half = hq >> 2, qw = hq & 3;
     const int r0w = half * 128 + qw * 32;                 // first block row of the pair (warps hq, hq + 8)
@@ -1037,7 +1042,7 @@ __global__ void __launch_bounds__(BT_THREADS, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == BT_CONS) tmem_dealloc(tmem, BT_TMEM_COLS);
+  if (warp == BT_W_PROD) tmem_dealloc(tmem, BT_TMEM_COLS);
 }
 
 // ------------------------------------------------------------------------------------------------ skinny
