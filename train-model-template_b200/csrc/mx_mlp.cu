@@ -3,16 +3,20 @@
 //   k_mlp_fwd   -- the forward epilogue (reference _fwd_kernel, scripts/fused_mlp.py:81-109):
 //                  reads gu = [x W_gate^T | x W_up^T] once, adds the LoRA-B terms, SwiGLU, writes h as
 //                  MXFP8 (codes + blocked scales) for the down GEMM and xS_down = h A_down^T.
-//   k_mlp_bwd   -- the backward epilogue (reference _bwd_kernel, scripts/fused_mlp.py:112-175):
+//   k_mlp_bwd_tc / k_mlp_bwd<32>
+//               -- the backward epilogue (reference _bwd_kernel, scripts/fused_mlp.py:112-175):
 //                  recomputes g, u, h from gu, dh = dh_mx + dxd A_down, SwiGLU backward, writes
 //                  [dg | du] as MXFP8 for the dx GEMM, and the LoRA gradient pieces dB_gate, dB_up,
 //                  dA_down (summed over rows) and dxa_gate, dxa_up, xS_down (summed over columns).
+//                  Rank 16 (k_mlp_bwd_tc) runs every rank-r product as tcgen05 MMAs into TMEM; rank 32
+//                  keeps the warp-level form.
 //   k_rowdot    -- out[T, n] = A[T, K] B[n, K]^T for the rank-n LoRA-A products (x S^T, dy B_down).
 //   k_coldot    -- out[K, n] = A[T, K]^T E[T, n] for the LoRA weight gradients (dA, dB_down).
 //   k_sum_*     -- fixed-order sums of the per-CTA partial buffers (deterministic, no atomics).
 //
-// All rank-r products run on the tensor cores with warp-level m16n8k16 bf16 MMAs; the element-wise
-// math keeps the reference's rounding points (bf16 after each fp32 expression it rounds).
+// The rank-r products run on the tensor cores (warp-level m16n8k16 bf16 MMAs, or tcgen05 MMAs in the
+// rank-16 backward); the element-wise math keeps the reference's rounding points (bf16 after each fp32
+// expression it rounds).
 #include <algorithm>
 #include <mutex>
 
