@@ -111,9 +111,10 @@ int mxm_mlp_fwd_epilogue(const void* gu, const void* xs, const void* bg, const v
                          int col_groups, void* stream);
 
 /* The gate|up GEMM with the forward epilogue fused in (reference gu GEMM + _fwd_kernel, scripts/fused_mlp.py:
- * 279-282 and :81-109): gu [M, 2N] bf16 = [x W_gate^T | x W_up^T] from MX codes qa [M, K] and qb = W_gu [2N, K]
- * (rows: gate then up) with their blocked scales; and from the same tiles qh / sh = MXFP8(h) [M, N],
- * h = bf16(silu(g) u), g = bf16(gu_gate + s_g xs_g bg^T), u likewise, and xsd [M, r] bf16 = bf16(h ad^T).
+ * 279-282 and :81-109): from MX codes qa [M, K] and qb = W_gu [2N, K] (rows: gate then up) with their blocked
+ * scales, g = bf16(bf16(x W_gate^T) + s_g xs_g bg^T), u likewise, qh / sh = MXFP8(h) [M, N] with
+ * h = bf16(silu(g) u), and xsd [M, r] bf16 = bf16(h ad^T).  gu [M, 2N] bf16 = [g | u], the LoRA terms
+ * included (what the backward needs: mxm_mlp_bwd_epilogue with gu_lora = 1).
  * xs [M, 2r] bf16 contiguous, bg / bu [N, r], ad [r, N] bf16 contiguous; r = 16; N % 128 == 0.
  * xsd_part: fp32 scratch of slots * M * r elements (mxm_gemm_glu_partition: per = tiles per work unit,
  * grid = CTAs launched, slots = units that can touch one row block).  For M >= 256 the work units are CTA
@@ -130,16 +131,18 @@ int mxm_gemm_glu(const void* qa, int64_t lda, const void* sa, const void* qb, in
 int mxm_mlp_bwd_partitions(int64_t T, int64_t N, int r, int* super_block, int* col_groups);
 
 /* Backward epilogue of the fused MLP (reference mlp_bwd / _bwd_kernel, scripts/fused_mlp.py:112-175,235-259).
- * Recomputes g, u, h from gu; dh = bf16(dhm + dxd ad); du = bf16(dh silu(g)); dg = bf16(dh u sig (g (1-sig) + 1));
+ * Recomputes g, u, h from gu (gu_lora = 0: gu = [x W_gate^T | x W_up^T] and g = bf16(gu_gate + s_g xs_g bg^T),
+ * u likewise, as the reference; gu_lora = 1, rank 16 only: gu already holds g | u, as mxm_gemm_glu writes it);
+ * dh = bf16(dhm + dxd ad); du = bf16(dh silu(g)); dg = bf16(dh u sig (g (1-sig) + 1));
  * q / s = MXFP8([dg | du]) [T, 2N] (skipped when q is NULL).  Partial sums (fp32, fixed-order reduction in
  * mxm_mlp_bwd_reduce): dxa_part [col_groups, T, 3r] = [dg bg | du bu | h ad^T], one slot per CTA that
  * worked on a row block (slots a row block does not use are left unwritten);
  * dbg_part / dbu_part [n_super, N, r] = dg^T xa_g / du^T xa_u; dad_part [n_super, r, N] = dxd^T h,
  * n_super = ceil(ceil128(T) / super_block). */
 int mxm_mlp_bwd_epilogue(const void* gu, const void* xs, const void* dhm, const void* dxd, const void* bg,
-                         const void* bu, const void* ad, int64_t T, int64_t N, int r, float s_g, float s_u, void* q,
-                         void* s, void* dxa_part, void* dbg_part, void* dbu_part, void* dad_part, int super_block,
-                         int col_groups, void* stream);
+                         const void* bu, const void* ad, int64_t T, int64_t N, int r, float s_g, float s_u,
+                         int gu_lora, void* q, void* s, void* dxa_part, void* dbg_part, void* dbu_part,
+                         void* dad_part, int super_block, int col_groups, void* stream);
 
 /* Fixed-order reduction of the backward partials (scripts/fused_mlp.py:258-259,316-326):
  * dxa bf16 [T, 2r] = [s_g sum(dxa_g) | s_u sum(dxa_u)], xsd bf16 [T, r] = sum(xS_down),

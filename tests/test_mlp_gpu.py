@@ -140,8 +140,9 @@ def test_need_out_false_and_determinism():
 @pytest.mark.parametrize("T,H,N", [(1, 1024, 3584), (77, 1024, 3584), (1000, 2048, 6144), (2049, 1024, 3584),
                                    (4096, 2048, 6144)])
 def test_gemm_glu_matches_two_passes(T, H, N):
-    """The gate|up GEMM with the fused forward epilogue gives the same gu and the same MXFP8(h) bytes as the
-    GEMM followed by the separate epilogue kernel; xS_down differs only by the fp32 summation order.
+    """The gate|up GEMM with the fused forward epilogue gives the same MXFP8(h) bytes as the GEMM followed by
+    the separate epilogue kernel, and gu = [g | u] = bf16(GEMM + s xa B^T) (the two-pass gu plus the LoRA
+    terms, up to the fp32 summation order of the rank-16 dot); xS_down differs only by that order too.
     T >= 256 runs the CTA-pair kernel (2049: an odd count of 128-row blocks, so the last pair's second CTA
     holds no rows), smaller T the single-CTA kernel."""
     import fused_mlp
@@ -163,7 +164,13 @@ def test_gemm_glu_matches_two_passes(T, H, N):
     torch.cuda.synchronize()
     import _mxlib
     assert _mxlib.device_error() == 0
-    assert torch.equal(gu, gu0)
+    lora = torch.cat([xs[:, :r].float() @ bg.float().t(), xs[:, r:].float() @ bu.float().t()], 1)
+    mag = torch.cat([xs[:, :r].float().abs() @ bg.float().abs().t(), xs[:, r:].float().abs() @ bu.float().abs().t()], 1)
+    ref = (gu0.float() + 2.0 * lora).to(torch.bfloat16)
+    assert float((gu != ref).float().mean()) < 1e-3
+    # one bf16 rounding apart, where the rank-16 dot may cancel: bounded by the magnitudes it sums
+    bound = (ref.float().abs() + gu0.float().abs() + 2.0 * mag) * 2.0 ** -7
+    assert bool(((gu.float() - ref.float()).abs() <= bound).all())
     assert torch.equal(qh.view(torch.uint8), qh0.view(torch.uint8))
     assert torch.equal(sh.view(torch.uint8), sh0.view(torch.uint8))
     d = (xsd.float() - xsd0.float()).abs()
@@ -226,7 +233,7 @@ def _codes_differ(a, b):
     return float(((a != b) & ~nan).mean())
 
 
-@pytest.mark.parametrize("T", [1024, 2049])
+@pytest.mark.parametrize("T", [1024, 2049, 4352])
 def test_mlp_2b_shape_vs_oracle(T):
     """The benchmarked shape (Qwen3.5-2B MLP: hidden 2048, intermediate 6144, r 16, alpha 32): y, dx and
     all six LoRA gradients within 5e-3 of the oracle.  T = 2049 is an odd count of 128-row blocks, so the
@@ -260,25 +267,53 @@ def test_epilogue_bytes_2b_vs_oracle(T):
     xd, dyd = x.to(dev), dy.to(dev)
     xs, q, sc = fused_mlp.rowdot_quant(xd, S)
     gu, qh, sh, xsd = fused_mlp.gemm_glu(q, sc, layer.hold.w, layer.hold.ws, xs, bg, bu, ad, s, s)
+    gu0 = mxfp8.mx_mm(q, layer.hold.w.t(), sc, layer.hold.ws)   # the GEMM alone: the oracle's input
     dxd, qd, sd = fused_mlp.rowdot_quant(dyd, bdT, post=s)
     wt, wts = mxfp8.mx_wt(layer.down)
     dhm = mxfp8.mx_mm(qd, wt.t(), sd, wts)
-    qg, sg, dxa, dbg, dbu, dad = fused_mlp.mlp_bwd(gu, xs, dhm, dxd, bg, bu, ad, s, s, True)
+    qg, sg, dxa, dbg, dbu, dad = fused_mlp.mlp_bwd(gu, xs, dhm, dxd, bg, bu, ad, s, s, True, gu_lora=True)
     torch.cuda.synchronize()
     import _mxlib
     assert _mxlib.device_error() == 0
     f = lambda t: t.float().cpu().numpy()  # noqa: E731
-    h_o, qh_o, sh_o, xsd_o = O.fwd_epilogue(f(gu), f(xs), f(bg), f(bu), f(ad), s, s)
+    g_o, u_o = O._gu(f(gu0), f(xs), f(bg), f(bu), s, s, N, r)   # the fused kernel's gu holds g | u
+    assert float((f(gu) != np.concatenate([g_o, u_o], 1)).mean()) < 1e-3
+    h_o, qh_o, sh_o, xsd_o = O.fwd_epilogue(f(gu0), f(xs), f(bg), f(bu), f(ad), s, s)
     assert _codes_differ(qh.view(torch.uint8).cpu().numpy(), qh_o) < 1e-3
     assert float((sh.view(torch.uint8).cpu().numpy() != sh_o).mean()) < 1e-3
     assert O.rel_fro(f(xsd), xsd_o) < 2e-3
-    e = O.bwd_epilogue(f(gu), f(xs), f(dhm), f(dxd), f(bg), f(bu), f(ad), s, s)
+    e = O.bwd_epilogue(f(gu0), f(xs), f(dhm), f(dxd), f(bg), f(bu), f(ad), s, s)
     assert _codes_differ(qg.view(torch.uint8).cpu().numpy(), e["q_dgu"]) < 1e-3
     assert float((sg.view(torch.uint8).cpu().numpy() != e["s_dgu"]).mean()) < 1e-3
     assert O.rel_fro(f(dbg), e["dBg"]) < 2e-3 and O.rel_fro(f(dbu), e["dBu"]) < 2e-3
     assert O.rel_fro(f(dad), e["dAd"]) < 2e-3
     assert O.rel_fro(f(dxa)[:, :r], e["dxa_g"]) < 2e-3 and O.rel_fro(f(dxa)[:, r:2 * r], e["dxa_u"]) < 2e-3
     assert O.rel_fro(f(dxa)[:, 2 * r:], e["xsd"]) < 2e-3
+
+
+@pytest.mark.parametrize("T,gu_lora", [(300, False), (4352, False), (4352, True)])
+def test_bwd_epilogue_without_codes(T, gu_lora):
+    """need_q = False (x needs no gradient): the backward epilogue skips the MXFP8 of [dg | du] and gives the
+    same partial products, bit for bit, as the run that writes the codes (those are checked against the
+    oracle above).  T = 300 leaves the last 256-row block mostly empty; 4352 = 17 blocks of 256."""
+    import fused_mlp
+    H, N, r, s = 2048, 6144, 16, 2.0
+    dev = torch.device("cuda")
+    g = torch.Generator().manual_seed(T)
+    gu = (torch.randn(T, 2 * N, generator=g) * 2).to(torch.bfloat16).to(dev)
+    xs = torch.randn(T, 2 * r, generator=g).to(torch.bfloat16).to(dev)
+    dhm = (torch.randn(T, N, generator=g) * 0.01).to(torch.bfloat16).to(dev)
+    dxd = (torch.randn(T, r, generator=g) * 0.01).to(torch.bfloat16).to(dev)
+    bg, bu = ((torch.randn(N, r, generator=g) * 0.05).to(torch.bfloat16).to(dev) for _ in range(2))
+    ad = (torch.randn(r, N, generator=g) * 0.05).to(torch.bfloat16).to(dev)
+    with_q = fused_mlp.mlp_bwd(gu, xs, dhm, dxd, bg, bu, ad, s, s, True, gu_lora=gu_lora)
+    no_q = fused_mlp.mlp_bwd(gu, xs, dhm, dxd, bg, bu, ad, s, s, False, gu_lora=gu_lora)
+    torch.cuda.synchronize()
+    import _mxlib
+    assert _mxlib.device_error() == 0
+    assert no_q[0] is None and no_q[1] is None
+    for a, b in zip(with_q[2:], no_q[2:]):
+        assert torch.equal(a, b)
 
 
 def test_configs0_exact():

@@ -50,7 +50,7 @@ _SIGS = {
                              _vp, _vp, _int, _vp],
     "mxm_mlp_bwd_partitions": [_i64, _i64, _int, ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_int)],
     "mxm_mlp_bwd_epilogue": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _int, ctypes.c_float, ctypes.c_float,
-                             _vp, _vp, _vp, _vp, _vp, _vp, _int, _int, _vp],
+                             _int, _vp, _vp, _vp, _vp, _vp, _vp, _int, _int, _vp],
     "mxm_mlp_bwd_reduce": [_vp, _vp, _vp, _vp, _i64, _i64, _int, ctypes.c_float, ctypes.c_float, _int, _int, _vp,
                            _vp, _vp, _vp, _vp, _vp],
     "mxm_rowdot": [_vp, _i64, _vp, _i64, _i64, _int, ctypes.c_float, _vp, _i64, _vp],

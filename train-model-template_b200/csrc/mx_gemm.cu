@@ -311,8 +311,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 // and stage the bf16 tile in shared memory (128-byte swizzle); after one named barrier each warp runs
 // the forward epilogue on 16 rows x 128 pairs of the staged tile -- the LoRA-B terms with mma.sync,
 // SwiGLU, the MXFP8 codes of h, and the per-row xS_down = h A_down^T accumulated in registers -- while
-// the MMAs of the next tile proceed, and four TMA stores, one per SwiGLU sub-step, write gu (the
-// backward reads it) from the staged tile in full 128-byte rows.  A CTA (pair) works through a contiguous range of tiles (column tiles fastest), so xS_down
+// the MMAs of the next tile proceed; g and u with their LoRA terms go back into the staged tile, from
+// which each warp writes its 16 rows of gu for the backward (two [16 x 64] TMA stores per finished
+// 64-column sub-tile, full 128-byte rows).  A CTA (pair) works through a contiguous range of tiles (column tiles fastest), so xS_down
 // accumulates over the columns of a row block and is written as one fp32 partial per (row block, CTA or
 // pair); a fixed-order reduction sums them.  Rank 16 only (the rank-32 slices do not fit shared memory).
 constexpr int GLU_STAGING = 2 * 2 * 128 * 128;   // g | u halves, two [128 x 64] bf16 sub-tiles each
@@ -614,7 +615,6 @@ MX_DEV void glu_body(const CUtensorMap* tmA, const CUtensorMap* tmB, const CUten
             }
         }
         acc_phase ^= 1;
-        fence_proxy_async();   // the staged tile is read by the TMA stores below
       }
       // 2. this tile's B_gate / B_up rows and A_down columns into shared memory
       for (int k = et; k < 128 * (R / 8); k += EPI_THREADS) {
@@ -635,22 +635,15 @@ MX_DEV void glu_body(const CUtensorMap* tmA, const CUtensorMap* tmB, const CUten
                      : "memory");
       }
       if (bar_any(1, EPI_THREADS, !acc_ok)) break;   // the epi_sync of this tile, and the give-up decision
-      // gu leaves from the staged tile as four [128 x 64] TMA stores (gate, up) x (sub-tile), rows >= M
-      // clipped, one per SwiGLU sub-step below: spread out, they hold the TMA unit back from the next
-      // tile's operand loads less than one 64 KB burst does
-      // 3. the forward epilogue on rows 16e .. 16e+15, two 64-column sub-tiles
+      // 3. the forward epilogue on rows 16e .. 16e+15, two 64-column sub-tiles.  g and u with their LoRA
+      // terms (the bf16 values the SwiGLU uses, which the backward would otherwise recompute) go back into
+      // the staged tile, and gu leaves from it per warp and finished sub-tile, rows >= M clipped
 #pragma unroll 1
       for (int sbk = 0; sbk < 2; ++sbk) {
         const uint32_t tg = s_stg + sbk * (128 * 128), tu = tg + 2 * 128 * 128;
         const uint32_t tbg = s_bg + sbk * (64 * R * 2), tbu = s_bu + sbk * (64 * R * 2), tad = s_ad + sbk * (R * 128);
 #pragma unroll
         for (int b = 0; b < 2; ++b) {
-          if (et == 0) {   // box (gate / up) x (sub-tile) number 2 sbk + b; gu is next read by the backward
-            const int bx = 2 * sbk + b, hh = bx >> 1, c2 = bx & 1;
-            tma_store_2d_hint(tmG, stg + (hh * 2 + c2) * (128 * 128), hh * N + tn * 128 + c2 * 64, (int)rowb,
-                              qr.pol);
-            bulk_commit();
-          }
           uint32_t hp[4][2];
 #pragma unroll
           for (int pp = 0; pp < 2; ++pp) {
@@ -676,11 +669,14 @@ MX_DEV void glu_body(const CUtensorMap* tmA, const CUtensorMap* tmB, const CUten
               const float* duv = qq ? du1 : du0;
 #pragma unroll
               for (int hh = 0; hh < 2; ++hh) {
-                const float2 gg = up2(rn2(__ffma2_rn(sg2, make_float2(dgv[2 * hh], dgv[2 * hh + 1]), up2(G[2 * qq + hh]))));
-                const float2 uu = up2(rn2(__ffma2_rn(su2, make_float2(duv[2 * hh], duv[2 * hh + 1]), up2(U[2 * qq + hh]))));
+                G[2 * qq + hh] = rn2(__ffma2_rn(sg2, make_float2(dgv[2 * hh], dgv[2 * hh + 1]), up2(G[2 * qq + hh])));
+                U[2 * qq + hh] = rn2(__ffma2_rn(su2, make_float2(duv[2 * hh], duv[2 * hh + 1]), up2(U[2 * qq + hh])));
+                const float2 gg = up2(G[2 * qq + hh]), uu = up2(U[2 * qq + hh]);
                 hp[2 * pp + qq][hh] = rn2(__fmul2_rn(__fmul2_rn(gg, sigmoid2(gg)), uu));
               }
             }
+            stsm4(tg + o_gu[p], G[0], G[1], G[2], G[3]);   // g, u with the LoRA terms, in place
+            stsm4(tu + o_gu[p], U[0], U[1], U[2], U[3]);
           }
           quant_block16p(hp, qr, (int64_t)tn * 128 + sbk * 64 + 32 * b, t);
 #pragma unroll
@@ -695,12 +691,23 @@ MX_DEV void glu_body(const CUtensorMap* tmA, const CUtensorMap* tmB, const CUten
             }
           }
         }
+        // this warp's 16 rows of sub-tile sbk of g and u are final: two [16 x 64] TMA stores (gu is next
+        // read by the backward), no wait on the other warps
+        fence_proxy_async();
+        __syncwarp();
+        if (lane == 0 && rowb + 16 * e < M) {
+#pragma unroll
+          for (int hh = 0; hh < 2; ++hh)
+            tma_store_2d_hint(tmG, stg + (hh * 2 + sbk) * (128 * 128) + e * (16 * 128), hh * N + tn * 128 + sbk * 64,
+                              (int)(rowb + 16 * e), qr.pol);
+          bulk_commit();
+        }
       }
-      if (et == 0) bulk_wait_read0();   // the gu stores have read the staged tile
+      if (lane == 0) bulk_wait_read0();   // this warp's gu stores have read the staged tile
       epi_sync();   // staged tile and slices are free for the next tile
       if (i % chunk == chunk - 1) flush((unit + (i / chunk) * units) % ncpr);
     }
-    if (et == 0) bulk_wait0();
+    if (lane == 0) bulk_wait0();
   }
 
   tc_fence_before();
@@ -930,7 +937,7 @@ extern "C" int mxm_gemm_glu(const void* qa, int64_t lda, const void* sa, const v
                                (uint64_t)ldb, BK, 128, CU_TENSOR_MAP_SWIZZLE_128B))
     return st;
   if (int st = mx_make_tmap_2d(&tmG, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, gu, (uint64_t)(2 * N), (uint64_t)M,
-                               (uint64_t)(4 * N), 64, BM, CU_TENSOR_MAP_SWIZZLE_128B))
+                               (uint64_t)(4 * N), 64, 16, CU_TENSOR_MAP_SWIZZLE_128B))
     return st;
   cudaStream_t st = (cudaStream_t)stream;
   if (pair) {

@@ -649,6 +649,9 @@ static_assert(BT_STAGE % 1024 == 0 && BT_RB % 1024 == 0, "backward epilogue: swi
 // products (2 buffers x 48)
 constexpr uint32_t BT_REC = 0, BT_ROWC = 192, BT_COLC = 288, BT_TMEM_COLS = 512;
 
+// GL: gu already holds g and u with their LoRA terms (the fused gate|up kernel writes them so): the LoRA-term
+// MMAs and adds of g and u are skipped, only dxd A_down is computed.
+template <bool GL>
 __global__ void __launch_bounds__(BT_THREADS, 1)
     k_mlp_bwd_tc(const __grid_constant__ CUtensorMap tm_gu, const __grid_constant__ CUtensorMap tm_dh,
                  const __grid_constant__ CUtensorMap tm_bg, const __grid_constant__ CUtensorMap tm_bu,
@@ -801,8 +804,10 @@ __global__ void __launch_bounds__(BT_THREADS, 1)
         for (int h = 0; h < 2; ++h) {   // rows 128 h .. 128 h + 127 (4 KB into each row buffer)
           const uint32_t d = tmem + BT_REC + 96 * h;
           const uint64_t ho = (uint64_t)(256 * h);
-          umma_bf16(d, a_xg + ho, b_g + so, ID_REC, 0u);
-          umma_bf16(d + 32, a_xu + ho, b_u + so, ID_REC, 0u);
+          if constexpr (!GL) {
+            umma_bf16(d, a_xg + ho, b_g + so, ID_REC, 0u);
+            umma_bf16(d + 32, a_xu + ho, b_u + so, ID_REC, 0u);
+          }
           umma_bf16(d + 64, a_xd + ho, b_d + so, ID_REC_AD, 0u);
         }
         umma_commit(lora_full);
@@ -920,8 +925,10 @@ __global__ void __launch_bounds__(BT_THREADS, 1)
 #pragma unroll
       for (int k = 0; k < 2; ++k) {   // 8 columns at a time: 16 c + 8 k ..
         uint32_t lg[8], lu[8], ld[8], G[4], U[4], D[4];
-        tmem_ld8(trec + 8 * k, lg);
-        tmem_ld8(trec + 32 + 8 * k, lu);
+        if constexpr (!GL) {
+          tmem_ld8(trec + 8 * k, lg);
+          tmem_ld8(trec + 32 + 8 * k, lu);
+        }
         tmem_ld8(trec + 64 + 8 * k, ld);
         const uint32_t a = sb + o_row + (((uint32_t)(2 * c + k) ^ sw) << 4);
         lds128(a, G);
@@ -935,8 +942,11 @@ __global__ void __launch_bounds__(BT_THREADS, 1)
         }
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          const float2 gg = up2(rn2(__ffma2_rn(sg2, make_float2(__uint_as_float(lg[2 * e]), __uint_as_float(lg[2 * e + 1])), up2(G[e]))));
-          const float2 uu = up2(rn2(__ffma2_rn(su2, make_float2(__uint_as_float(lu[2 * e]), __uint_as_float(lu[2 * e + 1])), up2(U[e]))));
+          float2 gg = up2(G[e]), uu = up2(U[e]);
+          if constexpr (!GL) {   // g = bf16(gu_gate + s_g xa_g B_gate^T), u likewise
+            gg = up2(rn2(__ffma2_rn(sg2, make_float2(__uint_as_float(lg[2 * e]), __uint_as_float(lg[2 * e + 1])), gg)));
+            uu = up2(rn2(__ffma2_rn(su2, make_float2(__uint_as_float(lu[2 * e]), __uint_as_float(lu[2 * e + 1])), uu)));
+          }
           const float2 sig = sigmoid2(gg);
           const float2 sl = __fmul2_rn(gg, sig);                                 // silu(g)
           ph[4 * k + e] = rn2(__fmul2_rn(sl, uu));                                // h = bf16(silu * u)
@@ -1820,13 +1830,15 @@ extern "C" int mxm_mlp_bwd_partitions(int64_t T, int64_t N, int r, int* super_bl
 
 extern "C" int mxm_mlp_bwd_epilogue(const void* gu, const void* xs, const void* dhm, const void* dxd, const void* bg,
                                     const void* bu, const void* ad, int64_t T, int64_t N, int r, float s_g, float s_u,
-                                    void* q, void* s, void* dxa_part, void* dbg_part, void* dbu_part,
+                                    int gu_lora, void* q, void* s, void* dxa_part, void* dbg_part, void* dbu_part,
                                     void* dad_part, int super_block, int col_groups, void* stream) {
   MX_CHECK_ARG(gu && xs && dhm && dxd && bg && bu && ad && dxa_part && dbg_part && dbu_part && dad_part,
                "mxm_mlp_bwd_epilogue: null pointer");
   MX_CHECK_ARG(T >= 1 && T < (1ll << 31) && N >= 128 && N % 128 == 0 && (r == 16 || r == 32),
                "mxm_mlp_bwd_epilogue: need T >= 1, N %% 128 == 0, r in {16, 32}");
   MX_CHECK_ARG((q == nullptr) == (s == nullptr), "mxm_mlp_bwd_epilogue: q and s go together");
+  MX_CHECK_ARG(gu_lora == 0 || gu_lora == 1, "mxm_mlp_bwd_epilogue: gu_lora is 0 or 1");
+  MX_CHECK_ARG(gu_lora == 0 || r == 16, "mxm_mlp_bwd_epilogue: gu with the LoRA terms added is a rank-16 layout");
   const BwdPlan p = bwd_plan(T, N, r);
   MX_CHECK_ARG(col_groups >= p.slots && super_block == p.sb,
                "mxm_mlp_bwd_epilogue: bad partition (%d, %d): use mxm_mlp_bwd_partitions", super_block, col_groups);
@@ -1871,14 +1883,16 @@ extern "C" int mxm_mlp_bwd_epilogue(const void* gu, const void* xs, const void* 
                                   CU_TENSOR_MAP_SWIZZLE_NONE))
         return e;
     }
-    cudaError_t e = mx_smem_attr((const void*)k_mlp_bwd_tc, BT_SMEM);
-    if (e != cudaSuccess) return mx_cuda_status(e, "mlp bwd epilogue: set smem");
-    k_mlp_bwd_tc<<<p.grid, BT_THREADS, BT_SMEM, st>>>(tgu, tdh, tbg, tbu, tad, txs, tdxd, tq, (uint8_t*)s,
-                                                      (float*)dxa_part, (float*)dbg_part, (float*)dbu_part,
-                                                      (float*)dad_part, (int)T, (int)tpad, (int)N, s_g, s_u, p.per,
-                                                      q != nullptr, mx_dev_error_ptr());
-    mx_note_launch();
-    return mx_launch_status("mlp bwd epilogue");
+    auto go = [&](auto kern) -> int {
+      cudaError_t e = mx_smem_attr((const void*)kern, BT_SMEM);
+      if (e != cudaSuccess) return mx_cuda_status(e, "mlp bwd epilogue: set smem");
+      kern<<<p.grid, BT_THREADS, BT_SMEM, st>>>(tgu, tdh, tbg, tbu, tad, txs, tdxd, tq, (uint8_t*)s, (float*)dxa_part,
+                                                (float*)dbg_part, (float*)dbu_part, (float*)dad_part, (int)T,
+                                                (int)tpad, (int)N, s_g, s_u, p.per, q != nullptr, mx_dev_error_ptr());
+      mx_note_launch();
+      return mx_launch_status("mlp bwd epilogue");
+    };
+    return gu_lora ? go(k_mlp_bwd_tc<true>) : go(k_mlp_bwd_tc<false>);
   }
   const size_t smem = bwd_smem(r);
   cudaError_t e = mx_smem_attr((const void*)k_mlp_bwd<32>, smem);

@@ -128,9 +128,10 @@ def mlp_fwd(gu, xs, bg, bu, ad, s_g, s_u, write_q):
 
 
 def gemm_glu(q, sc, w, ws, xs, bg, bu, ad, s_g, s_u):
-    """gu = [x W_gate^T | x W_up^T] and, from the same GEMM tiles, the forward epilogue (MXFP8(h), xS_down):
-    mx_mm + mlp_fwd in one kernel.  q / sc: MXFP8(x) [T, H]; w / ws: W_gu codes [2N, H] and scales.
-    -> (gu [T, 2N] bf16, q_h [T, N] fp8, s_h, xS_down [T, r] bf16).  Rank 16 only."""
+    """The gate|up GEMM and, from the same tiles, the forward epilogue (MXFP8(h), xS_down): mx_mm + mlp_fwd
+    in one kernel.  q / sc: MXFP8(x) [T, H]; w / ws: W_gu codes [2N, H] and scales.
+    -> (gu [T, 2N] bf16 = [g | u] with the LoRA terms added -- the values the SwiGLU used, which the
+    backward takes with gu_lora=True --, q_h [T, N] fp8, s_h, xS_down [T, r] bf16).  Rank 16 only."""
     T, H = q.shape
     N2 = w.shape[0]
     N, R = N2 // 2, ad.shape[0]
@@ -150,7 +151,7 @@ def gemm_glu(q, sc, w, ws, xs, bg, bu, ad, s_g, s_u):
 FUSE_GLU = [True]   # gate|up GEMM + forward epilogue in one kernel (rank 16); False: two passes
 
 
-def _bwd_launch(gu, xs, dhm, dxd, bg, bu, ad, s_g, s_u, need_q, zero_slots=False):
+def _bwd_launch(gu, xs, dhm, dxd, bg, bu, ad, s_g, s_u, need_q, zero_slots=False, gu_lora=False):
     T, N2 = gu.shape
     N, R = N2 // 2, ad.shape[0]
     dev = gu.device
@@ -166,15 +167,16 @@ def _bwd_launch(gu, xs, dhm, dxd, bg, bu, ad, s_g, s_u, need_q, zero_slots=False
     dbu = torch.empty((nsb, N, R), dtype=torch.float32, device=dev)
     dad = torch.empty((nsb, R, N), dtype=torch.float32, device=dev)
     _nx.call("mxm_mlp_bwd_epilogue", _nx.ptr(gu), _nx.ptr(xs), _nx.ptr(dhm), _nx.ptr(dxd), _nx.ptr(bg), _nx.ptr(bu),
-             _nx.ptr(ad), T, N, R, float(s_g), float(s_u), _nx.ptr(q), _nx.ptr(s), _nx.ptr(dxa), _nx.ptr(dbg),
-             _nx.ptr(dbu), _nx.ptr(dad), sb, ncg, _nx.stream_of(gu))
+             _nx.ptr(ad), T, N, R, float(s_g), float(s_u), int(gu_lora), _nx.ptr(q), _nx.ptr(s), _nx.ptr(dxa),
+             _nx.ptr(dbg), _nx.ptr(dbu), _nx.ptr(dad), sb, ncg, _nx.stream_of(gu))
     return q, s, (dxa, dbg, dbu, dad, sb, ncg)
 
 
-def mlp_bwd(gu, xs, dhm, dxd, bg, bu, ad, s_g, s_u, need_q):
+def mlp_bwd(gu, xs, dhm, dxd, bg, bu, ad, s_g, s_u, need_q, gu_lora=False):
     """-> (q_dgu [T, 2N] fp8, s_dgu, [dxa_gate | dxa_up | xS_down] [T, 3R] fp32 (dxa not yet scaled by s),
-    dBg, dBu [N, R] fp32 (not scaled), dAd [R, N]) -- scripts/fused_mlp.py:235-259."""
-    q, s, (dxa, dbg, dbu, dad, sb, ncg) = _bwd_launch(gu, xs, dhm, dxd, bg, bu, ad, s_g, s_u, need_q, True)
+    dBg, dBu [N, R] fp32 (not scaled), dAd [R, N]) -- scripts/fused_mlp.py:235-259.  gu as the reference
+    passes it ([x W_gate^T | x W_up^T]); gu_lora=True: gu as gemm_glu returns it (g | u, rank 16)."""
+    q, s, (dxa, dbg, dbu, dad, sb, ncg) = _bwd_launch(gu, xs, dhm, dxd, bg, bu, ad, s_g, s_u, need_q, True, gu_lora)
     red = lambda p: p[0] if p.shape[0] == 1 else p.sum(0)  # noqa: E731  (fixed order on one device)
     return (q, s.view(_E8) if need_q else None, red(dxa), red(dbg), red(dbu), red(dad))
 
@@ -204,8 +206,9 @@ class _MLP(torch.autograd.Function):
             bdT = _cast(("T", id(bd)), lambda: bd.t().contiguous())
             ST = _cast(("T", id(S)), lambda: S.t().contiguous())
         xs, q, sc = rowdot_quant(x2, S)                                  # [T, 2R] = xa_gate | xa_up; MXFP8(x)
-        if need_out and FUSE_GLU[0] and ad.shape[0] == 16 and hold.w.is_contiguous():
-            gu, qh, sh, xsd = gemm_glu(q, sc, hold.w, hold.ws, xs, bg, bu, ad, s_g, s_u)   # one pass over gu
+        gu_lora = need_out and FUSE_GLU[0] and ad.shape[0] == 16 and hold.w.is_contiguous()
+        if gu_lora:   # one pass: gu comes back as [g | u] with the LoRA terms added
+            gu, qh, sh, xsd = gemm_glu(q, sc, hold.w, hold.ws, xs, bg, bu, ad, s_g, s_u)
             del q, sc
         else:
             gu = mxfp8.mx_mm(q, hold.w.t(), sc, hold.ws)                 # [T, 2N] gate | up
@@ -219,6 +222,7 @@ class _MLP(torch.autograd.Function):
             STATS["bỏ đầu ra"] = STATS.get("bỏ đầu ra", 0) + 1
             y = x2.new_empty(x2.shape[0], down.out_features)
         ctx.save_for_backward(x2, xs, gu, S, bg, bu, ad, bd)
+        ctx.gu_lora = gu_lora
         ctx.meta = (hold, down, (s_g, s_u, s_d), dt, lead, K, x.dtype)
         ctx.tr = (bdT, ST)   # parameter-derived transposes (not activations)
         ctx.gdt = tuple(w.dtype for w in (Ag, Au, Bd))
@@ -242,7 +246,8 @@ class _MLP(torch.autograd.Function):
         wt, wts = mxfp8.mx_wt(down)
         dhm = mxfp8.mx_mm(qd, wt.t(), sd, wts)                           # [T, N]
         del qd, sd
-        qg, sg, (dxa_p, dbg_p, dbu_p, dad_p, sb, ncg) = _bwd_launch(gu, xs, dhm, dxd, bg, bu, ad, s_g, s_u, need_x)
+        qg, sg, (dxa_p, dbg_p, dbu_p, dad_p, sb, ncg) = _bwd_launch(gu, xs, dhm, dxd, bg, bu, ad, s_g, s_u, need_x,
+                                                                    gu_lora=ctx.gu_lora)
         del dhm
         dev = gu.device
         Ag, Bg, Au, Bu, Ad, Bd = ctx.params
