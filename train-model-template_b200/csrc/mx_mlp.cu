@@ -617,7 +617,8 @@ __global__ void __launch_bounds__(32 * (bwd_cons(R) + 1), 1)
 // [256 x 16] buffers, 32-byte swizzle).  Two warps issue the MMAs (one elected lane each, descriptors
 // computed once; a small MMA costs ~50 cycles of issue, so the two streams go out side by side):
 //   * warp 18: the LoRA terms xa_gate B_gate^T, xa_up B_up^T and dxd A_down of the tile (2 halves of 128
-//     rows x 3 x 32 TMEM columns), one item ahead of the element-wise warps;
+//     rows x 3 x 32 TMEM columns; only dxd A_down when gu already holds g | u), one item ahead of the
+//     element-wise warps;
 //   * warp 16, once those warps stored the tile's dg | du | h (bf16, [256 x 32] each, the g tile's layout) in
 //     shared memory: the per-row products [dg B_gate | du B_up | h A_down^T], accumulated in TMEM over the
 //     run's tiles of the row block (2 halves x 48 columns; B_gate / B_up slices read as MN-major B), and
