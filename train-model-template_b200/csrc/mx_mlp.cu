@@ -882,7 +882,7 @@ __global__ void __launch_bounds__(BT_THREADS, 1)
     const int64_t N2 = 2 * (int64_t)N;
     const uint64_t pol = l2_evict_first();
     // column products of local tile tt (warps 0-2, TMEM lane quarters 0-2: dg, du, h columns)
-    auto drain_col = [&](int tt) -> bool {
+    auto drain_col = [&](int tt, int64_t sbt, int64_t nt0) -> bool {
       const int b = tt & 1;
       if (!mbar_wait(&colp_full[b], (uint32_t)((tt >> 1) & 1), err, MX_DEV_TIMEOUT_EPILOGUE)) return false;
       tc_fence_after();
@@ -892,8 +892,7 @@ __global__ void __launch_bounds__(BT_THREADS, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&colp_empty[b]);
-      const int itt = it_lo + tt;
-      const int64_t sbt = itt / nt, n = (int64_t)(itt % nt) * BT_BN + lane;
+      const int64_t n = nt0 + lane;
       if (warp < 2) {   // [n_blocks, N, r]: element (n, j)
         uint4* P = reinterpret_cast<uint4*>((warp == 0 ? dbg_part : dbu_part) + (sbt * N + n) * R);
 #pragma unroll
@@ -909,11 +908,17 @@ __global__ void __launch_bounds__(BT_THREADS, 1)
     uint32_t phase = 0;
     int blk = -1;
     bool ok = true;
+    // the item's row block and first column, stepped per tile (no divisions in the loop), and this row's
+    // scale-byte offset up to the column block (the scale buffer is far below 2^31 bytes)
+    int sbi = it_lo / nt, n0 = (it_lo % nt) * BT_BN;
+    int row = 0, srow = 0;
     for (int t = 0; t < cnt; ++t) {
-      const int it = it_lo + t, sbi = it / nt, n0 = (it % nt) * BT_BN;
-      const bool last = t + 1 == cnt || (it + 1) % nt == 0;
-      if (t == 0 || n0 == 0) ++blk;
-      const int64_t row = (int64_t)sbi * BT_ROWS + rl;
+      const bool last = t + 1 == cnt || n0 + BT_BN == N;
+      if (t == 0 || n0 == 0) {
+        ++blk;
+        row = sbi * BT_ROWS + rl;
+        srow = (int)mx_scale_offset(row < Tpad ? row : 0, 0, N2);
+      }
       const bool good = ok && mbar_wait(&full[stage], phase, err, MX_DEV_TIMEOUT_EPILOGUE) &&
                         mbar_wait(lora_full, (uint32_t)(t & 1), err, MX_DEV_TIMEOUT_EPILOGUE);
       if (bar_any(pid, 64, !good)) {   // both warps of the pair leave together
@@ -1001,7 +1006,7 @@ __global__ void __launch_bounds__(BT_THREADS, 1)
         }
         // the scale bytes: dg's by the thread of column half 0, du's by the other
         if (row < Tpad)
-          stg8_if_hint(s + mx_scale_offset(row, (c == 0 ? n0 : N + n0) / 32, N2), c == 0 ? eg : eu, true, pol);
+          stg8_if_hint(s + srow + (((c == 0 ? n0 : N + n0) >> 7) << 9) + ((n0 >> 5) & 3), c == 0 ? eg : eu, true, pol);
       }
       // dg | du | h into the operand tiles, once the previous tile's products have read them
       if (t > 0 && !mbar_wait(op_empty, (uint32_t)((t - 1) & 1), err, MX_DEV_TIMEOUT_EPILOGUE)) ok = false;
@@ -1017,7 +1022,7 @@ __global__ void __launch_bounds__(BT_THREADS, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(op_full);
       }
-      if (ok && warp < 3 && t > 0 && !drain_col(t - 1)) ok = false;
+      if (ok && warp < 3 && t > 0 && !drain_col(t - 1, n0 ? sbi : sbi - 1, n0 ? n0 - BT_BN : N - BT_BN)) ok = false;
       if (ok && last) {   // leaving the row block: its per-row products into this CTA's slot
         if (!mbar_wait(row_full, (uint32_t)(blk & 1), err, MX_DEV_TIMEOUT_EPILOGUE)) {
           ok = false;
@@ -1050,8 +1055,12 @@ __global__ void __launch_bounds__(BT_THREADS, 1)
         stage = 0;
         phase ^= 1;
       }
+      if ((n0 += BT_BN) == N) {
+        n0 = 0;
+        ++sbi;
+      }
     }
-    if (ok && warp < 3 && cnt > 0) drain_col(cnt - 1);
+    if (ok && warp < 3 && cnt > 0) drain_col(cnt - 1, n0 ? sbi : sbi - 1, n0 ? n0 - BT_BN : N - BT_BN);
     if (write_q && lane == 0) bulk_wait0();   // the code stores are complete
   }
   tc_fence_before();
