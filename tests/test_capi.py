@@ -63,3 +63,31 @@ def test_noalloc_chunking_fits_the_fixed_scratch():
     assert chunks(20000, 2048, 64, 1024)[1] == 32             # the cap: 16 MiB / (2048 * 64 * 4 B)
     with pytest.raises(_mxlib.MXError):
         chunks(128, 131072, 64, 148)
+
+
+def _bwd_plan(T, N, r, sms=148):
+    """The backward epilogue's partition restated (host arithmetic): row blocks of 256 rows (rank 16) or
+    176 (rank 32), 32-column tiles column-fastest, contiguous runs of ceil(items / SMs) per CTA."""
+    sb = 256 if r == 16 else 176
+    nsb = -(-(-(-T // 128) * 128) // sb)
+    nt = N // 32
+    items = nsb * nt
+    per = -(-items // sms)
+    slots = max(((b + 1) * nt - 1) // per - (b * nt) // per + 1 for b in range(nsb))
+    return sb, max(slots, 1)
+
+
+def test_bwd_partition_and_argument_checks_without_gpu():
+    """mxm_mlp_bwd_partitions agrees with the restated plan, and mxm_mlp_bwd_epilogue rejects a gu_lora
+    flag it cannot honour before touching the device."""
+    import _mxlib
+    for T, N, r in ((1, 128, 16), (300, 6144, 16), (16384, 6144, 16), (142336, 6144, 16), (10752, 3584, 16),
+                    (2049, 3584, 32), (16384, 6144, 32)):
+        assert _mxlib.mlp_bwd_partitions(T, N, r) == _bwd_plan(T, N, r), (T, N, r)
+    p = ctypes.c_void_p(256)
+    for r, gu_lora in ((32, 1), (16, 2)):
+        sb, ncg = _bwd_plan(300, 6144, r)
+        with pytest.raises(_mxlib.MXError) as ei:
+            _mxlib.call("mxm_mlp_bwd_epilogue", p, p, p, p, p, p, p, 300, 6144, r, 2.0, 2.0, gu_lora, None, None, p, p,
+                        p, p, sb, ncg, None)
+        assert "gu_lora" in str(ei.value) or "rank-16" in str(ei.value)
