@@ -1267,10 +1267,27 @@ __global__ void __launch_bounds__(32 * (RD_CONS + 1), 1)
   const uint32_t s_a = smem_u32(sA), s_b = smem_u32(sB);
   int stage = 0;
   uint32_t phase = 0;
+  // MXFP8 store targets: lanes 4i .. 4i+3 hold row 8 pass + i of the warp's 16, (block 0 | 1) x
+  // (16-element half 0 | 1) of each 64-element k box
+  const uint32_t qblk = (uint32_t)((lane >> 1) & 1), qhalf = (uint32_t)(lane & 1);
   for (int rb = blockIdx.x; rb < nrb; rb += gridDim.x) {
     float acc[NJ / 8][4];
 #pragma unroll
     for (int j = 0; j < NJ / 8; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
+    // per row block: the two rows' code pointers, store predicates and scale offsets up to the k block
+    // (stepped per k box below, no 64-bit arithmetic in the loop)
+    uint8_t* qrow[2];
+    int64_t srow[2];
+    bool qlive[2];
+    if (QUANT) {
+#pragma unroll
+      for (int pass = 0; pass < 2; ++pass) {
+        const int64_t rg_ = (int64_t)rb * RD_ROWS + warp * 16 + 8 * pass + (lane >> 2);
+        qlive[pass] = rg_ < T;
+        qrow[pass] = q + (qlive[pass] ? rg_ : 0) * ldq + 32 * qblk + 16 * qhalf;
+        srow[pass] = mx_scale_offset(rg_, 0, scols);
+      }
+    }
     bool ok = true;
     for (int kb = 0; kb < nkb; ++kb) {
       if (!mbar_wait(&full[stage], phase, err, MX_DEV_TIMEOUT_EPILOGUE)) {
@@ -1296,11 +1313,10 @@ __global__ void __launch_bounds__(32 * (RD_CONS + 1), 1)
 #pragma unroll
         for (int pass = 0; pass < 2; ++pass) {
           const uint32_t row = (uint32_t)(warp * 16 + 8 * pass + (lane >> 2));
-          const uint32_t blk = (uint32_t)((lane >> 1) & 1), half = (uint32_t)(lane & 1);
           uint32_t v[8];
 #pragma unroll
           for (int c = 0; c < 2; ++c) {
-            const uint32_t a = ab + swz<128>(row, 4 * blk + 2 * half + (uint32_t)c);
+            const uint32_t a = ab + swz<128>(row, 4 * qblk + 2 * qhalf + (uint32_t)c);
             asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
                          : "=r"(v[4 * c]), "=r"(v[4 * c + 1]), "=r"(v[4 * c + 2]), "=r"(v[4 * c + 3]) : "r"(a));
           }
@@ -1317,14 +1333,12 @@ __global__ void __launch_bounds__(32 * (RD_CONS + 1), 1)
             const float2 x0 = __fmul2_rn(up2(v[2 * i]), r2), x1 = __fmul2_rn(up2(v[2 * i + 1]), r2);
             w[i] = nan_canon4(e4m3x2_sat(x0.x, x0.y) | (e4m3x2_sat(x1.x, x1.y) << 16));
           }
-          const int64_t rg_ = (int64_t)rb * RD_ROWS + row;
-          const bool live = rg_ < T;
-          const int64_t k0 = (int64_t)kb * RD_KB;
-          stg128_if(q + (live ? rg_ : 0) * ldq + k0 + 32 * blk + 16 * half, w[0], w[1], w[2], w[3], live);
+          stg128_if(qrow[pass] + kb * RD_KB, w[0], w[1], w[2], w[3], qlive[pass]);
           // the row's two scale bytes (k-blocks 2 kb, 2 kb + 1: adjacent in the blocked layout)
           const uint32_t e1 = __shfl_xor_sync(0xffffffffu, e, 2);
+          const int kba = kb_off + 2 * kb;
           if ((lane & 3) == 0)
-            *reinterpret_cast<uint16_t*>(s + mx_scale_offset(rg_, kb_off + (k0 >> 5), scols)) = (uint16_t)(e | (e1 << 8));
+            *reinterpret_cast<uint16_t*>(s + srow[pass] + ((kba >> 2) << 9) + (kba & 3)) = (uint16_t)(e | (e1 << 8));
         }
       }
       __syncwarp();
