@@ -551,11 +551,12 @@ MX_DEV void glu_body(const CUtensorMap* tmA, const CUtensorMap* tmB, const CUten
       }
     };
     uint32_t acc_phase = 0;
+    // tile_of stepped: the chunk (its row block and first column tile) is divided out once per chunk
+    int wc = unit, wii = 0, wtm = wc / ncpr, wtn0 = (wc % ncpr) * chunk;
     for (int i = 0; i < my_tiles; ++i) {
-      int tm, tn;
-      tile_of(i, tm, tn);
+      const int tm = wtm, tn = wtn0 + wii;
       const int64_t rowb = (int64_t)tm * TM_ROWS + rank * BM;   // this CTA's first row of the tile
-      if (i % chunk == 0) {              // a new chunk: this warp's rows of xs, zeroed xS_down sums
+      if (wii == 0) {                    // a new chunk: this warp's rows of xs, zeroed xS_down sums
         ra = rowb + e * 16 + g;
         rb = ra + 8;
         const bool va = ra < M, vb = rb < M;
@@ -705,7 +706,13 @@ MX_DEV void glu_body(const CUtensorMap* tmA, const CUtensorMap* tmB, const CUten
       }
       if (lane == 0) bulk_wait_read0();   // this warp's gu stores have read the staged tile
       epi_sync();   // staged tile and slices are free for the next tile
-      if (i % chunk == chunk - 1) flush((unit + (i / chunk) * units) % ncpr);
+      if (wii == chunk - 1) flush(wc % ncpr);
+      if (++wii == chunk) {
+        wii = 0;
+        wc += units;
+        wtm = wc / ncpr;
+        wtn0 = (wc % ncpr) * chunk;
+      }
     }
     if (lane == 0) bulk_wait0();
   }
